@@ -1,0 +1,706 @@
+// extern "C" entry points declared in include/fishai_cuda.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/fishai_cuda.h"
+#include "fa_host.hpp"
+#include "fa_kernels.hpp"
+#include "gguf.hpp"
+#include "model.hpp"
+
+namespace fa {
+int synth_write(const char *path, const fa_synth_spec *s, uint64_t seed);
+uint32_t n_ff_of(uint32_t n_embd, float mult);
+}  // namespace fa
+
+using namespace fa;
+
+struct fa_gguf {
+  std::unique_ptr<Gguf> g;
+};
+struct fa_model {
+  Model m;
+  std::vector<Workspace> compat;  // per-token workspaces for multi-token forward
+};
+struct fa_kv {
+  KvCache kv;
+};
+
+namespace {
+
+#define API_CUDA(expr)                                                                     \
+  do {                                                                                     \
+    cudaError_t e_ = (expr);                                                               \
+    if (e_ != cudaSuccess) return fail(FA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define API_NULL(p) \
+  if (!(p)) return fail(FA_ERR_INVALID, std::string(__func__) + ": null argument " #p)
+
+void copy_str(const std::string &s, char *buf, size_t cap) {
+  if (!buf || !cap) return;
+  size_t n = std::min(cap - 1, s.size());
+  std::memcpy(buf, s.data(), n);
+  buf[n] = 0;
+}
+
+int check_err_flags(Model &m, const SeqState *st_dev) {
+  SeqState st;
+  API_CUDA(cudaMemcpyAsync(&st, st_dev, sizeof st, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  if (st.err & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "a bounded device wait gave up");
+  if (st.err & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
+  if (st.err & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");
+  return FA_OK;
+}
+
+int set_state(Model &m, SeqState *dst, uint32_t token, uint32_t pos, uint32_t len, uint32_t n_feed) {
+  SeqState st{};
+  st.pos = pos;
+  st.len = len;
+  st.token = token;
+  st.n_feed = n_feed;
+  API_CUDA(cudaMemcpyAsync(dst, &st, sizeof st, cudaMemcpyHostToDevice, m.stream));
+  return FA_OK;
+}
+
+void drop_graph(Model &m) {
+  if (m.graph) {
+    cudaGraphExecDestroy(m.graph);
+    m.graph = nullptr;
+  }
+}
+
+int ensure_ids(Model &m, uint32_t n) {
+  if (n <= m.ws.max_ids) return FA_OK;
+  uint32_t cap = std::max<uint32_t>(n, 4096);
+  void *p = m.dmalloc((size_t)cap * 4);
+  if (!p) return fail(FA_ERR_OOM, "ids allocation failed");
+  m.ws.ids = (uint32_t *)p;
+  m.ws.max_ids = cap;
+  drop_graph(m);
+  return FA_OK;
+}
+
+int ensure_feed(Model &m, uint32_t n) {
+  if (n <= m.ws.max_feed) return FA_OK;
+  uint32_t cap = std::max<uint32_t>(n, 4096);
+  void *p = m.dmalloc((size_t)cap * 4);
+  if (!p) return fail(FA_ERR_OOM, "feed allocation failed");
+  m.ws.feed = (uint32_t *)p;
+  m.ws.max_feed = cap;
+  drop_graph(m);
+  return FA_OK;
+}
+
+int check_seq(const fa_kv *kv, uint32_t seq, uint64_t n_more) {
+  if (seq >= kv->kv.n_seq) return fail(FA_ERR_INVALID, "sequence index out of range");
+  if ((uint64_t)kv->kv.len[seq] + n_more > kv->kv.max_ctx) return fail(FA_ERR_CONTEXT, "KV cache capacity exceeded");
+  return FA_OK;
+}
+
+int create_kv(Model &m, uint32_t n_seq, uint32_t max_ctx, int dtype, KvCache *kv) {
+  if (!n_seq || !max_ctx) return fail(FA_ERR_INVALID, "fa_kv_create: zero size");
+  if (dtype != FA_KV_F32 && dtype != FA_KV_F16) return fail(FA_ERR_INVALID, "fa_kv_create: bad dtype");
+  API_CUDA(cudaSetDevice(m.device));
+  kv->m = &m;
+  m.live_kv.insert(kv);
+  kv->n_seq = n_seq;
+  kv->max_ctx = max_ctx;
+  kv->max_pages = (max_ctx + 15) / 16;
+  kv->f16 = dtype == FA_KV_F16;
+  kv->len.assign(n_seq, 0);
+  const uint64_t pages = (uint64_t)n_seq * kv->max_pages;
+  kv->layer_stride = pages * 2 * m.cfg.n_kv_heads * 16 * m.cfg.head_dim;
+  const uint64_t bytes = kv->layer_stride * m.cfg.n_layers * (kv->f16 ? 2 : 4);
+  if (cudaMalloc(&kv->base, bytes) != cudaSuccess) return fail(FA_ERR_OOM, "KV cache allocation failed");
+  API_CUDA(cudaMemset(kv->base, 0, bytes));
+  std::vector<uint32_t> pt(pages);
+  for (uint64_t i = 0; i < pages; ++i) pt[i] = (uint32_t)i;  // static page assignment per sequence
+  if (cudaMalloc(&kv->page_table, pages * 4) != cudaSuccess) return fail(FA_ERR_OOM, "page table allocation failed");
+  API_CUDA(cudaMemcpy(kv->page_table, pt.data(), pages * 4, cudaMemcpyHostToDevice));
+  return m.ensure_rope(max_ctx + 1);
+}
+
+// reference multi-token forward: every token at `pos`, all n tokens' K/V
+// appended before attention, no mask (src/model.rs:316-455)
+int forward_compat(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, uint32_t n, uint32_t pos,
+                   float *logits, uint32_t *argmax, float *hidden) {
+  Model &m = fm->m;
+  int rc;
+  while (fm->compat.size() < n) {
+    Workspace w;
+    if ((rc = m.alloc_workspace(w))) return rc;
+    fm->compat.push_back(w);
+  }
+  const uint32_t len0 = kv->kv.len[seq], d = m.cfg.n_embd, V = m.cfg.vocab_size;
+  for (uint32_t t = 0; t < n; ++t)
+    if ((rc = set_state(m, fm->compat[t].state, tokens[t], pos, len0 + t, 0))) return rc;
+  // attention of every token sees len0 + n entries: a state with len = len0+n-1
+  Workspace &w0 = fm->compat[0];
+  SeqState *attn_state = nullptr;
+  API_CUDA(cudaMalloc(&attn_state, sizeof(SeqState)));
+  struct F {
+    void *p;
+    ~F() { cudaFree(p); }
+  } free_attn{attn_state};
+  if ((rc = set_state(m, attn_state, 0, pos, len0 + n - 1, 0))) return rc;
+  float *hid_dev = nullptr;
+  if (hidden) API_CUDA(cudaMalloc(&hid_dev, (size_t)m.cfg.n_layers * n * d * 4));
+  struct F2 {
+    void *p;
+    ~F2() { cudaFree(p); }
+  } free_hid{hid_dev};
+  for (uint32_t t = 0; t < n; ++t)
+    if ((rc = m.enqueue_embed(fm->compat[t], fm->compat[t].state))) return rc;
+  for (uint32_t l = 0; l < m.cfg.n_layers; ++l) {
+    for (uint32_t t = 0; t < n; ++t)
+      if ((rc = m.enqueue_qkv(l, fm->compat[t], kv->kv, seq, fm->compat[t].state))) return rc;
+    for (uint32_t t = 0; t < n; ++t) {
+      if ((rc = m.enqueue_attn(l, fm->compat[t], kv->kv, seq, attn_state))) return rc;
+      float *dump = hid_dev ? hid_dev + ((size_t)l * n + t) * d : nullptr;
+      if ((rc = m.enqueue_post_attn(l, fm->compat[t], fm->compat[t].state, dump))) return rc;
+    }
+  }
+  for (uint32_t t = 0; t < n; ++t) {
+    if ((rc = m.enqueue_head(fm->compat[t], fm->compat[t].state))) return rc;
+    if (logits) API_CUDA(cudaMemcpyAsync(logits + (size_t)t * V, fm->compat[t].logits, (size_t)V * 4,
+                                         cudaMemcpyDeviceToHost, m.stream));
+  }
+  if (hidden) API_CUDA(cudaMemcpyAsync(hidden, hid_dev, (size_t)m.cfg.n_layers * n * d * 4, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  for (uint32_t t = 0; t < n; ++t) {
+    if ((rc = check_err_flags(m, fm->compat[t].state))) return rc;
+    if (argmax) {
+      SeqState st;
+      API_CUDA(cudaMemcpy(&st, fm->compat[t].state, sizeof st, cudaMemcpyDeviceToHost));
+      argmax[t] = ~(uint32_t)(st.argmax_key & 0xFFFFFFFFull);
+    }
+  }
+  (void)w0;
+  kv->kv.len[seq] = len0 + n;
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fa_last_error(char *buf, size_t cap) {
+  copy_str(last_error(), buf, cap);
+  return last_error().size();
+}
+
+const char *fa_version(void) { return "fishai-b200 0.1.0 (sm_100a)"; }
+
+// ------------------------------------------------------------------ GGUF
+int fa_gguf_open(const char *path, fa_gguf **out) {
+  API_NULL(path);
+  API_NULL(out);
+  int code = FA_OK;
+  Gguf *g = Gguf::open(path, &code);
+  if (!g) return code;
+  *out = new (std::nothrow) fa_gguf();
+  if (!*out) {
+    delete g;
+    return fail(FA_ERR_OOM, "out of memory");
+  }
+  (*out)->g.reset(g);
+  return FA_OK;
+}
+void fa_gguf_close(fa_gguf *g) { delete g; }
+int fa_gguf_version(const fa_gguf *g, uint32_t *v) {
+  API_NULL(g);
+  API_NULL(v);
+  *v = g->g->version;
+  return FA_OK;
+}
+int fa_gguf_alignment(const fa_gguf *g, uint64_t *a) {
+  API_NULL(g);
+  API_NULL(a);
+  *a = g->g->alignment;
+  return FA_OK;
+}
+int fa_gguf_tensor_count(const fa_gguf *g, size_t *n) {
+  API_NULL(g);
+  API_NULL(n);
+  *n = g->g->tensors.size();
+  return FA_OK;
+}
+static void fill_tinfo(const GgufTensor &t, uint32_t *n_dims, uint64_t dims[4], uint32_t *type, uint64_t *offset) {
+  if (n_dims) *n_dims = t.n_dims;
+  if (dims)
+    for (int i = 0; i < 4; ++i) dims[i] = t.dims[i];
+  if (type) *type = t.ggml_type;
+  if (offset) *offset = t.offset;
+}
+int fa_gguf_tensor_at(const fa_gguf *g, size_t i, char *name, size_t cap, uint32_t *n_dims, uint64_t dims[4],
+                      uint32_t *type, uint64_t *offset) {
+  API_NULL(g);
+  if (i >= g->g->tensors.size()) return fail(FA_ERR_INVALID, "tensor index out of range");
+  const GgufTensor &t = g->g->tensors[i];
+  copy_str(t.name, name, cap);
+  fill_tinfo(t, n_dims, dims, type, offset);
+  return FA_OK;
+}
+int fa_gguf_tensor_info(const fa_gguf *g, const char *name, uint32_t *n_dims, uint64_t dims[4], uint32_t *type,
+                        uint64_t *offset) {
+  API_NULL(g);
+  API_NULL(name);
+  const GgufTensor *t = g->g->tensor(name);
+  if (!t) return fail(FA_ERR_INVALID, std::string("tensor not found: ") + name);
+  fill_tinfo(*t, n_dims, dims, type, offset);
+  return FA_OK;
+}
+int fa_gguf_read_tensor_data(const fa_gguf *g, const char *name, void *out, size_t cap, size_t *size) {
+  API_NULL(g);
+  API_NULL(name);
+  API_NULL(size);
+  *size = 0;
+  const GgufTensor *t = g->g->tensor(name);
+  if (!t) return fail(FA_ERR_INVALID, std::string("tensor not found: ") + name);
+  size_t n = 0;
+  const uint8_t *p = g->g->tensor_data(*t, &n);
+  if (!p) return FA_OK;
+  *size = n;
+  if (out) std::memcpy(out, p, std::min(n, cap));
+  return FA_OK;
+}
+int fa_gguf_meta_u64(const fa_gguf *g, const char *key, uint64_t *v, int *found) {
+  API_NULL(g);
+  API_NULL(key);
+  API_NULL(found);
+  uint64_t x = 0;
+  *found = g->g->meta_u64(key, &x);
+  if (v && *found) *v = x;
+  return FA_OK;
+}
+int fa_gguf_meta_i64(const fa_gguf *g, const char *key, int64_t *v, int *found) {
+  API_NULL(g);
+  API_NULL(key);
+  API_NULL(found);
+  int64_t x = 0;
+  *found = g->g->meta_i64(key, &x);
+  if (v && *found) *v = x;
+  return FA_OK;
+}
+int fa_gguf_meta_f32(const fa_gguf *g, const char *key, float *v, int *found) {
+  API_NULL(g);
+  API_NULL(key);
+  API_NULL(found);
+  float x = 0;
+  *found = g->g->meta_f32(key, &x);
+  if (v && *found) *v = x;
+  return FA_OK;
+}
+int fa_gguf_meta_bool(const fa_gguf *g, const char *key, int *v, int *found) {
+  API_NULL(g);
+  API_NULL(key);
+  API_NULL(found);
+  bool x = false;
+  *found = g->g->meta_bool(key, &x);
+  if (v && *found) *v = x;
+  return FA_OK;
+}
+int fa_gguf_meta_string(const fa_gguf *g, const char *key, char *buf, size_t cap, int *found) {
+  API_NULL(g);
+  API_NULL(key);
+  API_NULL(found);
+  std::string s;
+  *found = g->g->meta_string(key, &s);
+  if (*found) copy_str(s, buf, cap);
+  return FA_OK;
+}
+int fa_gguf_vocab_size(const fa_gguf *g, uint64_t *v, int *found) {
+  API_NULL(g);
+  API_NULL(found);
+  uint64_t x = 0;
+  *found = g->g->vocab_size(&x);
+  if (v && *found) *v = x;
+  return FA_OK;
+}
+
+// ------------------------------------------------------------ config
+int fa_config_from_gguf(const fa_gguf *g, fa_config *cfg) {
+  API_NULL(g);
+  API_NULL(cfg);
+  return config_from_gguf(*g->g, cfg);
+}
+uint32_t fa_config_n_ff(uint32_t n_embd, float mult) { return n_ff_of(n_embd, mult); }
+
+// ------------------------------------------------------------ dequant
+int fa_dequantize_device(int type, const void *bytes_dev, size_t nbytes, size_t count, float *out_dev, void *stream) {
+  API_NULL(out_dev);
+  if (!type_known(type)) return fail(FA_ERR_UNSUPPORTED, "Unsupported ggml type for dequantization: " + std::to_string(type));
+  const size_t be = block_elems(type), bb = block_bytes(type);
+  const size_t whole = nbytes / bb * be;  // elements backed by complete blocks
+  const size_t n = std::min(count, whole);
+  if (type == FA_GGML_F32 && nbytes < count * 4) return fail(FA_ERR_INVALID, "Not enough data for F32");
+  if (n && launch_dequant_native(type, bytes_dev, n, out_dev, (cudaStream_t)stream))
+    return fail(FA_ERR_CUDA, "dequant launch failed");
+  return FA_OK;
+}
+
+int fa_dequantize(int type, const void *bytes, size_t nbytes, size_t count, float *out, size_t *n_out) {
+  API_NULL(out);
+  if (!type_known(type)) return fail(FA_ERR_UNSUPPORTED, "Unsupported ggml type for dequantization: " + std::to_string(type));
+  if (type == FA_GGML_F32 && nbytes < count * 4) return fail(FA_ERR_INVALID, "Not enough data for F32");
+  const size_t be = block_elems(type), bb = block_bytes(type);
+  // the reference stops at the first incomplete block (src/quant.rs:130)
+  const size_t n = std::min(count, nbytes / bb * be);
+  if (n_out) *n_out = n;
+  if (!n) return FA_OK;
+  void *d_in = nullptr;
+  float *d_out = nullptr;
+  API_CUDA(cudaMalloc(&d_in, nbytes));
+  if (cudaMalloc(&d_out, n * 4) != cudaSuccess) {
+    cudaFree(d_in);
+    return fail(FA_ERR_OOM, "device allocation failed");
+  }
+  int rc = FA_OK;
+  if (cudaMemcpy(d_in, bytes, nbytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+      launch_dequant_native(type, d_in, n, d_out, nullptr) ||
+      cudaMemcpy(out, d_out, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = fail(FA_ERR_CUDA, std::string("dequantize failed: ") + cudaGetErrorString(cudaGetLastError()));
+  cudaFree(d_in);
+  cudaFree(d_out);
+  return rc;
+}
+
+// ------------------------------------------------------------ model
+void fa_model_opts_default(fa_model_opts *o) {
+  if (!o) return;
+  std::memset(o, 0, sizeof *o);
+  o->use_graphs = 1;
+  o->use_pdl = 1;
+  o->tp_world = 1;
+}
+
+int fa_model_load(const char *path, const fa_model_opts *opts, fa_model **out) {
+  API_NULL(path);
+  API_NULL(out);
+  fa_model_opts o;
+  if (opts) o = *opts;
+  else fa_model_opts_default(&o);
+  if (o.tp_world > 1) return fail(FA_ERR_UNSUPPORTED, "tensor parallel load goes through fa_model_load with TP support");
+  fa_model *m = new (std::nothrow) fa_model();
+  if (!m) return fail(FA_ERR_OOM, "out of memory");
+  int rc = m->m.load(path, o);
+  if (rc) {
+    std::string e = last_error();
+    delete m;
+    return fail(rc, e);
+  }
+  *out = m;
+  return FA_OK;
+}
+void fa_model_free(fa_model *m) { delete m; }
+int fa_model_config(const fa_model *m, fa_config *cfg) {
+  API_NULL(m);
+  API_NULL(cfg);
+  *cfg = m->m.cfg;
+  return FA_OK;
+}
+int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *step_bytes) {
+  API_NULL(m);
+  if (device_bytes) *device_bytes = m->m.device_bytes;
+  if (step_bytes) *step_bytes = m->m.step_bytes;
+  return FA_OK;
+}
+void *fa_model_stream(fa_model *m) { return m ? (void *)m->m.stream : nullptr; }
+
+// ------------------------------------------------------------ KV cache
+int fa_kv_create(fa_model *m, uint32_t n_seq, uint32_t max_ctx, int32_t dtype, fa_kv **out) {
+  API_NULL(m);
+  API_NULL(out);
+  fa_kv *kv = new (std::nothrow) fa_kv();
+  if (!kv) return fail(FA_ERR_OOM, "out of memory");
+  int rc = create_kv(m->m, n_seq, max_ctx, dtype, &kv->kv);
+  if (rc) {
+    std::string e = last_error();
+    delete kv;
+    return fail(rc, e);
+  }
+  *out = kv;
+  return FA_OK;
+}
+void fa_kv_free(fa_kv *kv) { delete kv; }
+int fa_kv_clear(fa_kv *kv, int32_t seq) {
+  API_NULL(kv);
+  if (seq < 0) {
+    std::fill(kv->kv.len.begin(), kv->kv.len.end(), 0u);
+    return FA_OK;
+  }
+  if ((uint32_t)seq >= kv->kv.n_seq) return fail(FA_ERR_INVALID, "sequence index out of range");
+  kv->kv.len[seq] = 0;
+  return FA_OK;
+}
+int fa_kv_seq_len(const fa_kv *kv, uint32_t seq, uint32_t *len) {
+  API_NULL(kv);
+  API_NULL(len);
+  if (seq >= kv->kv.n_seq) return fail(FA_ERR_INVALID, "sequence index out of range");
+  *len = kv->kv.len[seq];
+  return FA_OK;
+}
+int fa_kv_get(const fa_kv *kv, uint32_t seq, uint32_t layer, float *k_host, float *v_host) {
+  API_NULL(kv);
+  const KvCache &c = kv->kv;
+  if (seq >= c.n_seq) return fail(FA_ERR_INVALID, "sequence index out of range");
+  if (layer >= c.m->cfg.n_layers)
+    return fail(FA_ERR_INVALID, "KV cache layer index out of range: " + std::to_string(layer));
+  const uint32_t KVH = c.m->cfg.n_kv_heads, hd = c.m->cfg.head_dim, len = c.len[seq];
+  const uint32_t pages = (len + 15) / 16;
+  const size_t page_elems = (size_t)2 * KVH * 16 * hd, esz = c.f16 ? 2 : 4;
+  std::vector<uint8_t> buf(page_elems * esz);
+  std::vector<uint32_t> pt(c.max_pages);
+  API_CUDA(cudaMemcpy(pt.data(), c.page_table + (size_t)seq * c.max_pages, c.max_pages * 4, cudaMemcpyDeviceToHost));
+  for (uint32_t p = 0; p < pages; ++p) {
+    const uint8_t *src = (const uint8_t *)c.base + ((size_t)layer * c.layer_stride + (size_t)pt[p] * page_elems) * esz;
+    API_CUDA(cudaMemcpy(buf.data(), src, buf.size(), cudaMemcpyDeviceToHost));
+    for (uint32_t s = 0; s < 16 && p * 16 + s < len; ++s)
+      for (uint32_t h = 0; h < KVH; ++h)
+        for (uint32_t dd = 0; dd < hd; ++dd)
+          for (int isv = 0; isv < 2; ++isv) {
+            const size_t idx = kv_index(0, isv, h, s, dd, KVH, hd);
+            float v;
+            if (c.f16) v = f16_to_f32(((const uint16_t *)buf.data())[idx]);
+            else v = ((const float *)buf.data())[idx];
+            float *dst = isv ? v_host : k_host;
+            if (dst) dst[((size_t)(p * 16 + s) * KVH + h) * hd + dd] = v;
+          }
+  }
+  return FA_OK;
+}
+
+// ------------------------------------------------------------ forward
+int fa_forward(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, uint32_t n, uint32_t pos, float *logits,
+               uint32_t *argmax, float *hidden) {
+  API_NULL(fm);
+  API_NULL(kv);
+  API_NULL(tokens);
+  if (!n) return fail(FA_ERR_INVALID, "fa_forward: empty token list");
+  Model &m = fm->m;
+  int rc;
+  if ((rc = check_seq(kv, seq, n))) return rc;
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= m.cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
+  if ((rc = m.ensure_rope(pos + 1))) return rc;
+  API_CUDA(cudaSetDevice(m.device));
+  if (n > 1) return forward_compat(fm, kv, seq, tokens, n, pos, logits, argmax, hidden);
+  float *hid_dev = nullptr;
+  if (hidden) API_CUDA(cudaMalloc(&hid_dev, (size_t)m.cfg.n_layers * m.cfg.n_embd * 4));
+  struct F {
+    void *p;
+    ~F() { cudaFree(p); }
+  } free_hid{hid_dev};
+  if ((rc = set_state(m, m.ws.state, tokens[0], pos, kv->kv.len[seq], 0))) return rc;
+  if (hidden) {
+    if ((rc = m.enqueue_step(kv->kv, seq, m.ws, hid_dev))) return rc;
+  } else {
+    if ((rc = m.run_steps(kv->kv, seq, 1))) return rc;
+  }
+  if (logits)
+    API_CUDA(cudaMemcpyAsync(logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
+  if (hidden)
+    API_CUDA(cudaMemcpyAsync(hidden, hid_dev, (size_t)m.cfg.n_layers * m.cfg.n_embd * 4, cudaMemcpyDeviceToHost, m.stream));
+  SeqState st;
+  API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  if (st.err) return check_err_flags(m, m.ws.state);
+  if (argmax) argmax[0] = st.token;
+  kv->kv.len[seq] += 1;
+  return FA_OK;
+}
+
+int fa_prefill(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, uint32_t n, uint32_t start_pos,
+               float *last_logits, uint32_t *last_argmax) {
+  API_NULL(fm);
+  API_NULL(kv);
+  API_NULL(tokens);
+  if (!n) return fail(FA_ERR_INVALID, "fa_prefill: empty token list");
+  Model &m = fm->m;
+  int rc;
+  if ((rc = check_seq(kv, seq, n))) return rc;
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= m.cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
+  if ((rc = m.ensure_rope(start_pos + n))) return rc;
+  API_CUDA(cudaSetDevice(m.device));
+  if ((rc = ensure_feed(m, n)) || (rc = ensure_ids(m, n))) return rc;
+  API_CUDA(cudaMemcpyAsync(m.ws.feed, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m.stream));
+  if ((rc = set_state(m, m.ws.state, 0, start_pos, kv->kv.len[seq], n))) return rc;
+  if ((rc = m.run_steps(kv->kv, seq, n))) return rc;
+  if (last_logits)
+    API_CUDA(cudaMemcpyAsync(last_logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
+  SeqState st;
+  API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  if (st.err) return check_err_flags(m, m.ws.state);
+  if (last_argmax) *last_argmax = st.token;
+  kv->kv.len[seq] += n;
+  return FA_OK;
+}
+
+int fa_decode_greedy(fa_model *fm, fa_kv *kv, uint32_t seq, uint32_t first_token, uint32_t pos, uint32_t steps,
+                     uint32_t *ids_host) {
+  API_NULL(fm);
+  API_NULL(kv);
+  Model &m = fm->m;
+  int rc;
+  if ((rc = check_seq(kv, seq, steps))) return rc;
+  if (first_token >= m.cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
+  if ((rc = m.ensure_rope(pos + steps))) return rc;
+  API_CUDA(cudaSetDevice(m.device));
+  if ((rc = ensure_ids(m, steps))) return rc;
+  if ((rc = set_state(m, m.ws.state, first_token, pos, kv->kv.len[seq], 0))) return rc;
+  if ((rc = m.run_steps(kv->kv, seq, steps))) return rc;
+  if (ids_host) API_CUDA(cudaMemcpyAsync(ids_host, m.ws.ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  if ((rc = check_err_flags(m, m.ws.state))) return rc;
+  kv->kv.len[seq] += steps;
+  return FA_OK;
+}
+
+// ------------------------------------------------------------ generation
+int fa_generate(fa_model *fm, const fa_gen_config *cfg, const uint32_t *prompt, uint32_t n_prompt, uint32_t *out,
+                uint32_t cap, uint32_t *n_out) {
+  API_NULL(fm);
+  API_NULL(cfg);
+  API_NULL(prompt);
+  API_NULL(n_out);
+  *n_out = 0;
+  // token_ids.last().unwrap() panics on an empty prompt in the reference
+  if (!n_prompt) return fail(FA_ERR_INVALID, "fa_generate: empty prompt");
+  const fa_sampler_config &sc = cfg->sampler;
+  const bool greedy_argmax = sc.temperature == 0.0f && sc.repetition_penalty == 1.0f && sc.frequency_penalty == 0.0f &&
+                             sc.presence_penalty == 0.0f;
+  if (!greedy_argmax) return fail(FA_ERR_UNSUPPORTED, "fa_generate: only greedy decoding without penalties so far");
+  Model &m = fm->m;
+  const uint32_t P = n_prompt, steps = std::max(P, cfg->max_tokens), G = steps - P;
+  for (uint32_t i = 0; i < P; ++i)
+    if (prompt[i] >= m.cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
+  int rc;
+  fa_kv kvh;
+  if ((rc = create_kv(m, 1, steps + 1, cfg->kv_dtype, &kvh.kv))) return rc;
+  if ((rc = ensure_feed(m, P + 1)) || (rc = ensure_ids(m, steps))) return rc;
+  std::vector<uint32_t> feed(prompt, prompt + P);
+  feed.push_back(prompt[P - 1]);  // generate_step re-feeds the last prompt token (src/model.rs:656-657)
+  API_CUDA(cudaMemcpyAsync(m.ws.feed, feed.data(), feed.size() * 4, cudaMemcpyHostToDevice, m.stream));
+  if ((rc = set_state(m, m.ws.state, 0, 0, 0, G ? P + 1 : P))) return rc;
+  std::vector<uint32_t> ids(steps);
+  uint32_t done = 0;
+  bool stopped = false;
+  uint32_t n_gen = 0;
+  while (done < steps && !stopped) {
+    const uint32_t chunk = std::min<uint32_t>(steps - done, cfg->n_stop ? 32 : steps);
+    if ((rc = m.run_steps(kvh.kv, 0, chunk))) return rc;
+    API_CUDA(cudaMemcpyAsync(ids.data() + done, m.ws.ids + done, (size_t)chunk * 4, cudaMemcpyDeviceToHost, m.stream));
+    API_CUDA(cudaStreamSynchronize(m.stream));
+    for (uint32_t s = done; s < done + chunk; ++s) {
+      if (s < P) continue;  // prefill logits are discarded
+      const uint32_t t = ids[s];
+      for (uint32_t j = 0; j < cfg->n_stop; ++j)
+        if (cfg->stop_ids[j] == t) stopped = true;
+      if (stopped) break;
+      if (out && n_gen < cap) out[n_gen] = t;
+      ++n_gen;
+    }
+    done += chunk;
+  }
+  if ((rc = check_err_flags(m, m.ws.state))) return rc;
+  if (m.graph_kv == &kvh.kv) drop_graph(m);
+  *n_out = n_gen;
+  return FA_OK;
+}
+
+// ------------------------------------------------------------ sampler
+struct fa_sampler {
+  fa_sampler_config cfg;
+  uint32_t n_seq, vocab;
+};
+int fa_sampler_create(const fa_sampler_config *cfg, uint32_t n_seq, uint32_t vocab, const uint64_t *seeds,
+                      fa_sampler **out) {
+  (void)cfg;
+  (void)n_seq;
+  (void)vocab;
+  (void)seeds;
+  (void)out;
+  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+}
+void fa_sampler_free(fa_sampler *s) { delete s; }
+int fa_sample_device(fa_sampler *, const float *, uint32_t, uint32_t *, uint32_t *, void *) {
+  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+}
+int fa_sample(fa_sampler *, uint32_t, const float *, uint32_t, uint32_t *) {
+  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+}
+int fa_sampler_observe(fa_sampler *, uint32_t, uint32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
+int fa_sampler_reset(fa_sampler *, int32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
+
+// ------------------------------------------------------------ profiling
+int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, uint64_t *bytes_per_launch) {
+  API_NULL(fm);
+  API_NULL(avg_ms);
+  Model &m = fm->m;
+  if (kind < 0 || kind > 4 || !reps) return fail(FA_ERR_INVALID, "fa_profile_gemv: bad kind or reps");
+  if (kind == 4 && m.tied) return fail(FA_ERR_INVALID, "fa_profile_gemv: tied head has no GEMV");
+  API_CUDA(cudaSetDevice(m.device));
+  fa_kv kvh;
+  int rc;
+  if ((rc = create_kv(m, 1, 16, FA_KV_F32, &kvh.kv))) return rc;
+  if ((rc = set_state(m, m.ws.state, 0, 0, 0, 0))) return rc;
+  const uint32_t L = m.cfg.n_layers;
+  auto launch = [&](uint32_t i) -> int {
+    const uint32_t l = i % L;
+    switch (kind) {
+      case 0: return m.enqueue_qkv(l, m.ws, kvh.kv, 0, m.ws.state);
+      case 4: return m.enqueue_head(m.ws, m.ws.state);
+      default: {
+        const LayerW &lw = m.layers[l];
+        const GemvPlan &P = kind == 1 ? lw.o : kind == 2 ? lw.gateup : lw.down;
+        GemvParams p = m.gemv_base(P);
+        p.pro = kind == 2 ? kProRmsNorm : kProPlain;
+        p.in = kind == 1 ? m.ws.attn_out : kind == 2 ? m.ws.x : m.ws.h;
+        p.norm_w = lw.ffn_norm;
+        p.ssq = m.ws.ssq_o;
+        p.n_ssq = (uint32_t)lw.o.chunks.size();
+        p.eps = m.cfg.norm_eps;
+        p.epi = kind == 2 ? kEpiSwiglu : kEpiStore;
+        p.out = kind == 2 ? m.ws.h : m.ws.logits;  // scratch destination
+        p.state = m.ws.state;
+        return launch_gemv(p, m.pdl, m.stream) ? fail(FA_ERR_CUDA, "gemv launch failed") : FA_OK;
+      }
+    }
+  };
+  for (uint32_t i = 0; i < std::min<uint32_t>(reps, 8); ++i)
+    if ((rc = launch(i))) return rc;  // warm-up
+  cudaEvent_t e0, e1;
+  API_CUDA(cudaEventCreate(&e0));
+  API_CUDA(cudaEventCreate(&e1));
+  API_CUDA(cudaEventRecord(e0, m.stream));
+  for (uint32_t i = 0; i < reps; ++i)
+    if ((rc = launch(i))) return rc;
+  API_CUDA(cudaEventRecord(e1, m.stream));
+  API_CUDA(cudaEventSynchronize(e1));
+  float ms = 0.0f;
+  API_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *avg_ms = ms / reps;
+  if (bytes_per_launch) {
+    const LayerW &lw = m.layers[0];
+    const GemvPlan &P = kind == 0 ? lw.qkv : kind == 1 ? lw.o : kind == 2 ? lw.gateup : kind == 3 ? lw.down : m.head;
+    *bytes_per_launch = P.native_bytes;
+  }
+  return check_err_flags(m, m.ws.state);
+}
+
+// ------------------------------------------------------------ synth
+int fa_synth_write(const char *path, const fa_synth_spec *spec, uint64_t seed) { return synth_write(path, spec, seed); }
+
+}  // extern "C"

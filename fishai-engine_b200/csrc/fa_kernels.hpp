@@ -1,0 +1,153 @@
+// Kernel parameter blocks and launchers (host-callable, defined in *.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fa_layout.hpp"
+
+namespace fa {
+
+// Error flags written by device code (host reads them after a step).
+enum : uint32_t {
+  kErrNone = 0,
+  kErrWaitTimeout = 1u << 0,  // a bounded mbarrier wait gave up
+  kErrBadToken = 1u << 1,     // token id >= vocab
+  kErrContext = 1u << 2,      // position beyond the KV capacity / RoPE table
+};
+
+// Per-sequence decode state kept in device memory so a captured CUDA graph
+// can be replayed step after step without host updates.
+// The reference keeps RoPE position and cache length apart: forward(pos)
+// rotates with `pos` but always appends to the end of the cache
+// (src/model.rs:367-374), so both are tracked.
+struct SeqState {
+  uint32_t pos;        // RoPE position of the token being processed
+  uint32_t len;        // KV entries already stored (write index of this token)
+  uint32_t token;      // token to process when the feed is exhausted
+  uint32_t step;       // steps completed (index into ids)
+  uint32_t fed;        // feed entries consumed
+  uint32_t n_feed;     // feed length
+  uint32_t err;        // kErr* flags raised on the device
+  uint32_t pad;
+  unsigned long long argmax_key;  // (float_key(max logit) << 32) | ~index
+};
+
+// ---- GEMV prologue / epilogue modes ----
+enum : int {
+  kProPlain = 0,    // x = in[k]
+  kProRmsNorm = 1,  // x = in[k] * (1/sqrt(sum(ssq)/n + eps)) * norm_w[k]      (src/tensor.rs:280-290)
+};
+enum : int {
+  kEpiStore = 0,    // y[col] = v
+  kEpiResid = 1,    // resid[col] += v ; ssq partial of the new resid       (src/model.rs:401, :423)
+  kEpiQkv = 2,      // RoPE(q,k) (src/model.rs:367-368), q -> qbuf, k/v -> KV cache at pos (src/kv_cache.rs:50-54)
+  kEpiSwiglu = 3,   // h[n] = silu(gate[n]) * up[n]                         (src/model.rs:413-417)
+  kEpiLogits = 4,   // logits[col] = v ; running argmax in SeqState          (src/model.rs:436-452)
+};
+
+struct KvView {
+  void *base;            // layer-0 base; layer l at base + l * layer_stride (elements)
+  uint64_t layer_stride; // elements per layer
+  const uint32_t *page_table;  // [n_seq][max_pages]
+  uint32_t max_pages;
+  uint32_t n_kv, head_dim;
+  int f16;               // 1: __half storage, 0: float
+};
+// element offset of (page, k/v, kv head, slot, dim) inside one layer
+__host__ __device__ inline uint64_t kv_index(uint32_t page, int is_v, uint32_t h, uint32_t slot, uint32_t d,
+                                             uint32_t n_kv, uint32_t hd) {
+  return ((((uint64_t)page * 2 + (uint64_t)is_v) * n_kv + h) * 16 + slot) * hd + d;
+}
+
+struct GemvParams {
+  const uint8_t *w;
+  const ChunkDesc *chunks;
+  uint32_t n_chunks;
+  const CtaRange *ranges;  // [n_ctas]
+  const uint16_t *contrib; // per chunk: indices of the CTAs with rows in it (ChunkDesc::contrib_off)
+  uint32_t n_ctas;
+  uint32_t max_chunks_per_cta;
+  uint32_t K, K8;
+  uint32_t CW;             // lane geometry: 256, 512 or 1024
+  uint32_t stage_bytes;    // capacity of one pipeline stage (multiple of 16)
+  uint32_t x_slot;         // floats of x (and norm weight) per stage slot
+  float *part;             // [n_ctas * max_chunks_per_cta][CW] chunk partials
+  uint32_t *counters;      // [n_chunks] arrival counters (zero between launches)
+  // prologue (inputs padded with zeros to K8)
+  int pro;
+  const float *in;         // [K8]
+  const float *norm_w;     // [K8]
+  const float *ssq;        // sum-of-squares partials of `in`
+  uint32_t n_ssq;
+  float eps;
+  // epilogue
+  int epi;
+  float *out;              // store / swiglu / logits / qkv(q part)
+  float *resid;            // kEpiResid
+  float *ssq_out;          // kEpiResid: [n_chunks]
+  // qkv
+  uint32_t q_dim, kv_dim;
+  const float *rope_tab;   // [max_pos][head_dim]: cos,sin pairs
+  uint32_t rope_max;       // positions in rope_tab
+  KvView kv;
+  uint32_t seq, layer;
+  SeqState *state;         // pos / argmax
+};
+
+// one-time per-device kernel attributes (dynamic smem)
+int gemv_init();
+int launch_gemv(const GemvParams &p, bool pdl, cudaStream_t st);
+size_t gemv_smem_bytes(const GemvParams &p);
+
+struct AttnParams {
+  const float *q;          // [H*hd]
+  KvView kv;
+  uint32_t seq, layer;
+  uint32_t n_heads, splits;
+  float scale;             // 1/sqrt(hd), computed as the reference does
+  float *part;             // [H][splits][2 + hd] split partials
+  uint32_t *counters;      // [n_kv] arrival counters (zero between launches)
+  float *out;              // [H*hd] combined attention output
+  SeqState *state;         // T = len + 1
+};
+int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st);
+
+struct EmbedParams {
+  const uint8_t *emb;      // native [V][d] blocks
+  const uint32_t *feed;    // tokens to feed first (state->n_feed of them)
+  int type;
+  uint32_t d, vocab;
+  float *x;                // [d] residual stream
+  float *ssq_out;          // [n_ssq] partial sums of squares
+  uint32_t n_ssq;          // CTAs
+  SeqState *state;
+};
+int launch_embed(const EmbedParams &p, bool pdl, cudaStream_t st);
+
+// step bookkeeping: token <- argmax, ids[step] = token, pos++, len++, step++, fed++
+int launch_step_end(SeqState *state, uint32_t *ids, uint32_t max_ids, bool pdl, cudaStream_t st);
+
+// tied output head (no output.weight): logits[j] = dot(xn, E[j]) with E
+// native [V][d] (transpose_2d + matmul, src/model.rs:447-452)
+struct TiedHeadParams {
+  const uint8_t *emb;
+  int type;
+  uint32_t d, vocab;
+  const float *x;          // residual stream [d] (normalised in-kernel)
+  const float *norm_w;
+  const float *ssq;
+  uint32_t n_ssq;
+  float eps;
+  float *logits;
+  SeqState *state;
+};
+int launch_tied_head(const TiedHeadParams &p, bool pdl, cudaStream_t st);
+
+// dequantisation / layout
+int launch_dequant_native(int type, const void *data, uint64_t count, float *out, cudaStream_t st);
+int launch_repack(int type, const void *src_a, const void *src_b, uint32_t K, uint32_t N, uint32_t CW, void *dst,
+                  uint64_t dst_off, cudaStream_t st);
+int launch_unpack(int type, const void *src, uint64_t src_off, uint32_t K, uint32_t N, uint32_t CW, float *out,
+                  cudaStream_t st);
+
+}  // namespace fa

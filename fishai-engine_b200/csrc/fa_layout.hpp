@@ -1,0 +1,80 @@
+// Device weight layout ("chunked row groups"), shared by host and device.
+//
+// A GGUF projection W is read by the reference as W[K][N] with N contiguous
+// (tensor::matmul, src/tensor.rs:244-258), so its quant blocks run along N.
+// On the device each weight is split into column chunks of width <= CW; a
+// chunk stores its rows in groups of 8 consecutive rows.  One group holds
+// exactly the native bytes of those 8 rows x w columns (no byte is added or
+// re-quantised), regrouped so that "lane" j of a warp finds the codes of its
+// 32 columns [32j, 32j+32) as one contiguous 16-byte (4-bit types) or 32-byte
+// (Q8_0) run, and the group size is a multiple of 16 bytes:
+//
+//   Q4_0 (blk 32):  codes  r*w/2 + 16j     (byte i: col i low nibble, col i+16 high nibble)
+//                   d      4w + (r*w/32 + j)*2               f16
+//   Q8_0 (blk 32):  codes  r*w + 32j       (byte i: col i, int8)
+//                   d      8w + (r*w/32 + j)*2               f16
+//   Q4_K (blk 256): codes  r*w/2 + 16j     (as Q4_0)
+//                   header 4w + (r*w/256 + s)*16             native d, dmin, scales[12]
+//   Q6_K (blk 256): ql     r*w/2 + 16j     (low 4 bits, as Q4_0)
+//                   qh     4w + r*w/4 + 8j (byte i: cols i, i+8, i+16, i+24 at bits 0-1,2-3,4-5,6-7)
+//                   scales 6w + r*w/16 + 2j   int8, cols [0,16) then [16,32)
+//                   d      8*(13w/16) + (r*w/256 + s)*2      f16
+//   F16:            r*2w + 64j ;   F32:  r*4w + 128j
+//
+// (r = row within the group, s = super-block within the row, j = 32-column
+// lane.)  Group bytes = 8 x native row bytes, a multiple of 16, so every
+// range of whole groups can be moved with one 1-D bulk TMA copy.
+#pragma once
+#include <stdint.h>
+
+#ifndef FA_HD
+#ifdef __CUDACC__
+#define FA_HD __host__ __device__
+#else
+#define FA_HD
+#endif
+#endif
+
+namespace fa {
+
+enum : int { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ4_1 = 3, kQ5_0 = 6, kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14 };
+
+// bytes of one row of `w` columns in native GGML blocks
+FA_HD inline uint32_t native_row_bytes(int type, uint32_t w) {
+  switch (type) {
+    case kF32: return 4 * w;
+    case kF16: return 2 * w;
+    case kQ4_0: return w / 32 * 18;
+    case kQ8_0: return w / 32 * 34;
+    case kQ4_K: return w / 256 * 144;
+    case kQ6_K: return w / 256 * 210;
+    default: return 0;
+  }
+}
+FA_HD inline uint32_t group_bytes(int type, uint32_t w) { return 8 * native_row_bytes(type, w); }
+FA_HD inline uint32_t type_block(int type) {
+  return (type == kQ4_K || type == kQ6_K) ? 256u : (type == kF32 || type == kF16) ? 1u : 32u;
+}
+FA_HD inline bool gemv_type_supported(int type) {
+  return type == kF32 || type == kF16 || type == kQ4_0 || type == kQ8_0 || type == kQ4_K || type == kQ6_K;
+}
+
+// One column chunk of a GEMV launch.  All chunks of a launch share K.
+struct ChunkDesc {
+  uint64_t offset;   // byte offset of the chunk's first row group in the weight buffer
+  uint32_t gbytes;   // bytes per 8-row group
+  uint16_t type;     // ggml type
+  uint16_t width;    // columns (multiple of 32; of 256 for K-quants)
+  uint32_t out_col;  // first output column of the chunk in the launch's output space
+  uint32_t contrib_off;  // first entry of this chunk in the launch's contributor list
+  uint32_t n_contrib;    // CTAs that contribute partial sums to this chunk
+  uint32_t pad;
+};
+
+// Contiguous range of (chunk, 8-row group) units streamed by one CTA:
+// from (c0, g0) inclusive to (c1, g1) exclusive, chunk-major order.
+struct CtaRange {
+  uint32_t c0, g0, c1, g1;
+};
+
+}  // namespace fa

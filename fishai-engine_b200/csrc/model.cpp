@@ -1,0 +1,620 @@
+// Host runtime: GGUF -> device weights (native blocks re-laid into column
+// chunks), workspaces, KV cache, and the per-token kernel sequence of
+// ModelWeights::forward (src/model.rs:316-455).
+#include "model.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace fa {
+
+#define CUDA_TRY(expr)                                                                    \
+  do {                                                                                    \
+    cudaError_t e_ = (expr);                                                              \
+    if (e_ != cudaSuccess) return fail(FA_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+static const char *kLayerNames[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                     "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+
+uint32_t n_ff_of(uint32_t n_embd, float mult) {  // src/model.rs:66-70
+  float raw = (float)n_embd * mult;
+  uint64_t r = (raw != raw || raw <= 0.0f) ? 0 : (uint64_t)raw;
+  return (uint32_t)((r + 255) / 256 * 256);
+}
+
+// ModelConfig::from_gguf, src/model.rs:92-180
+int config_from_gguf(const Gguf &g, fa_config *c) {
+  std::memset(c, 0, sizeof *c);
+  std::string arch;
+  if (!g.meta_string("general.architecture", &arch)) return fail(FA_ERR_GGUF, "missing general.architecture");
+  if (arch != "llama" && arch != "qwen2" && arch != "mistral" && arch != "phi")
+    return fail(FA_ERR_UNSUPPORTED, "unsupported model architecture: " + arch);
+  uint64_t v;
+  auto req = [&](const char *suffix, uint32_t *dst) {
+    std::string k = arch + "." + suffix;
+    if (!g.meta_u64(k, &v)) return fail(FA_ERR_GGUF, "missing " + k);
+    *dst = (uint32_t)v;
+    return FA_OK;
+  };
+  int rc;
+  if ((rc = req("block_count", &c->n_layers))) return rc;
+  if ((rc = req("attention.head_count", &c->n_heads))) return rc;
+  c->n_kv_heads = g.meta_u64(arch + ".attention.head_count_kv", &v) ? (uint32_t)v : c->n_heads;
+  if ((rc = req("embedding_length", &c->n_embd))) return rc;
+  if ((rc = req("context_length", &c->context_len))) return rc;
+  if (g.vocab_size(&v)) {
+    c->vocab_size = (uint32_t)v;
+  } else if (const GgufTensor *t = g.tensor("token_embd.weight")) {
+    c->vocab_size = c->n_embd ? (uint32_t)(t->nelement() / c->n_embd) : 0;
+  } else {
+    return fail(FA_ERR_GGUF, "cannot determine vocab size");
+  }
+  if (c->n_heads == 0) return fail(FA_ERR_GGUF, "attention.head_count is 0");
+  c->head_dim = c->n_embd / c->n_heads;
+  if (c->head_dim == 0) return fail(FA_ERR_GGUF, "n_embd not divisible by head count");
+  float f;
+  c->ffn_dim_multiplier = g.meta_f32(arch + ".feed_forward_length", &f) ? f / (float)c->n_embd : 2.667f;
+  c->norm_eps = g.meta_f32(arch + ".attention.layer_norm_rms_epsilon", &f) ? f : 1e-5f;
+  c->rope_base = g.meta_f32(arch + ".rope.freq_base", &f) ? f : 10000.0f;
+  c->rope_freq_dim = c->head_dim / 2;
+  c->n_ff = n_ff_of(c->n_embd, c->ffn_dim_multiplier);
+  c->n_ff_used = c->n_ff;
+  c->tied_output = g.tensor("output.weight") == nullptr;
+  return FA_OK;
+}
+
+void *Model::dmalloc(size_t bytes) {
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
+  allocs.push_back(p);
+  device_bytes += bytes;
+  return p;
+}
+
+Model::~Model() {
+  for (KvCache *kv : live_kv) kv->m = nullptr;  // caches may outlive the model
+  if (graph) cudaGraphExecDestroy(graph);
+  if (device >= 0) cudaSetDevice(device);
+  for (void *p : allocs) cudaFree(p);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+namespace {
+
+struct TensorRef {
+  const GgufTensor *t = nullptr;
+  const uint8_t *data = nullptr;
+  size_t nbytes = 0;
+  int type = 0;
+  uint64_t nelem = 0;
+};
+
+int get_tensor(const Gguf &g, const std::string &name, TensorRef *r) {
+  r->t = g.tensor(name);
+  if (!r->t) return fail(FA_ERR_GGUF, "tensor not found: " + name);
+  r->type = (int)r->t->ggml_type;
+  r->nelem = r->t->nelement();
+  if (!type_known(r->type)) return fail(FA_ERR_UNSUPPORTED, "unsupported ggml type " + std::to_string(r->type) + " for " + name);
+  r->data = g.tensor_data(*r->t, &r->nbytes);
+  if (!r->data) return fail(FA_ERR_GGUF, "tensor '" + name + "' has no data");
+  if (r->nbytes < type_nbytes(r->type, r->nelem / block_elems(r->type) * block_elems(r->type)))
+    return fail(FA_ERR_GGUF, "tensor '" + name + "' is truncated");
+  return FA_OK;
+}
+
+uint64_t chunked_bytes(int type, uint32_t K8, uint32_t N, uint32_t CW) {
+  uint64_t total = 0;
+  for (uint32_t c0 = 0; c0 < N; c0 += CW) total += (uint64_t)(K8 / 8) * group_bytes(type, std::min(CW, N - c0));
+  return total;
+}
+
+uint32_t pick_cw(int type, uint32_t N, bool paired) {
+  uint32_t cw = 256;
+  if (N >= 1024 * 37) cw = 1024;
+  else if (N >= 512 * 37) cw = 512;
+  if (paired && (type == kQ4_K || type == kQ6_K)) cw = std::max(cw, 512u);
+  return cw;
+}
+
+}  // namespace
+
+// One GEMV launch covering `parts` (tensors sharing K).  paired: parts[0]
+// and parts[1] are gate/up interleaved per chunk.
+static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts, const std::vector<uint32_t> &out_base,
+                      bool paired, uint32_t K, const std::vector<uint32_t> &widths, uint32_t CW, void *staging,
+                      void *staging2) {
+  P.K = K;
+  P.K8 = (K + 7) / 8 * 8;
+  P.CW = CW;
+  P.native_bytes = 0;
+  // sizes
+  std::vector<uint64_t> region;
+  uint64_t total = 0;
+  const size_t nparts = paired ? 1 : parts.size();
+  for (size_t i = 0; i < nparts; ++i) {
+    const uint32_t N = paired ? 2 * widths[0] : widths[i];
+    region.push_back(total);
+    total += (chunked_bytes(parts[i].type, P.K8, N, CW) + 255) / 256 * 256;
+  }
+  uint8_t *buf = (uint8_t *)m.dmalloc(total);
+  if (!buf) return fail(FA_ERR_OOM, "device allocation of " + std::to_string(total) + " weight bytes failed");
+  P.w = buf;
+  uint32_t max_gb = 0;
+  for (size_t i = 0; i < nparts; ++i) {
+    const TensorRef &a = parts[i];
+    const uint32_t N = widths[i];
+    const uint64_t nb = type_nbytes(a.type, (uint64_t)K * N);
+    CUDA_TRY(cudaMemcpyAsync(staging, a.data, nb, cudaMemcpyHostToDevice, m.stream));
+    P.native_bytes += nb;
+    if (paired) {
+      const TensorRef &b = parts[1];
+      if (b.type != a.type) return fail(FA_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a ggml type");
+      CUDA_TRY(cudaMemcpyAsync(staging2, b.data, nb, cudaMemcpyHostToDevice, m.stream));
+      P.native_bytes += nb;
+      if (launch_repack(a.type, staging, staging2, K, N, CW, buf, region[i], m.stream))
+        return fail(FA_ERR_CUDA, "repack launch failed");
+    } else {
+      if (launch_repack(a.type, staging, nullptr, K, N, CW, buf, region[i], m.stream))
+        return fail(FA_ERR_CUDA, "repack launch failed");
+    }
+    CUDA_TRY(cudaStreamSynchronize(m.stream));
+    const uint32_t Nv = paired ? 2 * N : N;
+    for (uint32_t c = 0, c0 = 0; c0 < Nv; c0 += CW, ++c) {
+      ChunkDesc d{};
+      const uint32_t w = std::min(CW, Nv - c0);
+      d.offset = region[i] + (uint64_t)c * (P.K8 / 8) * group_bytes(a.type, CW);
+      d.gbytes = group_bytes(a.type, w);
+      d.type = (uint16_t)a.type;
+      d.width = (uint16_t)w;
+      d.out_col = out_base[i] + c0;
+      P.chunks.push_back(d);
+      max_gb = std::max(max_gb, d.gbytes);
+    }
+  }
+  P.stage_bytes = std::max<uint32_t>(16384, (max_gb + 15) / 16 * 16);
+  uint32_t max_ng = 1;
+  for (const ChunkDesc &d : P.chunks) max_ng = std::max(max_ng, P.stage_bytes / d.gbytes);
+  P.x_slot = 8 * max_ng;
+  // stream-K split: CTA i streams bytes [i*B/P, (i+1)*B/P) of the chunk-major
+  // (chunk, 8-row group) sequence, rounded to whole groups
+  const uint32_t G = P.K8 / 8, nc = (uint32_t)P.chunks.size();
+  std::vector<uint64_t> start(nc + 1, 0);
+  for (uint32_t c = 0; c < nc; ++c) start[c + 1] = start[c] + (uint64_t)G * P.chunks[c].gbytes;
+  const uint64_t B = start[nc];
+  uint64_t units = (uint64_t)G * nc;
+  P.n_ctas = (uint32_t)std::min<uint64_t>(m.n_sm, units);
+  auto unit_at = [&](uint64_t b, uint32_t *c, uint32_t *g) {
+    uint32_t k = 0;
+    while (k + 1 < nc && start[k + 1] <= b) ++k;
+    uint64_t gg = (b - start[k] + P.chunks[k].gbytes / 2) / P.chunks[k].gbytes;
+    if (gg >= G) {
+      *c = k + 1;
+      *g = 0;
+    } else {
+      *c = k;
+      *g = (uint32_t)gg;
+    }
+  };
+  P.ranges.resize(P.n_ctas);
+  for (uint32_t i = 0; i < P.n_ctas; ++i) {
+    CtaRange &r = P.ranges[i];
+    unit_at(B * i / P.n_ctas, &r.c0, &r.g0);
+    unit_at(B * (i + 1) / P.n_ctas, &r.c1, &r.g1);
+  }
+  // contributors of each chunk (CTAs with a non-empty range touching it);
+  // rounding can leave some CTAs empty, so the list is explicit
+  std::vector<std::vector<uint16_t>> who(nc);
+  P.max_chunks_per_cta = 1;
+  for (uint32_t i = 0; i < P.n_ctas; ++i) {
+    const CtaRange &r = P.ranges[i];
+    if (r.c0 > r.c1 || (r.c0 == r.c1 && r.g0 >= r.g1)) continue;  // empty range
+    const uint32_t last = r.g1 > 0 ? r.c1 : r.c1 - 1;
+    P.max_chunks_per_cta = std::max(P.max_chunks_per_cta, last - r.c0 + 1);
+    for (uint32_t c = r.c0; c <= last; ++c) who[c].push_back((uint16_t)i);
+  }
+  P.contrib.clear();
+  for (uint32_t c = 0; c < nc; ++c) {
+    if (who[c].empty() || P.n_ctas > 65535) return fail(FA_ERR_INVALID, "GEMV split failed");
+    P.chunks[c].contrib_off = (uint32_t)P.contrib.size();
+    P.chunks[c].n_contrib = (uint32_t)who[c].size();
+    P.contrib.insert(P.contrib.end(), who[c].begin(), who[c].end());
+  }
+  P.d_chunks = (ChunkDesc *)m.dmalloc(P.chunks.size() * sizeof(ChunkDesc));
+  P.d_ranges = (CtaRange *)m.dmalloc(P.ranges.size() * sizeof(CtaRange));
+  P.d_contrib = (uint16_t *)m.dmalloc(P.contrib.size() * sizeof(uint16_t));
+  if (!P.d_chunks || !P.d_ranges || !P.d_contrib) return fail(FA_ERR_OOM, "GEMV table allocation failed");
+  CUDA_TRY(cudaMemcpy(P.d_contrib, P.contrib.data(), P.contrib.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(P.d_chunks, P.chunks.data(), P.chunks.size() * sizeof(ChunkDesc), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(P.d_ranges, P.ranges.data(), P.ranges.size() * sizeof(CtaRange), cudaMemcpyHostToDevice));
+  m.part_floats = std::max<size_t>(m.part_floats, (size_t)P.n_ctas * P.max_chunks_per_cta * P.CW);
+  m.max_chunks = std::max<uint32_t>(m.max_chunks, nc);
+  return FA_OK;
+}
+
+int Model::ensure_rope(uint32_t max_pos) {
+  if (max_pos <= rope_max) return FA_OK;
+  const uint32_t hd = cfg.head_dim, half = hd / 2;
+  std::vector<float> tab((size_t)max_pos * hd);
+  std::vector<float> freq(half);
+  for (uint32_t i = 0; i < half; ++i)  // rope_emb, src/tensor.rs:386-397
+    freq[i] = 1.0f / std::pow(cfg.rope_base, (2.0f * (float)i) / (float)hd);
+  for (uint32_t p = 0; p < max_pos; ++p)
+    for (uint32_t i = 0; i < half; ++i) {
+      const float ang = (float)p * freq[i];
+      tab[(size_t)p * hd + 2 * i] = std::cos(ang);
+      tab[(size_t)p * hd + 2 * i + 1] = std::sin(ang);
+    }
+  float *d = (float *)dmalloc(tab.size() * sizeof(float));
+  if (!d) return fail(FA_ERR_OOM, "rope table allocation failed");
+  CUDA_TRY(cudaMemcpy(d, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice));
+  rope_tab = d;
+  rope_max = max_pos;
+  if (graph) {  // captured graphs hold the old table pointer
+    cudaGraphExecDestroy(graph);
+    graph = nullptr;
+  }
+  return FA_OK;
+}
+
+int Model::load(const std::string &path, const fa_model_opts &o) {
+  device = o.device;
+  pdl = o.use_pdl != 0;
+  graphs = o.use_graphs != 0;
+  CUDA_TRY(cudaSetDevice(device));
+  CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  if (gemv_init()) return fail(FA_ERR_CUDA, "GEMV kernel attribute setup failed");
+  CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
+  int code = FA_OK;
+  gguf.reset(Gguf::open(path, &code));
+  if (!gguf) return code;
+  const Gguf &g = *gguf;
+  int rc = config_from_gguf(g, &cfg);
+  if (rc) return rc;
+  const uint32_t d = cfg.n_embd, H = cfg.n_heads, KVH = cfg.n_kv_heads, hd = cfg.head_dim;
+  if (KVH == 0 || H % KVH) return fail(FA_ERR_UNSUPPORTED, "head_count must be a multiple of head_count_kv");
+  if (H * hd != d || hd % 2 || hd > 128 || (H / KVH != 1 && H / KVH != 2 && H / KVH != 4 && H / KVH != 8)) return fail(FA_ERR_UNSUPPORTED, "unsupported head geometry");
+  const uint32_t qd = H * hd, kvd = KVH * hd;
+  TensorRef gate0;
+  if ((rc = get_tensor(g, "blk.0.ffn_gate.weight", &gate0))) return rc;
+  cfg.n_ff_used = (uint32_t)(gate0.nelem / d);
+  const uint32_t F = cfg.n_ff_used, V = cfg.vocab_size, L = cfg.n_layers;
+  // validate every tensor first
+  std::vector<std::vector<TensorRef>> lt(L, std::vector<TensorRef>(9));
+  size_t max_native = 0;
+  for (uint32_t l = 0; l < L; ++l)
+    for (int j = 0; j < 9; ++j) {
+      if ((rc = get_tensor(g, "blk." + std::to_string(l) + "." + kLayerNames[j] + ".weight", &lt[l][j]))) return rc;
+      max_native = std::max(max_native, lt[l][j].nbytes);
+    }
+  const uint64_t expect[9] = {d, (uint64_t)d * qd, (uint64_t)d * kvd, (uint64_t)d * kvd, (uint64_t)qd * d,
+                              d, (uint64_t)d * F, (uint64_t)d * F, (uint64_t)F * d};
+  const uint32_t widths[9] = {d, qd, kvd, kvd, d, d, F, F, d};
+  for (uint32_t l = 0; l < L; ++l)
+    for (int j = 0; j < 9; ++j) {
+      const TensorRef &t = lt[l][j];
+      if (t.nelem != expect[j])
+        return fail(FA_ERR_GGUF, "tensor blk." + std::to_string(l) + "." + kLayerNames[j] + " has " +
+                                     std::to_string(t.nelem) + " elements, expected " + std::to_string(expect[j]));
+      if (j != 0 && j != 5) {
+        if (!gemv_type_supported(t.type))
+          return fail(FA_ERR_UNSUPPORTED, std::string("ggml type not supported for projections: ") + std::to_string(t.type));
+        if (widths[j] % type_block(t.type)) return fail(FA_ERR_UNSUPPORTED, "projection width not block aligned");
+      }
+    }
+  TensorRef temb, onorm, out;
+  if ((rc = get_tensor(g, "token_embd.weight", &temb))) return rc;
+  if ((rc = get_tensor(g, "output_norm.weight", &onorm))) return rc;
+  if (temb.nelem != (uint64_t)V * d) return fail(FA_ERR_GGUF, "token_embd.weight size mismatch");
+  if (d % block_elems(temb.type)) return fail(FA_ERR_UNSUPPORTED, "embedding rows not block aligned");
+  tied = cfg.tied_output != 0;
+  if (!tied) {
+    if ((rc = get_tensor(g, "output.weight", &out))) return rc;
+    if (out.nelem != (uint64_t)V * d) return fail(FA_ERR_GGUF, "output.weight size mismatch");
+    if (!gemv_type_supported(out.type) || V % type_block(out.type))
+      return fail(FA_ERR_UNSUPPORTED, "output.weight type/width not supported");
+    max_native = std::max(max_native, out.nbytes);
+  }
+  void *staging = nullptr, *staging2 = nullptr;
+  CUDA_TRY(cudaMalloc(&staging, max_native));
+  CUDA_TRY(cudaMalloc(&staging2, max_native));
+  struct Free {
+    void *a, *b;
+    ~Free() {
+      cudaFree(a);
+      cudaFree(b);
+    }
+  } free_staging{staging, staging2};
+
+  auto upload_f32 = [&](const TensorRef &t, float **dst) -> int {
+    *dst = (float *)dmalloc((t.nelem + 8) * sizeof(float));  // read in whole 8-row groups
+    if (!*dst) return fail(FA_ERR_OOM, "norm allocation failed");
+    CUDA_TRY(cudaMemset(*dst, 0, (t.nelem + 8) * sizeof(float)));
+    CUDA_TRY(cudaMemcpyAsync(staging, t.data, type_nbytes(t.type, t.nelem), cudaMemcpyHostToDevice, stream));
+    if (launch_dequant_native(t.type, staging, t.nelem, *dst, stream)) return fail(FA_ERR_CUDA, "dequant launch failed");
+    CUDA_TRY(cudaStreamSynchronize(stream));
+    return FA_OK;
+  };
+
+  layers.resize(L);
+  step_bytes = 0;
+  for (uint32_t l = 0; l < L; ++l) {
+    LayerW &lw = layers[l];
+    auto &T = lt[l];
+    if ((rc = upload_f32(T[0], &lw.attn_norm))) return rc;
+    if ((rc = upload_f32(T[5], &lw.ffn_norm))) return rc;
+    if ((rc = build_plan(*this, lw.qkv, {T[1], T[2], T[3]}, {0, qd, qd + kvd}, false, d, {qd, kvd, kvd}, 256, staging,
+                         staging2)))
+      return rc;
+    if ((rc = build_plan(*this, lw.o, {T[4]}, {0}, false, qd, {d}, pick_cw(T[4].type, d, false), staging, staging2)))
+      return rc;
+    if ((rc = build_plan(*this, lw.gateup, {T[6], T[7]}, {0}, true, d, {F}, pick_cw(T[6].type, 2 * F, true), staging,
+                         staging2)))
+      return rc;
+    if ((rc = build_plan(*this, lw.down, {T[8]}, {0}, false, F, {d}, pick_cw(T[8].type, d, false), staging, staging2)))
+      return rc;
+    step_bytes += lw.qkv.native_bytes + lw.o.native_bytes + lw.gateup.native_bytes + lw.down.native_bytes;
+    step_bytes += type_nbytes(T[0].type, d) + type_nbytes(T[5].type, d);
+  }
+  if ((rc = upload_f32(onorm, &out_norm))) return rc;
+  step_bytes += type_nbytes(onorm.type, d);
+  emb_type = temb.type;
+  emb = dmalloc(type_nbytes(temb.type, temb.nelem));
+  if (!emb) return fail(FA_ERR_OOM, "embedding allocation failed");
+  CUDA_TRY(cudaMemcpy(emb, temb.data, type_nbytes(temb.type, temb.nelem), cudaMemcpyHostToDevice));
+  step_bytes += type_nbytes(temb.type, d);  // one embedding row per token
+  if (!tied) {
+    if ((rc = build_plan(*this, head, {out}, {0}, false, d, {V}, pick_cw(out.type, V, false), staging, staging2)))
+      return rc;
+    step_bytes += head.native_bytes;
+  } else {
+    step_bytes += type_nbytes(temb.type, temb.nelem);
+  }
+  // numerics constants computed on the host exactly as the reference does
+  attn_scale = 1.0f / std::sqrt((float)hd);  // src/tensor.rs:486
+  if ((rc = ensure_rope(std::max<uint32_t>(cfg.context_len, 16)))) return rc;
+  part = (float *)dmalloc(part_floats * sizeof(float));
+  counters = (uint32_t *)dmalloc((size_t)max_chunks * sizeof(uint32_t));
+  if (!part || !counters) return fail(FA_ERR_OOM, "GEMV scratch allocation failed");
+  CUDA_TRY(cudaMemset(counters, 0, (size_t)max_chunks * sizeof(uint32_t)));
+  if ((rc = alloc_workspace(ws))) return rc;
+  gguf.reset();  // host mapping no longer needed
+  return FA_OK;
+}
+
+// ---------------------------------------------------------------------------
+KvCache::~KvCache() {
+  if (m) {
+    cudaSetDevice(m->device);
+    m->live_kv.erase(this);
+    if (m->graph_kv == this) {
+      if (m->graph) cudaGraphExecDestroy(m->graph);
+      m->graph = nullptr;
+      m->graph_kv = nullptr;
+    }
+  }
+  cudaFree(base);
+  cudaFree(page_table);
+}
+
+KvView KvCache::view() const {
+  KvView v;
+  v.base = base;
+  v.layer_stride = layer_stride;
+  v.page_table = page_table;
+  v.max_pages = max_pages;
+  v.n_kv = m->cfg.n_kv_heads;
+  v.head_dim = m->cfg.head_dim;
+  v.f16 = f16;
+  return v;
+}
+
+GemvParams Model::gemv_base(const GemvPlan &P) const {
+  GemvParams p{};
+  p.w = P.w;
+  p.chunks = P.d_chunks;
+  p.n_chunks = (uint32_t)P.chunks.size();
+  p.ranges = P.d_ranges;
+  p.contrib = P.d_contrib;
+  p.n_ctas = P.n_ctas;
+  p.max_chunks_per_cta = P.max_chunks_per_cta;
+  p.K = P.K;
+  p.K8 = P.K8;
+  p.CW = P.CW;
+  p.stage_bytes = P.stage_bytes;
+  p.x_slot = P.x_slot;
+  p.part = part;
+  p.counters = counters;
+  return p;
+}
+
+int Model::enqueue_embed(Workspace &w, SeqState *st) {
+  EmbedParams ep{};
+  ep.emb = (const uint8_t *)emb;
+  ep.feed = w.feed;
+  ep.type = emb_type;
+  ep.d = cfg.n_embd;
+  ep.vocab = cfg.vocab_size;
+  ep.x = w.x;
+  ep.ssq_out = w.ssq_e;
+  ep.n_ssq = embed_ctas;
+  ep.state = st;
+  return launch_embed(ep, pdl, stream) ? fail(FA_ERR_CUDA, "embed launch failed") : FA_OK;
+}
+
+int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
+  const LayerW &lw = layers[l];
+  GemvParams p = gemv_base(lw.qkv);
+  p.pro = kProRmsNorm;
+  p.in = w.x;
+  p.norm_w = lw.attn_norm;
+  p.ssq = l == 0 ? w.ssq_e : w.ssq_d;
+  p.n_ssq = l == 0 ? embed_ctas : (uint32_t)layers[l - 1].down.chunks.size();
+  p.eps = cfg.norm_eps;
+  p.epi = kEpiQkv;
+  p.out = w.q;
+  p.q_dim = cfg.n_heads * cfg.head_dim;
+  p.kv_dim = cfg.n_kv_heads * cfg.head_dim;
+  p.rope_tab = rope_tab;
+  p.rope_max = rope_max;
+  p.kv = kv.view();
+  p.seq = seq;
+  p.layer = l;
+  p.state = st;
+  return launch_gemv(p, pdl, stream) ? fail(FA_ERR_CUDA, "qkv gemv launch failed") : FA_OK;
+}
+
+int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
+  AttnParams ap{};
+  ap.q = w.q;
+  ap.kv = kv.view();
+  ap.seq = seq;
+  ap.layer = l;
+  ap.n_heads = cfg.n_heads;
+  ap.splits = attn_splits;
+  ap.scale = attn_scale;
+  ap.part = w.attn_part;
+  ap.counters = w.attn_cnt;
+  ap.out = w.attn_out;
+  ap.state = st;
+  return launch_attention(ap, pdl, stream) ? fail(FA_ERR_CUDA, "attention launch failed") : FA_OK;
+}
+
+int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump) {
+  const LayerW &lw = layers[l];
+  GemvParams p = gemv_base(lw.o);
+  p.pro = kProPlain;
+  p.in = w.attn_out;
+  p.epi = kEpiResid;
+  p.resid = w.x;
+  p.ssq_out = w.ssq_o;
+  p.state = st;
+  if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "o gemv launch failed");
+  p = gemv_base(lw.gateup);
+  p.pro = kProRmsNorm;
+  p.in = w.x;
+  p.norm_w = lw.ffn_norm;
+  p.ssq = w.ssq_o;
+  p.n_ssq = (uint32_t)lw.o.chunks.size();
+  p.eps = cfg.norm_eps;
+  p.epi = kEpiSwiglu;
+  p.out = w.h;
+  p.state = st;
+  if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "gate/up gemv launch failed");
+  p = gemv_base(lw.down);
+  p.pro = kProPlain;
+  p.in = w.h;
+  p.epi = kEpiResid;
+  p.resid = w.x;
+  p.ssq_out = w.ssq_d;
+  p.state = st;
+  if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "down gemv launch failed");
+  if (hidden_dump)
+    CUDA_TRY(cudaMemcpyAsync(hidden_dump, w.x, cfg.n_embd * 4, cudaMemcpyDeviceToDevice, stream));
+  return FA_OK;
+}
+
+int Model::enqueue_head(Workspace &w, SeqState *st) {
+  const uint32_t L = cfg.n_layers;
+  const float *ssq_in = L ? w.ssq_d : w.ssq_e;
+  const uint32_t n_ssq = L ? (uint32_t)layers[L - 1].down.chunks.size() : embed_ctas;
+  if (!tied) {
+    GemvParams p = gemv_base(head);
+    p.pro = kProRmsNorm;
+    p.in = w.x;
+    p.norm_w = out_norm;
+    p.ssq = ssq_in;
+    p.n_ssq = n_ssq;
+    p.eps = cfg.norm_eps;
+    p.epi = kEpiLogits;
+    p.out = w.logits;
+    p.state = st;
+    return launch_gemv(p, pdl, stream) ? fail(FA_ERR_CUDA, "head gemv launch failed") : FA_OK;
+  }
+  TiedHeadParams tp{};
+  tp.emb = (const uint8_t *)emb;
+  tp.type = emb_type;
+  tp.d = cfg.n_embd;
+  tp.vocab = cfg.vocab_size;
+  tp.x = w.x;
+  tp.norm_w = out_norm;
+  tp.ssq = ssq_in;
+  tp.n_ssq = n_ssq;
+  tp.eps = cfg.norm_eps;
+  tp.logits = w.logits;
+  tp.state = st;
+  return launch_tied_head(tp, pdl, stream) ? fail(FA_ERR_CUDA, "tied head launch failed") : FA_OK;
+}
+
+int Model::enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump) {
+  int rc;
+  if ((rc = enqueue_embed(w, w.state))) return rc;
+  for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+    if ((rc = enqueue_qkv(l, w, kv, seq, w.state))) return rc;
+    if ((rc = enqueue_attn(l, w, kv, seq, w.state))) return rc;
+    if ((rc = enqueue_post_attn(l, w, w.state, hidden_dump ? hidden_dump + (size_t)l * cfg.n_embd : nullptr))) return rc;
+  }
+  if ((rc = enqueue_head(w, w.state))) return rc;
+  if (launch_step_end(w.state, w.ids, w.max_ids, pdl, stream)) return fail(FA_ERR_CUDA, "step_end launch failed");
+  return FA_OK;
+}
+
+int Model::alloc_workspace(Workspace &w) {
+  const uint32_t d = cfg.n_embd, qd = cfg.n_heads * cfg.head_dim;
+  const uint32_t L = cfg.n_layers;
+  w.x = (float *)dmalloc(((size_t)d + 8) * 4);  // +8: inputs are read in whole 8-row groups
+  w.q = (float *)dmalloc(qd * 4);
+  w.h = (float *)dmalloc(((size_t)cfg.n_ff_used + 8) * 4);
+  w.logits = (float *)dmalloc((size_t)cfg.vocab_size * 4);
+  w.attn_part = (float *)dmalloc((size_t)cfg.n_heads * attn_splits * (2 + cfg.head_dim) * 4);
+  w.attn_out = (float *)dmalloc(((size_t)qd + 8) * 4);
+  w.attn_cnt = (uint32_t *)dmalloc(cfg.n_kv_heads * 4);
+  w.ssq_e = (float *)dmalloc(embed_ctas * 4);
+  w.ssq_o = (float *)dmalloc((L ? layers[0].o.chunks.size() : 1) * 4);
+  w.ssq_d = (float *)dmalloc((L ? layers[0].down.chunks.size() : 1) * 4);
+  w.state = (SeqState *)dmalloc(sizeof(SeqState));
+  if (!w.x || !w.q || !w.h || !w.logits || !w.attn_part || !w.attn_out || !w.attn_cnt || !w.ssq_e || !w.ssq_o ||
+      !w.ssq_d || !w.state)
+    return fail(FA_ERR_OOM, "workspace allocation failed");
+  CUDA_TRY(cudaMemset(w.state, 0, sizeof(SeqState)));
+  CUDA_TRY(cudaMemset(w.attn_cnt, 0, cfg.n_kv_heads * 4));
+  CUDA_TRY(cudaMemset(w.x, 0, ((size_t)d + 8) * 4));
+  CUDA_TRY(cudaMemset(w.h, 0, ((size_t)cfg.n_ff_used + 8) * 4));
+  CUDA_TRY(cudaMemset(w.attn_out, 0, ((size_t)qd + 8) * 4));
+  return FA_OK;
+}
+
+int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
+  if (!graphs) {
+    for (uint32_t i = 0; i < n; ++i) {
+      int rc = enqueue_step(kv, seq, ws, nullptr);
+      if (rc) return rc;
+    }
+    return FA_OK;
+  }
+  if (!graph || graph_kv != &kv || graph_seq != seq) {
+    if (graph) {
+      cudaGraphExecDestroy(graph);
+      graph = nullptr;
+    }
+    CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(kv, seq, ws, nullptr);
+    cudaGraph_t gr = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(stream, &gr);
+    if (rc) {
+      if (gr) cudaGraphDestroy(gr);
+      return rc;
+    }
+    if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&graph, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(ce));
+    graph_kv = &kv;
+    graph_seq = seq;
+  }
+  for (uint32_t i = 0; i < n; ++i) CUDA_TRY(cudaGraphLaunch(graph, stream));
+  return FA_OK;
+}
+
+}  // namespace fa

@@ -1,0 +1,111 @@
+// Host runtime of the device token loop: model weights in device memory,
+// KV cache, per-sequence workspaces and the enqueue of one decode step.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "fa_host.hpp"
+#include "fa_kernels.hpp"
+#include "gguf.hpp"
+
+namespace fa {
+
+struct GemvPlan {
+  std::vector<ChunkDesc> chunks;
+  std::vector<CtaRange> ranges;
+  std::vector<uint16_t> contrib;
+  ChunkDesc *d_chunks = nullptr;
+  CtaRange *d_ranges = nullptr;
+  uint16_t *d_contrib = nullptr;
+  const uint8_t *w = nullptr;
+  uint32_t K = 0, K8 = 0, CW = 256, stage_bytes = 16384, x_slot = 64;
+  uint32_t n_ctas = 0, max_chunks_per_cta = 1;
+  uint64_t native_bytes = 0;  // algorithmic bytes (native GGML blocks)
+};
+
+struct LayerW {
+  GemvPlan qkv, o, gateup, down;
+  float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct Workspace {
+  float *x = nullptr, *q = nullptr, *h = nullptr, *logits = nullptr, *attn_part = nullptr, *attn_out = nullptr;
+  uint32_t *attn_cnt = nullptr;
+  float *ssq_e = nullptr, *ssq_o = nullptr, *ssq_d = nullptr;
+  float *hidden = nullptr;     // optional per-layer dump target
+  SeqState *state = nullptr;
+  uint32_t *ids = nullptr;     // generated ids (device)
+  uint32_t max_ids = 0;
+  uint32_t *feed = nullptr;    // tokens fed before argmax continuation (device)
+  uint32_t max_feed = 0;
+};
+
+struct KvCache;
+
+struct Model {
+  fa_config cfg{};
+  int device = 0;
+  bool pdl = true, graphs = true;
+  cudaStream_t stream = nullptr;
+  std::unique_ptr<Gguf> gguf;
+  std::vector<LayerW> layers;
+  GemvPlan head;
+  bool tied = false;
+  void *emb = nullptr;
+  int emb_type = 0;
+  float *out_norm = nullptr;
+  float *rope_tab = nullptr;
+  uint32_t rope_max = 0;
+  uint32_t attn_splits = 32;
+  int n_sm = 148;
+  float *part = nullptr;         // GEMV chunk partials, shared by every launch
+  uint32_t *counters = nullptr;  // GEMV chunk arrival counters
+  size_t part_floats = 0;
+  uint32_t max_chunks = 0;
+  uint32_t embed_ctas = 16;
+  float attn_scale = 1.0f;
+  Workspace ws;                 // single-sequence decode workspace
+  std::vector<void *> allocs;   // every device allocation, freed at teardown
+  std::set<KvCache *> live_kv;  // caches created on this model (detached at teardown)
+  uint64_t device_bytes = 0, step_bytes = 0;
+  // decode-step graph cache
+  cudaGraphExec_t graph = nullptr;
+  const KvCache *graph_kv = nullptr;
+  uint32_t graph_seq = 0;
+
+  ~Model();
+  int load(const std::string &path, const fa_model_opts &o);
+  int ensure_rope(uint32_t max_pos);
+  // pieces of one token step (embed -> layers -> head -> step_end)
+  int enqueue_embed(Workspace &w, SeqState *st);
+  int enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
+  int enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
+  int enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump);
+  int enqueue_head(Workspace &w, SeqState *st);
+  int enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump);
+  int alloc_workspace(Workspace &w);
+  // run `n` steps (graph replays when enabled)
+  int run_steps(const KvCache &kv, uint32_t seq, uint32_t n);
+  void *dmalloc(size_t bytes);
+  GemvParams gemv_base(const GemvPlan &P) const;
+};
+
+struct KvCache {
+  Model *m = nullptr;
+  void *base = nullptr;
+  uint32_t *page_table = nullptr;
+  uint32_t n_seq = 0, max_ctx = 0, max_pages = 0;
+  int f16 = 0;
+  uint64_t layer_stride = 0;  // elements
+  std::vector<uint32_t> len;  // positions stored per sequence
+  ~KvCache();
+  KvView view() const;
+};
+
+int config_from_gguf(const Gguf &g, fa_config *cfg);
+
+}  // namespace fa

@@ -1,0 +1,232 @@
+/*
+ * fishai_cuda.h — C ABI of the B200 (sm_100a) token loop that replaces the
+ * CPU forward pass of the fishai-engine crate.
+ *
+ * Every entry point returns an int status (FA_OK = 0, negative = error) and
+ * takes plain pointers and sizes.  Pointers named *_host are host memory
+ * owned by the caller; the library owns all device memory it allocates.
+ * A handle is not thread-safe: one thread (one stream) per model/kv/sampler.
+ * fa_last_error() returns the message of the calling thread's last failure.
+ *
+ * Each declaration names the reference item (file:line inside the reference
+ * crate) whose behaviour it provides.
+ */
+#ifndef FISHAI_CUDA_H
+#define FISHAI_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define FA_OK 0
+#define FA_ERR_INVALID (-1)      /* bad argument (reference: panics on misuse) */
+#define FA_ERR_GGUF (-2)         /* unreadable / corrupt GGUF (src/gguf.rs:438-561 Err) */
+#define FA_ERR_UNSUPPORTED (-3)  /* ggml type or architecture not supported */
+#define FA_ERR_OOM (-4)          /* device or host allocation failed */
+#define FA_ERR_CUDA (-5)         /* CUDA runtime error */
+#define FA_ERR_NCCL (-6)         /* collective error */
+#define FA_ERR_CONTEXT (-7)      /* KV cache full: context overflow */
+#define FA_ERR_TIMEOUT (-8)      /* a bounded device wait gave up */
+
+/* Copies the calling thread's last error message; returns its full length. */
+size_t fa_last_error(char *buf, size_t cap);
+/* Library version string. */
+const char *fa_version(void);
+
+/* ggml type ids (src/quant.rs:17-29) */
+#define FA_GGML_F32 0
+#define FA_GGML_F16 1
+#define FA_GGML_Q4_0 2
+#define FA_GGML_Q4_1 3
+#define FA_GGML_Q5_0 6
+#define FA_GGML_Q8_0 8
+#define FA_GGML_Q4_K 12
+#define FA_GGML_Q6_K 14
+
+/* ------------------------------------------------------------------ GGUF */
+typedef struct fa_gguf fa_gguf;
+
+/* GGUFFile::open (src/gguf.rs:438-561): mmap, header, metadata, tensor
+ * table, data offset aligned to general.alignment (default 32). */
+int fa_gguf_open(const char *path, fa_gguf **out);
+void fa_gguf_close(fa_gguf *g);
+int fa_gguf_version(const fa_gguf *g, uint32_t *version);
+int fa_gguf_alignment(const fa_gguf *g, uint64_t *alignment);
+int fa_gguf_tensor_count(const fa_gguf *g, size_t *count);
+/* tensor_names / tensor_info (src/gguf.rs:623-640): by index */
+int fa_gguf_tensor_at(const fa_gguf *g, size_t i, char *name, size_t name_cap, uint32_t *n_dims,
+                      uint64_t dims[4], uint32_t *ggml_type, uint64_t *offset);
+/* tensor_info by name; FA_ERR_INVALID if absent */
+int fa_gguf_tensor_info(const fa_gguf *g, const char *name, uint32_t *n_dims, uint64_t dims[4],
+                        uint32_t *ggml_type, uint64_t *offset);
+/* read_tensor_data (src/gguf.rs:645-672): byte size by the next-offset rule;
+ * copies min(size, cap) bytes when out_host != NULL; *size = 0 when empty */
+int fa_gguf_read_tensor_data(const fa_gguf *g, const char *name, void *out_host, size_t cap, size_t *size);
+/* metadata_u64 / _i64 / _f32 / _bool / _string (src/gguf.rs:570-614):
+ * *found = 0 when the key is absent or has another type */
+int fa_gguf_meta_u64(const fa_gguf *g, const char *key, uint64_t *v, int *found);
+int fa_gguf_meta_i64(const fa_gguf *g, const char *key, int64_t *v, int *found);
+int fa_gguf_meta_f32(const fa_gguf *g, const char *key, float *v, int *found);
+int fa_gguf_meta_bool(const fa_gguf *g, const char *key, int *v, int *found);
+int fa_gguf_meta_string(const fa_gguf *g, const char *key, char *buf, size_t cap, int *found);
+/* vocab_size (src/gguf.rs:748-758) */
+int fa_gguf_vocab_size(const fa_gguf *g, uint64_t *v, int *found);
+
+/* -------------------------------------------------------- ModelConfig */
+typedef struct {
+  uint32_t n_layers, n_heads, n_kv_heads, head_dim, n_embd, vocab_size, context_len;
+  float ffn_dim_multiplier, norm_eps, rope_base;
+  uint32_t rope_freq_dim;
+  uint32_t n_ff;        /* ModelConfig::n_ff() exactly as the reference computes it */
+  uint32_t n_ff_used;   /* width of the ffn tensors actually loaded */
+  int32_t tied_output;  /* 1 when output.weight is absent (embedding transpose) */
+} fa_config;
+
+/* ModelConfig::from_gguf (src/model.rs:92-180) */
+int fa_config_from_gguf(const fa_gguf *g, fa_config *cfg);
+/* ModelConfig::n_ff (src/model.rs:66-70) */
+uint32_t fa_config_n_ff(uint32_t n_embd, float ffn_dim_multiplier);
+
+/* ------------------------------------------------------- dequantisation */
+/* quant::dequantize (src/quant.rs:312-338), run on the device: host bytes
+ * in, host f32 out.  Supports F32, F16, Q4_0 (high nibble first), Q4_1,
+ * Q5_0, Q8_0 and the K-quants Q4_K, Q6_K.  *n_out may be < count when the
+ * data is short, as in the reference. */
+int fa_dequantize(int ggml_type, const void *bytes_host, size_t nbytes, size_t count, float *out_host,
+                  size_t *n_out);
+/* same on device buffers, enqueued on `stream` (cudaStream_t or NULL) */
+int fa_dequantize_device(int ggml_type, const void *bytes_dev, size_t nbytes, size_t count, float *out_dev,
+                         void *stream);
+
+/* ---------------------------------------------------------------- model */
+typedef struct fa_model fa_model;
+typedef struct {
+  int32_t device;       /* CUDA device ordinal */
+  int32_t use_graphs;   /* capture the decode step in a CUDA graph (default 1) */
+  int32_t use_pdl;      /* programmatic dependent launch between kernels (default 1) */
+  int32_t tp_rank, tp_world;  /* tensor parallel rank/world (1 = no TP) */
+  const void *nccl_id;  /* 128-byte ncclUniqueId when tp_world > 1 */
+} fa_model_opts;
+void fa_model_opts_default(fa_model_opts *o);
+
+/* GGUFFile::open + ModelConfig::from_gguf + ModelWeights::load_from_gguf
+ * (src/model.rs:252-298): weights are uploaded once in their native GGML
+ * blocks and re-laid in device memory into the column-chunk layout the
+ * kernels stream (same bytes per block). */
+int fa_model_load(const char *path, const fa_model_opts *opts, fa_model **out);
+void fa_model_free(fa_model *m);
+int fa_model_config(const fa_model *m, fa_config *cfg);
+/* bytes of weights resident on the device, and the algorithmic bytes one
+ * decode step streams (all weight tensors + one embedding row) */
+int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *step_bytes);
+/* the stream the model enqueues on (cudaStream_t) */
+void *fa_model_stream(fa_model *m);
+
+/* ------------------------------------------------------------- KV cache */
+typedef struct fa_kv fa_kv;
+#define FA_KV_F32 0
+#define FA_KV_F16 1
+/* KVCache::new (src/kv_cache.rs:27-40), device resident and paged:
+ * n_seq sequences, each up to max_ctx positions, pages of 16 positions. */
+int fa_kv_create(fa_model *m, uint32_t n_seq, uint32_t max_ctx, int32_t dtype, fa_kv **out);
+void fa_kv_free(fa_kv *kv);
+/* KVCache::clear (src/kv_cache.rs:98-103); seq < 0 clears every sequence */
+int fa_kv_clear(fa_kv *kv, int32_t seq);
+/* KVCache::seq_len_with_dim (src/kv_cache.rs:90-96) */
+int fa_kv_seq_len(const fa_kv *kv, uint32_t seq, uint32_t *len);
+/* KVCache::get (src/kv_cache.rs:66-69): k/v rows [0, len) of one layer as
+ * f32 [len][n_kv*head_dim]; FA_ERR_INVALID for a bad layer (the reference panics) */
+int fa_kv_get(const fa_kv *kv, uint32_t seq, uint32_t layer, float *k_host, float *v_host);
+
+/* -------------------------------------------------------------- forward */
+/* ModelWeights::forward (src/model.rs:316-455), reference semantics: all n
+ * tokens at position `pos`, no causal mask, KV appended for every token.
+ * logits_host: n*vocab floats or NULL; argmax_host: n ids or NULL (first
+ * index of the maximum logit); hidden_host: n_layers*n*n_embd residual
+ * values after each layer, or NULL. */
+int fa_forward(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t pos,
+               float *logits_host, uint32_t *argmax_host, float *hidden_host);
+/* Causal prefill: token t at position start_pos+t attends to positions
+ * [0, start_pos+t].  Equal to n single-token fa_forward calls.
+ * last_logits_host: vocab floats of the last token or NULL. */
+int fa_prefill(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t start_pos,
+               float *last_logits_host, uint32_t *last_argmax_host);
+
+/* ------------------------------------------------------------- sampling */
+typedef struct {
+  float temperature;            /* 0 = greedy */
+  uint32_t top_k;               /* 0 = off */
+  float top_p;                  /* 0 < p < 1 enables the reference's fixed-0.999 nucleus cut */
+  float repetition_penalty;     /* 1 = off */
+  float frequency_penalty, presence_penalty;
+} fa_sampler_config;
+typedef struct fa_sampler fa_sampler;
+/* Sampler::new (src/sampling.rs:95-104): n_seq independent samplers,
+ * sequence i draws its categorical uniforms from Philox4x32-10 keyed by
+ * seeds_host[i] (counter = its sample index). */
+int fa_sampler_create(const fa_sampler_config *cfg, uint32_t n_seq, uint32_t vocab, const uint64_t *seeds_host,
+                      fa_sampler **out);
+void fa_sampler_free(fa_sampler *s);
+/* Sampler::sample (src/sampling.rs:110-152) on device logits [n_seq][vocab]
+ * (or the first n rows); ids written to ids_dev (device) and, if non-NULL,
+ * ids_host. */
+int fa_sample_device(fa_sampler *s, const float *logits_dev, uint32_t n, uint32_t *ids_dev, uint32_t *ids_host,
+                     void *stream);
+/* Sampler::sample on host logits (copies in and out; the /api/sample path) */
+int fa_sample(fa_sampler *s, uint32_t seq, const float *logits_host, uint32_t vocab, uint32_t *id_host);
+/* Sampler::observe_token / reset (src/sampling.rs:155-165) */
+int fa_sampler_observe(fa_sampler *s, uint32_t seq, uint32_t token);
+int fa_sampler_reset(fa_sampler *s, int32_t seq);
+
+/* ----------------------------------------------------------- generation */
+typedef struct {
+  uint32_t max_tokens;          /* includes the prompt, as in src/model.rs:683-686 */
+  fa_sampler_config sampler;
+  const uint32_t *stop_ids; uint32_t n_stop;
+  uint64_t seed;
+  int32_t kv_dtype;             /* FA_KV_F32 (reference values) or FA_KV_F16 */
+} fa_gen_config;
+
+/* GenerationState::generate (src/model.rs:638-674): prefill, re-feed the
+ * last prompt token, then decode until max_tokens (prompt included) or a
+ * stop id.  Only token ids cross PCIe.  *n_out = generated ids. */
+int fa_generate(fa_model *m, const fa_gen_config *cfg, const uint32_t *prompt_host, uint32_t n_prompt,
+                uint32_t *out_host, uint32_t cap, uint32_t *n_out);
+
+/* Decode driver for benchmarks and the bench harness: after a prefill of
+ * `seq` in `kv`, run `steps` greedy decode steps starting from token
+ * `first_token` at position `pos` entirely on the device (CUDA graph per
+ * step), writing the ids to ids_host.  Used to time steady-state decode. */
+int fa_decode_greedy(fa_model *m, fa_kv *kv, uint32_t seq, uint32_t first_token, uint32_t pos, uint32_t steps,
+                     uint32_t *ids_host);
+
+/* Kernel timing for the roofline report: launches the decode GEMV of one
+ * kind (0 qkv, 1 attn_output, 2 ffn gate+up, 3 ffn_down, 4 output head)
+ * `reps` times, cycling through the layers so the weights stream from HBM
+ * (every layer's weights together exceed L2), and returns the average
+ * device time per launch (CUDA events on the model stream) and the
+ * algorithmic bytes one launch streams (native GGML block bytes). */
+int fa_profile_gemv(fa_model *m, int32_t kind, uint32_t reps, float *avg_ms, uint64_t *bytes_per_launch);
+
+/* ------------------------------------------------------ synthetic GGUF */
+typedef struct {
+  uint32_t n_layers, n_embd, n_heads, n_kv_heads, n_ff, vocab, context_len;
+  float rope_base, norm_eps, sigma;
+  int32_t type_embd, type_q, type_k, type_v, type_o, type_gate, type_up, type_down;
+  int32_t type_out;             /* -1: no output.weight (tied embedding head) */
+  uint32_t threads;             /* 0 = all cores */
+} fa_synth_spec;
+/* Writes a llama-architecture GGUF v3 with weights N(0, sigma) drawn from
+ * Philox4x32-10 (key = seed, tensor index) + Box-Muller, quantised by the
+ * reference's own Q8_0/Q4_0 rules (src/quant.rs:393-471) or this library's
+ * Q4_K/Q6_K encoders; norms are 1.0 in F32.  Metadata keys use the types
+ * the reference reads (feed_forward_length as FLOAT32). */
+int fa_synth_write(const char *path, const fa_synth_spec *spec, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

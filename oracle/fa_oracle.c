@@ -17,6 +17,7 @@
 #include <string.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
+#include <time.h>
 #include <unistd.h>
 
 static void set_err(char *err, size_t errlen, const char *fmt, ...) {
@@ -1275,6 +1276,37 @@ int or_forward(or_model *m, const uint32_t *tokens, size_t n, size_t pos, or_kv 
 int or_prefill(or_model *m, const uint32_t *tokens, size_t n, size_t pos0, or_kv *kv,
                float *last_logits, float *hidden) {
   return forward_impl(m, tokens, n, pos0, kv, last_logits, hidden, 1, 1, 1);
+}
+
+/* CPU-baseline sample: the matmuls of one layer in the reference's i-j-p
+ * order (src/tensor.rs:244-258) on f32 weights dequantised beforehand (the
+ * reference dequantises at load, src/model.rs:252-298).  Returns seconds
+ * spent in the matmuls for one token; *macs = multiply-adds performed. */
+double or_time_layer(or_model *m, size_t layer, double *macs) {
+  const or_config *c = &m->cfg;
+  size_t d = c->n_embd, qd = c->n_heads * c->head_dim, kvd = c->n_kv_heads * c->head_dim, F = c->n_ff_used;
+  const or_tensor *L = &m->layers[layer * T_PER_LAYER];
+  const int ids[7] = {T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN};
+  const size_t Ks[7] = {d, d, d, qd, d, d, F}, Ns[7] = {qd, kvd, kvd, d, F, F, d};
+  float *w[7];
+  for (int i = 0; i < 7; ++i) {
+    w[i] = (float *)malloc(Ks[i] * Ns[i] * sizeof(float));
+    tensor_slice(&L[ids[i]], 0, Ks[i] * Ns[i], w[i]);
+  }
+  float *x = (float *)malloc(F * sizeof(float)), *y = (float *)malloc((F > qd ? F : qd) * sizeof(float));
+  for (size_t i = 0; i < F; ++i) x[i] = 0.01f * (float)((i * 37) % 101) - 0.5f;
+  struct timespec t0, t1;
+  clock_gettime(CLOCK_MONOTONIC, &t0);
+  *macs = 0.0;
+  for (int i = 0; i < 7; ++i) {
+    or_matmul(x, w[i], 1, Ks[i], Ns[i], y);
+    *macs += (double)Ks[i] * Ns[i];
+  }
+  clock_gettime(CLOCK_MONOTONIC, &t1);
+  for (int i = 0; i < 7; ++i) free(w[i]);
+  free(x);
+  free(y);
+  return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
 }
 
 /* ------------------------------------------------------------------------ */

@@ -138,6 +138,10 @@ int or_forward(or_model *m, const uint32_t *tokens, size_t n, size_t pos, or_kv 
 int or_prefill(or_model *m, const uint32_t *tokens, size_t n, size_t pos0, or_kv *kv,
                float *last_logits, float *hidden);
 
+/* CPU-baseline sample: seconds for one token's matmuls of one layer in the
+ * reference's i-j-p order; *macs receives the multiply-add count */
+double or_time_layer(or_model *m, size_t layer, double *macs);
+
 /* ---- sampler (src/sampling.rs:14-310) ---- */
 typedef struct {
   float temperature; size_t top_k; float top_p;

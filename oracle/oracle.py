@@ -125,6 +125,7 @@ def lib():
         L.or_categorical_sample.argtypes = [fp, sz, C.c_float]; L.or_categorical_sample.restype = sz
         L.or_argmax.argtypes = [fp, sz]; L.or_argmax.restype = sz
         L.or_generate.argtypes = [vp, C.POINTER(_GenCfg), u32p, sz, u32p, sz, C.c_int]; L.or_generate.restype = C.c_long
+        L.or_time_layer.argtypes = [vp, sz, C.POINTER(C.c_double)]; L.or_time_layer.restype = C.c_double
     return _lib
 
 
@@ -348,6 +349,12 @@ class Model:
 
     def __del__(self):
         self.close()
+
+    def time_layer(self, layer=0):
+        """(seconds, macs) of one token's matmuls of `layer` in reference i-j-p order."""
+        macs = C.c_double()
+        s = lib().or_time_layer(self.h, layer, C.byref(macs))
+        return s, macs.value
 
     def kv(self, max_ctx, kv_f16=False):
         return KV(self, max_ctx, kv_f16)
