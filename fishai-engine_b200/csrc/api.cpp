@@ -2,7 +2,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
+#include <mutex>
 #include <memory>
 #include <new>
 #include <string>
@@ -641,6 +643,73 @@ int fa_sample(fa_sampler *, uint32_t, const float *, uint32_t, uint32_t *) {
 }
 int fa_sampler_observe(fa_sampler *, uint32_t, uint32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
 int fa_sampler_reset(fa_sampler *, int32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
+
+// ------------------------------------------------------------ attention
+namespace {
+constexpr uint32_t kSdpaSplits = 32;
+
+int sdpa_check(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H,
+               uint32_t KVH, uint32_t hd, const float *out) {
+  if (!q || !k || !v || !out) return fail(FA_ERR_INVALID, "fa_sdpa: null buffer");
+  if (!q_len || !kv_len || !H || !KVH || !hd) return fail(FA_ERR_INVALID, "fa_sdpa: zero size");
+  if (hd > 128 || H % KVH || (H / KVH != 1 && H / KVH != 2 && H / KVH != 4 && H / KVH != 8))
+    return fail(FA_ERR_UNSUPPORTED, "fa_sdpa: head_dim <= 128 and n_heads/n_kv_heads in {1,2,4,8}");
+  return FA_OK;
+}
+
+AttnParams sdpa_params(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H,
+                       uint32_t KVH, uint32_t hd, float *out, float *part, uint32_t *counters) {
+  AttnParams ap{};
+  ap.q = q;
+  ap.kc = k;
+  ap.vc = v;
+  ap.t_fixed = kv_len;
+  ap.q_rows = q_len;
+  ap.kv.n_kv = KVH;
+  ap.kv.head_dim = hd;
+  ap.kv.f16 = 0;
+  ap.n_heads = H;
+  ap.splits = kSdpaSplits;
+  ap.scale = 1.0f / std::sqrt((float)hd);  // src/tensor.rs:486
+  ap.part = part;
+  ap.counters = counters;
+  ap.out = out;
+  return ap;
+}
+
+std::mutex g_sdpa_mu;
+struct SdpaScratch {
+  void *buf = nullptr;
+  size_t bytes = 0;
+};
+SdpaScratch g_sdpa[64];  // per device
+}  // namespace
+
+int fa_sdpa(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H, uint32_t KVH,
+            uint32_t hd, float *out, void *stream) {
+  int rc = sdpa_check(q, k, v, q_len, kv_len, H, KVH, hd, out);
+  if (rc) return rc;
+  int dev = 0;
+  API_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FA_ERR_INVALID, "fa_sdpa: device ordinal out of range");
+  const size_t part_floats = (size_t)q_len * H * kSdpaSplits * (2 + hd);
+  const size_t need = part_floats * 4 + (size_t)q_len * KVH * 4;
+  std::lock_guard<std::mutex> lock(g_sdpa_mu);
+  SdpaScratch &s = g_sdpa[dev];
+  if (s.bytes < need) {
+    if (s.buf) cudaFree(s.buf);
+    s.buf = nullptr;
+    s.bytes = 0;
+    if (cudaMalloc(&s.buf, need) != cudaSuccess) return fail(FA_ERR_OOM, "fa_sdpa: scratch allocation failed");
+    s.bytes = need;
+  }
+  float *part = (float *)s.buf;
+  uint32_t *counters = (uint32_t *)(part + part_floats);
+  API_CUDA(cudaMemsetAsync(counters, 0, (size_t)q_len * KVH * 4, (cudaStream_t)stream));
+  AttnParams ap = sdpa_params(q, k, v, q_len, kv_len, H, KVH, hd, out, part, counters);
+  if (launch_attention(ap, false, (cudaStream_t)stream)) return fail(FA_ERR_CUDA, "fa_sdpa: launch failed");
+  return FA_OK;
+}
 
 // ------------------------------------------------------------ profiling
 int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, uint64_t *bytes_per_launch) {

@@ -33,7 +33,12 @@ __device__ void attn_body(const AttnParams &p) {
   const uint32_t split = blockIdx.x, kvh = blockIdx.y;
   const uint32_t hd = p.kv.head_dim, KVH = p.kv.n_kv;
   constexpr uint32_t rep = REP, dpl = DPL;
-  const uint32_t T = p.state->len + 1;
+  const uint32_t row = blockIdx.z;
+  const uint32_t T = p.kc ? p.t_fixed : p.state->len + 1;
+  const float *qrow = p.q + (uint64_t)row * p.n_heads * hd;
+  float *part = p.part + (uint64_t)row * p.n_heads * p.splits * (2 + hd);
+  uint32_t *counters = p.counters + (uint64_t)row * KVH;
+  float *outrow = p.out + (uint64_t)row * p.n_heads * hd;
   uint32_t L = (T + p.splits - 1) / p.splits;
   L = (L + 15) / 16 * 16;
   const uint32_t t0 = split * L, t1 = min(T, t0 + L);
@@ -44,7 +49,7 @@ __device__ void attn_body(const AttnParams &p) {
   for (uint32_t r = 0; r < rep; ++r)
     for (uint32_t i = 0; i < dpl; ++i) {
       const uint32_t d = lane + 32 * i;
-      q[r][i] = d < hd ? p.q[(kvh * rep + r) * hd + d] : 0.0f;
+      q[r][i] = d < hd ? qrow[(kvh * rep + r) * hd + d] : 0.0f;
     }
   float m[REP], l[REP], o[REP][DPL];
 #pragma unroll
@@ -54,16 +59,25 @@ __device__ void attn_body(const AttnParams &p) {
 #pragma unroll
     for (uint32_t i = 0; i < DPL; ++i) o[r][i] = 0.0f;
   }
-  const void *base = reinterpret_cast<const uint8_t *>(p.kv.base) +
-                     (uint64_t)p.layer * p.kv.layer_stride * (F16 ? 2 : 4);
-  const uint32_t *pt = p.kv.page_table + (uint64_t)p.seq * p.kv.max_pages;
+  const void *base = p.kc ? nullptr
+                         : reinterpret_cast<const uint8_t *>(p.kv.base) + (uint64_t)p.layer * p.kv.layer_stride * (F16 ? 2 : 4);
+  const uint32_t *pt = p.kc ? nullptr : p.kv.page_table + (uint64_t)p.seq * p.kv.max_pages;
   for (uint32_t t = t0 + warp; t < t1; t += kWarps) {
-    const uint32_t page = pt[t / 16], slot = t % 16;
     float kk[DPL], vv[DPL];
-    for (uint32_t i = 0; i < dpl; ++i) {
-      const uint32_t d = lane + 32 * i;
-      kk[i] = d < hd ? kv_load<F16>(base, kv_index(page, 0, kvh, slot, d, KVH, hd)) : 0.0f;
-      vv[i] = d < hd ? kv_load<F16>(base, kv_index(page, 1, kvh, slot, d, KVH, hd)) : 0.0f;
+    if (p.kc) {
+      const uint64_t rb = ((uint64_t)t * KVH + kvh) * hd;
+      for (uint32_t i = 0; i < dpl; ++i) {
+        const uint32_t d = lane + 32 * i;
+        kk[i] = d < hd ? p.kc[rb + d] : 0.0f;
+        vv[i] = d < hd ? p.vc[rb + d] : 0.0f;
+      }
+    } else {
+      const uint32_t page = pt[t / 16], slot = t % 16;
+      for (uint32_t i = 0; i < dpl; ++i) {
+        const uint32_t d = lane + 32 * i;
+        kk[i] = d < hd ? kv_load<F16>(base, kv_index(page, 0, kvh, slot, d, KVH, hd)) : 0.0f;
+        vv[i] = d < hd ? kv_load<F16>(base, kv_index(page, 1, kvh, slot, d, KVH, hd)) : 0.0f;
+      }
     }
     for (uint32_t r = 0; r < rep; ++r) {
       float s = 0.0f;
@@ -108,19 +122,19 @@ __device__ void attn_body(const AttnParams &p) {
       out = acc;
     }
     const uint32_t h = kvh * rep + r;
-    p.part[((uint64_t)h * p.splits + split) * (2 + hd) + c] = out;
+    part[((uint64_t)h * p.splits + split) * (2 + hd) + c] = out;
   }
   // the last split CTA of this kv head combines all splits (fixed order)
   __threadfence();
   __syncthreads();
   __shared__ uint32_t last;
-  if (threadIdx.x == 0) last = atomicAdd(p.counters + kvh, 1u) + 1 == p.splits;
+  if (threadIdx.x == 0) last = atomicAdd(counters + kvh, 1u) + 1 == p.splits;
   __syncthreads();
   if (!last) return;
   __threadfence();
   for (uint32_t idx = threadIdx.x; idx < rep * hd; idx += blockDim.x) {
     const uint32_t r = idx / hd, dd = idx % hd, h = kvh * rep + r;
-    const float *P = p.part + (uint64_t)h * p.splits * (2 + hd);
+    const float *P = part + (uint64_t)h * p.splits * (2 + hd);
     float M = -INFINITY;
     for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(P + s * (2 + hd)));
     float Lsum = 0.0f, o = 0.0f;
@@ -131,9 +145,9 @@ __device__ void attn_body(const AttnParams &p) {
       Lsum = fmaf(__ldcg(P + s * (2 + hd) + 1), e, Lsum);
       o = fmaf(__ldcg(P + s * (2 + hd) + 2 + dd), e, o);
     }
-    p.out[h * hd + dd] = o / Lsum;
+    outrow[h * hd + dd] = o / Lsum;
   }
-  if (threadIdx.x == 0) p.counters[kvh] = 0;
+  if (threadIdx.x == 0) counters[kvh] = 0;
 }
 
 template <bool F16, int REP, int DPL>
@@ -161,7 +175,7 @@ int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st) {
              : rep == 8 ? pick_dpl<8>(p.kv.head_dim, f16) : nullptr;
   if (!fn) return -1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.splits, p.kv.n_kv);
+  cfg.gridDim = dim3(p.splits, p.kv.n_kv, p.q_rows ? p.q_rows : 1);
   cfg.blockDim = dim3(kWarps * 32);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

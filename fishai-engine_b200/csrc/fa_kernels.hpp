@@ -100,7 +100,10 @@ int launch_gemv(const GemvParams &p, bool pdl, cudaStream_t st);
 size_t gemv_smem_bytes(const GemvParams &p);
 
 struct AttnParams {
-  const float *q;          // [H*hd]
+  const float *q;          // [H*hd] (per query row when q_rows > 1)
+  const float *kc, *vc;    // contiguous f32 K/V [T][n_kv*hd] (reference KVCache layout); null: paged kv
+  uint32_t t_fixed;        // positions when kc/vc are used (0: from state)
+  uint32_t q_rows;         // query rows (grid z); rows are independent (no mask)
   KvView kv;
   uint32_t seq, layer;
   uint32_t n_heads, splits;

@@ -468,6 +468,7 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
 int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
   AttnParams ap{};
   ap.q = w.q;
+  ap.q_rows = 1;
   ap.kv = kv.view();
   ap.seq = seq;
   ap.layer = l;

@@ -155,6 +155,19 @@ int fa_forward(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host
 int fa_prefill(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t start_pos,
                float *last_logits_host, uint32_t *last_argmax_host);
 
+/* ------------------------------------------------------------ attention */
+/* tensor::scaled_dot_product_attention (src/tensor.rs:451-551) with the GQA
+ * head expansion of src/model.rs:500-526 folded in, on device buffers:
+ * q [q_len][n_heads*head_dim], k/v [kv_len][n_kv_heads*head_dim] f32 (the
+ * full K/V, cache rows first: the reference's full_k/full_v), out
+ * [q_len][n_heads*head_dim].  Every query row attends to all kv_len rows (no
+ * mask), scores scaled by 1/sqrt(head_dim).  Split-K over positions with a
+ * deterministic combine; scratch comes from a per-device buffer the library
+ * allocates on first use and grows as needed (calls must not overlap).
+ * head_dim <= 128; n_heads / n_kv_heads in {1, 2, 4, 8}. */
+int fa_sdpa(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t q_len, uint32_t kv_len,
+            uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_dev, void *stream);
+
 /* ------------------------------------------------------------- sampling */
 typedef struct {
   float temperature;            /* 0 = greedy */
