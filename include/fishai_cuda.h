@@ -115,7 +115,7 @@ void fa_model_opts_default(fa_model_opts *o);
 /* GGUFFile::open + ModelConfig::from_gguf + ModelWeights::load_from_gguf
  * (src/model.rs:252-298): weights are uploaded once in their native GGML
  * blocks and re-laid in device memory into the column-chunk layout the
- * kernels stream (same bytes per block). */
+ * kernels stream (same bytes per block, regrouped per 8 rows and 32 columns). */
 int fa_model_load(const char *path, const fa_model_opts *opts, fa_model **out);
 void fa_model_free(fa_model *m);
 int fa_model_config(const fa_model *m, fa_config *cfg);
