@@ -103,6 +103,7 @@ SIGNATURES = {
     "fa_decode_greedy": ([_vp, _vp, _u32, _u32, _u32, _u32, _pu32], _i),
     "fa_profile_gemv": ([_vp, C.c_int32, _u32, _pf, _pu64], _i),
     "fa_sdpa": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp], _i),
+    "fa_sdpa_noalloc": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp], _i),
     "fa_synth_write": ([C.c_char_p, C.POINTER(fa_synth_spec), _u64], _i),
 }
 

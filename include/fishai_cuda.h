@@ -168,6 +168,26 @@ int fa_prefill(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host
 int fa_sdpa(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t q_len, uint32_t kv_len,
             uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_dev, void *stream);
 
+/* No counterpart in the reference.  fa_sdpa without any device allocation,
+ * for callers that must not call cudaMalloc: code whose device memory is
+ * handed out by its own allocator or pool (a cudaMalloc there would go around
+ * that budget), and code on a latency-critical path where an implicit
+ * allocation and the device-wide synchronisation that may come with it are
+ * not allowed.  Same arguments, numbers and limits as fa_sdpa; the caller
+ * passes every input and output buffer.  The split-K scratch is a fixed
+ * static device array inside the library (2 MiB + 4 KiB, held on every GPU
+ * that loads the library until the process exits), so
+ *   q_len * n_heads * 32 * (head_dim + 2) <= 524288 and
+ *   q_len * n_kv_heads <= 1024,
+ * else FA_ERR_INVALID (e.g. head_dim 128 allows q_len * n_heads <= 126).
+ * The first call on each device looks up the array's device address with
+ * that device current; make that first call before any stream capture.
+ * Every call on a device shares the one array: calls that overlap on the GPU
+ * (different streams, no ordering between them) race and give wrong output.
+ * The counters it needs at zero are cleared on `stream` by every call. */
+int fa_sdpa_noalloc(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t q_len, uint32_t kv_len,
+                    uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_dev, void *stream);
+
 /* ------------------------------------------------------------- sampling */
 typedef struct {
   float temperature;            /* 0 = greedy */
