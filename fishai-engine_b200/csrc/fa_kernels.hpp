@@ -68,7 +68,8 @@ struct GemvParams {
   uint32_t n_ctas;
   uint32_t max_chunks_per_cta;
   uint32_t K, K8;
-  uint32_t CW;             // lane geometry: 256, 512 or 1024
+  int mma;                 // 1: MMA tile layout (k_gemv_mma, 16-row groups), 0: 8-row groups (k_gemv)
+  uint32_t CW;             // chunk width: 256, 512 or 1024
   uint32_t stage_bytes;    // capacity of one pipeline stage (multiple of 16)
   uint32_t x_slot;         // floats of x (and norm weight) per stage slot
   float *part;             // [n_ctas * max_chunks_per_cta][CW] chunk partials
@@ -95,9 +96,13 @@ struct GemvParams {
 };
 
 // one-time per-device kernel attributes (dynamic smem)
+// launch_gemv dispatches on p.mma
 int gemv_init();
 int launch_gemv(const GemvParams &p, bool pdl, cudaStream_t st);
 size_t gemv_smem_bytes(const GemvParams &p);
+int gemv_mma_init();
+int launch_gemv_mma(const GemvParams &p, bool pdl, cudaStream_t st);
+size_t gemv_mma_smem_bytes(const GemvParams &p);
 
 struct AttnParams {
   const float *q;          // [H*hd] (per query row when q_rows > 1)
@@ -150,6 +155,9 @@ int launch_tied_head(const TiedHeadParams &p, bool pdl, cudaStream_t st);
 int launch_dequant_native(int type, const void *data, uint64_t count, float *out, cudaStream_t st);
 int launch_repack(int type, const void *src_a, const void *src_b, uint32_t K, uint32_t N, uint32_t CW, void *dst,
                   uint64_t dst_off, cudaStream_t st);
+// native -> MMA tile layout (K a multiple of 16, CW a multiple of 64)
+int launch_repack_mma(int type, const void *src_a, const void *src_b, uint32_t K, uint32_t N, uint32_t CW, void *dst,
+                      uint64_t dst_off, cudaStream_t st);
 int launch_unpack(int type, const void *src, uint64_t src_off, uint32_t K, uint32_t N, uint32_t CW, float *out,
                   cudaStream_t st);
 

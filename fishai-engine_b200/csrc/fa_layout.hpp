@@ -59,6 +59,44 @@ FA_HD inline bool gemv_type_supported(int type) {
   return type == kF32 || type == kF16 || type == kQ4_0 || type == kQ8_0 || type == kQ4_K || type == kQ6_K;
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core layout ("MMA tiles") for Q4_K, Q6_K, Q8_0 and Q4_0.
+//
+// A chunk of width w is stored as groups of 16 consecutive rows; a group
+// holds exactly the native bytes of those rows (16 * native_row_bytes).  The
+// codes are re-ordered for mma.sync.m16n8k16 with the weight as operand A:
+// A[m][k] = code of (row k, column m) of a 16 x 16 tile, so one tile is one
+// MMA.  Columns are cut into 64-wide slices (4 tiles; the last slice of a
+// chunk may hold 2 tiles) and lane l = 4g + c of a warp holds, per tile, the
+// eight fragment elements e = 0..7 at (m, k) = (g + 8*((e>>1)&1),
+// 2c + (e&1) + 8*(e>>2)).
+//
+//   Q4_K / Q4_0 codes:  slice i at 512 i, lane l at + 4 nt l, tile t at + 4t:
+//                       one u32 per tile, element e at bit 4(e>>1) + 16(e&1)
+//   Q6_K  low 4 bits:   as the Q4 codes (region 0, 8w bytes)
+//         high 2 bits:  region 8w: slice i at 256 i, lane l at + 8 l; word
+//                       h (tiles 2h, 2h+1), element e of tile t at bit
+//                       4(e>>1) + 16(e&1) + 2(t&1)
+//   Q8_0 codes (q+128): slice i at 1024 i, lane l at + 8 nt l, tile t at + 8t:
+//                       two u32, element e in word e>>2, byte 2(e&1) + ((e>>1)&1)
+//   Q4_K header:        region 8w, (super-block s, row r) at (16 s + r) * 16:
+//                       d, dmin, then the 12 scale bytes re-laid as eight
+//                       12-bit fields (sc | m << 6), field f at bit 12f
+//   Q6_K scales:        region 12w, int8 (16-col sub-block j, row r) at 16 j + r
+//        d:             region 13w, f16 (super-block s, row r) at (16 s + r) * 2
+//   Q8_0 / Q4_0 d:      region 16w / 8w, f16 (32-col block b, row r) at (16 b + r) * 2
+//
+// (nt = tiles in the slice.)  Q4_0 keeps its codes 0..15 (value d(q-8)), Q8_0
+// stores q+128 in 0..255 (value d(u-128)): the same information, re-encoded.
+// ---------------------------------------------------------------------------
+FA_HD inline bool mma_type(int type) { return type == kQ4_K || type == kQ6_K || type == kQ8_0 || type == kQ4_0; }
+FA_HD inline uint32_t mma_group_bytes(int type, uint32_t w) { return 16 * native_row_bytes(type, w); }
+// row m / column k of fragment element e of lane l inside a 16x16 tile
+FA_HD inline uint32_t frag_m(uint32_t l, uint32_t e) { return l / 4 + 8 * ((e >> 1) & 1); }
+FA_HD inline uint32_t frag_k(uint32_t l, uint32_t e) { return 2 * (l % 4) + (e & 1) + 8 * (e >> 2); }
+FA_HD inline uint32_t frag_q4_bit(uint32_t e) { return 4 * (e >> 1) + 16 * (e & 1); }
+FA_HD inline uint32_t frag_q8_byte(uint32_t e) { return 4 * (e >> 2) + 2 * (e & 1) + ((e >> 1) & 1); }
+
 // One column chunk of a GEMV launch.  All chunks of a launch share K.
 struct ChunkDesc {
   uint64_t offset;   // byte offset of the chunk's first row group in the weight buffer

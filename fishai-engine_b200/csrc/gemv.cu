@@ -18,6 +18,7 @@
 
 #include "fa_device.cuh"
 #include "fa_kernels.hpp"
+#include "gemv_epi.cuh"
 
 namespace fa {
 
@@ -226,7 +227,7 @@ __device__ __forceinline__ Smem carve(uint8_t *smem, const GemvParams &p) {
   return s;
 }
 
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
+__device__ __forceinline__ void consumer_bar() { epi::consumer_bar<kConsumerWarps>(); }
 
 // stage enumeration shared by producer and consumers: a stage holds up to NG
 // groups of one chunk; (c, g) walks the CTA's [start, end) range.
@@ -297,105 +298,6 @@ __device__ __forceinline__ void finalize(const Acc &A, float vals[32]) {
   }
 }
 
-__device__ __forceinline__ float silu_ref(float g) { return g * (1.0f / (1.0f + expf(-g))); }
-
-// sum of the chunk's published partials in CTA order (deterministic)
-__device__ __forceinline__ float chunk_sum(const GemvParams &p, const ChunkDesc &cd, uint32_t c, uint32_t col) {
-  float v = 0.0f;
-  for (uint32_t t = 0; t < cd.n_contrib; ++t) {
-    const uint32_t i = p.contrib[cd.contrib_off + t];
-    const uint32_t slot = i * p.max_chunks_per_cta + (c - p.ranges[i].c0);
-    v += __ldcg(p.part + (size_t)slot * p.CW + col);
-  }
-  return v;
-}
-
-// fused epilogue for chunk c, run by the 256 consumer threads of the CTA that
-// completed the chunk
-__device__ void epilogue(const GemvParams &p, const Smem &sm, const ChunkDesc &cd, uint32_t c, uint32_t tid,
-                         uint32_t warp, uint32_t lane) {
-  const uint32_t w = cd.width;
-  float local = 0.0f;
-  unsigned long long best = 0ull;
-  if (p.epi == kEpiSwiglu) {
-    const uint32_t half = w / 2;
-    for (uint32_t i = tid; i < half; i += kConsumerWarps * 32) {
-      const float gsum = chunk_sum(p, cd, c, i), usum = chunk_sum(p, cd, c, i + half);
-      p.out[cd.out_col / 2 + i] = __fmul_rn(silu_ref(gsum), usum);
-    }
-  } else {
-    const uint32_t pos = (p.epi == kEpiQkv) ? p.state->pos : 0;   // RoPE position
-    const uint32_t wpos = (p.epi == kEpiQkv) ? p.state->len : 0;  // cache slot written
-    if (p.epi == kEpiQkv && pos >= p.rope_max && tid == 0) atomicOr(&p.state->err, kErrContext);
-    for (uint32_t i = tid; i < w; i += kConsumerWarps * 32) {
-      const float v = chunk_sum(p, cd, c, i);
-      const uint32_t col = cd.out_col + i;
-      if (p.epi == kEpiStore) {
-        p.out[col] = v;
-      } else if (p.epi == kEpiResid) {
-        const float nv = p.resid[col] + v;
-        p.resid[col] = nv;
-        local = fmaf(nv, nv, local);
-      } else if (p.epi == kEpiLogits) {
-        if (p.out) p.out[col] = v;
-        const unsigned long long key = ((unsigned long long)float_key(v) << 32) | (unsigned long long)(~col);
-        best = key > best ? key : best;
-      } else {  // kEpiQkv
-        const uint32_t hd = p.kv.head_dim, half = hd / 2;
-        const bool is_q = col < p.q_dim, is_k = !is_q && col < p.q_dim + p.kv_dim;
-        float outv = v;
-        if ((is_q || is_k) && pos < p.rope_max) {
-          const uint32_t dd = (is_q ? col : col - p.q_dim) % hd;
-          const uint32_t ip = dd < half ? i + half : i - half;  // partner column (same chunk)
-          const float pv = chunk_sum(p, cd, c, ip);
-          const float *cs = p.rope_tab + (uint64_t)pos * hd + 2 * (dd % half);
-          const float cth = cs[0], sth = cs[1];
-          outv = dd < half ? __fsub_rn(__fmul_rn(v, cth), __fmul_rn(pv, sth))
-                           : __fadd_rn(__fmul_rn(pv, sth), __fmul_rn(v, cth));
-        }
-        if (is_q) {
-          p.out[col] = outv;
-        } else {
-          const uint32_t kc = is_k ? col - p.q_dim : col - p.q_dim - p.kv_dim;
-          const uint32_t page_idx = wpos / 16;
-          if (page_idx < p.kv.max_pages) {
-            const uint32_t page = p.kv.page_table[p.seq * p.kv.max_pages + page_idx];
-            const uint64_t idx = (uint64_t)p.layer * p.kv.layer_stride +
-                                 kv_index(page, is_k ? 0 : 1, kc / hd, wpos % 16, kc % hd, p.kv.n_kv, hd);
-            if (p.kv.f16) reinterpret_cast<__half *>(p.kv.base)[idx] = __float2half_rn(outv);
-            else reinterpret_cast<float *>(p.kv.base)[idx] = outv;
-          } else if (p.state) {
-            atomicOr(&p.state->err, kErrContext);
-          }
-        }
-      }
-    }
-  }
-  if (p.epi == kEpiResid || p.epi == kEpiLogits) {
-    for (int o = 16; o; o >>= 1) {
-      local += __shfl_xor_sync(0xFFFFFFFFu, local, o);
-      const unsigned long long ob = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-      best = ob > best ? ob : best;
-    }
-    unsigned long long *rk = reinterpret_cast<unsigned long long *>(sm.red + 32);
-    if (lane == 0) {
-      sm.red[warp] = local;
-      rk[warp] = best;
-    }
-    consumer_bar();
-    if (tid == 0) {
-      float s = 0.0f;
-      unsigned long long b = 0ull;
-      for (int i = 0; i < kConsumerWarps; ++i) {
-        s += sm.red[i];
-        b = rk[i] > b ? rk[i] : b;
-      }
-      if (p.epi == kEpiResid) p.ssq_out[c] = s;
-      else if (p.state && b) atomicMax(&p.state->argmax_key, b);
-    }
-  }
-}
-
 // publish this CTA's partial of chunk c; the last contributor reduces and
 // runs the epilogue
 template <int T>
@@ -430,7 +332,7 @@ __device__ __forceinline__ void flush(const GemvParams &p, const Smem &sm, const
   consumer_bar();
   if (*sm.flag) {
     __threadfence();
-    epilogue(p, sm, cd, c, tid, warp, lane);
+    epi::epilogue<kConsumerWarps>(p, sm.red, cd, c, tid, warp, lane);
     if (tid == 0) p.counters[c] = 0;  // ready for the next launch
   }
   consumer_bar();
@@ -580,6 +482,7 @@ int gemv_init() {
 }
 
 int launch_gemv(const GemvParams &p, bool pdl, cudaStream_t st) {
+  if (p.mma) return launch_gemv_mma(p, pdl, st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_ctas);
   cfg.blockDim = dim3(kThreads);

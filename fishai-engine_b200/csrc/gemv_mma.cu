@@ -1,0 +1,487 @@
+// Tensor-core dequant-GEMV for batch-1 decode, y[N] = x[K] . W[K][N] for
+// Q4_K, Q6_K, Q8_0 and Q4_0 weights in the MMA tile layout (fa_layout.hpp),
+// the reference's tensor::matmul orientation (src/tensor.rs:244-258).
+//
+// The multiply-add of every weight element runs on the tensor pipe as
+// mma.sync.m16n8k16 (bf16 in, f32 accumulate) with the weight codes as
+// operand A and per-row coefficients as operand B:
+//   * A: a weight code q (4, 6 or 8 bits) masked into the low bits of a bf16
+//     half is the bf16 subnormal q * 2^-133 — exact, one LOP3 per two codes,
+//     no conversion and no bias to subtract;
+//   * B: c = x[k] * d[k] * sc[k][block] (the dequantisation scale of row k
+//     for the tile's block times the activation), times 2^96, split exactly
+//     into three bf16 (hi + mid + lo = 24 bits) held in B columns 0..2.
+// D[m][0] + D[m][1] + D[m][2] = 2^-37 * sum_k q[k][m] * c[k]; the constant
+// parts of the dequantisation (Q4_K mins, the Q6_K/Q8_0/Q4_0 code offsets)
+// are per-block sums of c (or x*dmin*m) kept in f32 beside the MMA.
+//
+// Work split: persistent CTAs (one per SM) stream byte-balanced ranges of
+// (chunk, 16-row group) units (stream-K); a producer warp fills a 4-slot
+// shared-memory ring with 1-D bulk copies (weights of up to two groups plus
+// the matching x / norm-weight slices); each of the 16 consumer warps owns one
+// 64-column slice of the 1024-wide chunk, builds the B coefficients of its
+// slice for the stage in a private table and runs 4 (Q6_K: 8) MMAs per group.
+// At the end of its rows of a chunk a CTA publishes the chunk partial; the last
+// CTA to arrive sums the partials in a fixed order and runs the fused
+// epilogue (gemv_epi.cuh).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "fa_device.cuh"
+#include "fa_kernels.hpp"
+#include "gemv_epi.cuh"
+
+namespace fa {
+
+namespace {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kStages = 4;
+constexpr uint32_t kRows = 32;              // rows per stage: two 16-row groups
+constexpr uint32_t kTblWords = 2 * 4 * 24;  // per warp: groups x blocks x (3 splits x 4 lanes x 2 words)
+constexpr float kBScale = 0x1p96f;          // B = c * 2^96
+constexpr float kYScale = 0x1p37f;          // A = q * 2^-133  ->  y = D * 2^37
+
+struct Smem {
+  uint64_t *full, *empty;
+  uint32_t *flag;
+  float *red;
+  uint8_t *stages;
+  float *xs, *nw;
+  uint32_t *tbl;
+};
+
+__device__ __forceinline__ Smem carve(uint8_t *smem, const GemvParams &p) {
+  Smem s;
+  s.full = reinterpret_cast<uint64_t *>(smem);
+  s.empty = s.full + kStages;
+  s.flag = reinterpret_cast<uint32_t *>(smem + 64);
+  s.red = reinterpret_cast<float *>(smem + 128);  // 128 floats
+  uint32_t off = 128 + 512;
+  s.stages = smem + off;
+  off += kStages * p.stage_bytes;
+  s.xs = reinterpret_cast<float *>(smem + off);
+  off += kStages * kRows * 4;
+  s.nw = reinterpret_cast<float *>(smem + off);
+  off += kStages * kRows * 4;
+  s.tbl = reinterpret_cast<uint32_t *>(smem + off);
+  return s;
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// (v0, v1) -> hi + mid + lo, each a bf16 pair, exactly (8 + 8 + 8 bits);
+// written to the three split rows of the coefficient table
+__device__ __forceinline__ void split_store(float v0, float v1, uint32_t *dst) {
+  const uint32_t hi = bf2_bits(__floats2bfloat162_rn(v0, v1));
+  const float r0 = __fsub_rn(v0, bf_lo(hi)), r1 = __fsub_rn(v1, bf_hi(hi));
+  const uint32_t mid = bf2_bits(__floats2bfloat162_rn(r0, r1));
+  const float s0 = __fsub_rn(r0, bf_lo(mid)), s1 = __fsub_rn(r1, bf_hi(mid));
+  dst[0] = hi;
+  dst[8] = mid;
+  dst[16] = bf2_bits(__floats2bfloat162_rn(s0, s1));
+}
+
+// ---------------------------------------------------------------------------
+// per-type geometry: blocks (coefficient columns) per 64-column slice and the
+// factor of the per-block correction sum
+template <int T>
+struct Geo;
+template <>
+struct Geo<kQ4_K> {
+  static constexpr int J = 2;
+  static constexpr float kCorr = 1.0f;  // corr = sum x * (dmin * m)
+};
+template <>
+struct Geo<kQ6_K> {
+  static constexpr int J = 4;
+  static constexpr float kCorr = 32.0f;  // value (q - 32) * d * sc
+};
+template <>
+struct Geo<kQ8_0> {
+  static constexpr int J = 2;
+  static constexpr float kCorr = 128.0f;  // stored u = q + 128
+};
+template <>
+struct Geo<kQ4_0> {
+  static constexpr int J = 2;
+  static constexpr float kCorr = 8.0f;  // value (q - 8) * d
+};
+
+// Coefficients of this warp's slice for the stage.  Lane l handles the row
+// pair (2p, 2p+1), p = l % 16, for block jb = l / 16 (Q6_K: jb and jb + 2).
+// Table word of (group gi, block j, split s, pair p): (gi*J + j)*24 + s*8 +
+// (p%4)*2 + (p%8)/4, so fragment lane (g, c) reads words (g*4 + c)*2, +1.
+template <int T>
+__device__ __forceinline__ void build(const uint8_t *stage, uint32_t gbytes, uint32_t w, uint32_t slice,
+                                      uint32_t nblk, uint32_t ng, const float *xs, const float *nw, bool norm,
+                                      float inv, uint32_t lane, uint32_t *tbl, float (&corr)[2]) {
+  constexpr int J = Geo<T>::J;
+  const uint32_t p = lane & 15, jb = lane >> 4;
+  if (2 * p >= 16 * ng || jb >= nblk) return;
+  float2 x = *reinterpret_cast<const float2 *>(xs + 2 * p);
+  if (norm) {  // rms_norm: (x * inv) * w   (src/tensor.rs:280-290)
+    const float2 n = *reinterpret_cast<const float2 *>(nw + 2 * p);
+    x.x = __fmul_rn(__fmul_rn(x.x, inv), n.x);
+    x.y = __fmul_rn(__fmul_rn(x.y, inv), n.y);
+  }
+  const uint32_t gi = p >> 3, rr = 2 * (p & 7);
+  const uint8_t *G = stage + gi * gbytes;
+  uint32_t *dst = tbl + gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1);
+  if constexpr (T == kQ4_K) {
+    const uint32_t s = slice >> 2, sb = 2 * (slice & 3) + jb, bit = 12 * sb, fw = bit >> 5, fs = bit & 31;
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr) * 16);
+    const uint4 h1 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr + 1) * 16);
+    const uint32_t f0 = __funnelshift_r(fw == 0 ? h0.y : (fw == 1 ? h0.z : h0.w), fw == 0 ? h0.z : h0.w, fs);
+    const uint32_t f1 = __funnelshift_r(fw == 0 ? h1.y : (fw == 1 ? h1.z : h1.w), fw == 0 ? h1.z : h1.w, fs);
+    const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
+    const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
+    // d1 = d * sc, m1 = dmin * m as the dequantisation computes them
+    const float d10 = __fmul_rn(dd0.x, u2f_small(f0 & 63u)), m10 = __fmul_rn(dd0.y, u2f_small((f0 >> 6) & 63u));
+    const float d11 = __fmul_rn(dd1.x, u2f_small(f1 & 63u)), m11 = __fmul_rn(dd1.y, u2f_small((f1 >> 6) & 63u));
+    corr[0] = __fadd_rn(__fadd_rn(corr[0], __fmul_rn(x.x, m10)), __fmul_rn(x.y, m11));
+    split_store(__fmul_rn(__fmul_rn(x.x, d10), kBScale), __fmul_rn(__fmul_rn(x.y, d11), kBScale),
+                dst + jb * 24);
+  } else if constexpr (T == kQ6_K) {
+    const uint32_t s = slice >> 2;
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(G + 13 * w + (16 * s + rr) * 2));
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t j = jb + 2 * q;
+      const uint32_t scw = *reinterpret_cast<const uint16_t *>(G + 12 * w + (4 * slice + j) * 16 + rr);
+      const float sc0 = (float)(int)(int8_t)(scw & 0xFFu), sc1 = (float)(int)(int8_t)(scw >> 8);
+      const float c0 = __fmul_rn(x.x, __fmul_rn(dd.x, sc0)), c1 = __fmul_rn(x.y, __fmul_rn(dd.y, sc1));
+      corr[q] = __fadd_rn(__fadd_rn(corr[q], c0), c1);
+      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + j * 24);
+    }
+  } else {  // Q8_0 / Q4_0: one f16 d per row and 32-column block
+    const uint32_t off = (T == kQ8_0 ? 16 : 8) * w;
+    const float2 dd =
+        __half22float2(*reinterpret_cast<const __half2 *>(G + off + ((2 * slice + jb) * 16 + rr) * 2));
+    const float c0 = __fmul_rn(x.x, dd.x), c1 = __fmul_rn(x.y, dd.y);
+    corr[0] = __fadd_rn(__fadd_rn(corr[0], c0), c1);
+    split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + jb * 24);
+  }
+}
+
+// the MMAs of one 16-row group for this warp's slice (NT tiles)
+template <int T, int NT>
+__device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t slice, uint32_t lane,
+                                          const uint32_t *tblg, float (&D)[4][4], float (&Dh)[4][4]) {
+  constexpr int J = Geo<T>::J;
+  constexpr int JN = (NT == 4) ? J : J / 2;
+  const uint32_t g = lane >> 2, c = lane & 3;
+  uint32_t b[JN][2];
+#pragma unroll
+  for (int j = 0; j < JN; ++j) {
+    if (g < 3) {
+      const uint2 v = *reinterpret_cast<const uint2 *>(tblg + j * 24 + (g * 4 + c) * 2);
+      b[j][0] = v.x;
+      b[j][1] = v.y;
+    } else {
+      b[j][0] = b[j][1] = 0u;
+    }
+  }
+  if constexpr (T == kQ8_0) {
+    uint32_t q[2 * NT];
+    const uint4 *src = reinterpret_cast<const uint4 *>(G + 1024 * slice + 8 * NT * lane);
+#pragma unroll
+    for (int i = 0; i < NT / 2; ++i) {
+      const uint4 v = src[i];
+      q[4 * i] = v.x;
+      q[4 * i + 1] = v.y;
+      q[4 * i + 2] = v.z;
+      q[4 * i + 3] = v.w;
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint32_t P = q[2 * t], Q = q[2 * t + 1];
+      mma_bf16(D[t], P & 0x00FF00FFu, (P >> 8) & 0x00FF00FFu, Q & 0x00FF00FFu, (Q >> 8) & 0x00FF00FFu,
+               b[t >> 1][0], b[t >> 1][1]);
+    }
+  } else {
+    uint32_t q[NT];
+    if constexpr (NT == 4) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(G + 512 * slice + 16 * lane);
+      q[0] = v.x;
+      q[1] = v.y;
+      q[2] = v.z;
+      q[3] = v.w;
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2 *>(G + 512 * slice + 8 * lane);
+      q[0] = v.x;
+      q[1] = v.y;
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint32_t W = q[t], S = W >> 8;
+      const int j = (T == kQ6_K) ? t : (t >> 1);
+      mma_bf16(D[t], W & 0x000F000Fu, W & 0x00F000F0u, S & 0x000F000Fu, S & 0x00F000F0u, b[j][0], b[j][1]);
+    }
+    if constexpr (T == kQ6_K) {
+      const uint2 hw = *reinterpret_cast<const uint2 *>(G + 8 * w + 256 * slice + 8 * lane);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const uint32_t H = (t < 2 ? hw.x : hw.y) >> (2 * (t & 1)), S = H >> 8;
+        mma_bf16(Dh[t], H & 0x00030003u, H & 0x00300030u, S & 0x00030003u, S & 0x00300030u, b[t][0], b[t][1]);
+      }
+    }
+  }
+}
+
+// D -> column values of this warp's slice, minus the block corrections, into
+// the chunk partial (rows m >= 8 of the 4-bit layouts carry an extra x16)
+template <int T, int NT>
+__device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)[4][4], float (&Dh)[4][4],
+                                           float (&corr)[2]) {
+#pragma unroll
+  for (int o = 8; o; o >>= 1) {
+    corr[0] += __shfl_xor_sync(0xFFFFFFFFu, corr[0], o);
+    corr[1] += __shfl_xor_sync(0xFFFFFFFFu, corr[1], o);
+  }
+  const uint32_t g = lane >> 2, c = lane & 3;
+  constexpr float kHi = (T == kQ8_0) ? kYScale : kYScale * 0.0625f;
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    float d[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = (T == kQ6_K) ? fmaf(16.0f, Dh[t][i], D[t][i]) : D[t][i];
+    const float lo0 = __shfl_down_sync(0xFFFFFFFFu, d[0], 1), lo8 = __shfl_down_sync(0xFFFFFFFFu, d[2], 1);
+    const float cr = (T == kQ6_K) ? __shfl_sync(0xFFFFFFFFu, t < 2 ? corr[0] : corr[1], 16 * (t & 1))
+                                  : __shfl_sync(0xFFFFFFFFu, corr[0], 16 * (t >> 1));
+    const float cv = __fmul_rn(Geo<T>::kCorr, cr);
+    if (c == 0) {
+      __stcg(dst + 16 * t + g, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv));
+      __stcg(dst + 16 * t + g + 8, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[2], d[3]), lo8), kHi), cv));
+    }
+  }
+}
+
+// stage iteration over the CTA's (chunk, 16-row group) range, up to two
+// groups of one chunk per stage
+struct StageIt {
+  uint32_t c, g, ng, gend;
+  bool last_of_chunk;
+};
+__device__ __forceinline__ bool stage_set(const GemvParams &p, const CtaRange &R, StageIt &it) {
+  const uint32_t gtot = p.K / 16;
+  if (it.c > R.c1 || (it.c == R.c1 && it.g >= R.g1)) return false;
+  it.gend = it.c == R.c1 ? R.g1 : gtot;
+  it.ng = min(2u, it.gend - it.g);
+  it.last_of_chunk = it.g + it.ng == it.gend;
+  return true;
+}
+__device__ __forceinline__ bool stage_first(const GemvParams &p, const CtaRange &R, StageIt &it) {
+  it.c = R.c0;
+  it.g = R.g0;
+  return stage_set(p, R, it);
+}
+__device__ __forceinline__ bool stage_next(const GemvParams &p, const CtaRange &R, StageIt &it) {
+  it.g += it.ng;
+  if (it.g >= it.gend) {
+    it.c += 1;
+    it.g = 0;
+  }
+  return stage_set(p, R, it);
+}
+
+template <int T>
+__device__ __forceinline__ void run_stage(const GemvParams &p, const uint8_t *base, const ChunkDesc &cd, uint32_t ng,
+                                          const float *xs, const float *nw, bool norm, float inv, uint32_t warp,
+                                          uint32_t lane, uint32_t *tbl, float (&D)[4][4], float (&Dh)[4][4],
+                                          float (&corr)[2]) {
+  const uint32_t w = cd.width, nt = min(64u, w - 64 * warp) / 16;
+  const uint32_t nblk = (nt == 4) ? Geo<T>::J : Geo<T>::J / 2;
+  build<T>(base, cd.gbytes, w, warp, nblk, ng, xs, nw, norm, inv, lane, tbl, corr);
+  __syncwarp();
+  for (uint32_t gi = 0; gi < ng; ++gi) {
+    const uint8_t *G = base + gi * cd.gbytes;
+    const uint32_t *tblg = tbl + gi * Geo<T>::J * 24;
+    if (nt == 4) mma_group<T, 4>(G, w, warp, lane, tblg, D, Dh);
+    else mma_group<T, 2>(G, w, warp, lane, tblg, D, Dh);
+  }
+  __syncwarp();
+}
+
+template <int T>
+__device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc &cd, uint32_t slot, uint32_t warp,
+                                            uint32_t lane, float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
+  float *dst = p.part + (size_t)slot * p.CW + 64 * warp;
+  if (min(64u, cd.width - 64 * warp) == 64) flush_warp<T, 4>(dst, lane, D, Dh, corr);
+  else flush_warp<T, 2>(dst, lane, D, Dh, corr);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const Smem sm = carve(smem, p);
+  const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const CtaRange R = p.ranges[blockIdx.x];
+  const bool norm = p.pro == kProRmsNorm;
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  bool ok = true;
+  if (warp == kWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      StageIt it;
+      uint32_t s = 0;
+      bool more = stage_first(p, R, it);
+      // weights of the first slots before waiting on the previous kernel
+      for (; more && s < kStages; ++s) {
+        const ChunkDesc &cd = p.chunks[it.c];
+        const uint32_t wb = it.ng * cd.gbytes, xb = it.ng * 64 * (norm ? 2 : 1);
+        mbar_arrive_expect_tx(&sm.full[s], wb + xb);
+        bulk_g2s(sm.stages + s * p.stage_bytes, p.w + cd.offset + (uint64_t)it.g * cd.gbytes, wb, &sm.full[s]);
+        more = stage_next(p, R, it);
+      }
+      pdl_wait();
+      {  // activations of those slots
+        StageIt jt;
+        bool m2 = stage_first(p, R, jt);
+        for (uint32_t t = 0; m2 && t < s; ++t) {
+          bulk_g2s(sm.xs + t * kRows, p.in + jt.g * 16, jt.ng * 64, &sm.full[t]);
+          if (norm) bulk_g2s(sm.nw + t * kRows, p.norm_w + jt.g * 16, jt.ng * 64, &sm.full[t]);
+          m2 = stage_next(p, R, jt);
+        }
+      }
+      for (; more; ++s) {
+        const uint32_t slot = s % kStages;
+        if (!mbar_wait(&sm.empty[slot], ((s / kStages) - 1) & 1u)) {
+          ok = false;  // consumers time out on their own waits and unwind
+          break;
+        }
+        fence_proxy_async_smem();
+        const ChunkDesc &cd = p.chunks[it.c];
+        const uint32_t wb = it.ng * cd.gbytes, xb = it.ng * 64 * (norm ? 2 : 1);
+        mbar_arrive_expect_tx(&sm.full[slot], wb + xb);
+        bulk_g2s(sm.stages + slot * p.stage_bytes, p.w + cd.offset + (uint64_t)it.g * cd.gbytes, wb, &sm.full[slot]);
+        bulk_g2s(sm.xs + slot * kRows, p.in + it.g * 16, it.ng * 64, &sm.full[slot]);
+        if (norm) bulk_g2s(sm.nw + slot * kRows, p.norm_w + it.g * 16, it.ng * 64, &sm.full[slot]);
+        more = stage_next(p, R, it);
+      }
+    } else {
+      pdl_wait();
+    }
+  } else {
+    // ---------------- consumers ----------------
+    pdl_wait();
+    if (norm) {
+      if (warp == 0) {
+        float s = 0.0f;
+        for (uint32_t i = lane; i < p.n_ssq; i += 32) s += p.ssq[i];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (lane == 0) sm.red[96] = 1.0f / sqrtf(s / (float)p.K + p.eps);
+      }
+      epi::consumer_bar<kWarps>();
+    }
+    const float inv = norm ? sm.red[96] : 1.0f;
+    uint32_t *tbl = sm.tbl + warp * kTblWords;
+    float D[4][4], Dh[4][4], corr[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+    StageIt it;
+    uint32_t s = 0;
+    for (bool more = stage_first(p, R, it); more; more = stage_next(p, R, it), ++s) {
+      const uint32_t slot = s % kStages;
+      // after a timed-out wait the warp keeps the loop's barrier structure but
+      // skips the work; the error flag tells the host the result is void
+      if (ok && !mbar_wait(&sm.full[slot], (s / kStages) & 1u)) ok = false;
+      const ChunkDesc cd = p.chunks[it.c];
+      const bool active = ok && 64 * warp < cd.width;
+      if (active) {
+        const uint8_t *base = sm.stages + slot * p.stage_bytes;
+        const float *xs = sm.xs + slot * kRows, *nw = sm.nw + slot * kRows;
+        switch (cd.type) {
+          case kQ4_K: run_stage<kQ4_K>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
+          case kQ6_K: run_stage<kQ6_K>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
+          case kQ8_0: run_stage<kQ8_0>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
+          default: run_stage<kQ4_0>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[slot]);
+      if (it.last_of_chunk) {
+        const uint32_t slot_p = blockIdx.x * p.max_chunks_per_cta + (it.c - R.c0);
+        if (active) {
+          switch (cd.type) {
+            case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+            case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+            case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+            default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+        corr[0] = corr[1] = 0.0f;
+        __threadfence();
+        epi::consumer_bar<kWarps>();
+        if (tid == 0) {
+          const uint32_t old = atomicAdd(p.counters + it.c, 1u);
+          *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
+        }
+        epi::consumer_bar<kWarps>();
+        if (*sm.flag) {
+          __threadfence();
+          epi::epilogue<kWarps>(p, sm.red, cd, it.c, tid, warp, lane);
+          if (tid == 0) p.counters[it.c] = 0;  // ready for the next launch
+        }
+        epi::consumer_bar<kWarps>();
+      }
+    }
+  }
+  if (!ok && p.state) atomicOr(&p.state->err, kErrWaitTimeout);
+}
+
+size_t gemv_mma_smem_bytes(const GemvParams &p) {
+  return 128 + 512 + (size_t)kStages * p.stage_bytes + 2 * (size_t)kStages * kRows * 4 +
+         (size_t)kWarps * kTblWords * 4;
+}
+
+int gemv_mma_init() {
+  if (cudaFuncSetAttribute(k_gemv_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
+    return -1;
+  return 0;
+}
+
+int launch_gemv_mma(const GemvParams &p, bool pdl, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_ctas);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = gemv_mma_smem_bytes(p);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemv_mma, p) == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace fa

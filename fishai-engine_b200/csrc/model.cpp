@@ -104,12 +104,6 @@ int get_tensor(const Gguf &g, const std::string &name, TensorRef *r) {
   return FA_OK;
 }
 
-uint64_t chunked_bytes(int type, uint32_t K8, uint32_t N, uint32_t CW) {
-  uint64_t total = 0;
-  for (uint32_t c0 = 0; c0 < N; c0 += CW) total += (uint64_t)(K8 / 8) * group_bytes(type, std::min(CW, N - c0));
-  return total;
-}
-
 uint32_t pick_cw(int type, uint32_t N, bool paired) {
   uint32_t cw = 256;
   if (N >= 1024 * 37) cw = 1024;
@@ -121,14 +115,24 @@ uint32_t pick_cw(int type, uint32_t N, bool paired) {
 }  // namespace
 
 // One GEMV launch covering `parts` (tensors sharing K).  paired: parts[0]
-// and parts[1] are gate/up interleaved per chunk.
+// and parts[1] are gate/up interleaved per chunk.  Launches whose tensors are
+// all Q4_K / Q6_K / Q8_0 / Q4_0 (K a multiple of 16) use the tensor-core
+// kernel and its MMA tile layout with 1024-column chunks; others use the
+// 8-row-group layout.  cw_div: chunk width must be a multiple of it
+// (RoPE pairs of a head stay in one chunk).
 static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts, const std::vector<uint32_t> &out_base,
                       bool paired, uint32_t K, const std::vector<uint32_t> &widths, uint32_t CW, void *staging,
-                      void *staging2) {
+                      void *staging2, uint32_t cw_div = 1) {
+  bool mma = K % 16 == 0 && 1024 % cw_div == 0;
+  for (size_t i = 0; i < parts.size(); ++i) mma = mma && mma_type(parts[i].type) && widths[paired ? 0 : i] % 32 == 0;
+  if (mma) CW = 1024;
+  P.mma = mma;
   P.K = K;
   P.K8 = (K + 7) / 8 * 8;
   P.CW = CW;
   P.native_bytes = 0;
+  const uint32_t rows = mma ? K / 16 : P.K8 / 8;  // row groups per chunk
+  auto gbytes = [&](int type, uint32_t w) { return mma ? mma_group_bytes(type, w) : group_bytes(type, w); };
   // sizes
   std::vector<uint64_t> region;
   uint64_t total = 0;
@@ -136,7 +140,9 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
   for (size_t i = 0; i < nparts; ++i) {
     const uint32_t N = paired ? 2 * widths[0] : widths[i];
     region.push_back(total);
-    total += (chunked_bytes(parts[i].type, P.K8, N, CW) + 255) / 256 * 256;
+    uint64_t b = 0;
+    for (uint32_t c0 = 0; c0 < N; c0 += CW) b += (uint64_t)rows * gbytes(parts[i].type, std::min(CW, N - c0));
+    total += (b + 255) / 256 * 256;
   }
   uint8_t *buf = (uint8_t *)m.dmalloc(total);
   if (!buf) return fail(FA_ERR_OOM, "device allocation of " + std::to_string(total) + " weight bytes failed");
@@ -148,24 +154,24 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     const uint64_t nb = type_nbytes(a.type, (uint64_t)K * N);
     CUDA_TRY(cudaMemcpyAsync(staging, a.data, nb, cudaMemcpyHostToDevice, m.stream));
     P.native_bytes += nb;
+    const void *src_b = nullptr;
     if (paired) {
       const TensorRef &b = parts[1];
       if (b.type != a.type) return fail(FA_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a ggml type");
       CUDA_TRY(cudaMemcpyAsync(staging2, b.data, nb, cudaMemcpyHostToDevice, m.stream));
       P.native_bytes += nb;
-      if (launch_repack(a.type, staging, staging2, K, N, CW, buf, region[i], m.stream))
-        return fail(FA_ERR_CUDA, "repack launch failed");
-    } else {
-      if (launch_repack(a.type, staging, nullptr, K, N, CW, buf, region[i], m.stream))
-        return fail(FA_ERR_CUDA, "repack launch failed");
+      src_b = staging2;
     }
+    const int rc = mma ? launch_repack_mma(a.type, staging, src_b, K, N, CW, buf, region[i], m.stream)
+                       : launch_repack(a.type, staging, src_b, K, N, CW, buf, region[i], m.stream);
+    if (rc) return fail(FA_ERR_CUDA, "repack launch failed");
     CUDA_TRY(cudaStreamSynchronize(m.stream));
     const uint32_t Nv = paired ? 2 * N : N;
     for (uint32_t c = 0, c0 = 0; c0 < Nv; c0 += CW, ++c) {
       ChunkDesc d{};
       const uint32_t w = std::min(CW, Nv - c0);
-      d.offset = region[i] + (uint64_t)c * (P.K8 / 8) * group_bytes(a.type, CW);
-      d.gbytes = group_bytes(a.type, w);
+      d.offset = region[i] + (uint64_t)c * rows * gbytes(a.type, CW);
+      d.gbytes = gbytes(a.type, w);
       d.type = (uint16_t)a.type;
       d.width = (uint16_t)w;
       d.out_col = out_base[i] + c0;
@@ -173,13 +179,18 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
       max_gb = std::max(max_gb, d.gbytes);
     }
   }
-  P.stage_bytes = std::max<uint32_t>(16384, (max_gb + 15) / 16 * 16);
-  uint32_t max_ng = 1;
-  for (const ChunkDesc &d : P.chunks) max_ng = std::max(max_ng, P.stage_bytes / d.gbytes);
-  P.x_slot = 8 * max_ng;
+  if (mma) {
+    P.stage_bytes = 2 * ((max_gb + 15) / 16 * 16);  // two 16-row groups per stage
+    P.x_slot = 32;
+  } else {
+    P.stage_bytes = std::max<uint32_t>(16384, (max_gb + 15) / 16 * 16);
+    uint32_t max_ng = 1;
+    for (const ChunkDesc &d : P.chunks) max_ng = std::max(max_ng, P.stage_bytes / d.gbytes);
+    P.x_slot = 8 * max_ng;
+  }
   // stream-K split: CTA i streams bytes [i*B/P, (i+1)*B/P) of the chunk-major
-  // (chunk, 8-row group) sequence, rounded to whole groups
-  const uint32_t G = P.K8 / 8, nc = (uint32_t)P.chunks.size();
+  // (chunk, row group) sequence, rounded to whole groups
+  const uint32_t G = rows, nc = (uint32_t)P.chunks.size();
   std::vector<uint64_t> start(nc + 1, 0);
   for (uint32_t c = 0; c < nc; ++c) start[c + 1] = start[c] + (uint64_t)G * P.chunks[c].gbytes;
   const uint64_t B = start[nc];
@@ -264,7 +275,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   graphs = o.use_graphs != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init()) return fail(FA_ERR_CUDA, "GEMV kernel attribute setup failed");
+  if (gemv_init() || gemv_mma_init()) return fail(FA_ERR_CUDA, "GEMV kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;
   gguf.reset(Gguf::open(path, &code));
@@ -345,7 +356,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
     if ((rc = upload_f32(T[0], &lw.attn_norm))) return rc;
     if ((rc = upload_f32(T[5], &lw.ffn_norm))) return rc;
     if ((rc = build_plan(*this, lw.qkv, {T[1], T[2], T[3]}, {0, qd, qd + kvd}, false, d, {qd, kvd, kvd}, 256, staging,
-                         staging2)))
+                         staging2, hd)))
       return rc;
     if ((rc = build_plan(*this, lw.o, {T[4]}, {0}, false, qd, {d}, pick_cw(T[4].type, d, false), staging, staging2)))
       return rc;
@@ -421,6 +432,7 @@ GemvParams Model::gemv_base(const GemvPlan &P) const {
   p.max_chunks_per_cta = P.max_chunks_per_cta;
   p.K = P.K;
   p.K8 = P.K8;
+  p.mma = P.mma ? 1 : 0;
   p.CW = P.CW;
   p.stage_bytes = P.stage_bytes;
   p.x_slot = P.x_slot;

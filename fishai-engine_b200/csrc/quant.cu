@@ -150,6 +150,168 @@ __global__ void k_repack(int type, const uint8_t *__restrict__ src_a, const uint
   }
 }
 
+// ---------------------------------------------------------------------------
+// native [K][N] -> MMA tile layout (fa_layout.hpp), K a multiple of 16.
+// Virtual columns and gate/up pairing as in k_repack.
+// ---------------------------------------------------------------------------
+namespace {
+
+// raw code of (row, col): Q4_0 / Q4_K 0..15, Q6_K 0..63, Q8_0 q + 128
+__device__ __forceinline__ uint32_t native_code(int type, const uint8_t *row, uint32_t col) {
+  switch (type) {
+    case kQ4_0: {
+      const uint8_t byte = row[(col / 32) * 18 + 2 + (col % 32) / 2];
+      return (col & 1) ? (byte & 0xFu) : (byte >> 4);  // element 2j: high nibble (src/quant.rs:143-148)
+    }
+    case kQ8_0: return row[(col / 32) * 34 + 2 + col % 32] ^ 0x80u;
+    case kQ4_K: {
+      const uint32_t i = col % 256, sb = i / 32;
+      const uint8_t byte = row[(col / 256) * 144 + 16 + 32 * (i / 64) + i % 32];
+      return (sb & 1) ? (byte >> 4) : (byte & 0xFu);
+    }
+    default: {  // Q6_K
+      const uint8_t *b = row + (col / 256) * 210;
+      const uint32_t i = col % 256, h = i / 128, lp = i % 128, quad = lp / 32, l = lp % 32;
+      uint32_t lo = (quad & 1) ? b[64 * h + 32 + l] : b[64 * h + l];
+      lo = (quad >= 2) ? (lo >> 4) : (lo & 0xFu);
+      return lo | (((b[128 + 32 * h + l] >> (2 * quad)) & 3u) << 4);
+    }
+  }
+}
+
+struct VCol {
+  const uint8_t *src;
+  uint32_t col;
+};
+// virtual column -> (tensor, column): chunk c of a paired weight holds gate
+// columns [c*CW/2, c*CW/2 + w/2) then the same up columns
+__device__ __forceinline__ VCol vcol_map(const uint8_t *a, const uint8_t *b, uint32_t Nv, uint32_t CW, uint32_t v) {
+  if (!b) return {a, v};
+  const uint32_t c = v / CW, w = min(CW, Nv - c * CW), jc = v - c * CW, half = w / 2;
+  return jc < half ? VCol{a, c * (CW / 2) + jc} : VCol{b, c * (CW / 2) + jc - half};
+}
+
+__device__ __forceinline__ uint8_t *mma_group_ptr(uint8_t *dst, int type, uint32_t Nv, uint32_t CW, uint32_t G16,
+                                                  uint32_t c, uint32_t grp, uint32_t *w) {
+  *w = min(CW, Nv - c * CW);
+  return dst + (uint64_t)c * G16 * mma_group_bytes(type, CW) + (uint64_t)grp * mma_group_bytes(type, *w);
+}
+
+// one thread per (16-row group, 64-column slice, lane): the codes
+__global__ void k_repack_mma_codes(int type, const uint8_t *__restrict__ src_a, const uint8_t *__restrict__ src_b,
+                                   uint32_t N, uint32_t K, uint32_t CW, uint8_t *__restrict__ dst) {
+  const uint32_t Nv = src_b ? 2 * N : N, G16 = K / 16, nsl = (Nv + 63) / 64;
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)G16 * nsl * 32) return;
+  const uint32_t l = (uint32_t)(t % 32), si = (uint32_t)((t / 32) % nsl), grp = (uint32_t)(t / 32 / nsl);
+  const uint32_t c = si * 64 / CW, i = si - c * (CW / 64);
+  uint32_t w;
+  uint8_t *G = mma_group_ptr(dst, type, Nv, CW, G16, c, grp, &w);
+  const uint32_t nt = min(64u, w - 64 * i) / 16;
+  const uint32_t rb = native_row_bytes(type, N);
+  uint32_t hw[2] = {0, 0};
+  for (uint32_t tt = 0; tt < nt; ++tt) {
+    uint32_t word = 0, q8[2] = {0, 0};
+    for (uint32_t e = 0; e < 8; ++e) {
+      const uint32_t k = 16 * grp + frag_k(l, e), v = 64 * si + 16 * tt + frag_m(l, e);
+      const VCol vc = vcol_map(src_a, src_b, Nv, CW, v);
+      const uint32_t q = native_code(type, vc.src + (uint64_t)k * rb, vc.col);
+      if (type == kQ8_0) {
+        const uint32_t by = frag_q8_byte(e);
+        q8[by / 4] |= q << (8 * (by % 4));
+      } else {
+        word |= (q & 0xFu) << frag_q4_bit(e);
+        if (type == kQ6_K) hw[tt / 2] |= (q >> 4) << (frag_q4_bit(e) + 2 * (tt & 1));
+      }
+    }
+    if (type == kQ8_0) {
+      uint32_t *p = reinterpret_cast<uint32_t *>(G + 1024 * i + 8 * nt * l + 8 * tt);
+      p[0] = q8[0];
+      p[1] = q8[1];
+    } else {
+      *reinterpret_cast<uint32_t *>(G + 512 * i + 4 * nt * l + 4 * tt) = word;
+    }
+  }
+  if (type == kQ6_K) {
+    uint32_t *p = reinterpret_cast<uint32_t *>(G + 8 * w + 256 * i + 8 * l);
+    p[0] = hw[0];
+    p[1] = hw[1];
+  }
+}
+
+// one thread per (row, 16-column unit): scales and block metadata
+__global__ void k_repack_mma_meta(int type, const uint8_t *__restrict__ src_a, const uint8_t *__restrict__ src_b,
+                                  uint32_t N, uint32_t K, uint32_t CW, uint8_t *__restrict__ dst) {
+  const uint32_t Nv = src_b ? 2 * N : N, G16 = K / 16, units = Nv / 16;
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)K * units) return;
+  const uint32_t u = (uint32_t)(t % units), k = (uint32_t)(t / units);
+  const uint32_t v = 16 * u, c = v / CW, j16 = (v - c * CW) / 16, grp = k / 16, r = k % 16;
+  uint32_t w;
+  uint8_t *G = mma_group_ptr(dst, type, Nv, CW, G16, c, grp, &w);
+  const VCol vc = vcol_map(src_a, src_b, Nv, CW, v);
+  const uint8_t *row = vc.src + (uint64_t)k * native_row_bytes(type, N);
+  switch (type) {
+    case kQ4_K: {
+      if (j16 % 16) break;
+      const uint8_t *b = row + (vc.col / 256) * 144;
+      uint8_t *h = G + 8 * w + (16 * (j16 / 16) + r) * 16;
+      for (int x = 0; x < 4; ++x) h[x] = b[x];
+      uint32_t words[3] = {0, 0, 0};
+      const uint8_t *q = b + 4;
+      for (int f = 0; f < 8; ++f) {
+        int sc, m;
+        if (f < 4) {
+          sc = q[f] & 63;
+          m = q[f + 4] & 63;
+        } else {
+          sc = (q[f + 4] & 0xF) | ((q[f - 4] >> 6) << 4);
+          m = (q[f + 4] >> 4) | ((q[f] >> 6) << 4);
+        }
+        const uint64_t val = (uint64_t)(sc | (m << 6));
+        const uint32_t bit = 12 * f, wi = bit / 32, sh = bit % 32;
+        words[wi] |= (uint32_t)(val << sh);
+        if (sh + 12 > 32) words[wi + 1] |= (uint32_t)(val >> (32 - sh));
+      }
+      for (int x = 0; x < 12; ++x) h[4 + x] = (uint8_t)(words[x / 4] >> (8 * (x % 4)));
+      break;
+    }
+    case kQ6_K: {
+      const uint8_t *b = row + (vc.col / 256) * 210;
+      G[12 * w + 16 * j16 + r] = b[192 + (vc.col % 256) / 16];
+      if (j16 % 16 == 0) {
+        uint8_t *d = G + 13 * w + (16 * (j16 / 16) + r) * 2;
+        d[0] = b[208];
+        d[1] = b[209];
+      }
+      break;
+    }
+    default: {  // Q8_0 / Q4_0: f16 d per 32-column block
+      if (j16 % 2) break;
+      const uint8_t *b = row + (vc.col / 32) * (type == kQ8_0 ? 34 : 18);
+      uint8_t *d = G + (type == kQ8_0 ? 16 : 8) * w + (16 * (j16 / 2) + r) * 2;
+      d[0] = b[0];
+      d[1] = b[1];
+      break;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_repack_mma(int type, const void *src_a, const void *src_b, uint32_t K, uint32_t N, uint32_t CW, void *dst,
+                      uint64_t dst_off, cudaStream_t st) {
+  if (!mma_type(type) || K % 16 || CW % 64) return -1;
+  const uint32_t Nv = src_b ? 2 * N : N;
+  uint8_t *d = (uint8_t *)dst + dst_off;
+  const uint64_t n1 = (uint64_t)(K / 16) * ((Nv + 63) / 64) * 32, n2 = (uint64_t)K * (Nv / 16);
+  k_repack_mma_codes<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(type, (const uint8_t *)src_a,
+                                                                  (const uint8_t *)src_b, N, K, CW, d);
+  k_repack_mma_meta<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(type, (const uint8_t *)src_a,
+                                                                 (const uint8_t *)src_b, N, K, CW, d);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 int launch_repack(int type, const void *src_a, const void *src_b, uint32_t K, uint32_t N, uint32_t CW, void *dst,
                   uint64_t dst_off, cudaStream_t st) {
   uint32_t K8 = (K + 7) / 8 * 8;
