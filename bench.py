@@ -6,6 +6,8 @@ batch 1, a 2048-token prompt, then greedy decode.  One step = one decode
 token (one forward pass through the model + argmax, a CUDA-graph replay).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --profile gateup --layers 2 --reps 3   # one GEMV kind on a
+      reduced-depth model of the same shapes (small cases for ncu captures)
 
 With N > 1 (torchrun) every rank runs an independent replica (the decode
 path at batch 1 does not shard); value = all ranks' tokens / max rank time.
@@ -119,6 +121,28 @@ def cpu_baseline_sample(path: str, n_layers_total: int, layers: int):
     return 1.0 / sec_per_token, secs, layers
 
 
+PROFILE_KINDS = {"qkv": 0, "o": 1, "gateup": 2, "down": 3, "head": 4}
+
+
+def profile_one(args):
+    """Launch one GEMV kind `reps` times over every layer of a reduced-depth
+    model with the benchmark's shapes and types; print its device time."""
+    import ctypes as C
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights
+
+    path = synth.cached_preset(PRESET, n_layers=args.layers)
+    m = ModelWeights.load_from_gguf(path)
+    avg, nbytes = C.c_float(), C.c_uint64()
+    L.check(L.lib().fa_profile_gemv(m._h, PROFILE_KINDS[args.profile], args.reps, C.byref(avg), C.byref(nbytes)))
+    print(json.dumps({"profile": args.profile, "layers": args.layers, "reps": args.reps,
+                      "avg_launch_us": avg.value * 1000.0, "bytes_per_launch": nbytes.value,
+                      "achieved_gbs": nbytes.value / (avg.value / 1000.0) / 1e9}), flush=True)
+    m.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -128,7 +152,13 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--cpu-layers", type=int, default=4)
+    ap.add_argument("--profile", choices=list(PROFILE_KINDS), default=None,
+                    help="time one GEMV kind only, on a model with --layers layers")
+    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
+    if args.profile:
+        return profile_one(args)
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3

@@ -54,6 +54,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait on phase `parity` with the thread suspended between polls (the
+// hardware wakes it when the phase completes, so polling is rare); gives up
+// and returns false after `limit_ns` of wall time.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity), "r"(1000000u)
+        : "memory");
+    if (done) return true;
+    const uint64_t t = global_ns();
+    if (!t0) t0 = t;
+    else if (t - t0 > limit_ns) return false;
+  }
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // src, dst 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -71,6 +71,8 @@ struct GemvParams {
   int mma;                 // 1: MMA tile layout (k_gemv_mma, 16-row groups), 0: 8-row groups (k_gemv)
   uint32_t CW;             // chunk width: 256, 512 or 1024
   uint32_t stage_bytes;    // capacity of one pipeline stage (multiple of 16)
+  uint32_t n_stages;       // k_gemv_mma ring depth
+  uint32_t max_units;      // k_gemv_mma: most 16-row units of any CTA (x buffer size)
   uint32_t x_slot;         // floats of x (and norm weight) per stage slot
   float *part;             // [n_ctas * max_chunks_per_cta][CW] chunk partials
   uint32_t *counters;      // [n_chunks] arrival counters (zero between launches)
@@ -103,6 +105,10 @@ size_t gemv_smem_bytes(const GemvParams &p);
 int gemv_mma_init();
 int launch_gemv_mma(const GemvParams &p, bool pdl, cudaStream_t st);
 size_t gemv_mma_smem_bytes(const GemvParams &p);
+// ring depth that fits the shared-memory budget of one CTA (0: does not fit)
+uint32_t gemv_mma_stages(uint32_t stage_bytes, uint32_t max_units, size_t smem_budget);
+// row groups per pipeline stage for chunks of this type and group size
+uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type);
 
 struct AttnParams {
   const float *q;          // [H*hd] (per query row when q_rows > 1)

@@ -100,16 +100,16 @@ FA_HD inline uint32_t frag_q8_byte(uint32_t e) { return 4 * (e >> 2) + 2 * (e & 
 // One column chunk of a GEMV launch.  All chunks of a launch share K.
 struct ChunkDesc {
   uint64_t offset;   // byte offset of the chunk's first row group in the weight buffer
-  uint32_t gbytes;   // bytes per 8-row group
+  uint32_t gbytes;   // bytes per row group (8 rows; 16 in the MMA layout)
   uint16_t type;     // ggml type
   uint16_t width;    // columns (multiple of 32; of 256 for K-quants)
   uint32_t out_col;  // first output column of the chunk in the launch's output space
   uint32_t contrib_off;  // first entry of this chunk in the launch's contributor list
   uint32_t n_contrib;    // CTAs that contribute partial sums to this chunk
-  uint32_t pad;
+  uint32_t sgroups;      // row groups per pipeline stage (k_gemv_mma)
 };
 
-// Contiguous range of (chunk, 8-row group) units streamed by one CTA:
+// Contiguous range of (chunk, row group) units streamed by one CTA:
 // from (c0, g0) inclusive to (c1, g1) exclusive, chunk-major order.
 struct CtaRange {
   uint32_t c0, g0, c1, g1;

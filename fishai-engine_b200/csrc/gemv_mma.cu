@@ -16,11 +16,14 @@
 // are per-block sums of c (or x*dmin*m) kept in f32 beside the MMA.
 //
 // Work split: persistent CTAs (one per SM) stream byte-balanced ranges of
-// (chunk, 16-row group) units (stream-K); a producer warp fills a 4-slot
-// shared-memory ring with 1-D bulk copies (weights of up to two groups plus
-// the matching x / norm-weight slices); each of the 16 consumer warps owns one
-// 64-column slice of the 1024-wide chunk, builds the B coefficients of its
-// slice for the stage in a private table and runs 4 (Q6_K: 8) MMAs per group.
+// (chunk, 16-row group) units (stream-K).  A producer lane fills a shared-
+// memory ring (as many slots as fit, up to 12) with one large 1-D bulk copy
+// per stage (up to four groups, ~32 KB: per-copy overhead makes small copies
+// slow); weights are static, so it never waits for the previous kernel.  The
+// consumers load the CTA's slice of x once (normalised when the launch has an
+// RMSNorm prologue); each of the 16 consumer warps owns one 64-column slice
+// of the 1024-wide chunk, builds the B coefficients of its slice for the stage
+// in a private table and runs 4 (Q6_K: 8) MMAs per group.
 // At the end of its rows of a chunk a CTA publishes the chunk partial; the last
 // CTA to arrive sums the partials in a fixed order and runs the fused
 // epilogue (gemv_epi.cuh).
@@ -38,9 +41,14 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = (kWarps + 1) * 32;
-constexpr int kStages = 4;
-constexpr uint32_t kRows = 32;              // rows per stage: two 16-row groups
-constexpr uint32_t kTblWords = 2 * 4 * 24;  // per warp: groups x blocks x (3 splits x 4 lanes x 2 words)
+constexpr int kMaxStages = 12;              // ring depth is p.n_stages (set from the shared-memory budget)
+constexpr uint32_t kMaxStageGroups = 4;     // row groups per stage
+constexpr uint32_t kStageTarget = 36 * 1024;
+constexpr uint32_t kTblWords = 8 * 24;      // per warp: (groups x blocks <= 8) x (3 splits x 4 lanes x 2 words)
+constexpr uint32_t kZeroWords = 256;        // B fragment source of the lanes whose column is unused
+// shared memory: mbarriers + flag | reduction scratch | zero area | tables | x | ring
+constexpr uint32_t kOffRed = 256, kOffZero = kOffRed + 512, kOffTbl = kOffZero + 4 * kZeroWords,
+                   kOffX = kOffTbl + 4 * kWarps * kTblWords;
 constexpr float kBScale = 0x1p96f;          // B = c * 2^96
 constexpr float kYScale = 0x1p37f;          // A = q * 2^-133  ->  y = D * 2^37
 
@@ -48,25 +56,25 @@ struct Smem {
   uint64_t *full, *empty;
   uint32_t *flag;
   float *red;
-  uint8_t *stages;
-  float *xs, *nw;
-  uint32_t *tbl;
+  uint32_t *zero, *tbl;
+  float *xs;
+  uint8_t *ring;
 };
+
+__host__ __device__ inline uint32_t ring_offset(uint32_t max_units) {
+  return (kOffX + max_units * 64 + 127) / 128 * 128;
+}
 
 __device__ __forceinline__ Smem carve(uint8_t *smem, const GemvParams &p) {
   Smem s;
   s.full = reinterpret_cast<uint64_t *>(smem);
-  s.empty = s.full + kStages;
-  s.flag = reinterpret_cast<uint32_t *>(smem + 64);
-  s.red = reinterpret_cast<float *>(smem + 128);  // 128 floats
-  uint32_t off = 128 + 512;
-  s.stages = smem + off;
-  off += kStages * p.stage_bytes;
-  s.xs = reinterpret_cast<float *>(smem + off);
-  off += kStages * kRows * 4;
-  s.nw = reinterpret_cast<float *>(smem + off);
-  off += kStages * kRows * 4;
-  s.tbl = reinterpret_cast<uint32_t *>(smem + off);
+  s.empty = s.full + kMaxStages;
+  s.flag = reinterpret_cast<uint32_t *>(smem + 16 * kMaxStages);
+  s.red = reinterpret_cast<float *>(smem + kOffRed);
+  s.zero = reinterpret_cast<uint32_t *>(smem + kOffZero);
+  s.tbl = reinterpret_cast<uint32_t *>(smem + kOffTbl);
+  s.xs = reinterpret_cast<float *>(smem + kOffX);
+  s.ring = smem + ring_offset(p.max_units);
   return s;
 }
 
@@ -94,65 +102,87 @@ __device__ __forceinline__ void split_store(float v0, float v1, uint32_t *dst) {
 }
 
 // ---------------------------------------------------------------------------
-// per-type geometry: blocks (coefficient columns) per 64-column slice and the
-// factor of the per-block correction sum
+// per-type geometry: J = blocks (coefficient columns) per 64-column slice,
+// kCorr = factor of the per-block correction sum, PAIR_LANES: a builder lane
+// takes one row pair for every block of the slice (else lanes split blocks)
 template <int T>
 struct Geo;
 template <>
 struct Geo<kQ4_K> {
   static constexpr int J = 2;
   static constexpr float kCorr = 1.0f;  // corr = sum x * (dmin * m)
+  static constexpr bool PAIR_LANES = true;
 };
 template <>
 struct Geo<kQ6_K> {
   static constexpr int J = 4;
   static constexpr float kCorr = 32.0f;  // value (q - 32) * d * sc
+  static constexpr bool PAIR_LANES = false;
 };
 template <>
 struct Geo<kQ8_0> {
   static constexpr int J = 2;
   static constexpr float kCorr = 128.0f;  // stored u = q + 128
+  static constexpr bool PAIR_LANES = false;
 };
 template <>
 struct Geo<kQ4_0> {
   static constexpr int J = 2;
   static constexpr float kCorr = 8.0f;  // value (q - 8) * d
+  static constexpr bool PAIR_LANES = true;
 };
 
-// Coefficients of this warp's slice for the stage.  Lane l handles the row
-// pair (2p, 2p+1), p = l % 16, for block jb = l / 16 (Q6_K: jb and jb + 2).
-// Table word of (group gi, block j, split s, pair p): (gi*J + j)*24 + s*8 +
-// (p%4)*2 + (p%8)/4, so fragment lane (g, c) reads words (g*4 + c)*2, +1.
+// groups per stage for a chunk of this type and group size (the coefficient
+// table holds groups x blocks <= 8)
+__host__ __device__ inline uint32_t stage_groups(uint32_t gbytes, int type) {
+  const uint32_t cap = (type == kQ6_K || type == kQ8_0) ? 2u : kMaxStageGroups;
+  const uint32_t n = kStageTarget / gbytes;
+  return n < 1 ? 1 : (n > cap ? cap : n);
+}
+
+// Coefficients of this warp's slice for the stage (ng groups, rows of x in
+// xs).  Table word of (group gi, block j, split s, row pair p): (gi*J + j)*24
+// + s*8 + (p%4)*2 + (p%8)/4, so fragment lane (g, c) reads words (g*4+c)*2, +1.
 template <int T>
 __device__ __forceinline__ void build(const uint8_t *stage, uint32_t gbytes, uint32_t w, uint32_t slice,
-                                      uint32_t nblk, uint32_t ng, const float *xs, const float *nw, bool norm,
-                                      float inv, uint32_t lane, uint32_t *tbl, float (&corr)[2]) {
+                                      uint32_t nblk, uint32_t ng, const float *xs, uint32_t lane, uint32_t *tbl,
+                                      float (&corr)[2]) {
   constexpr int J = Geo<T>::J;
-  const uint32_t p = lane & 15, jb = lane >> 4;
-  if (2 * p >= 16 * ng || jb >= nblk) return;
-  float2 x = *reinterpret_cast<const float2 *>(xs + 2 * p);
-  if (norm) {  // rms_norm: (x * inv) * w   (src/tensor.rs:280-290)
-    const float2 n = *reinterpret_cast<const float2 *>(nw + 2 * p);
-    x.x = __fmul_rn(__fmul_rn(x.x, inv), n.x);
-    x.y = __fmul_rn(__fmul_rn(x.y, inv), n.y);
-  }
+  const uint32_t p = Geo<T>::PAIR_LANES ? lane : (lane & 15), jb = Geo<T>::PAIR_LANES ? 0 : (lane >> 4);
+  if (p >= 8 * ng || jb >= nblk) return;
+  const float2 x = *reinterpret_cast<const float2 *>(xs + 2 * p);
   const uint32_t gi = p >> 3, rr = 2 * (p & 7);
   const uint8_t *G = stage + gi * gbytes;
   uint32_t *dst = tbl + gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1);
   if constexpr (T == kQ4_K) {
-    const uint32_t s = slice >> 2, sb = 2 * (slice & 3) + jb, bit = 12 * sb, fw = bit >> 5, fs = bit & 31;
+    // the slice's two sub-blocks are adjacent 12-bit fields: 24 bits at bit 24*(slice%4)
+    const uint32_t s = slice >> 2, q4 = slice & 3, fs = (24 * q4) & 31;
     const uint4 h0 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr) * 16);
     const uint4 h1 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr + 1) * 16);
-    const uint32_t f0 = __funnelshift_r(fw == 0 ? h0.y : (fw == 1 ? h0.z : h0.w), fw == 0 ? h0.z : h0.w, fs);
-    const uint32_t f1 = __funnelshift_r(fw == 0 ? h1.y : (fw == 1 ? h1.z : h1.w), fw == 0 ? h1.z : h1.w, fs);
+    const uint32_t f0 = __funnelshift_r(q4 < 2 ? h0.y : (q4 == 2 ? h0.z : h0.w), q4 < 2 ? h0.z : h0.w, fs);
+    const uint32_t f1 = __funnelshift_r(q4 < 2 ? h1.y : (q4 == 2 ? h1.z : h1.w), q4 < 2 ? h1.z : h1.w, fs);
     const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
     const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
-    // d1 = d * sc, m1 = dmin * m as the dequantisation computes them
-    const float d10 = __fmul_rn(dd0.x, u2f_small(f0 & 63u)), m10 = __fmul_rn(dd0.y, u2f_small((f0 >> 6) & 63u));
-    const float d11 = __fmul_rn(dd1.x, u2f_small(f1 & 63u)), m11 = __fmul_rn(dd1.y, u2f_small((f1 >> 6) & 63u));
-    corr[0] = __fadd_rn(__fadd_rn(corr[0], __fmul_rn(x.x, m10)), __fmul_rn(x.y, m11));
-    split_store(__fmul_rn(__fmul_rn(x.x, d10), kBScale), __fmul_rn(__fmul_rn(x.y, d11), kBScale),
-                dst + jb * 24);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      // d1 = d * sc, m1 = dmin * m as the dequantisation computes them
+      const float d10 = __fmul_rn(dd0.x, u2f_small((f0 >> (12 * j)) & 63u));
+      const float d11 = __fmul_rn(dd1.x, u2f_small((f1 >> (12 * j)) & 63u));
+      const float m10 = __fmul_rn(dd0.y, u2f_small((f0 >> (12 * j + 6)) & 63u));
+      const float m11 = __fmul_rn(dd1.y, u2f_small((f1 >> (12 * j + 6)) & 63u));
+      corr[j] = __fadd_rn(__fadd_rn(corr[j], __fmul_rn(x.x, m10)), __fmul_rn(x.y, m11));
+      split_store(__fmul_rn(__fmul_rn(x.x, d10), kBScale), __fmul_rn(__fmul_rn(x.y, d11), kBScale), dst + j * 24);
+    }
+  } else if constexpr (T == kQ4_0) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j >= (int)nblk) break;
+      const float2 dd =
+          __half22float2(*reinterpret_cast<const __half2 *>(G + 8 * w + ((2 * slice + j) * 16 + rr) * 2));
+      const float c0 = __fmul_rn(x.x, dd.x), c1 = __fmul_rn(x.y, dd.y);
+      corr[j] = __fadd_rn(__fadd_rn(corr[j], c0), c1);
+      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + j * 24);
+    }
   } else if constexpr (T == kQ6_K) {
     const uint32_t s = slice >> 2;
     const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(G + 13 * w + (16 * s + rr) * 2));
@@ -165,34 +195,25 @@ __device__ __forceinline__ void build(const uint8_t *stage, uint32_t gbytes, uin
       corr[q] = __fadd_rn(__fadd_rn(corr[q], c0), c1);
       split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + j * 24);
     }
-  } else {  // Q8_0 / Q4_0: one f16 d per row and 32-column block
-    const uint32_t off = (T == kQ8_0 ? 16 : 8) * w;
+  } else {  // Q8_0: one f16 d per row and 32-column block
     const float2 dd =
-        __half22float2(*reinterpret_cast<const __half2 *>(G + off + ((2 * slice + jb) * 16 + rr) * 2));
+        __half22float2(*reinterpret_cast<const __half2 *>(G + 16 * w + ((2 * slice + jb) * 16 + rr) * 2));
     const float c0 = __fmul_rn(x.x, dd.x), c1 = __fmul_rn(x.y, dd.y);
     corr[0] = __fadd_rn(__fadd_rn(corr[0], c0), c1);
     split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + jb * 24);
   }
 }
 
-// the MMAs of one 16-row group for this warp's slice (NT tiles)
+// the MMAs of one 16-row group for this warp's slice (NT tiles); bsrc is
+// this lane's B-fragment source (its table column, or the zero area)
 template <int T, int NT>
 __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t slice, uint32_t lane,
-                                          const uint32_t *tblg, float (&D)[4][4], float (&Dh)[4][4]) {
+                                          const uint32_t *bsrc, float (&D)[4][4], float (&Dh)[4][4]) {
   constexpr int J = Geo<T>::J;
   constexpr int JN = (NT == 4) ? J : J / 2;
-  const uint32_t g = lane >> 2, c = lane & 3;
-  uint32_t b[JN][2];
+  uint2 b[JN];
 #pragma unroll
-  for (int j = 0; j < JN; ++j) {
-    if (g < 3) {
-      const uint2 v = *reinterpret_cast<const uint2 *>(tblg + j * 24 + (g * 4 + c) * 2);
-      b[j][0] = v.x;
-      b[j][1] = v.y;
-    } else {
-      b[j][0] = b[j][1] = 0u;
-    }
-  }
+  for (int j = 0; j < JN; ++j) b[j] = *reinterpret_cast<const uint2 *>(bsrc + j * 24);
   if constexpr (T == kQ8_0) {
     uint32_t q[2 * NT];
     const uint4 *src = reinterpret_cast<const uint4 *>(G + 1024 * slice + 8 * NT * lane);
@@ -208,7 +229,7 @@ __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t
     for (int t = 0; t < NT; ++t) {
       const uint32_t P = q[2 * t], Q = q[2 * t + 1];
       mma_bf16(D[t], P & 0x00FF00FFu, (P >> 8) & 0x00FF00FFu, Q & 0x00FF00FFu, (Q >> 8) & 0x00FF00FFu,
-               b[t >> 1][0], b[t >> 1][1]);
+               b[t >> 1].x, b[t >> 1].y);
     }
   } else {
     uint32_t q[NT];
@@ -227,14 +248,14 @@ __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t
     for (int t = 0; t < NT; ++t) {
       const uint32_t W = q[t], S = W >> 8;
       const int j = (T == kQ6_K) ? t : (t >> 1);
-      mma_bf16(D[t], W & 0x000F000Fu, W & 0x00F000F0u, S & 0x000F000Fu, S & 0x00F000F0u, b[j][0], b[j][1]);
+      mma_bf16(D[t], W & 0x000F000Fu, W & 0x00F000F0u, S & 0x000F000Fu, S & 0x00F000F0u, b[j].x, b[j].y);
     }
     if constexpr (T == kQ6_K) {
       const uint2 hw = *reinterpret_cast<const uint2 *>(G + 8 * w + 256 * slice + 8 * lane);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const uint32_t H = (t < 2 ? hw.x : hw.y) >> (2 * (t & 1)), S = H >> 8;
-        mma_bf16(Dh[t], H & 0x00030003u, H & 0x00300030u, S & 0x00030003u, S & 0x00300030u, b[t][0], b[t][1]);
+        mma_bf16(Dh[t], H & 0x00030003u, H & 0x00300030u, S & 0x00030003u, S & 0x00300030u, b[t].x, b[t].y);
       }
     }
   }
@@ -245,8 +266,9 @@ __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t
 template <int T, int NT>
 __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)[4][4], float (&Dh)[4][4],
                                            float (&corr)[2]) {
+  constexpr int kOff = Geo<T>::PAIR_LANES ? 16 : 8;  // builder lanes sharing a block
 #pragma unroll
-  for (int o = 8; o; o >>= 1) {
+  for (int o = kOff; o; o >>= 1) {
     corr[0] += __shfl_xor_sync(0xFFFFFFFFu, corr[0], o);
     corr[1] += __shfl_xor_sync(0xFFFFFFFFu, corr[1], o);
   }
@@ -258,8 +280,10 @@ __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)
 #pragma unroll
     for (int i = 0; i < 4; ++i) d[i] = (T == kQ6_K) ? fmaf(16.0f, Dh[t][i], D[t][i]) : D[t][i];
     const float lo0 = __shfl_down_sync(0xFFFFFFFFu, d[0], 1), lo8 = __shfl_down_sync(0xFFFFFFFFu, d[2], 1);
-    const float cr = (T == kQ6_K) ? __shfl_sync(0xFFFFFFFFu, t < 2 ? corr[0] : corr[1], 16 * (t & 1))
-                                  : __shfl_sync(0xFFFFFFFFu, corr[0], 16 * (t >> 1));
+    float cr;
+    if constexpr (Geo<T>::PAIR_LANES) cr = corr[t >> 1];
+    else if constexpr (T == kQ6_K) cr = __shfl_sync(0xFFFFFFFFu, t < 2 ? corr[0] : corr[1], 16 * (t & 1));
+    else cr = __shfl_sync(0xFFFFFFFFu, corr[0], 16 * (t >> 1));
     const float cv = __fmul_rn(Geo<T>::kCorr, cr);
     if (c == 0) {
       __stcg(dst + 16 * t + g, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv));
@@ -268,48 +292,40 @@ __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)
   }
 }
 
-// stage iteration over the CTA's (chunk, 16-row group) range, up to two
-// groups of one chunk per stage
-struct StageIt {
-  uint32_t c, g, ng, gend;
-  bool last_of_chunk;
+// stage sequence of a CTA: u = CTA-local index of the stage's first unit,
+// (c, g) its chunk and group, ng groups, last = the CTA's rows of chunk c end
+struct Stage {
+  uint32_t u, c, g, ng;
+  bool last;
 };
-__device__ __forceinline__ bool stage_set(const GemvParams &p, const CtaRange &R, StageIt &it) {
-  const uint32_t gtot = p.K / 16;
-  if (it.c > R.c1 || (it.c == R.c1 && it.g >= R.g1)) return false;
-  it.gend = it.c == R.c1 ? R.g1 : gtot;
-  it.ng = min(2u, it.gend - it.g);
-  it.last_of_chunk = it.g + it.ng == it.gend;
-  return true;
+__device__ __forceinline__ void stage_fill(const GemvParams &p, uint32_t n_units, uint32_t G, Stage &st) {
+  const uint32_t sg = p.chunks[st.c].sgroups;
+  st.ng = min(min(sg, G - st.g), n_units - st.u);
+  st.last = (st.g + st.ng == G) || (st.u + st.ng == n_units);
 }
-__device__ __forceinline__ bool stage_first(const GemvParams &p, const CtaRange &R, StageIt &it) {
-  it.c = R.c0;
-  it.g = R.g0;
-  return stage_set(p, R, it);
-}
-__device__ __forceinline__ bool stage_next(const GemvParams &p, const CtaRange &R, StageIt &it) {
-  it.g += it.ng;
-  if (it.g >= it.gend) {
-    it.c += 1;
-    it.g = 0;
+__device__ __forceinline__ void stage_advance(const GemvParams &p, uint32_t n_units, uint32_t G, Stage &st) {
+  st.u += st.ng;
+  st.g += st.ng;
+  if (st.g == G) {
+    st.g = 0;
+    st.c += 1;
   }
-  return stage_set(p, R, it);
+  if (st.u < n_units) stage_fill(p, n_units, G, st);
 }
 
 template <int T>
-__device__ __forceinline__ void run_stage(const GemvParams &p, const uint8_t *base, const ChunkDesc &cd, uint32_t ng,
-                                          const float *xs, const float *nw, bool norm, float inv, uint32_t warp,
-                                          uint32_t lane, uint32_t *tbl, float (&D)[4][4], float (&Dh)[4][4],
-                                          float (&corr)[2]) {
+__device__ __forceinline__ void run_stage(const uint8_t *base, const ChunkDesc &cd, uint32_t ng, const float *xs,
+                                          uint32_t warp, uint32_t lane, uint32_t *tbl, const uint32_t *bsrc,
+                                          float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
   const uint32_t w = cd.width, nt = min(64u, w - 64 * warp) / 16;
   const uint32_t nblk = (nt == 4) ? Geo<T>::J : Geo<T>::J / 2;
-  build<T>(base, cd.gbytes, w, warp, nblk, ng, xs, nw, norm, inv, lane, tbl, corr);
+  build<T>(base, cd.gbytes, w, warp, nblk, ng, xs, lane, tbl, corr);
   __syncwarp();
   for (uint32_t gi = 0; gi < ng; ++gi) {
-    const uint8_t *G = base + gi * cd.gbytes;
-    const uint32_t *tblg = tbl + gi * Geo<T>::J * 24;
-    if (nt == 4) mma_group<T, 4>(G, w, warp, lane, tblg, D, Dh);
-    else mma_group<T, 2>(G, w, warp, lane, tblg, D, Dh);
+    const uint8_t *Gp = base + gi * cd.gbytes;
+    const uint32_t *bg = bsrc + gi * Geo<T>::J * 24;
+    if (nt == 4) mma_group<T, 4>(Gp, w, warp, lane, bg, D, Dh);
+    else mma_group<T, 2>(Gp, w, warp, lane, bg, D, Dh);
   }
   __syncwarp();
 }
@@ -330,59 +346,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
   const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const CtaRange R = p.ranges[blockIdx.x];
   const bool norm = p.pro == kProRmsNorm;
+  const uint32_t G = p.K / 16;
+  const uint32_t start = R.c0 * G + R.g0, end = R.c1 * G + R.g1;
+  const uint32_t n_units = end > start ? end - start : 0;
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (uint32_t i = 0; i < p.n_stages; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kWarps);
     }
     fence_mbar_init();
   }
+  for (uint32_t i = tid; i < kZeroWords; i += kThreads) sm.zero[i] = 0u;
   __syncthreads();
   pdl_launch_dependents();
 
   bool ok = true;
   if (warp == kWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      StageIt it;
-      uint32_t s = 0;
-      bool more = stage_first(p, R, it);
-      // weights of the first slots before waiting on the previous kernel
-      for (; more && s < kStages; ++s) {
-        const ChunkDesc &cd = p.chunks[it.c];
-        const uint32_t wb = it.ng * cd.gbytes, xb = it.ng * 64 * (norm ? 2 : 1);
-        mbar_arrive_expect_tx(&sm.full[s], wb + xb);
-        bulk_g2s(sm.stages + s * p.stage_bytes, p.w + cd.offset + (uint64_t)it.g * cd.gbytes, wb, &sm.full[s]);
-        more = stage_next(p, R, it);
-      }
-      pdl_wait();
-      {  // activations of those slots
-        StageIt jt;
-        bool m2 = stage_first(p, R, jt);
-        for (uint32_t t = 0; m2 && t < s; ++t) {
-          bulk_g2s(sm.xs + t * kRows, p.in + jt.g * 16, jt.ng * 64, &sm.full[t]);
-          if (norm) bulk_g2s(sm.nw + t * kRows, p.norm_w + jt.g * 16, jt.ng * 64, &sm.full[t]);
-          m2 = stage_next(p, R, jt);
-        }
-      }
-      for (; more; ++s) {
-        const uint32_t slot = s % kStages;
-        if (!mbar_wait(&sm.empty[slot], ((s / kStages) - 1) & 1u)) {
+    // ---------------- producer: weights only (static, no dependency wait) ----------------
+    if (lane == 0 && n_units) {
+      Stage st{0, R.c0, R.g0, 0, false};
+      stage_fill(p, n_units, G, st);
+      for (uint32_t s = 0;; ++s) {
+        const uint32_t slot = s % p.n_stages;
+        if (s >= p.n_stages && !mbar_wait_sleep(&sm.empty[slot], ((s / p.n_stages) - 1) & 1u)) {
           ok = false;  // consumers time out on their own waits and unwind
           break;
         }
-        fence_proxy_async_smem();
-        const ChunkDesc &cd = p.chunks[it.c];
-        const uint32_t wb = it.ng * cd.gbytes, xb = it.ng * 64 * (norm ? 2 : 1);
-        mbar_arrive_expect_tx(&sm.full[slot], wb + xb);
-        bulk_g2s(sm.stages + slot * p.stage_bytes, p.w + cd.offset + (uint64_t)it.g * cd.gbytes, wb, &sm.full[slot]);
-        bulk_g2s(sm.xs + slot * kRows, p.in + it.g * 16, it.ng * 64, &sm.full[slot]);
-        if (norm) bulk_g2s(sm.nw + slot * kRows, p.norm_w + it.g * 16, it.ng * 64, &sm.full[slot]);
-        more = stage_next(p, R, it);
+        const ChunkDesc &cd = p.chunks[st.c];
+        const uint32_t wb = st.ng * cd.gbytes;
+        mbar_arrive_expect_tx(&sm.full[slot], wb);
+        bulk_g2s(sm.ring + slot * p.stage_bytes, p.w + cd.offset + (uint64_t)st.g * cd.gbytes, wb, &sm.full[slot]);
+        if (st.u + st.ng >= n_units) break;
+        stage_advance(p, n_units, G, st);
       }
-    } else {
-      pdl_wait();
     }
   } else {
     // ---------------- consumers ----------------
@@ -390,82 +387,104 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
     if (norm) {
       if (warp == 0) {
         float s = 0.0f;
-        for (uint32_t i = lane; i < p.n_ssq; i += 32) s += p.ssq[i];
+        for (uint32_t i = lane; i < p.n_ssq; i += 32) s += __ldcg(p.ssq + i);
 #pragma unroll
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
         if (lane == 0) sm.red[96] = 1.0f / sqrtf(s / (float)p.K + p.eps);
       }
       epi::consumer_bar<kWarps>();
     }
-    const float inv = norm ? sm.red[96] : 1.0f;
+    // the CTA's rows of x, in unit order: xs[16u + r] = x[16 g(u) + r]
+    {
+      const float inv = norm ? sm.red[96] : 1.0f;
+      for (uint32_t i = tid; i < n_units * 16; i += kWarps * 32) {
+        const uint32_t k = 16 * ((start + i / 16) % G) + (i & 15);
+        float v = __ldcg(p.in + k);
+        if (norm) v = __fmul_rn(__fmul_rn(v, inv), p.norm_w[k]);  // rms_norm (src/tensor.rs:280-290)
+        sm.xs[i] = v;
+      }
+    }
+    epi::consumer_bar<kWarps>();
     uint32_t *tbl = sm.tbl + warp * kTblWords;
+    const uint32_t *bsrc = ((lane >> 2) < 3 ? tbl + ((lane >> 2) * 4 + (lane & 3)) * 2 : sm.zero + (lane & 3) * 2);
     float D[4][4], Dh[4][4], corr[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int t = 0; t < 4; ++t)
 #pragma unroll
       for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-    StageIt it;
-    uint32_t s = 0;
-    for (bool more = stage_first(p, R, it); more; more = stage_next(p, R, it), ++s) {
-      const uint32_t slot = s % kStages;
-      // after a timed-out wait the warp keeps the loop's barrier structure but
-      // skips the work; the error flag tells the host the result is void
-      if (ok && !mbar_wait(&sm.full[slot], (s / kStages) & 1u)) ok = false;
-      const ChunkDesc cd = p.chunks[it.c];
-      const bool active = ok && 64 * warp < cd.width;
-      if (active) {
-        const uint8_t *base = sm.stages + slot * p.stage_bytes;
-        const float *xs = sm.xs + slot * kRows, *nw = sm.nw + slot * kRows;
-        switch (cd.type) {
-          case kQ4_K: run_stage<kQ4_K>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
-          case kQ6_K: run_stage<kQ6_K>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
-          case kQ8_0: run_stage<kQ8_0>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
-          default: run_stage<kQ4_0>(p, base, cd, it.ng, xs, nw, norm, inv, warp, lane, tbl, D, Dh, corr); break;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[slot]);
-      if (it.last_of_chunk) {
-        const uint32_t slot_p = blockIdx.x * p.max_chunks_per_cta + (it.c - R.c0);
+    if (n_units) {
+      Stage st{0, R.c0, R.g0, 0, false};
+      stage_fill(p, n_units, G, st);
+      for (uint32_t s = 0;; ++s) {
+        const uint32_t slot = s % p.n_stages;
+        // after a timed-out wait the warp keeps the loop's barrier structure but
+        // skips the work; the error flag tells the host the result is void
+        if (ok && !mbar_wait_sleep(&sm.full[slot], (s / p.n_stages) & 1u)) ok = false;
+        const ChunkDesc cd = p.chunks[st.c];
+        const bool active = ok && 64 * warp < cd.width;
         if (active) {
+          const uint8_t *base = sm.ring + slot * p.stage_bytes;
+          const float *xs = sm.xs + 16 * st.u;
           switch (cd.type) {
-            case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-            case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-            case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-            default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+            case kQ4_K: run_stage<kQ4_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
+            case kQ6_K: run_stage<kQ6_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
+            case kQ8_0: run_stage<kQ8_0>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
+            default: run_stage<kQ4_0>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (st.last) {
+          const uint32_t slot_p = blockIdx.x * p.max_chunks_per_cta + (st.c - R.c0);
+          if (active) {
+            switch (cd.type) {
+              case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+              case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+              case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+              default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+            }
+          }
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
+          for (int t = 0; t < 4; ++t)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-        corr[0] = corr[1] = 0.0f;
-        __threadfence();
-        epi::consumer_bar<kWarps>();
-        if (tid == 0) {
-          const uint32_t old = atomicAdd(p.counters + it.c, 1u);
-          *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
-        }
-        epi::consumer_bar<kWarps>();
-        if (*sm.flag) {
+            for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+          corr[0] = corr[1] = 0.0f;
           __threadfence();
-          epi::epilogue<kWarps>(p, sm.red, cd, it.c, tid, warp, lane);
-          if (tid == 0) p.counters[it.c] = 0;  // ready for the next launch
+          epi::consumer_bar<kWarps>();
+          if (tid == 0) {
+            const uint32_t old = atomicAdd(p.counters + st.c, 1u);
+            *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
+          }
+          epi::consumer_bar<kWarps>();
+          if (*sm.flag) {
+            __threadfence();
+            epi::epilogue<kWarps>(p, sm.red, cd, st.c, tid, warp, lane);
+            if (tid == 0) p.counters[st.c] = 0;  // ready for the next launch
+          }
+          epi::consumer_bar<kWarps>();
         }
-        epi::consumer_bar<kWarps>();
+        if (st.u + st.ng >= n_units) break;
+        stage_advance(p, n_units, G, st);
       }
     }
   }
   if (!ok && p.state) atomicOr(&p.state->err, kErrWaitTimeout);
 }
 
+uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type) { return stage_groups(gbytes, type); }
+
 size_t gemv_mma_smem_bytes(const GemvParams &p) {
-  return 128 + 512 + (size_t)kStages * p.stage_bytes + 2 * (size_t)kStages * kRows * 4 +
-         (size_t)kWarps * kTblWords * 4;
+  return ring_offset(p.max_units) + (size_t)p.n_stages * p.stage_bytes;
+}
+
+uint32_t gemv_mma_stages(uint32_t stage_bytes, uint32_t max_units, size_t smem_budget) {
+  const size_t fixed = ring_offset(max_units);
+  const size_t n = smem_budget > fixed ? (smem_budget - fixed) / stage_bytes : 0;
+  return (uint32_t)(n > kMaxStages ? kMaxStages : n);
 }
 
 int gemv_mma_init() {
-  if (cudaFuncSetAttribute(k_gemv_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
+  if (cudaFuncSetAttribute(k_gemv_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
     return -1;
   return 0;
 }

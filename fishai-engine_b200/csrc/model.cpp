@@ -175,13 +175,15 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
       d.type = (uint16_t)a.type;
       d.width = (uint16_t)w;
       d.out_col = out_base[i] + c0;
+      d.sgroups = mma ? gemv_mma_stage_groups(d.gbytes, a.type) : 0;
       P.chunks.push_back(d);
       max_gb = std::max(max_gb, d.gbytes);
     }
   }
   if (mma) {
-    P.stage_bytes = 2 * ((max_gb + 15) / 16 * 16);  // two 16-row groups per stage
-    P.x_slot = 32;
+    P.stage_bytes = 0;  // the largest stage (sgroups whole groups) of any chunk
+    for (const ChunkDesc &d : P.chunks) P.stage_bytes = std::max(P.stage_bytes, d.sgroups * d.gbytes);
+    P.x_slot = 0;
   } else {
     P.stage_bytes = std::max<uint32_t>(16384, (max_gb + 15) / 16 * 16);
     uint32_t max_ng = 1;
@@ -224,6 +226,17 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     const uint32_t last = r.g1 > 0 ? r.c1 : r.c1 - 1;
     P.max_chunks_per_cta = std::max(P.max_chunks_per_cta, last - r.c0 + 1);
     for (uint32_t c = r.c0; c <= last; ++c) who[c].push_back((uint16_t)i);
+  }
+  if (mma) {
+    P.max_units = 1;
+    for (const CtaRange &r : P.ranges) {
+      const uint64_t a = (uint64_t)r.c0 * G + r.g0, b = (uint64_t)r.c1 * G + r.g1;
+      if (b > a) P.max_units = std::max<uint32_t>(P.max_units, (uint32_t)(b - a));
+    }
+    P.n_stages = gemv_mma_stages(P.stage_bytes, P.max_units, 227 * 1024);
+    if (P.n_stages < 2)
+      return fail(FA_ERR_UNSUPPORTED, "GEMV pipeline does not fit in shared memory (" +
+                                          std::to_string(P.max_units) + " row groups per CTA)");
   }
   P.contrib.clear();
   for (uint32_t c = 0; c < nc; ++c) {
@@ -433,6 +446,8 @@ GemvParams Model::gemv_base(const GemvPlan &P) const {
   p.K = P.K;
   p.K8 = P.K8;
   p.mma = P.mma ? 1 : 0;
+  p.n_stages = P.n_stages;
+  p.max_units = P.max_units;
   p.CW = P.CW;
   p.stage_bytes = P.stage_bytes;
   p.x_slot = P.x_slot;

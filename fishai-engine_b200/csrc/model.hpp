@@ -23,7 +23,7 @@ struct GemvPlan {
   uint16_t *d_contrib = nullptr;
   const uint8_t *w = nullptr;
   bool mma = false;           // MMA tile layout (k_gemv_mma)
-  uint32_t K = 0, K8 = 0, CW = 256, stage_bytes = 16384, x_slot = 64;
+  uint32_t K = 0, K8 = 0, CW = 256, stage_bytes = 16384, x_slot = 64, n_stages = 0, max_units = 0;
   uint32_t n_ctas = 0, max_chunks_per_cta = 1;
   uint64_t native_bytes = 0;  // algorithmic bytes (native GGML blocks)
 };

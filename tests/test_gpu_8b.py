@@ -1,0 +1,43 @@
+"""Greedy identity at full size: the 8B-shaped Q4_K_M synthetic model (Q6_K
+attn_v / ffn_down / output head), a 2048-token uniform prompt, f32 KV cache.
+The first 64 generated ids must equal the oracle's, committed as
+tests/golden/8b_greedy.json by tests/golden/make_golden.py (the oracle needs
+tens of minutes for this run, so the ids are a fixture rather than recomputed).
+Generation follows GenerationState::generate (src/model.rs:638-705):
+sequential prefill, re-feed of the last prompt token, greedy argmax."""
+import hashlib
+import json
+import os
+
+import pytest
+
+from fishai_engine import synth
+from fishai_engine.model import GenerationConfig, GenerationState, ModelWeights
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "8b_greedy.json")
+
+
+def _digest(path, nbytes=1 << 24):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        h.update(f.read(nbytes))
+    return h.hexdigest()
+
+
+def test_8b_q4_k_m_first_64_greedy_ids_match_golden():
+    g = json.load(open(GOLDEN))
+    path = synth.cached_preset(g["preset"])
+    # the synthetic file is the one the golden was made from
+    assert _digest(path) == g["gguf_sha256_first16MiB"]
+    m = ModelWeights.load_from_gguf(path)
+    try:
+        prompt = g["prompt"]
+        st = GenerationState(m, GenerationConfig(max_tokens=len(prompt) + len(g["greedy_ids"]), temperature=0.0,
+                                                 top_k=0, top_p=1.0, repetition_penalty=1.0))
+        ids = st.generate(prompt)
+        assert len(ids) == 64
+        assert ids == g["greedy_ids"]
+    finally:
+        m.close()
