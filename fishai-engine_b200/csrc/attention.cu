@@ -4,12 +4,14 @@
 // head (src/model.rs:374-394, src/tensor.rs:451-551): s = (q.k)*scale,
 // softmax over every cached position, o = sum p*v; GQA query head h reads kv
 // head h / (H/KVH) (expand_kv_heads, src/model.rs:500-526) — no copy here,
-// the kv head is indexed directly.  Grid (splits, KVH); a CTA handles all
-// query heads of one kv head over one contiguous slice of positions, keeps
-// an online softmax per head and writes (max, sum, unnormalised o) partials
-// that the o-projection GEMV combines in its prologue.
+// the kv head is indexed directly.  Grid (splits, KVH, query rows); a CTA
+// handles all query heads of one kv head over one contiguous slice of
+// positions, keeps an online softmax per head and writes (max, sum,
+// unnormalised o) partials; the last split CTA of a kv head combines them.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <atomic>
 
 #include "fa_dequant.cuh"
 #include "fa_device.cuh"
@@ -20,20 +22,45 @@ namespace fa {
 namespace {
 constexpr int kWarps = 4;
 constexpr int kMaxRep = 8;   // query heads per kv head
+constexpr int kTile = 32;    // positions per warp tile (one per lane in the score phase)
 
-template <bool F16>
-__device__ __forceinline__ float kv_load(const void *base, uint64_t idx) {
-  if (F16) return __half2float(reinterpret_cast<const __half *>(base)[idx]);
-  return reinterpret_cast<const float *>(base)[idx];
+// dynamic shared memory of one CTA: q [REP][hd] | per warp V tile [32][hd] |
+// per warp p [32][REP] | merge scratch m, l [kWarps][REP], o [kWarps][REP][hd]
+__host__ __device__ inline size_t attn_smem(uint32_t rep, uint32_t hd, bool f16) {
+  return (size_t)rep * hd * 4 + (size_t)kWarps * kTile * hd * (f16 ? 2 : 4) + (size_t)kWarps * kTile * rep * 4 +
+         (size_t)kWarps * rep * 8 + (size_t)kWarps * rep * hd * 4;
 }
 
-template <bool F16, int REP, int DPL>
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ uint4 ldg_nc(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+template <bool F16>
+__device__ __forceinline__ float elem(const void *row, uint32_t d) {
+  if (F16) return __half2float(reinterpret_cast<const __half *>(row)[d]);
+  return reinterpret_cast<const float *>(row)[d];
+}
+
+// One CTA = (split, kv head, query row).  Warp w takes the 32-position tiles
+// w, w+4, ... of the split.  Score phase: lane t owns position t of the tile
+// and forms q_r . k_t for the REP query heads of the kv head from 16-byte
+// loads of its K row; online softmax across tiles per warp.  The tile's V rows
+// are copied to shared memory (cp.async) while the scores are computed; in
+// the PV phase lane l owns dims l, l+32, ...  Warps merge in a fixed order,
+// the split partial (max, sum, unnormalised o) goes to global memory and the
+// last split CTA of the kv head combines all splits (fixed order).
+template <bool F16, int REP>
 __device__ void attn_body(const AttnParams &p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t split = blockIdx.x, kvh = blockIdx.y;
-  const uint32_t hd = p.kv.head_dim, KVH = p.kv.n_kv;
-  constexpr uint32_t rep = REP, dpl = DPL;
-  const uint32_t row = blockIdx.z;
+  const uint32_t split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const uint32_t hd = p.kv.head_dim, KVH = p.kv.n_kv, esz = F16 ? 2 : 4;
   const uint32_t T = p.kc ? p.t_fixed : p.state->len + 1;
   const float *qrow = p.q + (uint64_t)row * p.n_heads * hd;
   float *part = p.part + (uint64_t)row * p.n_heads * p.splits * (2 + hd);
@@ -41,87 +68,180 @@ __device__ void attn_body(const AttnParams &p) {
   float *outrow = p.out + (uint64_t)row * p.n_heads * hd;
   uint32_t L = (T + p.splits - 1) / p.splits;
   L = (L + 15) / 16 * 16;
-  const uint32_t t0 = split * L, t1 = min(T, t0 + L);
-  __shared__ float sm_m[kWarps][REP], sm_l[kWarps][REP];
-  __shared__ float sm_o[kWarps][REP][DPL * 32];
+  const uint32_t t0 = min(T, split * L), t1 = min(T, t0 + L);
 
-  float q[REP][DPL];
-  for (uint32_t r = 0; r < rep; ++r)
-    for (uint32_t i = 0; i < dpl; ++i) {
-      const uint32_t d = lane + 32 * i;
-      q[r][i] = d < hd ? qrow[(kvh * rep + r) * hd + d] : 0.0f;
-    }
+  float *qs = reinterpret_cast<float *>(smem_raw);                       // [REP][hd]
+  uint8_t *vt = smem_raw + (size_t)REP * hd * 4;                         // [kWarps][32][hd]
+  float *ps = reinterpret_cast<float *>(vt + (size_t)kWarps * kTile * hd * esz);  // [kWarps][32][REP]
+  float *sm_m = ps + kWarps * kTile * REP, *sm_l = sm_m + kWarps * REP;  // [kWarps][REP]
+  float *sm_o = sm_l + kWarps * REP;                                     // [kWarps][REP][hd]
+  for (uint32_t i = threadIdx.x; i < REP * hd; i += blockDim.x) qs[i] = qrow[kvh * REP * hd + i];
+  __syncthreads();
+
+  const uint8_t *base = p.kc ? nullptr
+                             : reinterpret_cast<const uint8_t *>(p.kv.base) + (uint64_t)p.layer * p.kv.layer_stride * esz;
+  const uint32_t *pt = p.kc ? nullptr : p.kv.page_table + (uint64_t)p.seq * p.kv.max_pages;
+  auto row_ptr = [&](uint32_t t, int is_v) -> const uint8_t * {
+    if (p.kc) return reinterpret_cast<const uint8_t *>(is_v ? p.vc : p.kc) + ((uint64_t)t * KVH + kvh) * hd * 4;
+    return base + kv_index(pt[t / 16], is_v, kvh, t % 16, 0, KVH, hd) * esz;
+  };
+  constexpr uint32_t DPL = 4;  // dims per lane in the PV phase (hd <= 128)
   float m[REP], l[REP], o[REP][DPL];
 #pragma unroll
-  for (uint32_t r = 0; r < REP; ++r) {
+  for (int r = 0; r < REP; ++r) {
     m[r] = -INFINITY;
     l[r] = 0.0f;
 #pragma unroll
     for (uint32_t i = 0; i < DPL; ++i) o[r][i] = 0.0f;
   }
-  const void *base = p.kc ? nullptr
-                         : reinterpret_cast<const uint8_t *>(p.kv.base) + (uint64_t)p.layer * p.kv.layer_stride * (F16 ? 2 : 4);
-  const uint32_t *pt = p.kc ? nullptr : p.kv.page_table + (uint64_t)p.seq * p.kv.max_pages;
-  for (uint32_t t = t0 + warp; t < t1; t += kWarps) {
-    float kk[DPL], vv[DPL];
-    if (p.kc) {
-      const uint64_t rb = ((uint64_t)t * KVH + kvh) * hd;
-      for (uint32_t i = 0; i < dpl; ++i) {
-        const uint32_t d = lane + 32 * i;
-        kk[i] = d < hd ? p.kc[rb + d] : 0.0f;
-        vv[i] = d < hd ? p.vc[rb + d] : 0.0f;
+  uint8_t *vw = vt + (size_t)warp * kTile * hd * esz;
+  float *pw = ps + warp * kTile * REP;
+  const uint32_t vw_s = (uint32_t)__cvta_generic_to_shared(vw);
+  const uint32_t chunks = hd * esz / 16;  // 16-byte pieces of one row
+  const bool vec = (hd * esz) % 16 == 0;
+  for (uint32_t tb = t0 + warp * kTile; tb < t1; tb += kWarps * kTile) {
+    const uint32_t nv = min((uint32_t)kTile, t1 - tb);
+    // V rows of the tile -> shared memory (asynchronous when rows are whole
+    // 16-byte pieces, element by element otherwise)
+    if (vec) {
+      for (uint32_t i = lane; i < nv * chunks; i += 32) {
+        const uint32_t tt = i / chunks, c = i % chunks;
+        cp_async16(vw_s + (tt * chunks + c) * 16, row_ptr(tb + tt, 1) + c * 16);
       }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     } else {
-      const uint32_t page = pt[t / 16], slot = t % 16;
-      for (uint32_t i = 0; i < dpl; ++i) {
-        const uint32_t d = lane + 32 * i;
-        kk[i] = d < hd ? kv_load<F16>(base, kv_index(page, 0, kvh, slot, d, KVH, hd)) : 0.0f;
-        vv[i] = d < hd ? kv_load<F16>(base, kv_index(page, 1, kvh, slot, d, KVH, hd)) : 0.0f;
+      for (uint32_t i = lane; i < nv * hd; i += 32) {
+        const uint32_t tt = i / hd, d = i % hd;
+        if (F16) reinterpret_cast<__half *>(vw)[i] = reinterpret_cast<const __half *>(row_ptr(tb + tt, 1))[d];
+        else reinterpret_cast<float *>(vw)[i] = reinterpret_cast<const float *>(row_ptr(tb + tt, 1))[d];
       }
     }
-    for (uint32_t r = 0; r < rep; ++r) {
-      float s = 0.0f;
-      for (uint32_t i = 0; i < dpl; ++i) s = fmaf(q[r][i], kk[i], s);
+    // scores: lane = position
+    float s[REP];
 #pragma unroll
-      for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
-      s *= p.scale;
-      const float mn = fmaxf(m[r], s);
-      const float a = expf(m[r] - mn), b = expf(s - mn);
-      l[r] = fmaf(l[r], a, b);
-      for (uint32_t i = 0; i < dpl; ++i) o[r][i] = fmaf(o[r][i], a, b * vv[i]);
-      m[r] = mn;
+    for (int r = 0; r < REP; ++r) s[r] = 0.0f;
+    const bool valid = lane < nv;
+    if (valid && !vec) {
+      const uint8_t *kr = row_ptr(tb + lane, 0);
+      for (uint32_t d = 0; d < hd; ++d) {
+        const float kd = elem<F16>(kr, d);
+#pragma unroll
+        for (int r = 0; r < REP; ++r) s[r] = fmaf(qs[r * hd + d], kd, s[r]);
+      }
+    } else if (valid) {
+      const uint8_t *kr = row_ptr(tb + lane, 0);
+      for (uint32_t c0 = 0; c0 < chunks; c0 += 8) {
+        uint4 kv8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (c0 + j < chunks) kv8[j] = ldg_nc(kr + (c0 + j) * 16);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (c0 + j >= chunks) break;
+          const uint32_t w4[4] = {kv8[j].x, kv8[j].y, kv8[j].z, kv8[j].w};
+          float kf[8];
+          uint32_t nk;
+          if (F16) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w4[e]));
+              kf[2 * e] = f.x;
+              kf[2 * e + 1] = f.y;
+            }
+            nk = 8;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) kf[e] = __uint_as_float(w4[e]);
+            nk = 4;
+          }
+          const uint32_t d0 = (c0 + j) * (F16 ? 8 : 4);
+#pragma unroll
+          for (int r = 0; r < REP; ++r) {
+            const float4 qa = *reinterpret_cast<const float4 *>(qs + r * hd + d0);
+            s[r] = fmaf(qa.x, kf[0], s[r]);
+            s[r] = fmaf(qa.y, kf[1], s[r]);
+            s[r] = fmaf(qa.z, kf[2], s[r]);
+            s[r] = fmaf(qa.w, kf[3], s[r]);
+            if (nk == 8) {
+              const float4 qb = *reinterpret_cast<const float4 *>(qs + r * hd + d0 + 4);
+              s[r] = fmaf(qb.x, kf[4], s[r]);
+              s[r] = fmaf(qb.y, kf[5], s[r]);
+              s[r] = fmaf(qb.z, kf[6], s[r]);
+              s[r] = fmaf(qb.w, kf[7], s[r]);
+            }
+          }
+        }
+      }
     }
+    // online softmax over the tile
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float sv = valid ? s[r] * p.scale : -INFINITY;
+      float mt = sv;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, off));
+      const float mn = fmaxf(m[r], mt);
+      const float alpha = expf(m[r] - mn);  // m[r] = -inf on the first tile: alpha = 0
+      const float pv = valid ? expf(sv - mn) : 0.0f;
+      float ls = pv;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) ls += __shfl_xor_sync(0xFFFFFFFFu, ls, off);
+      l[r] = fmaf(l[r], alpha, ls);
+      m[r] = mn;
+#pragma unroll
+      for (uint32_t i = 0; i < DPL; ++i) o[r][i] *= alpha;
+      pw[lane * REP + r] = pv;
+    }
+    if (vec) cp_async_wait_all();
+    __syncwarp();
+    // PV: lane owns dims lane + 32 i
+    for (uint32_t tt = 0; tt < nv; ++tt) {
+      float pr[REP];
+#pragma unroll
+      for (int r = 0; r < REP; ++r) pr[r] = pw[tt * REP + r];
+      const uint8_t *vr = vw + (size_t)tt * hd * esz;
+#pragma unroll
+      for (uint32_t i = 0; i < DPL; ++i) {
+        const uint32_t d = lane + 32 * i;
+        if (d < hd) {
+          const float v = elem<F16>(vr, d);
+#pragma unroll
+          for (int r = 0; r < REP; ++r) o[r][i] = fmaf(pr[r], v, o[r][i]);
+        }
+      }
+    }
+    __syncwarp();
   }
   // merge the warps (fixed order)
-  for (uint32_t r = 0; r < rep; ++r) {
+  for (uint32_t r = 0; r < REP; ++r) {
     if (lane == 0) {
-      sm_m[warp][r] = m[r];
-      sm_l[warp][r] = l[r];
+      sm_m[warp * REP + r] = m[r];
+      sm_l[warp * REP + r] = l[r];
     }
-    for (uint32_t i = 0; i < dpl; ++i) {
+    for (uint32_t i = 0; i < DPL; ++i) {
       const uint32_t d = lane + 32 * i;
-      if (d < hd) sm_o[warp][r][d] = o[r][i];
+      if (d < hd) sm_o[(warp * REP + r) * hd + d] = o[r][i];
     }
   }
   __syncthreads();
-  for (uint32_t idx = threadIdx.x; idx < rep * (hd + 2); idx += blockDim.x) {
+  for (uint32_t idx = threadIdx.x; idx < REP * (hd + 2); idx += blockDim.x) {
     const uint32_t r = idx / (hd + 2), c = idx % (hd + 2);
     float M = -INFINITY;
-    for (int wv = 0; wv < kWarps; ++wv) M = fmaxf(M, sm_m[wv][r]);
+    for (int wv = 0; wv < kWarps; ++wv) M = fmaxf(M, sm_m[wv * REP + r]);
     float out;
     if (c == 0) {
       out = M;
     } else {
       float acc = 0.0f;
       for (int wv = 0; wv < kWarps; ++wv) {
-        const float mw = sm_m[wv][r];
+        const float mw = sm_m[wv * REP + r];
         if (mw == -INFINITY) continue;
         const float e = expf(mw - M);
-        acc = fmaf(c == 1 ? sm_l[wv][r] : sm_o[wv][r][c - 2], e, acc);
+        acc = fmaf(c == 1 ? sm_l[wv * REP + r] : sm_o[(wv * REP + r) * hd + c - 2], e, acc);
       }
       out = acc;
     }
-    const uint32_t h = kvh * rep + r;
+    const uint32_t h = kvh * REP + r;
     part[((uint64_t)h * p.splits + split) * (2 + hd) + c] = out;
   }
   // the last split CTA of this kv head combines all splits (fixed order)
@@ -132,8 +252,8 @@ __device__ void attn_body(const AttnParams &p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (uint32_t idx = threadIdx.x; idx < rep * hd; idx += blockDim.x) {
-    const uint32_t r = idx / hd, dd = idx % hd, h = kvh * rep + r;
+  for (uint32_t idx = threadIdx.x; idx < REP * hd; idx += blockDim.x) {
+    const uint32_t r = idx / hd, dd = idx % hd, h = kvh * REP + r;
     const float *P = part + (uint64_t)h * p.splits * (2 + hd);
     float M = -INFINITY;
     for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(P + s * (2 + hd)));
@@ -150,33 +270,48 @@ __device__ void attn_body(const AttnParams &p) {
   if (threadIdx.x == 0) counters[kvh] = 0;
 }
 
-template <bool F16, int REP, int DPL>
+template <bool F16, int REP>
 __global__ void __launch_bounds__(kWarps * 32) k_attention(const AttnParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  attn_body<F16, REP, DPL>(p);
+  attn_body<F16, REP>(p);
 }
 
 template <int REP>
-void *pick_dpl(uint32_t hd, bool f16) {
-  if (hd <= 32) return f16 ? (void *)k_attention<true, REP, 1> : (void *)k_attention<false, REP, 1>;
-  if (hd <= 64) return f16 ? (void *)k_attention<true, REP, 2> : (void *)k_attention<false, REP, 2>;
-  return f16 ? (void *)k_attention<true, REP, 4> : (void *)k_attention<false, REP, 4>;
+void *pick(bool f16) {
+  return f16 ? (void *)k_attention<true, REP> : (void *)k_attention<false, REP>;
+}
+void *pick_kernel(uint32_t rep, bool f16) {
+  return rep == 1 ? pick<1>(f16) : rep == 2 ? pick<2>(f16) : rep == 4 ? pick<4>(f16) : rep == 8 ? pick<8>(f16) : nullptr;
 }
 }  // namespace
 
+// once per device: allow the kernels' dynamic shared memory
+int attention_init() {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  if (done.load() & (1ull << dev)) return 0;
+  for (uint32_t rep : {1u, 2u, 4u, 8u})
+    for (bool f16 : {false, true})
+      if (cudaFuncSetAttribute(pick_kernel(rep, f16), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)attn_smem(rep, 128, f16)) != cudaSuccess)
+        return -1;
+  done.fetch_or(1ull << dev);
+  return 0;
+}
+
 int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st) {
-  const uint32_t rep = p.n_heads / p.kv.n_kv;
-  if (p.kv.head_dim > 128 || rep > kMaxRep || p.n_heads % p.kv.n_kv) return -1;
+  const uint32_t rep = p.n_heads / p.kv.n_kv, hd = p.kv.head_dim;
   const bool f16 = p.kv.f16 != 0;
-  void *fn = rep == 1 ? pick_dpl<1>(p.kv.head_dim, f16)
-             : rep == 2 ? pick_dpl<2>(p.kv.head_dim, f16)
-             : rep == 4 ? pick_dpl<4>(p.kv.head_dim, f16)
-             : rep == 8 ? pick_dpl<8>(p.kv.head_dim, f16) : nullptr;
+  if (hd > 128 || rep > kMaxRep || p.n_heads % p.kv.n_kv) return -1;
+  void *fn = pick_kernel(rep, f16);
   if (!fn) return -1;
+  if (attention_init()) return -1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.kv.n_kv, p.q_rows ? p.q_rows : 1);
   cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = attn_smem(rep, hd, f16);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -124,6 +124,9 @@ struct AttnParams {
   float *out;              // [H*hd] combined attention output
   SeqState *state;         // T = len + 1
 };
+// attention_init: once per device (current), before the first launch_attention
+// of a stream capture; launch_attention calls it as well
+int attention_init();
 int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st);
 
 struct EmbedParams {

@@ -44,7 +44,7 @@ constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kMaxStages = 12;              // ring depth is p.n_stages (set from the shared-memory budget)
 constexpr uint32_t kMaxStageGroups = 4;     // row groups per stage
 constexpr uint32_t kStageTarget = 36 * 1024;
-constexpr uint32_t kTblWords = 8 * 24;      // per warp: (groups x blocks <= 8) x (3 splits x 4 lanes x 2 words)
+constexpr uint32_t kTblWords = 8 * 24;      // one table: (groups x blocks <= 8) x (3 splits x 4 lanes x 2 words)
 constexpr uint32_t kZeroWords = 256;        // B fragment source of the lanes whose column is unused
 // shared memory: mbarriers + flag | reduction scratch | zero area | tables | x | ring
 constexpr uint32_t kOffRed = 256, kOffZero = kOffRed + 512, kOffTbl = kOffZero + 4 * kZeroWords,
@@ -85,20 +85,48 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// explicit shared-window accesses (32-bit addresses)
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ float2 h2f2_bits(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+}
+
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // (v0, v1) -> hi + mid + lo, each a bf16 pair, exactly (8 + 8 + 8 bits);
-// written to the three split rows of the coefficient table
-__device__ __forceinline__ void split_store(float v0, float v1, uint32_t *dst) {
+// written to the three split rows of the coefficient table (word stride 8)
+__device__ __forceinline__ void split_store(float v0, float v1, uint32_t dst) {
   const uint32_t hi = bf2_bits(__floats2bfloat162_rn(v0, v1));
   const float r0 = __fsub_rn(v0, bf_lo(hi)), r1 = __fsub_rn(v1, bf_hi(hi));
   const uint32_t mid = bf2_bits(__floats2bfloat162_rn(r0, r1));
   const float s0 = __fsub_rn(r0, bf_lo(mid)), s1 = __fsub_rn(r1, bf_hi(mid));
-  dst[0] = hi;
-  dst[8] = mid;
-  dst[16] = bf2_bits(__floats2bfloat162_rn(s0, s1));
+  sts32(dst, hi);
+  sts32(dst + 32, mid);
+  sts32(dst + 64, bf2_bits(__floats2bfloat162_rn(s0, s1)));
 }
 
 // ---------------------------------------------------------------------------
@@ -140,29 +168,29 @@ __host__ __device__ inline uint32_t stage_groups(uint32_t gbytes, int type) {
   return n < 1 ? 1 : (n > cap ? cap : n);
 }
 
-// Coefficients of this warp's slice for the stage (ng groups, rows of x in
+// Coefficients of this warp's slice for the stage (ng groups, rows of x at
 // xs).  Table word of (group gi, block j, split s, row pair p): (gi*J + j)*24
 // + s*8 + (p%4)*2 + (p%8)/4, so fragment lane (g, c) reads words (g*4+c)*2, +1.
+// All addresses are shared-window byte addresses.
 template <int T>
-__device__ __forceinline__ void build(const uint8_t *stage, uint32_t gbytes, uint32_t w, uint32_t slice,
-                                      uint32_t nblk, uint32_t ng, const float *xs, uint32_t lane, uint32_t *tbl,
-                                      float (&corr)[2]) {
+__device__ __forceinline__ void build(uint32_t stage, uint32_t gbytes, uint32_t w, uint32_t slice, uint32_t nblk,
+                                      uint32_t ng, uint32_t xs, uint32_t lane, uint32_t tbl, float (&corr)[2]) {
   constexpr int J = Geo<T>::J;
   const uint32_t p = Geo<T>::PAIR_LANES ? lane : (lane & 15), jb = Geo<T>::PAIR_LANES ? 0 : (lane >> 4);
   if (p >= 8 * ng || jb >= nblk) return;
-  const float2 x = *reinterpret_cast<const float2 *>(xs + 2 * p);
+  const uint2 xb = lds64(xs + 8 * p);
+  const float x0 = __uint_as_float(xb.x), x1 = __uint_as_float(xb.y);
   const uint32_t gi = p >> 3, rr = 2 * (p & 7);
-  const uint8_t *G = stage + gi * gbytes;
-  uint32_t *dst = tbl + gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1);
+  const uint32_t G = stage + gi * gbytes;
+  const uint32_t dst = tbl + 4 * (gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1));
   if constexpr (T == kQ4_K) {
     // the slice's two sub-blocks are adjacent 12-bit fields: 24 bits at bit 24*(slice%4)
     const uint32_t s = slice >> 2, q4 = slice & 3, fs = (24 * q4) & 31;
-    const uint4 h0 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr) * 16);
-    const uint4 h1 = *reinterpret_cast<const uint4 *>(G + 8 * w + (16 * s + rr + 1) * 16);
+    const uint4 h0 = lds128(G + 8 * w + (16 * s + rr) * 16);
+    const uint4 h1 = lds128(G + 8 * w + (16 * s + rr + 1) * 16);
     const uint32_t f0 = __funnelshift_r(q4 < 2 ? h0.y : (q4 == 2 ? h0.z : h0.w), q4 < 2 ? h0.z : h0.w, fs);
     const uint32_t f1 = __funnelshift_r(q4 < 2 ? h1.y : (q4 == 2 ? h1.z : h1.w), q4 < 2 ? h1.z : h1.w, fs);
-    const float2 dd0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
-    const float2 dd1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
+    const float2 dd0 = h2f2_bits(h0.x), dd1 = h2f2_bits(h1.x);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       // d1 = d * sc, m1 = dmin * m as the dequantisation computes them
@@ -170,56 +198,53 @@ __device__ __forceinline__ void build(const uint8_t *stage, uint32_t gbytes, uin
       const float d11 = __fmul_rn(dd1.x, u2f_small((f1 >> (12 * j)) & 63u));
       const float m10 = __fmul_rn(dd0.y, u2f_small((f0 >> (12 * j + 6)) & 63u));
       const float m11 = __fmul_rn(dd1.y, u2f_small((f1 >> (12 * j + 6)) & 63u));
-      corr[j] = __fadd_rn(__fadd_rn(corr[j], __fmul_rn(x.x, m10)), __fmul_rn(x.y, m11));
-      split_store(__fmul_rn(__fmul_rn(x.x, d10), kBScale), __fmul_rn(__fmul_rn(x.y, d11), kBScale), dst + j * 24);
+      corr[j] = __fadd_rn(__fadd_rn(corr[j], __fmul_rn(x0, m10)), __fmul_rn(x1, m11));
+      split_store(__fmul_rn(__fmul_rn(x0, d10), kBScale), __fmul_rn(__fmul_rn(x1, d11), kBScale), dst + 96 * j);
     }
   } else if constexpr (T == kQ4_0) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       if (j >= (int)nblk) break;
-      const float2 dd =
-          __half22float2(*reinterpret_cast<const __half2 *>(G + 8 * w + ((2 * slice + j) * 16 + rr) * 2));
-      const float c0 = __fmul_rn(x.x, dd.x), c1 = __fmul_rn(x.y, dd.y);
+      const float2 dd = h2f2_bits(lds32(G + 8 * w + ((2 * slice + j) * 16 + rr) * 2));
+      const float c0 = __fmul_rn(x0, dd.x), c1 = __fmul_rn(x1, dd.y);
       corr[j] = __fadd_rn(__fadd_rn(corr[j], c0), c1);
-      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + j * 24);
+      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * j);
     }
   } else if constexpr (T == kQ6_K) {
     const uint32_t s = slice >> 2;
-    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(G + 13 * w + (16 * s + rr) * 2));
+    const float2 dd = h2f2_bits(lds32(G + 13 * w + (16 * s + rr) * 2));
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint32_t j = jb + 2 * q;
-      const uint32_t scw = *reinterpret_cast<const uint16_t *>(G + 12 * w + (4 * slice + j) * 16 + rr);
+      const uint32_t scw = lds16(G + 12 * w + (4 * slice + j) * 16 + rr);
       const float sc0 = (float)(int)(int8_t)(scw & 0xFFu), sc1 = (float)(int)(int8_t)(scw >> 8);
-      const float c0 = __fmul_rn(x.x, __fmul_rn(dd.x, sc0)), c1 = __fmul_rn(x.y, __fmul_rn(dd.y, sc1));
+      const float c0 = __fmul_rn(x0, __fmul_rn(dd.x, sc0)), c1 = __fmul_rn(x1, __fmul_rn(dd.y, sc1));
       corr[q] = __fadd_rn(__fadd_rn(corr[q], c0), c1);
-      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + j * 24);
+      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * j);
     }
   } else {  // Q8_0: one f16 d per row and 32-column block
-    const float2 dd =
-        __half22float2(*reinterpret_cast<const __half2 *>(G + 16 * w + ((2 * slice + jb) * 16 + rr) * 2));
-    const float c0 = __fmul_rn(x.x, dd.x), c1 = __fmul_rn(x.y, dd.y);
+    const float2 dd = h2f2_bits(lds32(G + 16 * w + ((2 * slice + jb) * 16 + rr) * 2));
+    const float c0 = __fmul_rn(x0, dd.x), c1 = __fmul_rn(x1, dd.y);
     corr[0] = __fadd_rn(__fadd_rn(corr[0], c0), c1);
-    split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + jb * 24);
+    split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * jb);
   }
 }
 
 // the MMAs of one 16-row group for this warp's slice (NT tiles); bsrc is
 // this lane's B-fragment source (its table column, or the zero area)
 template <int T, int NT>
-__device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t slice, uint32_t lane,
-                                          const uint32_t *bsrc, float (&D)[4][4], float (&Dh)[4][4]) {
+__device__ __forceinline__ void mma_group(uint32_t G, uint32_t w, uint32_t slice, uint32_t lane, uint32_t bsrc,
+                                          float (&D)[4][4], float (&Dh)[4][4]) {
   constexpr int J = Geo<T>::J;
   constexpr int JN = (NT == 4) ? J : J / 2;
   uint2 b[JN];
 #pragma unroll
-  for (int j = 0; j < JN; ++j) b[j] = *reinterpret_cast<const uint2 *>(bsrc + j * 24);
+  for (int j = 0; j < JN; ++j) b[j] = lds64(bsrc + 96 * j);
   if constexpr (T == kQ8_0) {
     uint32_t q[2 * NT];
-    const uint4 *src = reinterpret_cast<const uint4 *>(G + 1024 * slice + 8 * NT * lane);
 #pragma unroll
     for (int i = 0; i < NT / 2; ++i) {
-      const uint4 v = src[i];
+      const uint4 v = lds128(G + 1024 * slice + 8 * NT * lane + 16 * i);
       q[4 * i] = v.x;
       q[4 * i + 1] = v.y;
       q[4 * i + 2] = v.z;
@@ -234,13 +259,13 @@ __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t
   } else {
     uint32_t q[NT];
     if constexpr (NT == 4) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(G + 512 * slice + 16 * lane);
+      const uint4 v = lds128(G + 512 * slice + 16 * lane);
       q[0] = v.x;
       q[1] = v.y;
       q[2] = v.z;
       q[3] = v.w;
     } else {
-      const uint2 v = *reinterpret_cast<const uint2 *>(G + 512 * slice + 8 * lane);
+      const uint2 v = lds64(G + 512 * slice + 8 * lane);
       q[0] = v.x;
       q[1] = v.y;
     }
@@ -251,7 +276,7 @@ __device__ __forceinline__ void mma_group(const uint8_t *G, uint32_t w, uint32_t
       mma_bf16(D[t], W & 0x000F000Fu, W & 0x00F000F0u, S & 0x000F000Fu, S & 0x00F000F0u, b[j].x, b[j].y);
     }
     if constexpr (T == kQ6_K) {
-      const uint2 hw = *reinterpret_cast<const uint2 *>(G + 8 * w + 256 * slice + 8 * lane);
+      const uint2 hw = lds64(G + 8 * w + 256 * slice + 8 * lane);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const uint32_t H = (t < 2 ? hw.x : hw.y) >> (2 * (t & 1)), S = H >> 8;
@@ -314,16 +339,14 @@ __device__ __forceinline__ void stage_advance(const GemvParams &p, uint32_t n_un
 }
 
 template <int T>
-__device__ __forceinline__ void run_stage(const uint8_t *base, const ChunkDesc &cd, uint32_t ng, const float *xs,
-                                          uint32_t warp, uint32_t lane, uint32_t *tbl, const uint32_t *bsrc,
-                                          float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
+__device__ __forceinline__ void run_stage(uint32_t base, const ChunkDesc &cd, uint32_t ng, uint32_t xs, uint32_t warp,
+                                          uint32_t lane, uint32_t tbl, uint32_t bsrc, float (&D)[4][4],
+                                          float (&Dh)[4][4], float (&corr)[2]) {
   const uint32_t w = cd.width, nt = min(64u, w - 64 * warp) / 16;
-  const uint32_t nblk = (nt == 4) ? Geo<T>::J : Geo<T>::J / 2;
-  build<T>(base, cd.gbytes, w, warp, nblk, ng, xs, lane, tbl, corr);
+  build<T>(base, cd.gbytes, w, warp, (nt == 4) ? Geo<T>::J : Geo<T>::J / 2, ng, xs, lane, tbl, corr);
   __syncwarp();
   for (uint32_t gi = 0; gi < ng; ++gi) {
-    const uint8_t *Gp = base + gi * cd.gbytes;
-    const uint32_t *bg = bsrc + gi * Geo<T>::J * 24;
+    const uint32_t Gp = base + gi * cd.gbytes, bg = bsrc + gi * Geo<T>::J * 96;
     if (nt == 4) mma_group<T, 4>(Gp, w, warp, lane, bg, D, Dh);
     else mma_group<T, 2>(Gp, w, warp, lane, bg, D, Dh);
   }
@@ -405,8 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
       }
     }
     epi::consumer_bar<kWarps>();
-    uint32_t *tbl = sm.tbl + warp * kTblWords;
-    const uint32_t *bsrc = ((lane >> 2) < 3 ? tbl + ((lane >> 2) * 4 + (lane & 3)) * 2 : sm.zero + (lane & 3) * 2);
+    const uint32_t tbl = smem_u32(sm.tbl + warp * kTblWords);
+    const uint32_t bsrc = (lane >> 2) < 3 ? tbl + 8 * ((lane >> 2) * 4 + (lane & 3)) : smem_u32(sm.zero) + 8 * (lane & 3);
+    const uint32_t ring = smem_u32(sm.ring), xs0 = smem_u32(sm.xs);
     float D[4][4], Dh[4][4], corr[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int t = 0; t < 4; ++t)
@@ -423,8 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
         const ChunkDesc cd = p.chunks[st.c];
         const bool active = ok && 64 * warp < cd.width;
         if (active) {
-          const uint8_t *base = sm.ring + slot * p.stage_bytes;
-          const float *xs = sm.xs + 16 * st.u;
+          const uint32_t base = ring + slot * p.stage_bytes, xs = xs0 + 64 * st.u;
           switch (cd.type) {
             case kQ4_K: run_stage<kQ4_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
             case kQ6_K: run_stage<kQ6_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;

@@ -288,7 +288,8 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   graphs = o.use_graphs != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init() || gemv_mma_init()) return fail(FA_ERR_CUDA, "GEMV kernel attribute setup failed");
+  if (gemv_init() || gemv_mma_init() || attention_init())
+    return fail(FA_ERR_CUDA, "kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;
   gguf.reset(Gguf::open(path, &code));
