@@ -117,16 +117,24 @@ __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinter
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// (v0, v1) -> hi + mid + lo, each a bf16 pair, exactly (8 + 8 + 8 bits);
+// v -> hi + mid + lo, each a bf16 pair, exactly (8 + 8 + 8 bits): the
+// residuals v - hi and r - mid are exact in f32 (one packed FMA each);
 // written to the three split rows of the coefficient table (word stride 8)
-__device__ __forceinline__ void split_store(float v0, float v1, uint32_t dst) {
-  const uint32_t hi = bf2_bits(__floats2bfloat162_rn(v0, v1));
-  const float r0 = __fsub_rn(v0, bf_lo(hi)), r1 = __fsub_rn(v1, bf_hi(hi));
-  const uint32_t mid = bf2_bits(__floats2bfloat162_rn(r0, r1));
-  const float s0 = __fsub_rn(r0, bf_lo(mid)), s1 = __fsub_rn(r1, bf_hi(mid));
+__device__ __forceinline__ void split_store(float2 v, uint32_t dst) {
+  const float2 m1 = make_float2(-1.0f, -1.0f);
+  const uint32_t hi = bf2_bits(__floats2bfloat162_rn(v.x, v.y));
+  const float2 r = __ffma2_rn(make_float2(bf_lo(hi), bf_hi(hi)), m1, v);
+  const uint32_t mid = bf2_bits(__floats2bfloat162_rn(r.x, r.y));
+  const float2 t = __ffma2_rn(make_float2(bf_lo(mid), bf_hi(mid)), m1, r);
   sts32(dst, hi);
   sts32(dst + 32, mid);
-  sts32(dst + 64, bf2_bits(__floats2bfloat162_rn(s0, s1)));
+  sts32(dst + 64, bf2_bits(__floats2bfloat162_rn(t.x, t.y)));
+}
+
+// two small non-negative integers (< 2^23) -> floats, exactly
+__device__ __forceinline__ float2 u2f2(uint32_t a, uint32_t b, float bias) {
+  return __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | a), __uint_as_float(0x4B000000u | b)),
+                    make_float2(-8388608.0f - bias, -8388608.0f - bias));
 }
 
 // ---------------------------------------------------------------------------
@@ -144,19 +152,19 @@ struct Geo<kQ4_K> {
 template <>
 struct Geo<kQ6_K> {
   static constexpr int J = 4;
-  static constexpr float kCorr = 32.0f;  // value (q - 32) * d * sc
+  static constexpr float kCorr = 0x1p-91f;  // 32 * 2^-96: value (q - 32) * d * sc, corr sums c * 2^96
   static constexpr bool PAIR_LANES = false;
 };
 template <>
 struct Geo<kQ8_0> {
   static constexpr int J = 2;
-  static constexpr float kCorr = 128.0f;  // stored u = q + 128
+  static constexpr float kCorr = 0x1p-89f;  // 128 * 2^-96: stored u = q + 128, corr sums c * 2^96
   static constexpr bool PAIR_LANES = false;
 };
 template <>
 struct Geo<kQ4_0> {
   static constexpr int J = 2;
-  static constexpr float kCorr = 8.0f;  // value (q - 8) * d
+  static constexpr float kCorr = 0x1p-93f;  // 8 * 2^-96: value (q - 8) * d, corr sums c * 2^96
   static constexpr bool PAIR_LANES = true;
 };
 
@@ -179,7 +187,8 @@ __device__ __forceinline__ void build(uint32_t stage, uint32_t gbytes, uint32_t 
   const uint32_t p = Geo<T>::PAIR_LANES ? lane : (lane & 15), jb = Geo<T>::PAIR_LANES ? 0 : (lane >> 4);
   if (p >= 8 * ng || jb >= nblk) return;
   const uint2 xb = lds64(xs + 8 * p);
-  const float x0 = __uint_as_float(xb.x), x1 = __uint_as_float(xb.y);
+  const float2 x = make_float2(__uint_as_float(xb.x), __uint_as_float(xb.y));
+  const float2 xs96 = __fmul2_rn(x, make_float2(kBScale, kBScale));
   const uint32_t gi = p >> 3, rr = 2 * (p & 7);
   const uint32_t G = stage + gi * gbytes;
   const uint32_t dst = tbl + 4 * (gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1));
@@ -190,43 +199,39 @@ __device__ __forceinline__ void build(uint32_t stage, uint32_t gbytes, uint32_t 
     const uint4 h1 = lds128(G + 8 * w + (16 * s + rr + 1) * 16);
     const uint32_t f0 = __funnelshift_r(q4 < 2 ? h0.y : (q4 == 2 ? h0.z : h0.w), q4 < 2 ? h0.z : h0.w, fs);
     const uint32_t f1 = __funnelshift_r(q4 < 2 ? h1.y : (q4 == 2 ? h1.z : h1.w), q4 < 2 ? h1.z : h1.w, fs);
-    const float2 dd0 = h2f2_bits(h0.x), dd1 = h2f2_bits(h1.x);
+    const float2 dd0 = h2f2_bits(h0.x), dd1 = h2f2_bits(h1.x);    // (d, dmin) of the two rows
+    const float2 xd = __fmul2_rn(xs96, make_float2(dd0.x, dd1.x));  // x * d * 2^96
+    const float2 xm = __fmul2_rn(x, make_float2(dd0.y, dd1.y));     // x * dmin
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      // d1 = d * sc, m1 = dmin * m as the dequantisation computes them
-      const float d10 = __fmul_rn(dd0.x, u2f_small((f0 >> (12 * j)) & 63u));
-      const float d11 = __fmul_rn(dd1.x, u2f_small((f1 >> (12 * j)) & 63u));
-      const float m10 = __fmul_rn(dd0.y, u2f_small((f0 >> (12 * j + 6)) & 63u));
-      const float m11 = __fmul_rn(dd1.y, u2f_small((f1 >> (12 * j + 6)) & 63u));
-      corr[j] = __fadd_rn(__fadd_rn(corr[j], __fmul_rn(x0, m10)), __fmul_rn(x1, m11));
-      split_store(__fmul_rn(__fmul_rn(x0, d10), kBScale), __fmul_rn(__fmul_rn(x1, d11), kBScale), dst + 96 * j);
+      const float2 sc = u2f2((f0 >> (12 * j)) & 63u, (f1 >> (12 * j)) & 63u, 0.0f);
+      const float2 m = u2f2((f0 >> (12 * j + 6)) & 63u, (f1 >> (12 * j + 6)) & 63u, 0.0f);
+      corr[j] = fmaf(xm.x, m.x, fmaf(xm.y, m.y, corr[j]));
+      split_store(__fmul2_rn(xd, sc), dst + 96 * j);
     }
   } else if constexpr (T == kQ4_0) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       if (j >= (int)nblk) break;
-      const float2 dd = h2f2_bits(lds32(G + 8 * w + ((2 * slice + j) * 16 + rr) * 2));
-      const float c0 = __fmul_rn(x0, dd.x), c1 = __fmul_rn(x1, dd.y);
-      corr[j] = __fadd_rn(__fadd_rn(corr[j], c0), c1);
-      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * j);
+      const float2 c = __fmul2_rn(xs96, h2f2_bits(lds32(G + 8 * w + ((2 * slice + j) * 16 + rr) * 2)));
+      corr[j] += c.x + c.y;
+      split_store(c, dst + 96 * j);
     }
   } else if constexpr (T == kQ6_K) {
     const uint32_t s = slice >> 2;
-    const float2 dd = h2f2_bits(lds32(G + 13 * w + (16 * s + rr) * 2));
+    const float2 xd = __fmul2_rn(xs96, h2f2_bits(lds32(G + 13 * w + (16 * s + rr) * 2)));
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint32_t j = jb + 2 * q;
       const uint32_t scw = lds16(G + 12 * w + (4 * slice + j) * 16 + rr);
-      const float sc0 = (float)(int)(int8_t)(scw & 0xFFu), sc1 = (float)(int)(int8_t)(scw >> 8);
-      const float c0 = __fmul_rn(x0, __fmul_rn(dd.x, sc0)), c1 = __fmul_rn(x1, __fmul_rn(dd.y, sc1));
-      corr[q] = __fadd_rn(__fadd_rn(corr[q], c0), c1);
-      split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * j);
+      const float2 c = __fmul2_rn(xd, u2f2((scw & 0xFFu) ^ 0x80u, (scw >> 8) ^ 0x80u, 128.0f));  // int8 scales
+      corr[q] += c.x + c.y;
+      split_store(c, dst + 96 * j);
     }
   } else {  // Q8_0: one f16 d per row and 32-column block
-    const float2 dd = h2f2_bits(lds32(G + 16 * w + ((2 * slice + jb) * 16 + rr) * 2));
-    const float c0 = __fmul_rn(x0, dd.x), c1 = __fmul_rn(x1, dd.y);
-    corr[0] = __fadd_rn(__fadd_rn(corr[0], c0), c1);
-    split_store(__fmul_rn(c0, kBScale), __fmul_rn(c1, kBScale), dst + 96 * jb);
+    const float2 c = __fmul2_rn(xs96, h2f2_bits(lds32(G + 16 * w + ((2 * slice + jb) * 16 + rr) * 2)));
+    corr[0] += c.x + c.y;
+    split_store(c, dst + 96 * jb);
   }
 }
 
@@ -338,19 +343,44 @@ __device__ __forceinline__ void stage_advance(const GemvParams &p, uint32_t n_un
   if (st.u < n_units) stage_fill(p, n_units, G, st);
 }
 
+// The stages of one chunk segment of the CTA's range (seg groups starting at
+// CTA-local unit u): wait, build the coefficients, run the MMAs, release the
+// slot.  slot / phase walk the ring.
 template <int T>
-__device__ __forceinline__ void run_stage(uint32_t base, const ChunkDesc &cd, uint32_t ng, uint32_t xs, uint32_t warp,
-                                          uint32_t lane, uint32_t tbl, uint32_t bsrc, float (&D)[4][4],
-                                          float (&Dh)[4][4], float (&corr)[2]) {
-  const uint32_t w = cd.width, nt = min(64u, w - 64 * warp) / 16;
-  build<T>(base, cd.gbytes, w, warp, (nt == 4) ? Geo<T>::J : Geo<T>::J / 2, ng, xs, lane, tbl, corr);
-  __syncwarp();
-  for (uint32_t gi = 0; gi < ng; ++gi) {
-    const uint32_t Gp = base + gi * cd.gbytes, bg = bsrc + gi * Geo<T>::J * 96;
-    if (nt == 4) mma_group<T, 4>(Gp, w, warp, lane, bg, D, Dh);
-    else mma_group<T, 2>(Gp, w, warp, lane, bg, D, Dh);
+__device__ __forceinline__ void segment(const GemvParams &p, const Smem &sm, const ChunkDesc &cd, uint32_t seg,
+                                        uint32_t u, uint32_t warp, uint32_t lane, uint32_t tbl, uint32_t bsrc,
+                                        uint32_t ring, uint32_t xs0, uint32_t &slot, uint32_t &phase, bool &ok,
+                                        float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
+  const uint32_t w = cd.width, sg = cd.sgroups, gbytes = cd.gbytes;
+  const bool active = 64 * warp < w;
+  const uint32_t nt = active ? min(64u, w - 64 * warp) / 16 : 0;
+  const uint32_t nblk = (nt == 4) ? Geo<T>::J : Geo<T>::J / 2;
+  for (uint32_t done = 0; done < seg;) {
+    const uint32_t ng = min(sg, seg - done);
+    // after a timed-out wait the warp keeps the loop structure but skips the
+    // work; the error flag tells the host the result is void
+    if (ok && !mbar_wait_sleep(&sm.full[slot], phase)) ok = false;
+    if (active && ok) {
+      const uint32_t base = ring + slot * p.stage_bytes;
+      build<T>(base, gbytes, w, warp, nblk, ng, xs0 + 64 * (u + done), lane, tbl, corr);
+      __syncwarp();
+      if (nt == 4) {
+#pragma unroll
+        for (uint32_t gi = 0; gi < kMaxStageGroups; ++gi)
+          if (gi < ng) mma_group<T, 4>(base + gi * gbytes, w, warp, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
+      } else {
+        for (uint32_t gi = 0; gi < ng; ++gi)
+          mma_group<T, 2>(base + gi * gbytes, w, warp, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    done += ng;
+    if (++slot == p.n_stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
   }
-  __syncwarp();
 }
 
 template <int T>
@@ -436,59 +466,46 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
     for (int t = 0; t < 4; ++t)
 #pragma unroll
       for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-    if (n_units) {
-      Stage st{0, R.c0, R.g0, 0, false};
-      stage_fill(p, n_units, G, st);
-      for (uint32_t s = 0;; ++s) {
-        const uint32_t slot = s % p.n_stages;
-        // after a timed-out wait the warp keeps the loop's barrier structure but
-        // skips the work; the error flag tells the host the result is void
-        if (ok && !mbar_wait_sleep(&sm.full[slot], (s / p.n_stages) & 1u)) ok = false;
-        const ChunkDesc cd = p.chunks[st.c];
-        const bool active = ok && 64 * warp < cd.width;
-        if (active) {
-          const uint32_t base = ring + slot * p.stage_bytes, xs = xs0 + 64 * st.u;
-          switch (cd.type) {
-            case kQ4_K: run_stage<kQ4_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
-            case kQ6_K: run_stage<kQ6_K>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
-            case kQ8_0: run_stage<kQ8_0>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
-            default: run_stage<kQ4_0>(base, cd, st.ng, xs, warp, lane, tbl, bsrc, D, Dh, corr); break;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[slot]);
-        if (st.last) {
-          const uint32_t slot_p = blockIdx.x * p.max_chunks_per_cta + (st.c - R.c0);
-          if (active) {
-            switch (cd.type) {
-              case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-              case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-              case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-              default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-            }
-          }
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-          corr[0] = corr[1] = 0.0f;
-          __threadfence();
-          epi::consumer_bar<kWarps>();
-          if (tid == 0) {
-            const uint32_t old = atomicAdd(p.counters + st.c, 1u);
-            *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
-          }
-          epi::consumer_bar<kWarps>();
-          if (*sm.flag) {
-            __threadfence();
-            epi::epilogue<kWarps>(p, sm.red, cd, st.c, tid, warp, lane);
-            if (tid == 0) p.counters[st.c] = 0;  // ready for the next launch
-          }
-          epi::consumer_bar<kWarps>();
-        }
-        if (st.u + st.ng >= n_units) break;
-        stage_advance(p, n_units, G, st);
+    uint32_t slot = 0, phase = 0;
+    for (uint32_t u = 0, c = R.c0, g = R.g0; u < n_units; ++c, g = 0) {
+      const ChunkDesc cd = p.chunks[c];
+      const uint32_t seg = min(G - g, n_units - u);
+      switch (cd.type) {
+        case kQ4_K: segment<kQ4_K>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        case kQ6_K: segment<kQ6_K>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        case kQ8_0: segment<kQ8_0>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        default: segment<kQ4_0>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
       }
+      u += seg;
+      // the CTA's rows of chunk c are done: publish the partial; the last
+      // contributing CTA sums the partials and runs the epilogue
+      const uint32_t slot_p = blockIdx.x * p.max_chunks_per_cta + (c - R.c0);
+      if (ok && 64 * warp < cd.width) {
+        switch (cd.type) {
+          case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+      corr[0] = corr[1] = 0.0f;
+      __threadfence();
+      epi::consumer_bar<kWarps>();
+      if (tid == 0) {
+        const uint32_t old = atomicAdd(p.counters + c, 1u);
+        *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
+      }
+      epi::consumer_bar<kWarps>();
+      if (*sm.flag) {
+        __threadfence();
+        epi::epilogue<kWarps>(p, sm.red, cd, c, tid, warp, lane);
+        if (tid == 0) p.counters[c] = 0;  // ready for the next launch
+      }
+      epi::consumer_bar<kWarps>();
     }
   }
   if (!ok && p.state) atomicOr(&p.state->err, kErrWaitTimeout);
