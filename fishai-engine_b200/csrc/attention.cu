@@ -23,6 +23,7 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kMaxRep = 8;   // query heads per kv head
 constexpr int kTile = 32;    // positions per warp tile (one per lane in the score phase)
+constexpr uint32_t kMaxSplits = 64;
 
 // dynamic shared memory of one CTA: q [REP][hd] | per warp V tile [32][hd] |
 // per warp p [32][REP] | merge scratch m, l [kWarps][REP], o [kWarps][REP][hd]
@@ -252,20 +253,43 @@ __device__ void attn_body(const AttnParams &p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // per query head: max over splits, weights exp(m_s - M), total sum (warp
+  // reductions, fixed order); then each output dim from independent loads
+  __shared__ float ecoef[kMaxRep * kMaxSplits];
+  __shared__ float lsum[kMaxRep];
+  for (uint32_t r = warp; r < REP; r += kWarps) {
+    const float *P = part + (uint64_t)(kvh * REP + r) * p.splits * (2 + hd);
+    float M = -INFINITY;
+    for (uint32_t s = lane; s < p.splits; s += 32) M = fmaxf(M, __ldcg(P + s * (2 + hd)));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, off));
+    float Ls = 0.0f;
+    for (uint32_t s = lane; s < p.splits; s += 32) {
+      const float ms = __ldcg(P + s * (2 + hd));
+      const float e = ms == -INFINITY ? 0.0f : expf(ms - M);
+      ecoef[r * kMaxSplits + s] = e;
+      Ls = fmaf(__ldcg(P + s * (2 + hd) + 1), e, Ls);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) Ls += __shfl_xor_sync(0xFFFFFFFFu, Ls, off);
+    if (lane == 0) lsum[r] = Ls;
+  }
+  __syncthreads();
   for (uint32_t idx = threadIdx.x; idx < REP * hd; idx += blockDim.x) {
     const uint32_t r = idx / hd, dd = idx % hd, h = kvh * REP + r;
-    const float *P = part + (uint64_t)h * p.splits * (2 + hd);
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(P + s * (2 + hd)));
-    float Lsum = 0.0f, o = 0.0f;
-    for (uint32_t s = 0; s < p.splits; ++s) {
-      const float m = __ldcg(P + s * (2 + hd));
-      if (m == -INFINITY) continue;
-      const float e = expf(m - M);
-      Lsum = fmaf(__ldcg(P + s * (2 + hd) + 1), e, Lsum);
-      o = fmaf(__ldcg(P + s * (2 + hd) + 2 + dd), e, o);
+    const float *P = part + (uint64_t)h * p.splits * (2 + hd) + 2 + dd;
+    const float *ec = ecoef + r * kMaxSplits;
+    float o = 0.0f;
+    uint32_t sp = 0;
+    for (; sp + 8 <= p.splits; sp += 8) {
+      float a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = __ldcg(P + (sp + j) * (2 + hd));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o = fmaf(a[j], ec[sp + j], o);
     }
-    outrow[h * hd + dd] = o / Lsum;
+    for (; sp < p.splits; ++sp) o = fmaf(__ldcg(P + sp * (2 + hd)), ec[sp], o);
+    outrow[h * hd + dd] = o / lsum[r];
   }
   if (threadIdx.x == 0) counters[kvh] = 0;
 }
@@ -304,7 +328,7 @@ int attention_init() {
 int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st) {
   const uint32_t rep = p.n_heads / p.kv.n_kv, hd = p.kv.head_dim;
   const bool f16 = p.kv.f16 != 0;
-  if (hd > 128 || rep > kMaxRep || p.n_heads % p.kv.n_kv) return -1;
+  if (hd > 128 || rep > kMaxRep || p.n_heads % p.kv.n_kv || !p.splits || p.splits > kMaxSplits) return -1;
   void *fn = pick_kernel(rep, f16);
   if (!fn) return -1;
   if (attention_init()) return -1;

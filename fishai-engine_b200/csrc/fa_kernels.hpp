@@ -64,7 +64,7 @@ struct GemvParams {
   const ChunkDesc *chunks;
   uint32_t n_chunks;
   const CtaRange *ranges;  // [n_ctas]
-  const uint16_t *contrib; // per chunk: indices of the CTAs with rows in it (ChunkDesc::contrib_off)
+  const uint32_t *contrib; // per chunk: partial slots of the CTAs with rows in it (ChunkDesc::contrib_off)
   uint32_t n_ctas;
   uint32_t max_chunks_per_cta;
   uint32_t K, K8;

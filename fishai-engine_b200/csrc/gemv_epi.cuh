@@ -16,14 +16,21 @@ __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" 
 
 __device__ __forceinline__ float silu_ref(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
-// sum of the chunk's published partials in CTA order (deterministic)
+// sum of the chunk's published partials in contributor order (deterministic);
+// the partial loads are issued eight at a time so their latencies overlap
 __device__ __forceinline__ float chunk_sum(const GemvParams &p, const ChunkDesc &cd, uint32_t c, uint32_t col) {
+  const uint32_t *sl = p.contrib + cd.contrib_off, n = cd.n_contrib;
+  const float *part = p.part + col;
   float v = 0.0f;
-  for (uint32_t t = 0; t < cd.n_contrib; ++t) {
-    const uint32_t i = p.contrib[cd.contrib_off + t];
-    const uint32_t slot = i * p.max_chunks_per_cta + (c - p.ranges[i].c0);
-    v += __ldcg(p.part + (size_t)slot * p.CW + col);
+  uint32_t t = 0;
+  for (; t + 8 <= n; t += 8) {
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = __ldcg(part + (size_t)__ldg(sl + t + j) * p.CW);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v += a[j];
   }
+  for (; t < n; ++t) v += __ldcg(part + (size_t)__ldg(sl + t) * p.CW);
   return v;
 }
 

@@ -243,13 +243,13 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     if (who[c].empty() || P.n_ctas > 65535) return fail(FA_ERR_INVALID, "GEMV split failed");
     P.chunks[c].contrib_off = (uint32_t)P.contrib.size();
     P.chunks[c].n_contrib = (uint32_t)who[c].size();
-    P.contrib.insert(P.contrib.end(), who[c].begin(), who[c].end());
+    for (uint16_t i : who[c]) P.contrib.push_back(i * P.max_chunks_per_cta + (c - P.ranges[i].c0));
   }
   P.d_chunks = (ChunkDesc *)m.dmalloc(P.chunks.size() * sizeof(ChunkDesc));
   P.d_ranges = (CtaRange *)m.dmalloc(P.ranges.size() * sizeof(CtaRange));
-  P.d_contrib = (uint16_t *)m.dmalloc(P.contrib.size() * sizeof(uint16_t));
+  P.d_contrib = (uint32_t *)m.dmalloc(P.contrib.size() * sizeof(uint32_t));
   if (!P.d_chunks || !P.d_ranges || !P.d_contrib) return fail(FA_ERR_OOM, "GEMV table allocation failed");
-  CUDA_TRY(cudaMemcpy(P.d_contrib, P.contrib.data(), P.contrib.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(P.d_contrib, P.contrib.data(), P.contrib.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(P.d_chunks, P.chunks.data(), P.chunks.size() * sizeof(ChunkDesc), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(P.d_ranges, P.ranges.data(), P.ranges.size() * sizeof(CtaRange), cudaMemcpyHostToDevice));
   m.part_floats = std::max<size_t>(m.part_floats, (size_t)P.n_ctas * P.max_chunks_per_cta * P.CW);

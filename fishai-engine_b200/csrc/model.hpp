@@ -17,10 +17,10 @@ namespace fa {
 struct GemvPlan {
   std::vector<ChunkDesc> chunks;
   std::vector<CtaRange> ranges;
-  std::vector<uint16_t> contrib;
+  std::vector<uint32_t> contrib;  // per chunk: partial slot of each contributing CTA
   ChunkDesc *d_chunks = nullptr;
   CtaRange *d_ranges = nullptr;
-  uint16_t *d_contrib = nullptr;
+  uint32_t *d_contrib = nullptr;
   const uint8_t *w = nullptr;
   bool mma = false;           // MMA tile layout (k_gemv_mma)
   uint32_t K = 0, K8 = 0, CW = 256, stage_bytes = 16384, x_slot = 64, n_stages = 0, max_units = 0;
