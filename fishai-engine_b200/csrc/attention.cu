@@ -275,21 +275,31 @@ __device__ void attn_body(const AttnParams &p) {
     if (lane == 0) lsum[r] = Ls;
   }
   __syncthreads();
-  for (uint32_t idx = threadIdx.x; idx < REP * hd; idx += blockDim.x) {
-    const uint32_t r = idx / hd, dd = idx % hd, h = kvh * REP + r;
-    const float *P = part + (uint64_t)h * p.splits * (2 + hd) + 2 + dd;
+  // output: warp per query head, lane per 4 dims; the splits' o vectors are
+  // loaded 16 at a time (independent loads), summed in split order
+  for (uint32_t r = warp; r < REP; r += kWarps) {
+    const uint32_t h = kvh * REP + r;
+    const float *P = part + (uint64_t)h * p.splits * (2 + hd) + 2;
     const float *ec = ecoef + r * kMaxSplits;
-    float o = 0.0f;
-    uint32_t sp = 0;
-    for (; sp + 8 <= p.splits; sp += 8) {
-      float a[8];
+    for (uint32_t d0 = 4 * lane; d0 < hd; d0 += 128) {
+      const uint32_t nd = min(4u, hd - d0);
+      float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (uint32_t sp = 0; sp < p.splits; sp += 16) {
+        float a[16][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) a[j] = __ldcg(P + (sp + j) * (2 + hd));
+        for (int j = 0; j < 16; ++j)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o = fmaf(a[j], ec[sp + j], o);
+          for (uint32_t e = 0; e < 4; ++e)
+            a[j][e] = (sp + j < p.splits && e < nd) ? __ldcg(P + (sp + j) * (2 + hd) + d0 + e) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (sp + j >= p.splits) break;
+#pragma unroll
+          for (uint32_t e = 0; e < 4; ++e) o[e] = fmaf(a[j][e], ec[sp + j], o[e]);
+        }
+      }
+      for (uint32_t e = 0; e < nd; ++e) outrow[h * hd + d0 + e] = o[e] / lsum[r];
     }
-    for (; sp < p.splits; ++sp) o = fmaf(__ldcg(P + sp * (2 + hd)), ec[sp], o);
-    outrow[h * hd + dd] = o / lsum[r];
   }
   if (threadIdx.x == 0) counters[kvh] = 0;
 }
