@@ -152,6 +152,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--cpu-layers", type=int, default=4)
+    ap.add_argument("--step-kernel", type=int, choices=[0, 1], default=0,
+                    help="1: each decode step is one persistent kernel launch")
     ap.add_argument("--profile", choices=list(PROFILE_KINDS), default=None,
                     help="time one GEMV kind only, on a model with --layers layers")
     ap.add_argument("--layers", type=int, default=2)
@@ -201,7 +203,7 @@ def main():
 
     from fishai_engine.model import ModelWeights
 
-    m = ModelWeights.load_from_gguf(path, device=local)
+    m = ModelWeights.load_from_gguf(path, device=local, use_step_kernel=bool(args.step_kernel))
     cfg = m.config
     dev_bytes, step_weight_bytes = m.weight_bytes()
     P, K, W = args.prompt, args.steps, args.warmup
@@ -299,6 +301,7 @@ def main():
         "dtype": "f32 activations, Q4_K/Q6_K weights, f16 KV" if args.kv == "f16" else "f32",
         "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
         "config": {"workload": WORKLOAD, "batch": 1, "prompt": P, "kv_cache": args.kv,
+                   "step_kernel": m.step_kernel_active,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (4.9 GB of weights streamed per step)"},
         "roofline": {"bound": "hbm", "kernel": "k_gemv (fused ffn gate+up, Q4_K)", "achieved": achieved,

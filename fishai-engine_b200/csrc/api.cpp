@@ -56,7 +56,10 @@ int check_err_flags(Model &m, const SeqState *st_dev) {
   SeqState st;
   API_CUDA(cudaMemcpyAsync(&st, st_dev, sizeof st, cudaMemcpyDeviceToHost, m.stream));
   API_CUDA(cudaStreamSynchronize(m.stream));
-  if (st.err & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "a bounded device wait gave up");
+  if (st.err & kErrWaitTimeout) {
+    m.step_kv = nullptr;  // the step kernel's phase counters are void: upload a fresh plan next time
+    return fail(FA_ERR_TIMEOUT, "a bounded device wait gave up");
+  }
   if (st.err & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
   if (st.err & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");
   return FA_OK;
@@ -72,11 +75,13 @@ int set_state(Model &m, SeqState *dst, uint32_t token, uint32_t pos, uint32_t le
   return FA_OK;
 }
 
+// captured graphs and the uploaded step plan hold workspace pointers
 void drop_graph(Model &m) {
   if (m.graph) {
     cudaGraphExecDestroy(m.graph);
     m.graph = nullptr;
   }
+  m.step_kv = nullptr;
 }
 
 int ensure_ids(Model &m, uint32_t n) {
@@ -416,6 +421,7 @@ int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *s
   return FA_OK;
 }
 void *fa_model_stream(fa_model *m) { return m ? (void *)m->m.stream : nullptr; }
+int fa_model_step_kernel_active(const fa_model *m) { return m && m->m.step_ok ? 1 : 0; }
 
 // ------------------------------------------------------------ KV cache
 int fa_kv_create(fa_model *m, uint32_t n_seq, uint32_t max_ctx, int32_t dtype, fa_kv **out) {

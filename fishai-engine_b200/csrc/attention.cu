@@ -298,7 +298,9 @@ __device__ void attn_body(const AttnParams &p) {
           for (uint32_t e = 0; e < 4; ++e) o[e] = fmaf(a[j][e], ec[sp + j], o[e]);
         }
       }
-      for (uint32_t e = 0; e < nd; ++e) outrow[h * hd + d0 + e] = o[e] / lsum[r];
+#pragma unroll
+      for (uint32_t e = 0; e < 4; ++e)
+        if (e < nd) outrow[h * hd + d0 + e] = o[e] / lsum[r];
     }
   }
   if (threadIdx.x == 0) counters[kvh] = 0;

@@ -76,6 +76,7 @@ struct GemvParams {
   uint32_t x_slot;         // floats of x (and norm weight) per stage slot
   float *part;             // [n_ctas * max_chunks_per_cta][CW] chunk partials
   uint32_t *counters;      // [n_chunks] arrival counters (zero between launches)
+  uint32_t *done;          // optional: +1 per completed chunk (launches that wait on this one)
   // prologue (inputs padded with zeros to K8)
   int pro;
   const float *in;         // [K8]
@@ -107,6 +108,10 @@ int launch_gemv_mma(const GemvParams &p, bool pdl, cudaStream_t st);
 size_t gemv_mma_smem_bytes(const GemvParams &p);
 // ring depth that fits the shared-memory budget of one CTA (0: does not fit)
 uint32_t gemv_mma_stages(uint32_t stage_bytes, uint32_t max_units, size_t smem_budget);
+// shared-memory offsets of the GEMV layout: the coefficient tables, and the
+// ring after the x slice of max_units row groups
+uint32_t gemv_mma_table_offset();
+uint32_t gemv_mma_ring_offset(uint32_t max_units);
 // row groups per pipeline stage for chunks of this type and group size
 uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type);
 
@@ -140,6 +145,38 @@ struct EmbedParams {
   SeqState *state;
 };
 int launch_embed(const EmbedParams &p, bool pdl, cudaStream_t st);
+
+// ---- persistent decode step: every phase of one token in one launch ----
+enum : uint32_t { kPhEmbed = 0, kPhGemv = 1, kPhAttn = 2 };
+struct StepPhase {
+  uint32_t kind;       // kPh*
+  uint32_t idx;        // GEMV: index into StepParams::gemv; attention: layer
+  uint32_t dep;        // phase this one waits for (~0u: none)
+  uint32_t dep_count;  // completions of `dep` per step
+};
+struct StepParams {
+  const StepPhase *phases;
+  uint32_t n_phases;
+  const GemvParams *gemv;   // full launch parameters of every GEMV phase (one ring geometry)
+  AttnParams attn;          // attention parameters; layer taken from the phase
+  EmbedParams embed;        // n_ssq = the grid size (one partial per CTA)
+  uint32_t *done;           // [n_phases] completion counters, monotonic across steps
+  uint32_t *sync;           // [0] steps completed, [1] CTAs finished (monotonic)
+  uint32_t *ids;            // generated ids (or null)
+  uint32_t max_ids;
+  uint32_t n_stages, stage_bytes, max_units;  // ring geometry of the GEMV phases
+  uint32_t attn_groups;     // attention work groups (4 warps each) per CTA
+  uint32_t n_ctas;
+};
+// bytes of shared memory one attention work group needs, and the launch
+int step_attn_group_bytes(uint32_t rep, uint32_t hd);
+int step_init();
+// returns the cudaError_t of the launch (0: success)
+int launch_step(const StepParams &p, size_t smem, cudaStream_t st);
+}  // namespace fa
+#include <string>
+namespace fa {
+std::string step_occupancy_report(const StepParams &p, size_t smem);
 
 // step bookkeeping: token <- argmax, ids[step] = token, pos++, len++, step++, fed++
 int launch_step_end(SeqState *state, uint32_t *ids, uint32_t max_ids, bool pdl, cudaStream_t st);

@@ -58,7 +58,7 @@ __device__ void epilogue(const GemvParams &p, float *red, const ChunkDesc &cd, u
       if (p.epi == kEpiStore) {
         p.out[col] = v;
       } else if (p.epi == kEpiResid) {
-        const float nv = p.resid[col] + v;
+        const float nv = __ldcg(p.resid + col) + v;
         p.resid[col] = nv;
         local = fmaf(nv, nv, local);
       } else if (p.epi == kEpiLogits) {

@@ -286,9 +286,10 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   device = o.device;
   pdl = o.use_pdl != 0;
   graphs = o.use_graphs != 0;
+  want_step = o.use_step_kernel != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init() || gemv_mma_init() || attention_init())
+  if (gemv_init() || gemv_mma_init() || attention_init() || step_init())
     return fail(FA_ERR_CUDA, "kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;
@@ -404,6 +405,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   if (!part || !counters) return fail(FA_ERR_OOM, "GEMV scratch allocation failed");
   CUDA_TRY(cudaMemset(counters, 0, (size_t)max_chunks * sizeof(uint32_t)));
   if ((rc = alloc_workspace(ws))) return rc;
+  if ((rc = setup_step_kernel())) return rc;
   gguf.reset();  // host mapping no longer needed
   return FA_OK;
 }
@@ -418,6 +420,7 @@ KvCache::~KvCache() {
       m->graph = nullptr;
       m->graph_kv = nullptr;
     }
+    if (m->step_kv == this) m->step_kv = nullptr;
   }
   cudaFree(base);
   cudaFree(page_table);
@@ -599,7 +602,7 @@ int Model::alloc_workspace(Workspace &w) {
   w.attn_part = (float *)dmalloc((size_t)cfg.n_heads * attn_splits * (2 + cfg.head_dim) * 4);
   w.attn_out = (float *)dmalloc(((size_t)qd + 8) * 4);
   w.attn_cnt = (uint32_t *)dmalloc(cfg.n_kv_heads * 4);
-  w.ssq_e = (float *)dmalloc(embed_ctas * 4);
+  w.ssq_e = (float *)dmalloc((size_t)std::max<uint32_t>(embed_ctas, (uint32_t)n_sm) * 4);
   w.ssq_o = (float *)dmalloc((L ? layers[0].o.chunks.size() : 1) * 4);
   w.ssq_d = (float *)dmalloc((L ? layers[0].down.chunks.size() : 1) * 4);
   w.state = (SeqState *)dmalloc(sizeof(SeqState));
@@ -615,11 +618,21 @@ int Model::alloc_workspace(Workspace &w) {
 }
 
 int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
-  if (!graphs) {
-    for (uint32_t i = 0; i < n; ++i) {
-      int rc = enqueue_step(kv, seq, ws, nullptr);
-      if (rc) return rc;
+  int rc;
+  if (step_ok && (rc = prepare_step(kv, seq))) return rc;
+  auto one_step = [&]() -> int {
+    if (step_ok) {
+      const int e = launch_step(step, step_smem, stream);
+      if (e) return fail(FA_ERR_CUDA, std::string("step kernel launch failed: ") + cudaGetErrorString((cudaError_t)e) +
+                                          " (smem " + std::to_string(step_smem) + ", " +
+                                          step_occupancy_report(step, step_smem) + ")");
+      return FA_OK;
     }
+    return enqueue_step(kv, seq, ws, nullptr);
+  };
+  if (!graphs) {
+    for (uint32_t i = 0; i < n; ++i)
+      if ((rc = one_step())) return rc;
     return FA_OK;
   }
   if (!graph || graph_kv != &kv || graph_seq != seq) {
@@ -628,7 +641,7 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
       graph = nullptr;
     }
     CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(kv, seq, ws, nullptr);
+    rc = one_step();
     cudaGraph_t gr = nullptr;
     cudaError_t ce = cudaStreamEndCapture(stream, &gr);
     if (rc) {
@@ -643,6 +656,165 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
     graph_seq = seq;
   }
   for (uint32_t i = 0; i < n; ++i) CUDA_TRY(cudaGraphLaunch(graph, stream));
+  return FA_OK;
+}
+
+// The persistent step kernel serves models whose projections are all in the
+// MMA layout with an untied head and head_dim a multiple of 8 (<= 128).
+int Model::setup_step_kernel() {
+  const uint32_t L = cfg.n_layers, hd = cfg.head_dim, rep = cfg.n_heads / cfg.n_kv_heads;
+  bool ok = !tied && L > 0 && head.mma && hd % 8 == 0 && hd <= 128 && cfg.n_heads % cfg.n_kv_heads == 0 &&
+            (rep == 1 || rep == 2 || rep == 4 || rep == 8) && attn_splits <= 64;
+  for (const LayerW &lw : layers) ok = ok && lw.qkv.mma && lw.o.mma && lw.gateup.mma && lw.down.mma;
+  if (!ok || !want_step) return FA_OK;
+  const uint32_t n_phases = 1 + 5 * L + 1, n_gemv = 4 * L + 1;
+  d_phases = (StepPhase *)dmalloc(n_phases * sizeof(StepPhase));
+  d_gemv = (GemvParams *)dmalloc(n_gemv * sizeof(GemvParams));
+  d_step_done = (uint32_t *)dmalloc(n_phases * sizeof(uint32_t));
+  d_step_sync = (uint32_t *)dmalloc(2 * sizeof(uint32_t));
+  if (!d_phases || !d_gemv || !d_step_done || !d_step_sync) return fail(FA_ERR_OOM, "step plan allocation failed");
+  step_ok = true;
+  return FA_OK;
+}
+
+int Model::prepare_step(const KvCache &kv, uint32_t seq) {
+  if (step_kv == &kv && step_seq == seq) return FA_OK;
+  const uint32_t L = cfg.n_layers, KVH = cfg.n_kv_heads, hd = cfg.head_dim, rep = cfg.n_heads / KVH;
+  // ring geometry shared by every GEMV phase; the attention groups' scratch
+  // overlays the tables and the x slice, which sizes the x slice from below
+  uint32_t stage_bytes = head.stage_bytes, max_units = head.max_units;
+  for (const LayerW &lw : layers)
+    for (const GemvPlan *P : {&lw.qkv, &lw.o, &lw.gateup, &lw.down}) {
+      stage_bytes = std::max(stage_bytes, P->stage_bytes);
+      max_units = std::max(max_units, P->max_units);
+    }
+  const uint32_t groups = 2, gbytes = (uint32_t)step_attn_group_bytes(rep, hd);
+  // (the ring offset is rounded to 128 bytes, so grow unit by unit until it fits)
+  while (gemv_mma_ring_offset(max_units) - gemv_mma_table_offset() < groups * gbytes) ++max_units;
+  const uint32_t n_stages = gemv_mma_stages(stage_bytes, max_units, 227 * 1024);
+  if (n_stages < 2) return fail(FA_ERR_UNSUPPORTED, "step kernel ring does not fit in shared memory");
+  std::vector<StepPhase> ph;
+  std::vector<GemvParams> gp;
+  auto add_gemv = [&](GemvParams p, uint32_t dep, uint32_t dep_count) {
+    p.stage_bytes = stage_bytes;
+    p.n_stages = n_stages;
+    p.max_units = max_units;
+    p.done = d_step_done + ph.size();
+    ph.push_back({kPhGemv, (uint32_t)gp.size(), dep, dep_count});
+    gp.push_back(p);
+  };
+  const uint32_t grid = (uint32_t)n_sm;
+  ph.push_back({kPhEmbed, 0, ~0u, 0});
+  uint32_t prev = 0, prev_count = grid;  // the phase the next RMSNorm input comes from
+  for (uint32_t l = 0; l < L; ++l) {
+    const LayerW &lw = layers[l];
+    GemvParams p = gemv_base(lw.qkv);
+    p.pro = kProRmsNorm;
+    p.in = ws.x;
+    p.norm_w = lw.attn_norm;
+    p.ssq = l == 0 ? ws.ssq_e : ws.ssq_d;
+    p.n_ssq = l == 0 ? grid : (uint32_t)layers[l - 1].down.chunks.size();
+    p.eps = cfg.norm_eps;
+    p.epi = kEpiQkv;
+    p.out = ws.q;
+    p.q_dim = cfg.n_heads * hd;
+    p.kv_dim = KVH * hd;
+    p.rope_tab = rope_tab;
+    p.rope_max = rope_max;
+    p.kv = kv.view();
+    p.seq = seq;
+    p.layer = l;
+    p.state = ws.state;
+    const uint32_t q_qkv = (uint32_t)ph.size();
+    add_gemv(p, prev, prev_count);
+    const uint32_t q_attn = (uint32_t)ph.size();
+    ph.push_back({kPhAttn, l, q_qkv, (uint32_t)lw.qkv.chunks.size()});
+    p = gemv_base(lw.o);
+    p.pro = kProPlain;
+    p.in = ws.attn_out;
+    p.epi = kEpiResid;
+    p.resid = ws.x;
+    p.ssq_out = ws.ssq_o;
+    p.state = ws.state;
+    const uint32_t q_o = (uint32_t)ph.size();
+    add_gemv(p, q_attn, KVH);
+    p = gemv_base(lw.gateup);
+    p.pro = kProRmsNorm;
+    p.in = ws.x;
+    p.norm_w = lw.ffn_norm;
+    p.ssq = ws.ssq_o;
+    p.n_ssq = (uint32_t)lw.o.chunks.size();
+    p.eps = cfg.norm_eps;
+    p.epi = kEpiSwiglu;
+    p.out = ws.h;
+    p.state = ws.state;
+    const uint32_t q_gu = (uint32_t)ph.size();
+    add_gemv(p, q_o, (uint32_t)lw.o.chunks.size());
+    p = gemv_base(lw.down);
+    p.pro = kProPlain;
+    p.in = ws.h;
+    p.epi = kEpiResid;
+    p.resid = ws.x;
+    p.ssq_out = ws.ssq_d;
+    p.state = ws.state;
+    prev = (uint32_t)ph.size();
+    prev_count = (uint32_t)lw.down.chunks.size();
+    add_gemv(p, q_gu, (uint32_t)lw.gateup.chunks.size());
+  }
+  GemvParams p = gemv_base(head);
+  p.pro = kProRmsNorm;
+  p.in = ws.x;
+  p.norm_w = out_norm;
+  p.ssq = ws.ssq_d;
+  p.n_ssq = (uint32_t)layers[L - 1].down.chunks.size();
+  p.eps = cfg.norm_eps;
+  p.epi = kEpiLogits;
+  p.out = ws.logits;
+  p.state = ws.state;
+  add_gemv(p, prev, prev_count);
+  CUDA_TRY(cudaMemcpy(d_phases, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(d_gemv, gp.data(), gp.size() * sizeof(GemvParams), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemset(d_step_done, 0, ph.size() * sizeof(uint32_t)));
+  CUDA_TRY(cudaMemset(d_step_sync, 0, 2 * sizeof(uint32_t)));
+  StepParams sp{};
+  sp.phases = d_phases;
+  sp.n_phases = (uint32_t)ph.size();
+  sp.gemv = d_gemv;
+  AttnParams &ap = sp.attn;
+  ap.q = ws.q;
+  ap.q_rows = 1;
+  ap.kv = kv.view();
+  ap.seq = seq;
+  ap.n_heads = cfg.n_heads;
+  ap.splits = attn_splits;
+  ap.scale = attn_scale;
+  ap.part = ws.attn_part;
+  ap.counters = ws.attn_cnt;
+  ap.out = ws.attn_out;
+  ap.state = ws.state;
+  EmbedParams &ep = sp.embed;
+  ep.emb = (const uint8_t *)emb;
+  ep.feed = ws.feed;
+  ep.type = emb_type;
+  ep.d = cfg.n_embd;
+  ep.vocab = cfg.vocab_size;
+  ep.x = ws.x;
+  ep.ssq_out = ws.ssq_e;
+  ep.n_ssq = grid;
+  ep.state = ws.state;
+  sp.done = d_step_done;
+  sp.sync = d_step_sync;
+  sp.ids = ws.ids;
+  sp.max_ids = ws.max_ids;
+  sp.n_stages = n_stages;
+  sp.stage_bytes = stage_bytes;
+  sp.max_units = max_units;
+  sp.attn_groups = groups;
+  sp.n_ctas = grid;
+  step = sp;
+  step_smem = gemv_mma_ring_offset(max_units) + (size_t)n_stages * stage_bytes;
+  step_kv = &kv;
+  step_seq = seq;
   return FA_OK;
 }
 

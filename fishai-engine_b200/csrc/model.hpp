@@ -73,6 +73,16 @@ struct Model {
   std::vector<void *> allocs;   // every device allocation, freed at teardown
   std::set<KvCache *> live_kv;  // caches created on this model (detached at teardown)
   uint64_t device_bytes = 0, step_bytes = 0;
+  // persistent decode-step kernel (all GEMVs in the MMA layout, untied head)
+  bool want_step = false;            // requested by the load options
+  bool step_ok = false;
+  const KvCache *step_kv = nullptr;   // (kv, seq) the uploaded plan is for
+  uint32_t step_seq = 0;
+  StepParams step{};
+  size_t step_smem = 0;
+  StepPhase *d_phases = nullptr;
+  GemvParams *d_gemv = nullptr;
+  uint32_t *d_step_done = nullptr, *d_step_sync = nullptr;
   // decode-step graph cache
   cudaGraphExec_t graph = nullptr;
   const KvCache *graph_kv = nullptr;
@@ -88,6 +98,8 @@ struct Model {
   int enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump);
   int enqueue_head(Workspace &w, SeqState *st);
   int enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump);
+  int setup_step_kernel();                               // eligibility + device tables (at load)
+  int prepare_step(const KvCache &kv, uint32_t seq);     // upload the step plan for (kv, seq)
   int alloc_workspace(Workspace &w);
   // run `n` steps (graph replays when enabled)
   int run_steps(const KvCache &kv, uint32_t seq, uint32_t n);

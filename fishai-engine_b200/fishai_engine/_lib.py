@@ -35,7 +35,7 @@ class fa_config(C.Structure):
 
 class fa_model_opts(C.Structure):
     _fields_ = [("device", C.c_int32), ("use_graphs", C.c_int32), ("use_pdl", C.c_int32), ("tp_rank", C.c_int32),
-                ("tp_world", C.c_int32), ("nccl_id", C.c_void_p)]
+                ("tp_world", C.c_int32), ("nccl_id", C.c_void_p), ("use_step_kernel", C.c_int32)]
 
 
 class fa_sampler_config(C.Structure):
@@ -86,6 +86,7 @@ SIGNATURES = {
     "fa_model_config": ([_vp, C.POINTER(fa_config)], _i),
     "fa_model_weight_bytes": ([_vp, _pu64, _pu64], _i),
     "fa_model_stream": ([_vp], _vp),
+    "fa_model_step_kernel_active": ([_vp], _i),
     "fa_kv_create": ([_vp, _u32, _u32, C.c_int32, C.POINTER(_vp)], _i),
     "fa_kv_free": ([_vp], None),
     "fa_kv_clear": ([_vp, C.c_int32], _i),

@@ -109,6 +109,8 @@ typedef struct {
   int32_t use_pdl;      /* programmatic dependent launch between kernels (default 1) */
   int32_t tp_rank, tp_world;  /* tensor parallel rank/world (1 = no TP) */
   const void *nccl_id;  /* 128-byte ncclUniqueId when tp_world > 1 */
+  int32_t use_step_kernel;  /* run each decode step as one persistent kernel when the
+                               model qualifies (MMA-layout projections, untied head) */
 } fa_model_opts;
 void fa_model_opts_default(fa_model_opts *o);
 
@@ -124,6 +126,8 @@ int fa_model_config(const fa_model *m, fa_config *cfg);
 int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *step_bytes);
 /* the stream the model enqueues on (cudaStream_t) */
 void *fa_model_stream(fa_model *m);
+/* 1 when decode steps run as the persistent step kernel, else 0 */
+int fa_model_step_kernel_active(const fa_model *m);
 
 /* ------------------------------------------------------------- KV cache */
 typedef struct fa_kv fa_kv;

@@ -27,12 +27,14 @@ def _digest(path, nbytes=1 << 24):
 
 
 @pytest.mark.skipif(not os.path.exists(GOLDEN), reason="fixture not generated: python tests/golden/make_golden.py 8b")
-def test_8b_q4_k_m_first_64_greedy_ids_match_golden():
+@pytest.mark.parametrize("step_kernel", [False, True])
+def test_8b_q4_k_m_first_64_greedy_ids_match_golden(step_kernel):
     g = json.load(open(GOLDEN))
     path = synth.cached_preset(g["preset"])
     # the synthetic file is the one the golden was made from
     assert _digest(path) == g["gguf_sha256_first16MiB"]
-    m = ModelWeights.load_from_gguf(path)
+    m = ModelWeights.load_from_gguf(path, use_step_kernel=step_kernel)
+    assert m.step_kernel_active == step_kernel
     try:
         prompt = g["prompt"]
         st = GenerationState(m, GenerationConfig(max_tokens=len(prompt) + len(g["greedy_ids"]), temperature=0.0,

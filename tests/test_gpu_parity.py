@@ -71,12 +71,14 @@ def test_dequant_short_data_truncates():
     assert dequantize(raw, O.Q8_0, 96).size == 64
 
 
-def _model_pair(path, resident=False):
-    return ModelWeights.load_from_gguf(path), O.Model(path, resident=resident, threads=os.cpu_count() or 4)
+def _model_pair(path, resident=False, step=False):
+    dev = ModelWeights.load_from_gguf(path, use_step_kernel=step)
+    assert dev.step_kernel_active == step
+    return dev, O.Model(path, resident=resident, threads=os.cpu_count() or 4)
 
 
-def _forward_parity(path, n_tokens=6, kv_dtype=L.KV_F32, check_hidden=True, seed=0):
-    dev, ref = _model_pair(path)
+def _forward_parity(path, n_tokens=6, kv_dtype=L.KV_F32, check_hidden=True, seed=0, step=False):
+    dev, ref = _model_pair(path, step=step)
     V = dev.config.vocab_size
     rng = np.random.default_rng(seed)
     toks = rng.integers(3, V, n_tokens).tolist()
@@ -84,7 +86,11 @@ def _forward_parity(path, n_tokens=6, kv_dtype=L.KV_F32, check_hidden=True, seed
     kv_r = ref.kv(64, kv_f16=kv_dtype == L.KV_F16)
     worst = 0.0
     for i, t in enumerate(toks):
-        lg_d, am_d, hid_d = dev.forward([t], i, kv_d, return_argmax=True, hidden=True)
+        # a hidden-state dump runs the per-kernel step, so the step kernel is checked on logits and cache
+        if check_hidden:
+            lg_d, am_d, hid_d = dev.forward([t], i, kv_d, return_argmax=True, hidden=True)
+        else:
+            lg_d, am_d = dev.forward([t], i, kv_d, return_argmax=True)
         lg_r, hid_r = ref.forward([t], i, kv_r, algo=1, hidden=True)
         worst = max(worst, max_abs_rel(lg_d, lg_r))
         if check_hidden:
@@ -136,6 +142,39 @@ def test_f16_kv_cache_parity(tmpdir_m):
     # device f16 cache against the oracle with f16-rounded K/V
     p = synth.write_preset("tiny-q8_0", str(tmpdir_m / "tiny16.gguf"))
     _forward_parity(p, kv_dtype=L.KV_F16, check_hidden=False)
+
+
+# the persistent step kernel (one launch per token): same bars as the per-kernel path
+@pytest.mark.parametrize("name,spec", [
+    ("tiny", None),                                            # Q8_0, 4 q heads per kv head
+    ("kq", dict()),                                            # Q4_K / Q6_K mix, 2 per kv head
+    ("q40", dict(type_embd=O.Q4_0, type_q=O.Q4_0, type_k=O.Q4_0, type_v=O.Q4_0, type_o=O.Q4_0, type_gate=O.Q4_0,
+                 type_up=O.Q4_0, type_down=O.Q4_0, type_out=O.Q6_K, n_kv_heads=8, rope_base=10000.0)),  # MHA
+    ("mq8", dict(n_kv_heads=1, type_k=O.Q8_0, type_v=O.Q8_0)),  # 8 per kv head
+])
+def test_step_kernel_forward_parity(tmpdir_m, name, spec):
+    path = str(tmpdir_m / f"step_{name}.gguf")
+    p = synth.write_preset("tiny-q8_0", path) if spec is None else synth.write(path, 5, **_kquant_spec(**spec))
+    worst, dev, ref, kv_d, kv_r = _forward_parity(p, n_tokens=8, check_hidden=False, step=True)
+    for layer in (0, dev.config.n_layers - 1):
+        kd, vd = kv_d.get(layer)
+        kr, vr = kv_r.get(layer)
+        assert max_abs_rel(kd, kr) <= TOL_F32 and max_abs_rel(vd, vr) <= TOL_F32
+
+
+def test_step_kernel_f16_kv_parity(tmpdir_m):
+    p = synth.write_preset("tiny-q8_0", str(tmpdir_m / "step16.gguf"))
+    _forward_parity(p, kv_dtype=L.KV_F16, check_hidden=False, step=True)
+
+
+def test_step_kernel_greedy_generate_matches_oracle(tmpdir_m):
+    p = synth.write_preset("tiny-q8_0", str(tmpdir_m / "stepg.gguf"))
+    dev, ref = _model_pair(p, step=True)
+    prompt = np.random.default_rng(1).integers(3, 32000, 40).tolist()
+    n_gen = 96
+    st = GenerationState(dev, GenerationConfig(max_tokens=40 + n_gen, temperature=0.0, top_k=0, top_p=1.0,
+                                               repetition_penalty=1.0))
+    assert st.generate(prompt) == ref.generate(prompt, 40 + n_gen, fast=True).tolist()
 
 
 def test_compat_multi_token_forward(tmpdir_m):
