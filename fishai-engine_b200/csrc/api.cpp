@@ -197,6 +197,86 @@ int forward_compat(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens
 
 }  // namespace
 
+struct fa_sampler {
+  fa_sampler_config cfg{};
+  uint32_t n_seq = 0, vocab = 0, pow2 = 0;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t *freq = nullptr, *ids = nullptr;
+  uint64_t *seeds = nullptr, *counters = nullptr;
+  float *probs = nullptr, *in = nullptr;
+  unsigned long long *keys = nullptr;
+  ~fa_sampler() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void *q : {(void *)freq, (void *)ids, (void *)seeds, (void *)counters, (void *)probs, (void *)in, (void *)keys})
+      if (q) cudaFree(q);
+    if (stream) cudaStreamDestroy(stream);
+  }
+  SamplerParams params(uint32_t n) const {
+    SamplerParams p{};
+    p.temperature = cfg.temperature;
+    p.top_p = cfg.top_p;
+    p.rep = cfg.repetition_penalty;
+    p.freq_pen = cfg.frequency_penalty;
+    p.pres_pen = cfg.presence_penalty;
+    p.top_k = cfg.top_k;
+    p.n = n;
+    p.ld = n;
+    p.vocab = vocab;
+    p.freq = freq;
+    p.seeds = seeds;
+    p.counters = counters;
+    p.probs = probs;
+    p.keys = keys;
+    p.pow2 = pow2;
+    p.ids = ids;
+    return p;
+  }
+};
+
+namespace {
+// the whole-row sort scratch, allocated on first use
+int sampler_keys(fa_sampler *s, SamplerParams &p) {
+  if (!sample_needs_sort(p) || s->keys) return FA_OK;
+  uint32_t p2 = 2;
+  while (p2 < s->vocab) p2 <<= 1;
+  if (cudaMalloc(&s->keys, (size_t)s->n_seq * p2 * sizeof(unsigned long long)) != cudaSuccess)
+    return fail(FA_ERR_OOM, "sampler sort scratch allocation failed");
+  s->pow2 = p2;
+  p.keys = s->keys;
+  p.pow2 = p2;
+  return FA_OK;
+}
+
+int sampler_new(const fa_sampler_config &cfg, uint32_t n_seq, uint32_t vocab, const uint64_t *seeds,
+                std::unique_ptr<fa_sampler> *out) {
+  if (!n_seq || !vocab) return fail(FA_ERR_INVALID, "fa_sampler_create: zero size");
+  std::unique_ptr<fa_sampler> s(new (std::nothrow) fa_sampler());
+  if (!s) return fail(FA_ERR_OOM, "sampler allocation failed");
+  s->cfg = cfg;
+  s->n_seq = n_seq;
+  s->vocab = vocab;
+  API_CUDA(cudaGetDevice(&s->device));
+  if (sampler_init()) return fail(FA_ERR_CUDA, "sampler kernel setup failed");
+  API_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  const size_t rows = (size_t)n_seq * vocab;
+  API_CUDA(cudaMalloc(&s->freq, rows * 4));
+  API_CUDA(cudaMalloc(&s->probs, rows * 4));
+  API_CUDA(cudaMalloc(&s->in, (size_t)vocab * 4));
+  API_CUDA(cudaMalloc(&s->ids, (size_t)n_seq * 4));
+  API_CUDA(cudaMalloc(&s->seeds, (size_t)n_seq * 8));
+  API_CUDA(cudaMalloc(&s->counters, (size_t)n_seq * 8));
+  API_CUDA(cudaMemset(s->freq, 0, rows * 4));
+  API_CUDA(cudaMemset(s->counters, 0, (size_t)n_seq * 8));
+  std::vector<uint64_t> sd(n_seq);
+  for (uint32_t i = 0; i < n_seq; ++i) sd[i] = seeds ? seeds[i] : i;
+  API_CUDA(cudaMemcpy(s->seeds, sd.data(), (size_t)n_seq * 8, cudaMemcpyHostToDevice));
+  *out = std::move(s);
+  return FA_OK;
+}
+}  // namespace
+
 extern "C" {
 
 size_t fa_last_error(char *buf, size_t cap) {
@@ -584,10 +664,6 @@ int fa_generate(fa_model *fm, const fa_gen_config *cfg, const uint32_t *prompt, 
   *n_out = 0;
   // token_ids.last().unwrap() panics on an empty prompt in the reference
   if (!n_prompt) return fail(FA_ERR_INVALID, "fa_generate: empty prompt");
-  const fa_sampler_config &sc = cfg->sampler;
-  const bool greedy_argmax = sc.temperature == 0.0f && sc.repetition_penalty == 1.0f && sc.frequency_penalty == 0.0f &&
-                             sc.presence_penalty == 0.0f;
-  if (!greedy_argmax) return fail(FA_ERR_UNSUPPORTED, "fa_generate: only greedy decoding without penalties so far");
   Model &m = fm->m;
   const uint32_t P = n_prompt, steps = std::max(P, cfg->max_tokens), G = steps - P;
   for (uint32_t i = 0; i < P; ++i)
@@ -596,6 +672,28 @@ int fa_generate(fa_model *fm, const fa_gen_config *cfg, const uint32_t *prompt, 
   fa_kv kvh;
   if ((rc = create_kv(m, 1, steps + 1, cfg->kv_dtype, &kvh.kv))) return rc;
   if ((rc = ensure_feed(m, P + 1)) || (rc = ensure_ids(m, steps))) return rc;
+  // Sampler::sample after every generated step on the device: its id is the
+  // next input and is observed; Sampler::reset per call (src/model.rs:645)
+  std::unique_ptr<fa_sampler> smp;
+  const uint64_t seed = cfg->seed;
+  if ((rc = sampler_new(cfg->sampler, 1, m.cfg.vocab_size, &seed, &smp))) return rc;
+  SamplerParams sp = smp->params(m.cfg.vocab_size);
+  if ((rc = sampler_keys(smp.get(), sp))) return rc;
+  sp.logits = m.ws.logits;
+  sp.state = m.ws.state;
+  sp.gen_ids = m.ws.ids;
+  sp.max_ids = m.ws.max_ids;
+  sp.sample_from = P;
+  sp.observe = 1;
+  drop_graph(m);
+  m.gen_sample = &sp;
+  struct Unhook {
+    Model &m;
+    ~Unhook() {
+      m.gen_sample = nullptr;
+      drop_graph(m);
+    }
+  } unhook{m};
   std::vector<uint32_t> feed(prompt, prompt + P);
   feed.push_back(prompt[P - 1]);  // generate_step re-feeds the last prompt token (src/model.rs:656-657)
   API_CUDA(cudaMemcpyAsync(m.ws.feed, feed.data(), feed.size() * 4, cudaMemcpyHostToDevice, m.stream));
@@ -621,34 +719,101 @@ int fa_generate(fa_model *fm, const fa_gen_config *cfg, const uint32_t *prompt, 
     done += chunk;
   }
   if ((rc = check_err_flags(m, m.ws.state))) return rc;
-  if (m.graph_kv == &kvh.kv) drop_graph(m);
   *n_out = n_gen;
   return FA_OK;
 }
 
 // ------------------------------------------------------------ sampler
-struct fa_sampler {
-  fa_sampler_config cfg;
-  uint32_t n_seq, vocab;
-};
 int fa_sampler_create(const fa_sampler_config *cfg, uint32_t n_seq, uint32_t vocab, const uint64_t *seeds,
                       fa_sampler **out) {
-  (void)cfg;
-  (void)n_seq;
-  (void)vocab;
-  (void)seeds;
-  (void)out;
-  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+  API_NULL(cfg);
+  API_NULL(out);
+  *out = nullptr;
+  std::unique_ptr<fa_sampler> s;
+  const int rc = sampler_new(*cfg, n_seq, vocab, seeds, &s);
+  if (rc) return rc;
+  *out = s.release();
+  return FA_OK;
 }
+
 void fa_sampler_free(fa_sampler *s) { delete s; }
-int fa_sample_device(fa_sampler *, const float *, uint32_t, uint32_t *, uint32_t *, void *) {
-  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+
+int fa_sample_device(fa_sampler *s, const float *logits_dev, uint32_t n, uint32_t *ids_dev, uint32_t *ids_host,
+                     void *stream) {
+  API_NULL(s);
+  API_NULL(logits_dev);
+  if (!n || n > s->n_seq) return fail(FA_ERR_INVALID, "fa_sample_device: row count out of range");
+  API_CUDA(cudaSetDevice(s->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s->stream;
+  SamplerParams p = s->params(s->vocab);
+  p.logits = logits_dev;
+  if (ids_dev) p.ids = ids_dev;
+  int rc;
+  if ((rc = sampler_keys(s, p))) return rc;
+  if (launch_sample(p, n, st)) return fail(FA_ERR_CUDA, "sampler launch failed");
+  if (ids_host) {
+    API_CUDA(cudaMemcpyAsync(ids_host, p.ids, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    API_CUDA(cudaStreamSynchronize(st));
+  }
+  return FA_OK;
 }
-int fa_sample(fa_sampler *, uint32_t, const float *, uint32_t, uint32_t *) {
-  return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet");
+
+int fa_sample(fa_sampler *s, uint32_t seq, const float *logits_host, uint32_t vocab, uint32_t *id_host) {
+  API_NULL(s);
+  API_NULL(id_host);
+  if (seq >= s->n_seq) return fail(FA_ERR_INVALID, "fa_sample: sequence index out of range");
+  if (vocab > s->vocab) return fail(FA_ERR_INVALID, "fa_sample: more logits than the sampler's vocabulary");
+  if (!vocab) {  // argmax of an empty vector is 0 (src/sampling.rs:297-310)
+    *id_host = 0;
+    return FA_OK;
+  }
+  API_NULL(logits_host);
+  API_CUDA(cudaSetDevice(s->device));
+  SamplerParams p = s->params(vocab);
+  p.row0 = seq;
+  p.logits = s->in;
+  int rc;
+  if ((rc = sampler_keys(s, p))) return rc;
+  API_CUDA(cudaMemcpyAsync(s->in, logits_host, (size_t)vocab * 4, cudaMemcpyHostToDevice, s->stream));
+  if (launch_sample(p, 1, s->stream)) return fail(FA_ERR_CUDA, "sampler launch failed");
+  API_CUDA(cudaMemcpyAsync(id_host, s->ids + seq, 4, cudaMemcpyDeviceToHost, s->stream));
+  API_CUDA(cudaStreamSynchronize(s->stream));
+  return FA_OK;
 }
-int fa_sampler_observe(fa_sampler *, uint32_t, uint32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
-int fa_sampler_reset(fa_sampler *, int32_t) { return fail(FA_ERR_UNSUPPORTED, "device sampler not built yet"); }
+
+int fa_sampler_observe(fa_sampler *s, uint32_t seq, uint32_t token) {
+  API_NULL(s);
+  if (seq >= s->n_seq) return fail(FA_ERR_INVALID, "fa_sampler_observe: sequence index out of range");
+  // ids at or beyond the vocabulary cannot change a sample of <= vocab logits
+  if (token >= s->vocab) return FA_OK;
+  API_CUDA(cudaSetDevice(s->device));
+  if (launch_sampler_observe(s->freq, s->vocab, seq, token, s->stream)) return fail(FA_ERR_CUDA, "observe launch failed");
+  API_CUDA(cudaStreamSynchronize(s->stream));
+  return FA_OK;
+}
+
+int fa_sampler_reset(fa_sampler *s, int32_t seq) {
+  API_NULL(s);
+  if (seq >= (int32_t)s->n_seq) return fail(FA_ERR_INVALID, "fa_sampler_reset: sequence index out of range");
+  API_CUDA(cudaSetDevice(s->device));
+  const size_t row = (size_t)s->vocab * 4;
+  if (seq < 0) API_CUDA(cudaMemsetAsync(s->freq, 0, row * s->n_seq, s->stream));
+  else API_CUDA(cudaMemsetAsync((uint8_t *)s->freq + row * seq, 0, row, s->stream));
+  API_CUDA(cudaStreamSynchronize(s->stream));
+  return FA_OK;
+}
+
+int fa_sampler_freq(fa_sampler *s, uint32_t seq, uint32_t token, uint32_t *count) {
+  API_NULL(s);
+  API_NULL(count);
+  if (seq >= s->n_seq) return fail(FA_ERR_INVALID, "fa_sampler_freq: sequence index out of range");
+  *count = 0;
+  if (token >= s->vocab) return FA_OK;
+  API_CUDA(cudaSetDevice(s->device));
+  API_CUDA(cudaStreamSynchronize(s->stream));
+  API_CUDA(cudaMemcpy(count, s->freq + (size_t)seq * s->vocab + token, 4, cudaMemcpyDeviceToHost));
+  return FA_OK;
+}
 
 // ------------------------------------------------------------ attention
 namespace {

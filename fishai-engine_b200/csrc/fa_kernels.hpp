@@ -183,6 +183,39 @@ int launch_step_end(SeqState *state, uint32_t *ids, uint32_t max_ids, bool pdl, 
 
 // tied output head (no output.weight): logits[j] = dot(xn, E[j]) with E
 // native [V][d] (transpose_2d + matmul, src/model.rs:447-452)
+// ---- Sampler::sample (src/sampling.rs:110-152), one CTA per sequence ----
+constexpr uint32_t kSampleFastK = 2048;  // top-k up to this many candidates stays in shared memory
+struct SamplerParams {
+  float temperature, top_p, rep, freq_pen, pres_pen;
+  uint32_t top_k;
+  uint32_t n;                 // logits per row (the vector Sampler::sample receives)
+  uint32_t row0;              // first sequence row of the launch (CTA i samples row row0 + i)
+  const float *logits;        // row r at logits + (r - row0) * ld
+  uint32_t ld;
+  uint32_t vocab;             // allocated row length of freq / probs
+  uint32_t *freq;             // [n_seq][vocab] token_freq (token_present == freq > 0)
+  const uint64_t *seeds;      // [n_seq] Philox4x32-10 keys
+  uint64_t *counters;         // [n_seq] samples drawn so far (the Philox counter)
+  float *probs;               // [n_seq][vocab] scratch
+  unsigned long long *keys;   // [n_seq][pow2] scratch of the full-sort path (null if unused)
+  uint32_t pow2;
+  uint32_t *ids;              // [n_seq] sampled id per row (may be null)
+  // decode-loop hookup (b = 1 generation): sample only steps >= sample_from,
+  // then the id becomes the next input token and is observed
+  SeqState *state;
+  uint32_t *gen_ids, max_ids, sample_from;
+  int observe;
+};
+int sampler_init();
+int launch_sample(const SamplerParams &p, uint32_t rows, cudaStream_t st);
+int launch_sampler_observe(uint32_t *freq, uint32_t vocab, uint32_t seq, uint32_t token, cudaStream_t st);
+// true when a launch with these settings sorts the whole row (needs p.keys)
+inline bool sample_needs_sort(const SamplerParams &p) {
+  const bool topk = p.top_k > 0 && p.top_k < p.n, topp = p.top_p > 0.0f && p.top_p < 1.0f;
+  const bool fast = topk && p.top_k <= kSampleFastK;
+  return !fast && (topk || topp);
+}
+
 struct TiedHeadParams {
   const uint8_t *emb;
   int type;

@@ -289,7 +289,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   want_step = o.use_step_kernel != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init() || gemv_mma_init() || attention_init() || step_init())
+  if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init())
     return fail(FA_ERR_CUDA, "kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;
@@ -626,16 +626,19 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
       if (e) return fail(FA_ERR_CUDA, std::string("step kernel launch failed: ") + cudaGetErrorString((cudaError_t)e) +
                                           " (smem " + std::to_string(step_smem) + ", " +
                                           step_occupancy_report(step, step_smem) + ")");
-      return FA_OK;
+    } else {
+      const int rc2 = enqueue_step(kv, seq, ws, nullptr);
+      if (rc2) return rc2;
     }
-    return enqueue_step(kv, seq, ws, nullptr);
+    if (gen_sample && launch_sample(*gen_sample, 1, stream)) return fail(FA_ERR_CUDA, "sampler launch failed");
+    return FA_OK;
   };
   if (!graphs) {
     for (uint32_t i = 0; i < n; ++i)
       if ((rc = one_step())) return rc;
     return FA_OK;
   }
-  if (!graph || graph_kv != &kv || graph_seq != seq) {
+  if (!graph || graph_kv != &kv || graph_seq != seq || graph_sample != gen_sample) {
     if (graph) {
       cudaGraphExecDestroy(graph);
       graph = nullptr;
@@ -654,6 +657,7 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
     if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(ce));
     graph_kv = &kv;
     graph_seq = seq;
+    graph_sample = gen_sample;
   }
   for (uint32_t i = 0; i < n; ++i) CUDA_TRY(cudaGraphLaunch(graph, stream));
   return FA_OK;

@@ -87,6 +87,8 @@ struct Model {
   cudaGraphExec_t graph = nullptr;
   const KvCache *graph_kv = nullptr;
   uint32_t graph_seq = 0;
+  // device sampler run after every step of a generation (null: argmax only)
+  const SamplerParams *gen_sample = nullptr, *graph_sample = nullptr;
 
   ~Model();
   int load(const std::string &path, const fa_model_opts &o);

@@ -160,6 +160,7 @@ class GenerationState:
         self.kv_cache = None
         self.sampler_config = SamplerConfig(config.temperature, config.top_k, config.top_p,
                                             config.repetition_penalty, 0.0, 0.0)
+        self.sampler = None  # generate_step's Sampler (generate() runs its own on the device)
 
     def _gen_c(self):
         stops = np.asarray(self.config.stop_token_ids or [0], dtype=np.uint32)
@@ -183,15 +184,16 @@ class GenerationState:
         return gen
 
     def generate_step(self, token_id: int) -> Optional[int]:
-        """src/model.rs:681-705 (greedy argmax of the device logits)"""
+        """src/model.rs:681-705: forward, Sampler::sample on the device, observe"""
         if len(self.token_ids) >= self.config.max_tokens:
             return None
         if self.kv_cache is None:
             self.kv_cache = KVCache(self.model, max(self.config.max_tokens + 1, 16), 1, self.kv_dtype)
-        logits, am = self.model.forward([token_id], self.pos, self.kv_cache, return_argmax=True)
-        if self.sampler_config.temperature != 0.0 or self.sampler_config.repetition_penalty != 1.0:
-            raise L.FishaiError(L.ERR_UNSUPPORTED, "generate_step: only greedy decoding without penalties so far")
-        nxt = int(am[0])
+        if self.sampler is None:
+            self.sampler = Sampler(self.sampler_config, self.model.config.vocab_size, self.seed)
+        logits = self.model.forward([token_id], self.pos, self.kv_cache)
+        nxt = self.sampler.sample(logits)
+        self.sampler.observe_token(nxt)
         self.token_ids.append(nxt)
         self.pos += 1
         if nxt in self.config.stop_token_ids:
@@ -202,5 +204,7 @@ class GenerationState:
         """src/model.rs:710-715"""
         if self.kv_cache is not None:
             self.kv_cache.clear()
+        if self.sampler is not None:
+            self.sampler.reset()
         self.token_ids = []
         self.pos = 0

@@ -66,3 +66,9 @@ class Sampler:
 
     def reset(self):
         L.check(L.lib().fa_sampler_reset(self._h, -1))
+
+    def token_freq(self, token_id: int) -> int:
+        """token_freq[token_id] (0 for ids never observed)"""
+        c = C.c_uint32()
+        L.check(L.lib().fa_sampler_freq(self._h, 0, token_id, C.byref(c)))
+        return c.value

@@ -216,7 +216,9 @@ int fa_sample_device(fa_sampler *s, const float *logits_dev, uint32_t n, uint32_
 int fa_sample(fa_sampler *s, uint32_t seq, const float *logits_host, uint32_t vocab, uint32_t *id_host);
 /* Sampler::observe_token / reset (src/sampling.rs:155-165) */
 int fa_sampler_observe(fa_sampler *s, uint32_t seq, uint32_t token);
-int fa_sampler_reset(fa_sampler *s, int32_t seq);
+int fa_sampler_reset(fa_sampler *s, int32_t seq);  /* seq < 0: every sequence */
+/* token_freq[token] of sequence seq (0 for ids never observed) */
+int fa_sampler_freq(fa_sampler *s, uint32_t seq, uint32_t token, uint32_t *count);
 
 /* ----------------------------------------------------------- generation */
 typedef struct {
