@@ -944,3 +944,76 @@ int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, ui
 int fa_synth_write(const char *path, const fa_synth_spec *spec, uint64_t seed) { return synth_write(path, spec, seed); }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ token-parallel GEMM
+namespace {
+uint16_t f32_to_bf16_rn(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)((u >> 16) | ((u & 0xFFFFu) ? 0x40u : 0u));
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+const GemvPlan *plan_of(Model &m, int32_t proj, uint32_t layer) {
+  if (proj == 4) return &m.head;
+  if (layer >= m.layers.size()) return nullptr;
+  const LayerW &lw = m.layers[layer];
+  switch (proj) {
+    case 0: return &lw.qkv;
+    case 1: return &lw.o;
+    case 2: return &lw.gateup;
+    case 3: return &lw.down;
+    default: return nullptr;
+  }
+}
+struct DevBuf {
+  void *p = nullptr;
+  ~DevBuf() { if (p) cudaFree(p); }
+};
+}  // namespace
+
+extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const float *x_host, uint32_t T,
+                              float *y_host, uint32_t *n_out) {
+  API_NULL(fm);
+  API_NULL(x_host);
+  API_NULL(n_out);
+  Model &m = fm->m;
+  const GemvPlan *P = plan_of(m, proj, layer);
+  if (!P) return fail(FA_ERR_INVALID, "fa_gemm_tokens: projection or layer out of range");
+  if (!P->mma || P->qg_tiles.empty()) return fail(FA_ERR_UNSUPPORTED, "fa_gemm_tokens: projection not in the MMA layout");
+  if (!T) return fail(FA_ERR_INVALID, "fa_gemm_tokens: zero tokens");
+  *n_out = P->n_out;
+  if (!y_host) return FA_OK;
+  API_CUDA(cudaSetDevice(m.device));
+  const uint32_t K = P->K, N = P->n_out;
+  std::vector<uint16_t> xb((size_t)T * K);
+  for (size_t i = 0; i < xb.size(); ++i) xb[i] = f32_to_bf16_rn(x_host[i]);
+  DevBuf x, y, err;
+  API_CUDA(cudaMalloc(&x.p, xb.size() * 2));
+  API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
+  API_CUDA(cudaMalloc(&err.p, 4));
+  API_CUDA(cudaMemcpyAsync(x.p, xb.data(), xb.size() * 2, cudaMemcpyHostToDevice, m.stream));
+  API_CUDA(cudaMemsetAsync(y.p, 0, (size_t)T * N * 4, m.stream));
+  API_CUDA(cudaMemsetAsync(err.p, 0, 4, m.stream));
+  QgXMap map;
+  const uint32_t bn = T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  if (qgemm_make_xmap(&map, x.p, K, T, bn)) return fail(FA_ERR_CUDA, "tensor map encoding failed");
+  QgParams p{};
+  p.w = P->w;
+  p.chunks = P->d_chunks;
+  p.tiles = P->d_qg_tiles;
+  p.n_tiles = (uint32_t)P->qg_tiles.size();
+  p.K = K;
+  p.T = T;
+  p.out = (float *)y.p;
+  p.ldo = N;
+  p.epi = kQgStore;
+  p.err = (uint32_t *)err.p;
+  if (launch_qgemm(p, map, (uint32_t)m.n_sm, m.stream)) return fail(FA_ERR_CUDA, "token GEMM launch failed");
+  uint32_t e = 0;
+  API_CUDA(cudaMemcpyAsync(y_host, y.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaMemcpyAsync(&e, err.p, 4, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaStreamSynchronize(m.stream));
+  if (e) return fail(FA_ERR_TIMEOUT, "token GEMM: a bounded device wait gave up");
+  return FA_OK;
+}

@@ -183,6 +183,31 @@ int launch_step_end(SeqState *state, uint32_t *ids, uint32_t max_ids, bool pdl, 
 
 // tied output head (no output.weight): logits[j] = dot(xn, E[j]) with E
 // native [V][d] (transpose_2d + matmul, src/model.rs:447-452)
+// ---- token-parallel dequant-GEMM on tcgen05 (prefill, batched decode) ----
+struct QgTile {        // 128-column output tile of one chunk
+  uint32_t chunk, col0, ncols, pad;
+};
+enum : int { kQgStore = 0, kQgResid = 1 };
+struct QgParams {
+  const uint8_t *w;          // MMA-layout weight buffer of the projection group
+  const ChunkDesc *chunks;
+  const QgTile *tiles;
+  uint32_t n_tiles;
+  uint32_t K;                // rows (multiple of 16)
+  uint32_t T;                // tokens
+  float *out;                // Y[t][out_col] (launch output space), row stride ldo
+  uint32_t ldo;
+  int epi;                   // kQgStore: Y = X W; kQgResid: Y += X W
+  uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
+};
+struct QgXMap {              // TMA tensor map of a bf16 activation buffer X[T_rows][K]
+  alignas(64) unsigned char bytes[128];
+  uint32_t bn;               // tokens per tile: 64, 128 or 256
+};
+int qgemm_init();
+int qgemm_make_xmap(QgXMap *map, const void *x_bf16, uint32_t K, uint32_t T_rows, uint32_t bn);
+int launch_qgemm(const QgParams &p, const QgXMap &map, uint32_t n_sm, cudaStream_t st);
+
 // ---- Sampler::sample (src/sampling.rs:110-152), one CTA per sequence ----
 constexpr uint32_t kSampleFastK = 2048;  // top-k up to this many candidates stays in shared memory
 struct SamplerParams {

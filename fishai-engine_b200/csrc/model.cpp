@@ -180,6 +180,8 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
       max_gb = std::max(max_gb, d.gbytes);
     }
   }
+  P.n_out = 0;
+  for (const ChunkDesc &d : P.chunks) P.n_out = std::max<uint32_t>(P.n_out, d.out_col + d.width);
   if (mma) {
     P.stage_bytes = 0;  // the largest stage (sgroups whole groups) of any chunk
     for (const ChunkDesc &d : P.chunks) P.stage_bytes = std::max(P.stage_bytes, d.sgroups * d.gbytes);
@@ -252,6 +254,15 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
   CUDA_TRY(cudaMemcpy(P.d_contrib, P.contrib.data(), P.contrib.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(P.d_chunks, P.chunks.data(), P.chunks.size() * sizeof(ChunkDesc), cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMemcpy(P.d_ranges, P.ranges.data(), P.ranges.size() * sizeof(CtaRange), cudaMemcpyHostToDevice));
+  if (mma) {  // 128-column output tiles of the token-parallel GEMM
+    P.qg_tiles.clear();
+    for (uint32_t c = 0; c < nc; ++c)
+      for (uint32_t c0 = 0; c0 < P.chunks[c].width; c0 += 128)
+        P.qg_tiles.push_back({c, c0, std::min<uint32_t>(128, P.chunks[c].width - c0), 0});
+    P.d_qg_tiles = (QgTile *)m.dmalloc(P.qg_tiles.size() * sizeof(QgTile));
+    if (!P.d_qg_tiles) return fail(FA_ERR_OOM, "GEMM tile table allocation failed");
+    CUDA_TRY(cudaMemcpy(P.d_qg_tiles, P.qg_tiles.data(), P.qg_tiles.size() * sizeof(QgTile), cudaMemcpyHostToDevice));
+  }
   m.part_floats = std::max<size_t>(m.part_floats, (size_t)P.n_ctas * P.max_chunks_per_cta * P.CW);
   m.max_chunks = std::max<uint32_t>(m.max_chunks, nc);
   return FA_OK;
@@ -289,7 +300,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   want_step = o.use_step_kernel != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init())
+  if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init() || qgemm_init())
     return fail(FA_ERR_CUDA, "kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;

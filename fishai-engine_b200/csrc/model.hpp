@@ -26,6 +26,9 @@ struct GemvPlan {
   uint32_t K = 0, K8 = 0, CW = 256, stage_bytes = 16384, x_slot = 64, n_stages = 0, max_units = 0;
   uint32_t n_ctas = 0, max_chunks_per_cta = 1;
   uint64_t native_bytes = 0;  // algorithmic bytes (native GGML blocks)
+  std::vector<QgTile> qg_tiles;  // token-parallel GEMM output tiles (MMA layout only)
+  QgTile *d_qg_tiles = nullptr;
+  uint32_t n_out = 0;            // width of the launch output space
 };
 
 struct LayerW {

@@ -1,0 +1,504 @@
+// Token-parallel dequant-GEMM on the 5th-generation tensor cores (tcgen05):
+// Y[t][n] = sum_k X[t][k] * W[k][n] for T tokens at once (prefill, batched
+// decode), W in the MMA tile layout of the decode GEMV (Q4_K, Q6_K, Q8_0,
+// Q4_0; src/tensor.rs:244-258 computes the same product in f32).
+//
+// bf16 operands, f32 accumulation in tensor memory:
+//   A = W^T tile: 128 weight columns x 64 rows, dequantised by 8 producer
+//       warps from the packed codes straight into the K-major 128-byte
+//       swizzled shared-memory layout the MMA reads (d*sc*q - dmin*m etc. in
+//       f32, rounded once to bf16)
+//   B = X tile: BN tokens x 64 rows of bf16 activations, loaded by a TMA
+//       tensor copy with the same 128-byte swizzle (no multicast)
+//   D = 128 x BN f32 accumulator in TMEM (two buffers: the epilogue of one
+//       tile overlaps the MMAs of the next)
+// Roles per CTA (one persistent CTA per SM): warp 0 TMA for X, warp 1 MMA
+// issue (one elected lane) and TMEM owner, warps 2-9 dequantisation, warps
+// 10-13 epilogue (tcgen05.ld, optional residual add, f32 stores).
+// Every mbarrier wait is bounded; on expiry the CTA raises p.err, the other
+// roles stop at their next wait, the MMA warp drains its last commit and the
+// tensor memory is always released.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include "fa_device.cuh"
+#include "fa_kernels.hpp"
+
+namespace fa {
+namespace {
+
+constexpr uint32_t kBM = 128, kBK = 64;          // weight columns (MMA M) and rows per k-step
+constexpr uint32_t kDeq = 8;                     // dequant warps: one (16-row group, 64-column slice) each
+constexpr uint32_t kEpi0 = 2 + kDeq;             // first epilogue warp
+constexpr uint32_t kQThreads = (kEpi0 + 4) * 32; // 448
+constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB
+
+template <uint32_t BN>
+struct QCfg {
+  static constexpr uint32_t kBTile = BN * kBK * 2;
+  static constexpr uint32_t kStage = kATile + kBTile;
+  static constexpr uint32_t kStages = (192 * 1024) / kStage > 8 ? 8 : (192 * 1024) / kStage;
+  static constexpr uint32_t kBarOff = kStages * kStage;
+  static constexpr uint32_t kSmem = 1024 + kBarOff + 256;   // 1 KB alignment slack, barriers
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  // tcgen05 instruction descriptor: f32 D, bf16 A and B, both K-major, M = 128, N = BN
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((kBM >> 4) << 24);
+};
+
+struct QBars {
+  uint64_t full_a[8], full_b[8], empty[8], acc_full[2], acc_empty[2], done;
+  uint32_t tmem, abort;
+};
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B,
+// 8-row groups 1024 B apart; the start address advances 32 B per 16-wide k step
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int32_t c0, int32_t c1, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// W^T element pair (column n, rows k and k+1; k even) of the A tile at `a`
+__device__ __forceinline__ void put_pair(uint32_t a, uint32_t n, uint32_t k, float lo, float hi) {
+  sts32(a + n * 128 + ((((k >> 3) ^ (n & 7)) << 4) | ((k & 7) << 1)), pack_bf16(lo, hi));
+}
+__device__ __forceinline__ uint4 ldg128(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+__device__ __forceinline__ float ldg_h(const uint8_t *p) {
+  return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(p))));
+}
+
+// bounded wait that also gives up once another role has aborted
+__device__ __forceinline__ bool qwait(uint64_t *bar, uint32_t parity, QBars &b) {
+  if (*reinterpret_cast<volatile uint32_t *>(&b.abort)) return false;
+  if (mbar_wait_sleep(bar, parity)) return true;
+  atomicExch(&b.abort, 1u);
+  return false;
+}
+// the same, agreed by the whole warp (every lane polls; one failure fails all)
+__device__ __forceinline__ bool qwait_warp(uint64_t *bar, uint32_t parity, QBars &b) {
+  return __all_sync(0xFFFFFFFFu, qwait(bar, parity, b));
+}
+
+// One (16-row group, 64-column slice) unit of the A tile: lane l = 4g + c
+// owns, per 16x16 tile t, the weight columns g and g+8 and the rows 2c,
+// 2c+1, 2c+8, 2c+9 of the group (the mma.sync fragment order the layout
+// stores).  `rows` = group rows at k offset 16*gi of the tile.
+template <int T>
+__device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t i, uint32_t lane, uint32_t a,
+                                         uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3;
+  const uint32_t nt = min(64u, w - 64 * i) / 16;
+  const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  // code words: Q4 types one u32 per tile, Q8_0 two
+  uint32_t q[8];
+  if (T == kQ8_0) {
+    const uint8_t *p = G + 1024 * i + 8 * nt * lane;
+    const uint4 v0 = ldg128(p);
+    q[0] = v0.x; q[1] = v0.y; q[2] = v0.z; q[3] = v0.w;
+    if (nt == 4) {
+      const uint4 v1 = ldg128(p + 16);
+      q[4] = v1.x; q[5] = v1.y; q[6] = v1.z; q[7] = v1.w;
+    } else {
+      q[4] = q[5] = q[6] = q[7] = 0u;
+    }
+  } else {
+    const uint8_t *p = G + 512 * i + 4 * nt * lane;
+    if (nt == 4) {
+      const uint4 v = ldg128(p);
+      q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
+    } else {
+      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+      q[0] = v.x; q[1] = v.y; q[2] = q[3] = 0u;
+    }
+  }
+  // per (row, 32-column block) scale and offset: value = A * code - B
+  float sa[4][2], sb[4][2];
+  if (T == kQ4_K) {
+    const uint32_t s = i >> 2, f0 = 2 * (i & 3);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 h = ldg128(G + 8 * w + (16 * s + rr[j]) * 16);
+      const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+      const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+      const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const uint32_t bit = 12 * (f0 + b);
+        const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
+                                      : (h.w >> (bit - 64));
+        sa[j][b] = d * (float)(fld & 63u);
+        sb[j][b] = dm * (float)((fld >> 6) & 63u);
+      }
+    }
+  } else if (T == kQ6_K) {
+    const uint32_t s = i >> 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = ldg_h(G + 13 * w + (16 * s + rr[j]) * 2);
+      sa[j][0] = d;  // the int8 sub-scale varies per tile: applied below
+      sb[j][0] = 0.0f;
+      sa[j][1] = d;
+      sb[j][1] = 0.0f;
+    }
+  } else {
+    const uint32_t dreg = (T == kQ8_0) ? 16 : 8;
+    const float off = (T == kQ8_0) ? 128.0f : 8.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float d = ldg_h(G + dreg * w + (16 * (2 * i + b) + rr[j]) * 2);
+        sa[j][b] = d;
+        sb[j][b] = d * off;
+      }
+  }
+  uint32_t hw[2] = {0u, 0u};
+  if (T == kQ6_K) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(G + 8 * w + 256 * i + 8 * lane));
+    hw[0] = v.x;
+    hw[1] = v.y;
+  }
+#pragma unroll
+  for (uint32_t t = 0; t < 4; ++t) {
+    if (t >= nt) break;
+    const uint32_t b = t >> 1;
+    float A[4], B[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      A[j] = sa[j][b];
+      B[j] = sb[j][b];
+    }
+    if (T == kQ6_K) {  // value = d * sc * (q - 32), sc per (row, 16-column sub-block 4i + t)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float sc = (float)(int8_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]);
+        A[j] = A[j] * sc;
+        B[j] = A[j] * 32.0f;
+      }
+    }
+    // codes of the 8 fragment elements: (col g | g+8) x (rows 2c, 2c+1 | 2c+8, 2c+9)
+    uint32_t e[8];
+    if (T == kQ8_0) {
+      const uint32_t P = q[2 * t], Q = q[2 * t + 1];
+      e[0] = P & 0xFFu; e[1] = (P >> 16) & 0xFFu; e[2] = (P >> 8) & 0xFFu; e[3] = P >> 24;
+      e[4] = Q & 0xFFu; e[5] = (Q >> 16) & 0xFFu; e[6] = (Q >> 8) & 0xFFu; e[7] = Q >> 24;
+    } else {
+      const uint32_t W = q[t];
+      e[0] = W & 0xFu; e[1] = (W >> 16) & 0xFu; e[2] = (W >> 4) & 0xFu; e[3] = (W >> 20) & 0xFu;
+      e[4] = (W >> 8) & 0xFu; e[5] = (W >> 24) & 0xFu; e[6] = (W >> 12) & 0xFu; e[7] = W >> 28;
+      if (T == kQ6_K) {
+        const uint32_t H = hw[b] >> (2 * (t & 1));
+        const uint32_t pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+#pragma unroll
+        for (int x = 0; x < 8; ++x) e[x] |= ((H >> pos[x]) & 3u) << 4;
+      }
+    }
+    // element x: col g + 8*((x>>1)&1), row index j = (x&1) + 2*(x>>2)
+    const uint32_t n = n0 + 16 * t + g;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {     // rows 2c,2c+1 then 2c+8,2c+9
+#pragma unroll
+      for (int col = 0; col < 2; ++col) {      // column g then g+8
+        const int x0 = 4 * half + 2 * col, x1 = x0 + 1;
+        const int j0 = 2 * half, j1 = 2 * half + 1;
+        const float v0 = fmaf(A[j0], (float)e[x0], -B[j0]);
+        const float v1 = fmaf(A[j1], (float)e[x1], -B[j1]);
+        put_pair(a, n + 8 * col, k0 + rr[j0], v0, v1);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void zero_unit(uint32_t w, uint32_t i, uint32_t lane, uint32_t a, uint32_t n0,
+                                          uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3, nt = min(64u, w - 64 * i) / 16;
+  for (uint32_t t = 0; t < nt; ++t)
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int col = 0; col < 2; ++col) put_pair(a, n0 + 16 * t + g + 8 * col, k0 + 2 * c + 8 * half, 0.0f, 0.0f);
+}
+
+template <uint32_t BN>
+__global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
+  using C = QCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t qsm_raw[];
+  const uint32_t raw = smem_u32(qsm_raw), pad = (1024u - (raw & 1023u)) & 1023u;
+  uint8_t *base = qsm_raw + pad;
+  const uint32_t sbase = raw + pad;
+  QBars &b = *reinterpret_cast<QBars *>(base + C::kBarOff);
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t G16 = p.K / 16, ksteps = (G16 + 3) / 4, t_tiles = (p.T + BN - 1) / BN;
+  const uint32_t n_work = p.n_tiles * t_tiles;
+  if (tid == 0) {
+    for (uint32_t s = 0; s < C::kStages; ++s) {
+      mbar_init(&b.full_a[s], kDeq);
+      mbar_init(&b.full_b[s], 1);
+      mbar_init(&b.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&b.acc_full[a], 1);
+      mbar_init(&b.acc_empty[a], 4);
+    }
+    mbar_init(&b.done, 1);
+    b.abort = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 1) {  // tensor memory: two accumulators of BN columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&b.tmem)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = b.tmem;
+
+  if (warp == 0) {
+    // ---- X tiles by TMA ----
+    if (lane == 0) {
+      uint32_t s = 0, ph = 1, pending = 0, last_ph = 0;  // pending: stages with a load issued (bit mask)
+      for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+        const uint32_t tt = wk % t_tiles;
+        for (uint32_t ks = 0; ks < ksteps; ++ks) {
+          if (!qwait(&b.empty[s], ph, b)) goto tma_out;
+          mbar_arrive_expect_tx(&b.full_b[s], C::kBTile);
+          tma_load_2d(base + s * C::kStage + kATile, &xmap, (int32_t)(ks * kBK), (int32_t)(tt * BN), &b.full_b[s]);
+          pending |= 1u << s;
+          last_ph = (last_ph & ~(1u << s)) | ((ph ^ 1u) << s);  // consumer parity of this load
+          if (++s == C::kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    tma_out:
+      // no copy may still be writing shared memory when the CTA exits
+      for (uint32_t x = 0; x < C::kStages; ++x)
+        if (pending & (1u << x)) mbar_wait_sleep(&b.full_b[x], (last_ph >> x) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issue ----
+    uint32_t s = 0, ph = 0, acc = 0, aph = 1;
+    bool issued = false;
+    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+      if (!qwait_warp(&b.acc_empty[acc], aph, b)) break;
+      tc_fence_after();
+      const uint32_t dt = tmem + acc * BN;
+      bool ok = true;
+      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        if (!qwait_warp(&b.full_a[s], ph, b) || !qwait_warp(&b.full_b[s], ph, b)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = sbase + s * C::kStage, b0 = a0 + kATile;
+#pragma unroll
+          for (uint32_t kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16(dt, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + 32 * kk), C::kIdesc, (ks | kk) != 0);
+          umma_commit(&b.empty[s]);
+        }
+        __syncwarp();
+        issued = true;
+        if (++s == C::kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&b.acc_full[acc]);
+      __syncwarp();
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1u;
+      }
+    }
+    // drain: every MMA this CTA issued completes before the memory is released
+    if (issued) {
+      if (lane == 0) umma_commit(&b.done);
+      __syncwarp();
+      if (!mbar_wait_sleep(&b.done, 0)) atomicExch(&b.abort, 1u);
+    }
+  } else if (warp < kEpi0) {
+    // ---- dequantisation: unit (group gi, slice si) of every stage ----
+    const uint32_t d = warp - 2, gi = d >> 1, si = d & 1;
+    uint32_t s = 0, ph = 1;
+    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+      const QgTile tl = p.tiles[wk / t_tiles];
+      const ChunkDesc cd = p.chunks[tl.chunk];
+      const uint32_t i = tl.col0 / 64 + si, n0 = 64 * si;
+      const bool active = n0 < tl.ncols;
+      bool ok = true;
+      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        const uint32_t grp = 4 * ks + gi;
+        if (!qwait_warp(&b.empty[s], ph, b)) {
+          ok = false;
+          break;
+        }
+        const uint32_t a = sbase + s * C::kStage;
+        if (active) {
+          if (grp < G16) {
+            const uint8_t *G = p.w + cd.offset + (uint64_t)grp * cd.gbytes;
+            switch (cd.type) {
+              case kQ4_K: deq_unit<kQ4_K>(G, cd.width, i, lane, a, n0, 16 * gi); break;
+              case kQ6_K: deq_unit<kQ6_K>(G, cd.width, i, lane, a, n0, 16 * gi); break;
+              case kQ8_0: deq_unit<kQ8_0>(G, cd.width, i, lane, a, n0, 16 * gi); break;
+              default: deq_unit<kQ4_0>(G, cd.width, i, lane, a, n0, 16 * gi); break;
+            }
+          } else {
+            zero_unit(cd.width, i, lane, a, n0, 16 * gi);
+          }
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b.full_a[s]);
+        if (++s == C::kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ---- epilogue warpgroup: TMEM lanes 32*(warp%4) .. +32 ----
+    const uint32_t q4 = warp & 3, m = 32 * q4 + lane;
+    uint32_t acc = 0, aph = 0;
+    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+      if (!qwait_warp(&b.acc_full[acc], aph, b)) break;
+      tc_fence_after();
+      const QgTile tl = p.tiles[wk / t_tiles];
+      const uint32_t t0 = (wk % t_tiles) * BN, col_out = p.chunks[tl.chunk].out_col + tl.col0;
+      const bool mine = m < tl.ncols;
+      for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((32 * q4) << 16) + acc * BN + c0, v);
+        if (mine) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t t = t0 + c0 + j;
+            if (t < p.T) {
+              float *o = p.out + (size_t)t * p.ldo + col_out + m;
+              const float y = __uint_as_float(v[j]);
+              if (p.epi == kQgResid) *o += y;
+              else *o = y;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b.acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1u;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && b.abort && p.err) atomicOr(p.err, kErrWaitTimeout);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+template <uint32_t BN>
+int launch_bn(const QgParams &p, const void *tmap, uint32_t grid, cudaStream_t st) {
+  const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(tmap);
+  k_qgemm<BN><<<grid, kQThreads, QCfg<BN>::kSmem, st>>>(p, *m);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+}  // namespace
+
+int qgemm_init() {
+  if (cudaFuncSetAttribute(k_qgemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<64>::kSmem) ||
+      cudaFuncSetAttribute(k_qgemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<128>::kSmem) ||
+      cudaFuncSetAttribute(k_qgemm<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<256>::kSmem))
+    return -1;
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return -1;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  return 0;
+}
+
+// bf16 activations X[T_rows][K] (row stride K*2 bytes): tiles of 64 rows x bn
+// tokens with the 128-byte swizzle; rows beyond T_rows read as zero
+int qgemm_make_xmap(QgXMap *map, const void *x_bf16, uint32_t K, uint32_t T_rows, uint32_t bn) {
+  if (!g_encode || !map || !x_bf16 || K % 8 || !T_rows || (bn != 64 && bn != 128 && bn != 256)) return -1;
+  if (reinterpret_cast<uintptr_t>(x_bf16) % 16) return -1;
+  const cuuint64_t dims[2] = {K, T_rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {kBK, bn};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(reinterpret_cast<CUtensorMap *>(map->bytes), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                              const_cast<void *>(x_bf16), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  map->bn = bn;
+  return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+int launch_qgemm(const QgParams &p, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
+  if (!p.T || !p.n_tiles || p.K % 16 || !p.w || !p.out) return -1;
+  const uint32_t t_tiles = (p.T + map.bn - 1) / map.bn;
+  const uint32_t work = p.n_tiles * t_tiles, grid = work < n_sm ? work : n_sm;
+  switch (map.bn) {
+    case 64: return launch_bn<64>(p, map.bytes, grid, st);
+    case 128: return launch_bn<128>(p, map.bytes, grid, st);
+    case 256: return launch_bn<256>(p, map.bytes, grid, st);
+    default: return -1;
+  }
+}
+
+}  // namespace fa

@@ -220,6 +220,15 @@ int fa_sampler_reset(fa_sampler *s, int32_t seq);  /* seq < 0: every sequence */
 /* token_freq[token] of sequence seq (0 for ids never observed) */
 int fa_sampler_freq(fa_sampler *s, uint32_t seq, uint32_t token, uint32_t *count);
 
+/* ------------------------------------------------ token-parallel GEMM */
+/* Y[T][n_out] = X[T][K] . W for one weight group of the model (proj 0 qkv,
+ * 1 o, 2 gate/up interleaved per 1024-column chunk, 3 down, 4 output head)
+ * on the tcgen05 path that prefill and batched decode use: X rounded to bf16,
+ * W dequantised to bf16 (d*sc*q - dmin*m in f32, rounded once), f32
+ * accumulation.  Host buffers; y_host NULL only reports n_out. */
+int fa_gemm_tokens(fa_model *m, int32_t proj, uint32_t layer, const float *x_host, uint32_t T, float *y_host,
+                   uint32_t *n_out);
+
 /* ----------------------------------------------------------- generation */
 typedef struct {
   uint32_t max_tokens;          /* includes the prompt, as in src/model.rs:683-686 */
