@@ -619,6 +619,17 @@ int fa_prefill(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
     if (tokens[i] >= m.cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
   if ((rc = m.ensure_rope(start_pos + n))) return rc;
   API_CUDA(cudaSetDevice(m.device));
+  if (m.want_tc_prefill && m.tc_ok) {  // bf16 tensor-core path
+    if ((rc = m.prefill_tc(kv->kv, seq, tokens, n, start_pos))) return rc;
+    if (last_logits)
+      API_CUDA(cudaMemcpyAsync(last_logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
+    SeqState st;
+    API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
+    API_CUDA(cudaStreamSynchronize(m.stream));
+    if (last_argmax) *last_argmax = ~(uint32_t)(st.argmax_key & 0xFFFFFFFFull);
+    kv->kv.len[seq] += n;
+    return FA_OK;
+  }
   if ((rc = ensure_feed(m, n)) || (rc = ensure_ids(m, n))) return rc;
   API_CUDA(cudaMemcpyAsync(m.ws.feed, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m.stream));
   if ((rc = set_state(m, m.ws.state, 0, start_pos, kv->kv.len[seq], n))) return rc;
@@ -947,13 +958,7 @@ int fa_synth_write(const char *path, const fa_synth_spec *spec, uint64_t seed) {
 
 // ------------------------------------------------------------ token-parallel GEMM
 namespace {
-uint16_t f32_to_bf16_rn(float f) {
-  uint32_t u;
-  std::memcpy(&u, &f, 4);
-  if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)((u >> 16) | ((u & 0xFFFFu) ? 0x40u : 0u));
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
-}
+
 const GemvPlan *plan_of(Model &m, int32_t proj, uint32_t layer) {
   if (proj == 4) return &m.head;
   if (layer >= m.layers.size()) return nullptr;
@@ -987,7 +992,7 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   API_CUDA(cudaSetDevice(m.device));
   const uint32_t K = P->K, N = P->n_out;
   std::vector<uint16_t> xb((size_t)T * K);
-  for (size_t i = 0; i < xb.size(); ++i) xb[i] = f32_to_bf16_rn(x_host[i]);
+  for (size_t i = 0; i < xb.size(); ++i) xb[i] = f32_to_f16(x_host[i]);
   DevBuf x, y, err;
   API_CUDA(cudaMalloc(&x.p, xb.size() * 2));
   API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
@@ -1017,3 +1022,52 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   if (e) return fail(FA_ERR_TIMEOUT, "token GEMM: a bounded device wait gave up");
   return FA_OK;
 }
+
+// Device time of the token GEMM on device-resident operands (X: T x K bf16
+// of a fixed pattern, Y f32): average over `reps` launches after one warm-up.
+extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint32_t T, uint32_t reps, float *avg_ms,
+                               double *flop) {
+  API_NULL(fm);
+  API_NULL(avg_ms);
+  Model &m = fm->m;
+  const GemvPlan *P = plan_of(m, proj, layer);
+  if (!P || !P->mma || P->qg_tiles.empty() || !T || !reps) return fail(FA_ERR_INVALID, "fa_profile_gemm: bad arguments");
+  API_CUDA(cudaSetDevice(m.device));
+  const uint32_t K = P->K, N = P->n_out;
+  DevBuf x, y;
+  API_CUDA(cudaMalloc(&x.p, (size_t)T * K * 2));
+  API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
+  API_CUDA(cudaMemsetAsync(x.p, 0x1C, (size_t)T * K * 2, m.stream));  // f16 0x1C1C ~ 0.0041
+  QgXMap map;
+  if (qgemm_make_xmap(&map, x.p, K, T, T <= 64 ? 64 : T <= 128 ? 128 : 256)) return fail(FA_ERR_CUDA, "tensor map encoding failed");
+  QgParams p{};
+  p.w = P->w;
+  p.chunks = P->d_chunks;
+  p.tiles = P->d_qg_tiles;
+  p.n_tiles = (uint32_t)P->qg_tiles.size();
+  p.K = K;
+  p.T = T;
+  p.out = (float *)y.p;
+  p.ldo = N;
+  p.epi = kQgStore;
+  cudaEvent_t e0, e1;
+  API_CUDA(cudaEventCreate(&e0));
+  API_CUDA(cudaEventCreate(&e1));
+  int rc = FA_OK;
+  if (launch_qgemm(p, map, (uint32_t)m.n_sm, m.stream)) rc = fail(FA_ERR_CUDA, "token GEMM launch failed");
+  cudaEventRecord(e0, m.stream);
+  for (uint32_t r = 0; r < reps && rc == FA_OK; ++r)
+    if (launch_qgemm(p, map, (uint32_t)m.n_sm, m.stream)) rc = fail(FA_ERR_CUDA, "token GEMM launch failed");
+  cudaEventRecord(e1, m.stream);
+  cudaError_t ce = cudaEventSynchronize(e1);
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("token GEMM: ") + cudaGetErrorString(ce));
+  *avg_ms = ms / (float)reps;
+  if (flop) *flop = 2.0 * T * (double)K * N;
+  return FA_OK;
+}
+

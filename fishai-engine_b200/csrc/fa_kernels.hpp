@@ -13,6 +13,7 @@ enum : uint32_t {
   kErrWaitTimeout = 1u << 0,  // a bounded mbarrier wait gave up
   kErrBadToken = 1u << 1,     // token id >= vocab
   kErrContext = 1u << 2,      // position beyond the KV capacity / RoPE table
+  kErrRange = 1u << 3,        // an activation outside the f16 range of the tensor-core path
 };
 
 // Per-sequence decode state kept in device memory so a captured CUDA graph
@@ -200,13 +201,34 @@ struct QgParams {
   int epi;                   // kQgStore: Y = X W; kQgResid: Y += X W
   uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
 };
-struct QgXMap {              // TMA tensor map of a bf16 activation buffer X[T_rows][K]
+struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
   alignas(64) unsigned char bytes[128];
   uint32_t bn;               // tokens per tile: 64, 128 or 256
 };
 int qgemm_init();
-int qgemm_make_xmap(QgXMap *map, const void *x_bf16, uint32_t K, uint32_t T_rows, uint32_t bn);
+int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows, uint32_t bn);
 int launch_qgemm(const QgParams &p, const QgXMap &map, uint32_t n_sm, cudaStream_t st);
+
+// ---- token-parallel forward pieces (prefill.cu) ----
+struct AttnRowsParams {
+  const void *qh;            // f16 [T][Hq*hd], rotated
+  uint32_t T, Hq, Hkv, hd;
+  uint32_t len0;             // cache slots before the first token; token t sees [0, len0 + t]
+  KvView kv;
+  uint32_t seq, layer;
+  float scale_log2;          // log2(e) / sqrt(hd)
+  void *out;                 // f16 [T][Hq*hd]
+};
+int launch_embed_rows(const void *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab, float *x,
+                      uint32_t *err, cudaStream_t st);
+int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, uint32_t d, void *out, uint32_t *err,
+                       cudaStream_t st);
+int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                        uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
+                        void *qh, uint32_t *err, cudaStream_t st);
+int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st);
+int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st);
+int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st);
 
 // ---- Sampler::sample (src/sampling.rs:110-152), one CTA per sequence ----
 constexpr uint32_t kSampleFastK = 2048;  // top-k up to this many candidates stays in shared memory

@@ -298,6 +298,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   pdl = o.use_pdl != 0;
   graphs = o.use_graphs != 0;
   want_step = o.use_step_kernel != 0;
+  want_tc_prefill = o.use_tc_prefill != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init() || qgemm_init())
@@ -681,6 +682,9 @@ int Model::setup_step_kernel() {
   bool ok = !tied && L > 0 && head.mma && hd % 8 == 0 && hd <= 128 && cfg.n_heads % cfg.n_kv_heads == 0 &&
             (rep == 1 || rep == 2 || rep == 4 || rep == 8) && attn_splits <= 64;
   for (const LayerW &lw : layers) ok = ok && lw.qkv.mma && lw.o.mma && lw.gateup.mma && lw.down.mma;
+  // the tensor-core prefill needs every layer projection in the MMA layout
+  tc_ok = L > 0 && (hd == 64 || hd == 128) && cfg.n_heads % cfg.n_kv_heads == 0;
+  for (const LayerW &lw : layers) tc_ok = tc_ok && lw.qkv.mma && lw.o.mma && lw.gateup.mma && lw.down.mma;
   if (!ok || !want_step) return FA_OK;
   const uint32_t n_phases = 1 + 5 * L + 1, n_gemv = 4 * L + 1;
   d_phases = (StepPhase *)dmalloc(n_phases * sizeof(StepPhase));
@@ -833,4 +837,118 @@ int Model::prepare_step(const KvCache &kv, uint32_t seq) {
   return FA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Token-parallel prefill: per layer RMSNorm rows -> qkv GEMM -> RoPE + KV
+// append -> causal attention -> o GEMM (+residual) -> RMSNorm rows -> gate/up
+// GEMM -> SwiGLU -> down GEMM (+residual), in chunks of up to 2048 tokens.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kPrefillChunk = 2048;
+
+int Model::ensure_prefill_ws(uint32_t cap) {
+  if (cap <= pws.cap) return FA_OK;
+  const uint32_t d = cfg.n_embd, qd = cfg.n_heads * cfg.head_dim, F = layers[0].down.K;
+  const uint32_t qkv_n = layers[0].qkv.n_out, gu_n = layers[0].gateup.n_out;
+  PrefillWs w;
+  w.cap = cap;
+  w.tok = (uint32_t *)dmalloc((size_t)cap * 4);
+  w.err = (uint32_t *)dmalloc(4);
+  w.X = (float *)dmalloc((size_t)cap * d * 4);
+  w.QKV = (float *)dmalloc((size_t)cap * qkv_n * 4);
+  w.GU = (float *)dmalloc((size_t)cap * gu_n * 4);
+  w.Xn = dmalloc((size_t)cap * d * 2);
+  w.Qh = dmalloc((size_t)cap * qd * 2);
+  w.Ob = dmalloc((size_t)cap * qd * 2);
+  w.Hb = dmalloc((size_t)cap * F * 2);
+  if (!w.tok || !w.err || !w.X || !w.QKV || !w.GU || !w.Xn || !w.Qh || !w.Ob || !w.Hb)
+    return fail(FA_ERR_OOM, "prefill workspace allocation failed");
+  const uint32_t bns[3] = {64, 128, 256};
+  for (int b = 0; b < 3; ++b)
+    if (qgemm_make_xmap(&w.mxn[b], w.Xn, d, cap, bns[b]) || qgemm_make_xmap(&w.mob[b], w.Ob, qd, cap, bns[b]) ||
+        qgemm_make_xmap(&w.mhb[b], w.Hb, F, cap, bns[b]))
+      return fail(FA_ERR_CUDA, "tensor map encoding failed");
+  pws = w;  // the previous buffers stay owned by `allocs` until teardown
+  return FA_OK;
+}
+
+int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi) {
+  QgParams p{};
+  p.w = P.w;
+  p.chunks = P.d_chunks;
+  p.tiles = P.d_qg_tiles;
+  p.n_tiles = (uint32_t)P.qg_tiles.size();
+  p.K = P.K;
+  p.T = T;
+  p.out = out;
+  p.ldo = ldo;
+  p.epi = epi;
+  p.err = pws.err;
+  return launch_qgemm(p, map, (uint32_t)n_sm, stream) ? fail(FA_ERR_CUDA, "token GEMM launch failed") : FA_OK;
+}
+
+int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t n, uint32_t start_pos) {
+  if (!tc_ok) return fail(FA_ERR_UNSUPPORTED, "tensor-core prefill needs every projection in the MMA layout");
+  const uint32_t d = cfg.n_embd, hd = cfg.head_dim, Hq = cfg.n_heads, Hkv = cfg.n_kv_heads;
+  const uint32_t F = layers[0].down.K, qkv_n = layers[0].qkv.n_out, gu_n = layers[0].gateup.n_out;
+  int rc;
+  if ((rc = ensure_rope(start_pos + n + 1)) || (rc = ensure_prefill_ws(std::min(n, kPrefillChunk)))) return rc;
+  CUDA_TRY(cudaMemsetAsync(pws.err, 0, 4, stream));
+  const KvView kvv = kv.view();
+  const float scale_log2 = (1.0f / std::sqrt((float)hd)) * 1.4426950408889634f;
+  uint32_t T = 0;
+  for (uint32_t i0 = 0; i0 < n; i0 += pws.cap) {
+    T = std::min(pws.cap, n - i0);
+    const uint32_t len0 = kv.len[seq] + i0, pos0 = start_pos + i0;
+    const int b = T <= 64 ? 0 : T <= 128 ? 1 : 2;
+    CUDA_TRY(cudaMemcpyAsync(pws.tok, toks + i0, (size_t)T * 4, cudaMemcpyHostToDevice, stream));
+    if (launch_embed_rows(emb, emb_type, pws.tok, T, d, cfg.vocab_size, pws.X, pws.err, stream))
+      return fail(FA_ERR_CUDA, "embed launch failed");
+    for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+      const LayerW &lw = layers[l];
+      if (launch_norm_rows_h(pws.X, lw.attn_norm, cfg.norm_eps, T, d, pws.Xn, pws.err, stream))
+        return fail(FA_ERR_CUDA, "norm launch failed");
+      if ((rc = run_qgemm(lw.qkv, pws.mxn[b], T, pws.QKV, qkv_n, kQgStore))) return rc;
+      if (launch_rope_kv_rows(pws.QKV, T, Hq, Hkv, hd, rope_tab, rope_max, pos0, len0, kvv, seq, l, pws.Qh, pws.err,
+                              stream))
+        return fail(FA_ERR_CUDA, "rope launch failed");
+      AttnRowsParams ap{};
+      ap.qh = pws.Qh;
+      ap.T = T;
+      ap.Hq = Hq;
+      ap.Hkv = Hkv;
+      ap.hd = hd;
+      ap.len0 = len0;
+      ap.kv = kvv;
+      ap.seq = seq;
+      ap.layer = l;
+      ap.scale_log2 = scale_log2;
+      ap.out = pws.Ob;
+      if (launch_attn_rows(ap, stream)) return fail(FA_ERR_CUDA, "prefill attention launch failed");
+      if ((rc = run_qgemm(lw.o, pws.mob[b], T, pws.X, d, kQgResid))) return rc;
+      if (launch_norm_rows_h(pws.X, lw.ffn_norm, cfg.norm_eps, T, d, pws.Xn, pws.err, stream))
+        return fail(FA_ERR_CUDA, "norm launch failed");
+      if ((rc = run_qgemm(lw.gateup, pws.mxn[b], T, pws.GU, gu_n, kQgStore))) return rc;
+      if (launch_swiglu_rows(pws.GU, T, F, lw.gateup.CW, pws.Hb, pws.err, stream))
+        return fail(FA_ERR_CUDA, "swiglu launch failed");
+      if ((rc = run_qgemm(lw.down, pws.mhb[b], T, pws.X, d, kQgResid))) return rc;
+    }
+  }
+  // the last token through the decode head: logits + argmax
+  const uint32_t n_ssq = (uint32_t)layers[cfg.n_layers - 1].down.chunks.size();
+  if (launch_last_row(pws.X, T - 1, d, ws.x, ws.ssq_d, n_ssq, stream)) return fail(FA_ERR_CUDA, "last row launch failed");
+  SeqState st{};
+  st.pos = start_pos + n - 1;
+  st.len = kv.len[seq] + n - 1;
+  CUDA_TRY(cudaMemcpyAsync(ws.state, &st, sizeof st, cudaMemcpyHostToDevice, stream));
+  if ((rc = enqueue_head(ws, ws.state))) return rc;
+  uint32_t e = 0;
+  CUDA_TRY(cudaMemcpyAsync(&e, pws.err, 4, cudaMemcpyDeviceToHost, stream));
+  CUDA_TRY(cudaStreamSynchronize(stream));
+  if (e & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "prefill: a bounded device wait gave up");
+  if (e & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
+  if (e & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");
+  if (e & kErrRange) return fail(FA_ERR_UNSUPPORTED, "an activation exceeds the f16 range of the tensor-core prefill");
+  return FA_OK;
+}
+
 }  // namespace fa
+

@@ -50,6 +50,15 @@ struct Workspace {
 
 struct KvCache;
 
+// buffers of the token-parallel (tensor-core) prefill, `cap` tokens per chunk
+struct PrefillWs {
+  uint32_t cap = 0;
+  uint32_t *tok = nullptr, *err = nullptr;
+  float *X = nullptr, *QKV = nullptr, *GU = nullptr;
+  void *Xn = nullptr, *Qh = nullptr, *Ob = nullptr, *Hb = nullptr;
+  QgXMap mxn[3], mob[3], mhb[3];  // TMA maps of Xn, Ob, Hb for 64, 128, 256 tokens per tile
+};
+
 struct Model {
   fa_config cfg{};
   int device = 0;
@@ -86,6 +95,15 @@ struct Model {
   StepPhase *d_phases = nullptr;
   GemvParams *d_gemv = nullptr;
   uint32_t *d_step_done = nullptr, *d_step_sync = nullptr;
+  // token-parallel prefill (bf16 tensor cores)
+  bool want_tc_prefill = false, tc_ok = false;
+  PrefillWs pws;
+  int ensure_prefill_ws(uint32_t cap);
+  int run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi);
+  // prompt tokens [0, n) at positions start_pos.., appended after the cache's
+  // current length; leaves the last token's logits in ws.logits and the
+  // argmax in ws.state->argmax_key
+  int prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t start_pos);
   // decode-step graph cache
   cudaGraphExec_t graph = nullptr;
   const KvCache *graph_kv = nullptr;

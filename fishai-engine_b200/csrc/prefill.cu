@@ -1,0 +1,352 @@
+// Token-parallel forward pieces for prefill and batched steps (the f16
+// tensor-core path; ModelWeights::forward, src/model.rs:316-455, per token):
+//   k_embed_rows      X[t] = E[tok[t]] (src/model.rs:338-343)
+//   k_norm_rows_h     Xn[t] = f16(rms_norm(X[t]) * w) (src/tensor.rs:280-290)
+//   k_rope_kv_rows    RoPE of q and k (half split, src/model.rs:469-491), K/V
+//                     appended to the paged cache, q to f16 for attention
+//   k_attn_causal     causal flash attention over the paged cache: token t
+//                     sees cache slots [0, len0 + t] (the sequential forwards
+//                     of a prompt), GQA by index; mma.sync f16, f32 softmax
+//   k_swiglu_rows     H[t] = f16(silu(gate) * up) from the interleaved
+//                     gate/up GEMM output (src/model.rs:413-420)
+//   k_last_row        the last token's hidden state and its sum of squares
+//                     into the decode workspace for the output head
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "fa_dequant.cuh"
+#include "fa_device.cuh"
+#include "fa_kernels.hpp"
+
+namespace fa {
+namespace {
+
+__global__ void k_embed_rows(const uint8_t *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab,
+                             float *x, uint32_t *err) {
+  const uint32_t t = blockIdx.x;
+  if (t >= T) return;
+  uint32_t id = tok[t];
+  if (id >= vocab) {
+    if (threadIdx.x == 0 && err) atomicOr(err, kErrBadToken);
+    id = 0;
+  }
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x)
+    x[(size_t)t * d + i] = dequant_native_elem(type, emb, (uint64_t)id * d + i);
+}
+
+__device__ float block_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  const uint32_t w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.0f;
+  for (uint32_t i = 0; i < nw; ++i) s += red[i];
+  __syncthreads();
+  return s;
+}
+
+constexpr float kHalfMax = 65504.0f;
+
+__global__ void k_norm_rows_h(const float *x, const float *w, float eps, uint32_t d, __half *out, uint32_t *err) {
+  __shared__ float red[32];
+  const float *r = x + (size_t)blockIdx.x * d;
+  float s = 0.0f;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) s = fmaf(r[i], r[i], s);
+  s = block_sum(s, red);
+  const float inv = 1.0f / sqrtf(s / (float)d + eps);
+  bool bad = false;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(r[i], inv), w[i]);
+    bad |= !(fabsf(v) <= kHalfMax);
+    out[(size_t)blockIdx.x * d + i] = __float2half_rn(v);
+  }
+  if (bad && err) atomicOr(err, kErrRange);
+}
+
+// one CTA per token; rows of QKV: [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)]
+__global__ void k_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                               uint32_t rope_max, uint32_t pos0, uint32_t len0, KvView kv, uint32_t seq, uint32_t layer,
+                               __half *qh, uint32_t *err) {
+  const uint32_t t = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
+  const float *row = qkv + (size_t)t * (qd + 2 * kd);
+  const uint32_t pos = pos0 + t, slot = len0 + t;
+  if (pos >= rope_max || slot / 16 >= kv.max_pages) {
+    if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
+    return;
+  }
+  const float *cs = rope + (size_t)pos * hd;
+  const uint32_t page = kv.page_table[seq * kv.max_pages + slot / 16];
+  const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
+  for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) {
+    float v = row[j];
+    const bool is_q = j < qd, is_k = !is_q && j < qd + kd;
+    if (is_q || is_k) {
+      const uint32_t base = is_q ? 0 : qd, dd = (j - base) % hd, hb = j - dd;
+      const float cth = cs[2 * (dd % half)], sth = cs[2 * (dd % half) + 1];
+      const float pv = dd < half ? row[hb + dd + half] : row[hb + dd - half];
+      v = dd < half ? __fsub_rn(__fmul_rn(v, cth), __fmul_rn(pv, sth)) : __fadd_rn(__fmul_rn(pv, sth), __fmul_rn(v, cth));
+    }
+    if (is_q) {
+      qh[(size_t)t * qd + j] = __float2half_rn(v);
+    } else {
+      const uint32_t kc = is_k ? j - qd : j - qd - kd;
+      const uint64_t idx = lbase + kv_index(page, is_k ? 0 : 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
+      if (kv.f16) reinterpret_cast<__half *>(kv.base)[idx] = __float2half_rn(v);
+      else reinterpret_cast<float *>(kv.base)[idx] = v;
+    }
+  }
+}
+
+// ---- causal flash attention (mma.sync m16n8k16 f16, f32 accumulation) ----
+constexpr uint32_t kAQ = 64, kAK = 64;  // query rows and cache slots per tile
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+// byte offset of 16-byte chunk c of row r in a tile of rows of `rb` bytes
+// (chunks XOR-swizzled by row so 8 consecutive rows hit distinct banks)
+__device__ __forceinline__ uint32_t sw_off(uint32_t r, uint32_t c, uint32_t rb) { return r * rb + ((c ^ (r & 7)) << 4); }
+
+// stage cache slots [s0, s0 + 64) of (kv head, K or V) into a tile of rows of
+// HD f16; slots >= s_end read as zero
+template <uint32_t HD, bool F16>
+__device__ __forceinline__ void load_kv_tile(const KvView &kv, uint64_t lbase, const uint32_t *pt, uint32_t kvh,
+                                             int is_v, uint32_t s0, uint32_t s_end, uint32_t tile) {
+  constexpr uint32_t CH = HD / 8;  // 16-byte chunks per row
+  for (uint32_t i = threadIdx.x; i < kAK * CH; i += blockDim.x) {
+    const uint32_t r = i / CH, c = i % CH, s = s0 + r;
+    const uint32_t dst = tile + sw_off(r, c, HD * 2);
+    if (s >= s_end) {
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
+      continue;
+    }
+    const uint64_t idx = lbase + kv_index(pt[s / 16], is_v, kvh, s % 16, 8 * c, kv.n_kv, HD);
+    if (F16) {
+      const __half *src = reinterpret_cast<const __half *>(kv.base) + idx;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    } else {
+      const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(kv.base) + idx);
+      const float4 a = __ldcg(src), b = __ldcg(src + 1);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pack_h2(a.x, a.y)), "r"(pack_h2(a.z, a.w)),
+                   "r"(pack_h2(b.x, b.y)), "r"(pack_h2(b.z, b.w))
+                   : "memory");
+    }
+  }
+}
+
+// grid (query tiles, q heads); 4 warps x 16 query rows
+template <uint32_t HD, bool F16>
+__global__ void __launch_bounds__(128) k_attn_causal(const __half *qh, uint32_t T, uint32_t Hq, uint32_t Hkv,
+                                                     uint32_t len0, KvView kv, uint32_t seq, uint32_t layer,
+                                                     float scale_log2, __half *out) {
+  extern __shared__ __align__(128) uint8_t asm_raw[];
+  constexpr uint32_t RB = HD * 2, KT = HD / 16, NT = kAK / 8, OT = HD / 8;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const uint32_t h = blockIdx.y, kvh = h / (Hq / Hkv), t0 = blockIdx.x * kAQ;
+  const uint32_t ks_tile = smem_u32(asm_raw), vs_tile = ks_tile + kAK * RB;
+  const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
+  const uint32_t *pt = kv.page_table + (size_t)seq * kv.max_pages;
+  const uint32_t last_t = min(T, t0 + kAQ) - 1, s_end = len0 + last_t + 1;  // slots this tile may read
+  // Q fragments of this warp's 16 rows (rows >= T read as zero)
+  uint32_t qa[KT][4];
+  {
+    const uint32_t r0 = t0 + 16 * warp + g, r1 = r0 + 8;
+#pragma unroll
+    for (uint32_t kt = 0; kt < KT; ++kt) {
+      const uint32_t d0 = 16 * kt + 2 * c;
+      auto ld = [&](uint32_t r, uint32_t d) -> uint32_t {
+        return r < T ? *reinterpret_cast<const uint32_t *>(qh + (size_t)r * Hq * HD + h * HD + d) : 0u;
+      };
+      qa[kt][0] = ld(r0, d0);
+      qa[kt][1] = ld(r1, d0);
+      qa[kt][2] = ld(r0, d0 + 8);
+      qa[kt][3] = ld(r1, d0 + 8);
+    }
+  }
+  float o[OT][4];
+#pragma unroll
+  for (uint32_t j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  const uint32_t q0 = t0 + 16 * warp + g, q1 = q0 + 8;  // query tokens of this lane's rows
+  for (uint32_t s0 = 0; s0 < s_end; s0 += kAK) {
+    load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 0, s0, s_end, ks_tile);
+    load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 1, s0, s_end, vs_tile);
+    if (F16) asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    // S = Q K^T for 16 rows x 64 slots
+    float s[NT][4];
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+    for (uint32_t kt = 0; kt < KT; ++kt) {
+#pragma unroll
+      for (uint32_t j = 0; j < NT; j += 2) {
+        // matrices: (slots 8j.., dims 16kt), (8j.., 16kt+8), (8j+8.., 16kt), (8j+8.., 16kt+8)
+        const uint32_t mi = lane >> 3, r = 8 * j + 8 * (mi >> 1) + (lane & 7), ch = 2 * kt + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(ks_tile + sw_off(r, ch, RB), b0, b1, b2, b3);
+        mma_f16(s[j], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b0, b1);
+        mma_f16(s[j + 1], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b2, b3);
+      }
+    }
+    // causal mask, online softmax (base 2)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j) {
+      const uint32_t sl = s0 + 8 * j + 2 * c;
+#pragma unroll
+      for (uint32_t e = 0; e < 2; ++e) {
+        s[j][e] = (sl + e <= len0 + q0 && sl + e < s_end) ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][2 + e] = (sl + e <= len0 + q1 && sl + e < s_end) ? s[j][2 + e] * scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[j][e]);
+        mx1 = fmaxf(mx1, s[j][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, off));
+    }
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float a0 = n0 == -INFINITY ? 1.0f : exp2f(m0 - n0), a1 = n1 == -INFINITY ? 1.0f : exp2f(m1 - n1);
+    float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j) {
+#pragma unroll
+      for (uint32_t e = 0; e < 2; ++e) {
+        s[j][e] = n0 == -INFINITY ? 0.0f : exp2f(s[j][e] - n0);
+        s[j][2 + e] = n1 == -INFINITY ? 0.0f : exp2f(s[j][2 + e] - n1);
+        ls0 += s[j][e];
+        ls1 += s[j][2 + e];
+      }
+    }
+    l0 = fmaf(l0, a0, ls0);
+    l1 = fmaf(l1, a1, ls1);
+    m0 = n0;
+    m1 = n1;
+#pragma unroll
+    for (uint32_t j = 0; j < OT; ++j) {
+      o[j][0] *= a0;
+      o[j][1] *= a0;
+      o[j][2] *= a1;
+      o[j][3] *= a1;
+    }
+    // O += P V: P (16 x 64) as A fragments, V rows of slots via transposed ldmatrix
+#pragma unroll
+    for (uint32_t kt = 0; kt < kAK / 16; ++kt) {
+      const uint32_t pa0 = pack_h2(s[2 * kt][0], s[2 * kt][1]), pa1 = pack_h2(s[2 * kt][2], s[2 * kt][3]);
+      const uint32_t pa2 = pack_h2(s[2 * kt + 1][0], s[2 * kt + 1][1]), pa3 = pack_h2(s[2 * kt + 1][2], s[2 * kt + 1][3]);
+#pragma unroll
+      for (uint32_t j = 0; j < OT; j += 2) {
+        // matrices: (slots 16kt.., dims 8j), (16kt+8.., 8j), (16kt.., 8j+8), (16kt+8.., 8j+8)
+        const uint32_t mi = lane >> 3, r = 16 * kt + 8 * (mi & 1) + (lane & 7), ch = j + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vs_tile + sw_off(r, ch, RB), b0, b1, b2, b3);
+        mma_f16(o[j], pa0, pa1, pa2, pa3, b0, b1);
+        mma_f16(o[j + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  // rows: lane sums across the 4 lanes of a row, then O / l
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, off);
+    l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, off);
+  }
+  const float i0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, i1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
+#pragma unroll
+  for (uint32_t j = 0; j < OT; ++j) {
+    const uint32_t d = 8 * j + 2 * c;
+    if (q0 < T) *reinterpret_cast<__half2 *>(out + (size_t)q0 * Hq * HD + h * HD + d) = __floats2half2_rn(o[j][0] * i0, o[j][1] * i0);
+    if (q1 < T) *reinterpret_cast<__half2 *>(out + (size_t)q1 * Hq * HD + h * HD + d) = __floats2half2_rn(o[j][2] * i1, o[j][3] * i1);
+  }
+}
+
+// gate/up launch space: chunk c (width w_c) holds gate f in [c*CW/2, +w_c/2)
+// at c*CW + local, then the same up columns
+__global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
+  const uint32_t t = blockIdx.y, f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  const uint32_t c = f / (CW / 2), local = f - c * (CW / 2), wc = min(CW, 2 * F - c * CW);
+  const float *row = gu + (size_t)t * 2 * F;
+  const float gv = row[c * CW + local], uv = row[c * CW + wc / 2 + local];
+  const float v = gv * (1.0f / (1.0f + expf(-gv))) * uv;
+  if (!(fabsf(v) <= kHalfMax) && err) atomicOr(err, kErrRange);
+  h[(size_t)t * F + f] = __float2half_rn(v);
+}
+
+// last token's row -> x, its sum of squares -> ssq[0] (the rest zero)
+__global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq) {
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = X[(size_t)row * d + i];
+    x[i] = v;
+    s = fmaf(v, v, s);
+  }
+  s = block_sum(s, red);
+  for (uint32_t i = threadIdx.x; i < n_ssq; i += blockDim.x) ssq[i] = i == 0 ? s : 0.0f;
+}
+
+template <uint32_t HD, bool F16>
+int launch_attn_hd(const AttnRowsParams &p, cudaStream_t st) {
+  const uint32_t smem = 2 * kAK * HD * 2;  // K and V tiles: 32 KB at head_dim 128
+  const dim3 grid((p.T + kAQ - 1) / kAQ, p.Hq);
+  k_attn_causal<HD, F16><<<grid, 128, smem, st>>>((const __half *)p.qh, p.T, p.Hq, p.Hkv, p.len0, p.kv, p.seq,
+                                                  p.layer, p.scale_log2, (__half *)p.out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace
+
+int launch_embed_rows(const void *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab, float *x,
+                      uint32_t *err, cudaStream_t st) {
+  k_embed_rows<<<T, 256, 0, st>>>((const uint8_t *)emb, type, tok, T, d, vocab, x, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, uint32_t d, void *out, uint32_t *err,
+                       cudaStream_t st) {
+  k_norm_rows_h<<<T, 256, 0, st>>>(x, w, eps, d, (__half *)out, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                        uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
+                        void *qh, uint32_t *err, cudaStream_t st) {
+  k_rope_kv_rows<<<T, 256, 0, st>>>(qkv, T, Hq, Hkv, hd, rope, rope_max, pos0, len0, kv, seq, layer, (__half *)qh, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
+  if (p.Hq % p.Hkv) return -1;
+  if (p.hd == 128) return p.kv.f16 ? launch_attn_hd<128, true>(p, st) : launch_attn_hd<128, false>(p, st);
+  if (p.hd == 64) return p.kv.f16 ? launch_attn_hd<64, true>(p, st) : launch_attn_hd<64, false>(p, st);
+  return -1;
+}
+int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
+  k_swiglu_rows<<<dim3((F + 255) / 256, T), 256, 0, st>>>(gu, F, CW, (__half *)h, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st) {
+  k_last_row<<<1, 256, 0, st>>>(X, row, d, x, ssq, n_ssq);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace fa

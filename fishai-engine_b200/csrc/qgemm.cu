@@ -3,12 +3,14 @@
 // decode), W in the MMA tile layout of the decode GEMV (Q4_K, Q6_K, Q8_0,
 // Q4_0; src/tensor.rs:244-258 computes the same product in f32).
 //
-// bf16 operands, f32 accumulation in tensor memory:
+// f16 operands (11 mantissa bits: 8x less rounding than bf16 at the same
+// tensor throughput; the activation producers flag values beyond the f16
+// range), f32 accumulation in tensor memory:
 //   A = W^T tile: 128 weight columns x 64 rows, dequantised by 8 producer
 //       warps from the packed codes straight into the K-major 128-byte
 //       swizzled shared-memory layout the MMA reads (d*sc*q - dmin*m etc. in
-//       f32, rounded once to bf16)
-//   B = X tile: BN tokens x 64 rows of bf16 activations, loaded by a TMA
+//       f32, rounded once to f16)
+//   B = X tile: BN tokens x 64 rows of f16 activations, loaded by a TMA
 //       tensor copy with the same 128-byte swizzle (no multicast)
 //   D = 128 x BN f32 accumulator in TMEM (two buffers: the epilogue of one
 //       tile overlaps the MMAs of the next)
@@ -19,7 +21,7 @@
 // roles stop at their next wait, the MMA warp drains its last commit and the
 // tensor memory is always released.
 #include <cuda.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -43,8 +45,8 @@ struct QCfg {
   static constexpr uint32_t kBarOff = kStages * kStage;
   static constexpr uint32_t kSmem = 1024 + kBarOff + 256;   // 1 KB alignment slack, barriers
   static constexpr uint32_t kTmemCols = 2 * BN;
-  // tcgen05 instruction descriptor: f32 D, bf16 A and B, both K-major, M = 128, N = BN
-  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((kBM >> 4) << 24);
+  // tcgen05 instruction descriptor: f32 D, f16 A and B (format 0), both K-major, M = 128, N = BN
+  static constexpr uint32_t kIdesc = (1u << 4) | ((BN >> 3) << 17) | ((kBM >> 4) << 24);
 };
 
 struct QBars {
@@ -92,8 +94,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
@@ -101,7 +103,7 @@ __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
 }
 // W^T element pair (column n, rows k and k+1; k even) of the A tile at `a`
 __device__ __forceinline__ void put_pair(uint32_t a, uint32_t n, uint32_t k, float lo, float hi) {
-  sts32(a + n * 128 + ((((k >> 3) ^ (n & 7)) << 4) | ((k & 7) << 1)), pack_bf16(lo, hi));
+  sts32(a + n * 128 + ((((k >> 3) ^ (n & 7)) << 4) | ((k & 7) << 1)), pack_f16(lo, hi));
 }
 __device__ __forceinline__ uint4 ldg128(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 __device__ __forceinline__ float ldg_h(const uint8_t *p) {
@@ -472,17 +474,17 @@ int qgemm_init() {
   return 0;
 }
 
-// bf16 activations X[T_rows][K] (row stride K*2 bytes): tiles of 64 rows x bn
+// f16 activations X[T_rows][K] (row stride K*2 bytes): tiles of 64 rows x bn
 // tokens with the 128-byte swizzle; rows beyond T_rows read as zero
-int qgemm_make_xmap(QgXMap *map, const void *x_bf16, uint32_t K, uint32_t T_rows, uint32_t bn) {
-  if (!g_encode || !map || !x_bf16 || K % 8 || !T_rows || (bn != 64 && bn != 128 && bn != 256)) return -1;
-  if (reinterpret_cast<uintptr_t>(x_bf16) % 16) return -1;
+int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows, uint32_t bn) {
+  if (!g_encode || !map || !x_f16 || K % 8 || !T_rows || (bn != 64 && bn != 128 && bn != 256)) return -1;
+  if (reinterpret_cast<uintptr_t>(x_f16) % 16) return -1;
   const cuuint64_t dims[2] = {K, T_rows};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
   const cuuint32_t box[2] = {kBK, bn};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = g_encode(reinterpret_cast<CUtensorMap *>(map->bytes), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                              const_cast<void *>(x_bf16), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUresult r = g_encode(reinterpret_cast<CUtensorMap *>(map->bytes), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                              const_cast<void *>(x_f16), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   map->bn = bn;

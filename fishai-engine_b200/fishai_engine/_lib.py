@@ -35,7 +35,8 @@ class fa_config(C.Structure):
 
 class fa_model_opts(C.Structure):
     _fields_ = [("device", C.c_int32), ("use_graphs", C.c_int32), ("use_pdl", C.c_int32), ("tp_rank", C.c_int32),
-                ("tp_world", C.c_int32), ("nccl_id", C.c_void_p), ("use_step_kernel", C.c_int32)]
+                ("tp_world", C.c_int32), ("nccl_id", C.c_void_p), ("use_step_kernel", C.c_int32),
+                ("use_tc_prefill", C.c_int32)]
 
 
 class fa_sampler_config(C.Structure):
@@ -102,6 +103,7 @@ SIGNATURES = {
     "fa_sampler_reset": ([_vp, C.c_int32], _i),
     "fa_sampler_freq": ([_vp, _u32, _u32, _pu32], _i),
     "fa_gemm_tokens": ([_vp, C.c_int32, _u32, _pf, _u32, _pf, _pu32], _i),
+    "fa_profile_gemm": ([_vp, C.c_int32, _u32, _u32, _u32, _pf, C.POINTER(C.c_double)], _i),
     "fa_generate": ([_vp, C.POINTER(fa_gen_config), _pu32, _u32, _pu32, _u32, _pu32], _i),
     "fa_decode_greedy": ([_vp, _vp, _u32, _u32, _u32, _u32, _pu32], _i),
     "fa_profile_gemv": ([_vp, C.c_int32, _u32, _pf, _pu64], _i),

@@ -64,12 +64,14 @@ class ModelWeights:
 
     @classmethod
     def load_from_gguf(cls, gguf, config: Optional[ModelConfig] = None, device: int = 0, use_graphs: bool = True,
-                       use_pdl: bool = True, use_step_kernel: bool = False) -> "ModelWeights":
+                       use_pdl: bool = True, use_step_kernel: bool = False,
+                       use_tc_prefill: bool = False) -> "ModelWeights":
         path = gguf.path if isinstance(gguf, GGUFFile) else str(gguf)
         o = L.fa_model_opts()
         L.lib().fa_model_opts_default(C.byref(o))
         o.device, o.use_graphs, o.use_pdl = device, int(use_graphs), int(use_pdl)
         o.use_step_kernel = int(use_step_kernel)
+        o.use_tc_prefill = int(use_tc_prefill)
         h = C.c_void_p()
         L.check(L.lib().fa_model_load(path.encode(), C.byref(o), C.byref(h)))
         c = L.fa_config()

@@ -111,6 +111,8 @@ typedef struct {
   const void *nccl_id;  /* 128-byte ncclUniqueId when tp_world > 1 */
   int32_t use_step_kernel;  /* run each decode step as one persistent kernel when the
                                model qualifies (MMA-layout projections, untied head) */
+  int32_t use_tc_prefill;   /* fa_prefill on the f16 tensor-core path (tcgen05 GEMMs, flash
+                               attention): max-abs-rel 1e-2 of the f32 path instead of 1e-4 */
 } fa_model_opts;
 void fa_model_opts_default(fa_model_opts *o);
 
@@ -223,11 +225,16 @@ int fa_sampler_freq(fa_sampler *s, uint32_t seq, uint32_t token, uint32_t *count
 /* ------------------------------------------------ token-parallel GEMM */
 /* Y[T][n_out] = X[T][K] . W for one weight group of the model (proj 0 qkv,
  * 1 o, 2 gate/up interleaved per 1024-column chunk, 3 down, 4 output head)
- * on the tcgen05 path that prefill and batched decode use: X rounded to bf16,
- * W dequantised to bf16 (d*sc*q - dmin*m in f32, rounded once), f32
+ * on the tcgen05 path that prefill and batched decode use: X rounded to f16,
+ * W dequantised to f16 (d*sc*q - dmin*m in f32, rounded once), f32
  * accumulation.  Host buffers; y_host NULL only reports n_out. */
 int fa_gemm_tokens(fa_model *m, int32_t proj, uint32_t layer, const float *x_host, uint32_t T, float *y_host,
                    uint32_t *n_out);
+
+/* device time (ms, average of reps launches) of that GEMM for T tokens on
+ * device-resident operands, and its flop count 2*T*K*n_out */
+int fa_profile_gemm(fa_model *m, int32_t proj, uint32_t layer, uint32_t T, uint32_t reps, float *avg_ms,
+                    double *flop);
 
 /* ----------------------------------------------------------- generation */
 typedef struct {

@@ -1,7 +1,7 @@
-"""Token-parallel dequant-GEMM (tcgen05, bf16 operands, f32 accumulation)
-against the oracle's dequantised weights: Y = bf16(X) . bf16(W) in f64.
+"""Token-parallel dequant-GEMM (tcgen05, f16 operands, f32 accumulation)
+against the oracle's dequantised weights: Y = f16(X) . f16(W) in f64.
 The only differences left are the f32 accumulation order and a rare 1-ulp
-bf16 rounding difference of a weight, so the bar is 1e-3 of max |Y|."""
+f16 rounding difference of a weight, so the bar is 1e-3 of max |Y|."""
 import ctypes as C
 
 import numpy as np
@@ -15,10 +15,8 @@ from fishai_engine.model import ModelWeights
 pytestmark = pytest.mark.gpu
 
 
-def bf16(a):
-    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    return u.astype(np.uint32).view(np.float32)
+def f16(a):
+    return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float64)
 
 
 def _w(g, name):
@@ -90,6 +88,6 @@ def test_token_gemm_matches_dequantised_weights(model, proj, T):
     x = np.random.default_rng(proj * 1000 + T).normal(0.0, 1.0, (T, W.shape[0])).astype(np.float32)
     y = _gemm(dev, proj, layer, x)
     assert y.shape == (T, W.shape[1])
-    ref = bf16(x).astype(np.float64) @ bf16(W).astype(np.float64)
+    ref = f16(x) @ f16(W)
     err = np.max(np.abs(y - ref)) / np.max(np.abs(ref))
     assert err <= 1e-3, err
