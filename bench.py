@@ -30,6 +30,7 @@ METRIC = "decode tok/s at 8B Q4_K_M (b=1)"
 PRESET = "llama3-8b-q4_k_m"
 WORKLOAD = "llama3-8b-shaped Q4_K_M synthetic GGUF, batch 1, 2048-token prompt, greedy decode"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def measured_peaks():
@@ -39,6 +40,17 @@ def measured_peaks():
             d = json.load(f)
         return float(d.get("hbm_gbs", FALLBACK_HBM_GBS)), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    """dense 16-bit tensor peak (TFLOP/s): the measured burst figure for kernels timed alone"""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -152,6 +164,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
     ap.add_argument("--cpu-layers", type=int, default=4)
+    ap.add_argument("--prefill", choices=["tc", "exact"], default="tc",
+                    help="tc: f16 tensor-core prefill (tcgen05 GEMMs, flash attention); exact: f32 token steps")
     ap.add_argument("--step-kernel", type=int, choices=[0, 1], default=0,
                     help="1: each decode step is one persistent kernel launch")
     ap.add_argument("--profile", choices=list(PROFILE_KINDS), default=None,
@@ -203,7 +217,8 @@ def main():
 
     from fishai_engine.model import ModelWeights
 
-    m = ModelWeights.load_from_gguf(path, device=local, use_step_kernel=bool(args.step_kernel))
+    m = ModelWeights.load_from_gguf(path, device=local, use_step_kernel=bool(args.step_kernel),
+                                    use_tc_prefill=args.prefill == "tc")
     cfg = m.config
     dev_bytes, step_weight_bytes = m.weight_bytes()
     P, K, W = args.prompt, args.steps, args.warmup
@@ -213,11 +228,21 @@ def main():
     prompt = np.random.default_rng(2 + rank).integers(3, cfg.vocab_size, P).tolist()
     stream = torch.cuda.ExternalStream(L.lib().fa_model_stream(m._h))
 
-    # prefill (token-by-token causal steps, the f32-exact path)
+    # prefill: one untimed run into a scratch cache (workspace, tensor maps),
+    # then the timed prefill of the prompt (host ids in, last logits out)
+    if args.prefill == "tc":
+        kv_w = m.new_kv_cache(P + 8, dtype=kv_dtype)
+        m.prefill(prompt, 0, kv_w)
+        del kv_w
     torch.cuda.synchronize()
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pe0.record(stream)
     t0 = time.perf_counter()
     _, tok = m.prefill(prompt, 0, kv)
     prefill_s = time.perf_counter() - t0
+    pe1.record(stream)
+    pe1.synchronize()
+    prefill_dev_s = pe0.elapsed_time(pe1) / 1000.0
     pos = P
     ids = m.decode_greedy(kv, tok, pos, W)  # warm-up (graph capture + steady state)
     pos += W
@@ -286,6 +311,28 @@ def main():
     step_bytes = step_weight_bytes + kv_bytes
     step_gbs = step_bytes * (K / (ms / 1000.0)) / 1e9
 
+    # prefill roofline: tensor-bound; linear flops 2 x (layer weights) per token
+    # plus causal attention 4 L Hq hd P(P+1)/2, against the measured dense peak
+    d, hd, F = cfg.n_embd, cfg.head_dim, cfg.n_ff_used
+    lin = cfg.n_layers * (d * cfg.n_heads * hd * 2 + 2 * d * cfg.n_kv_heads * hd + 3 * d * F)
+    pf_flops = 2.0 * lin * P + 4.0 * cfg.n_layers * cfg.n_heads * hd * P * (P + 1) / 2 + 2.0 * d * cfg.vocab_size
+    tpeak, tpeak_src = measured_tensor_peak()
+    gemm_ms, gemm_fl = C.c_float(), C.c_double()
+    gemm = None
+    if args.prefill == "tc":
+        L.check(L.lib().fa_profile_gemm(m._h, 2, 0, P, 5, C.byref(gemm_ms), C.byref(gemm_fl)))
+        gemm = {"kernel": "k_qgemm (gate+up, Q4_K, tcgen05 f16)", "tokens": P, "avg_launch_us": gemm_ms.value * 1e3,
+                "achieved": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
+                "frac": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12 / tpeak}
+    prefill = {"value": P / prefill_s, "unit": "tok/s", "tokens": P,
+               "path": ("f16 tensor cores: tcgen05 dequant-GEMMs, causal flash attention (mma.sync), chunks of 2048"
+                        if args.prefill == "tc" else "causal token-by-token steps (f32 path)"),
+               "device_s": prefill_dev_s,
+               "roofline": {"bound": "tensor", "flops": pf_flops, "achieved": pf_flops / prefill_dev_s / 1e12,
+                            "peak": tpeak, "unit": "TFLOP/s", "frac": pf_flops / prefill_dev_s / 1e12 / tpeak,
+                            "peak_source": tpeak_src},
+               "gemm": gemm}
+
     cpu = None
     if rank == 0 and world == 1 and args.cpu_layers > 0:
         v, secs, layers = cpu_baseline_sample(path, cfg.n_layers, args.cpu_layers)
@@ -314,7 +361,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 40,
                 "api": "fa_forward (one token id in, argmax id out per step)"},
-        "prefill": {"value": P / prefill_s, "unit": "tok/s", "path": "causal token-by-token steps (f32 path)"},
+        "prefill": prefill,
         "gpu_launches": launches_per_step * K,
         "clocks": clocks,
     }
