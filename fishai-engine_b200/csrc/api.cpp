@@ -1071,3 +1071,23 @@ extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint3
   return FA_OK;
 }
 
+extern "C" int fa_decode_batch(fa_model *fm, fa_kv *kv, uint32_t b, const uint32_t *tokens, const uint32_t *pos,
+                               fa_sampler *s, uint32_t steps, uint32_t *ids_out, float *logits_out) {
+  API_NULL(fm);
+  API_NULL(kv);
+  API_NULL(tokens);
+  API_NULL(pos);
+  API_NULL(s);
+  API_NULL(ids_out);
+  if (!steps) return FA_OK;
+  Model &m = fm->m;
+  if (b > s->n_seq) return fail(FA_ERR_INVALID, "fa_decode_batch: more sequences than sampler rows");
+  if (m.cfg.vocab_size > s->vocab) return fail(FA_ERR_INVALID, "fa_decode_batch: sampler vocabulary too small");
+  API_CUDA(cudaSetDevice(m.device));
+  SamplerParams sp = s->params(m.cfg.vocab_size);
+  int rc;
+  if ((rc = sampler_keys(s, sp))) return rc;
+  API_CUDA(cudaStreamSynchronize(s->stream));  // observes / resets queued on the sampler's stream
+  return m.decode_batch(kv->kv, b, tokens, pos, sp, steps, ids_out, logits_out);
+}
+

@@ -62,7 +62,9 @@ __device__ void attn_body(const AttnParams &p) {
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const uint32_t hd = p.kv.head_dim, KVH = p.kv.n_kv, esz = F16 ? 2 : 4;
-  const uint32_t T = p.kc ? p.t_fixed : p.state->len + 1;
+  // batched decode: row r is cache sequence row_seq0 + r with its own length
+  const uint32_t T = p.kc ? p.t_fixed : (p.row_states ? p.row_states[row].len : p.state->len) + 1;
+  const uint32_t seq = p.row_states ? p.row_seq0 + row : p.seq;
   const float *qrow = p.q + (uint64_t)row * p.n_heads * hd;
   float *part = p.part + (uint64_t)row * p.n_heads * p.splits * (2 + hd);
   uint32_t *counters = p.counters + (uint64_t)row * KVH;
@@ -81,7 +83,7 @@ __device__ void attn_body(const AttnParams &p) {
 
   const uint8_t *base = p.kc ? nullptr
                              : reinterpret_cast<const uint8_t *>(p.kv.base) + (uint64_t)p.layer * p.kv.layer_stride * esz;
-  const uint32_t *pt = p.kc ? nullptr : p.kv.page_table + (uint64_t)p.seq * p.kv.max_pages;
+  const uint32_t *pt = p.kc ? nullptr : p.kv.page_table + (uint64_t)seq * p.kv.max_pages;
   auto row_ptr = [&](uint32_t t, int is_v) -> const uint8_t * {
     if (p.kc) return reinterpret_cast<const uint8_t *>(is_v ? p.vc : p.kc) + ((uint64_t)t * KVH + kvh) * hd * 4;
     return base + kv_index(pt[t / 16], is_v, kvh, t % 16, 0, KVH, hd) * esz;

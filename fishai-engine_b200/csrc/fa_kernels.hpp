@@ -129,6 +129,8 @@ struct AttnParams {
   uint32_t *counters;      // [n_kv] arrival counters (zero between launches)
   float *out;              // [H*hd] combined attention output
   SeqState *state;         // T = len + 1
+  const SeqState *row_states;  // batched decode: per query row state (T = len + 1), cache sequence row_seq0 + row
+  uint32_t row_seq0;
 };
 // attention_init: once per device (current), before the first launch_attention
 // of a stream capture; launch_attention calls it as well
@@ -229,6 +231,15 @@ int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv,
 int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st);
 int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st);
 int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st);
+// batched decode: per-row RoPE + KV append (row r = cache sequence seq0 + r at
+// states[r].pos / .len, q -> qf f32), f32 -> f16 with the range flag, and the
+// per-step bookkeeping (positions + 1, ids -> hist[step][r], step + 1)
+int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                         uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
+                         float *qf, uint32_t *err, cudaStream_t st);
+int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st);
+int launch_batch_step_end(SeqState *states, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
+                          uint32_t *step, cudaStream_t st);
 
 // ---- Sampler::sample (src/sampling.rs:110-152), one CTA per sequence ----
 constexpr uint32_t kSampleFastK = 2048;  // top-k up to this many candidates stays in shared memory

@@ -950,5 +950,166 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
   return FA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Batched decode: b sequences advance one token per step; the projections run
+// as f16 tcgen05 GEMMs with T = b, attention per row over the row's own cache
+// sequence, then Sampler::sample per row.  One step is a captured CUDA graph.
+// ---------------------------------------------------------------------------
+int Model::ensure_batch_ws(uint32_t b) {
+  if (b <= bws.cap) return FA_OK;
+  const uint32_t d = cfg.n_embd, qd = cfg.n_heads * cfg.head_dim, F = layers[0].down.K, V = cfg.vocab_size;
+  const uint32_t qkv_n = layers[0].qkv.n_out, gu_n = layers[0].gateup.n_out, KVH = cfg.n_kv_heads;
+  BatchWs w;
+  w.cap = b;
+  w.splits = std::max<uint32_t>(1, std::min<uint32_t>(32, (8 * (uint32_t)n_sm + b * KVH - 1) / (b * KVH)));
+  w.X = (float *)dmalloc((size_t)b * d * 4);
+  w.QKV = (float *)dmalloc((size_t)b * qkv_n * 4);
+  w.Qf = (float *)dmalloc((size_t)b * qd * 4);
+  w.Of = (float *)dmalloc((size_t)b * qd * 4);
+  w.GU = (float *)dmalloc((size_t)b * gu_n * 4);
+  w.logits = (float *)dmalloc((size_t)b * V * 4);
+  w.part = (float *)dmalloc((size_t)b * cfg.n_heads * w.splits * (2 + cfg.head_dim) * 4);
+  w.Xn = dmalloc((size_t)b * d * 2);
+  w.Oh = dmalloc((size_t)b * qd * 2);
+  w.Hb = dmalloc((size_t)b * F * 2);
+  w.counters = (uint32_t *)dmalloc((size_t)b * KVH * 4);
+  w.err = (uint32_t *)dmalloc(4);
+  w.step = (uint32_t *)dmalloc(4);
+  w.states = (SeqState *)dmalloc((size_t)b * sizeof(SeqState));
+  if (!w.X || !w.QKV || !w.Qf || !w.Of || !w.GU || !w.logits || !w.part || !w.Xn || !w.Oh || !w.Hb || !w.counters ||
+      !w.err || !w.step || !w.states)
+    return fail(FA_ERR_OOM, "batched decode workspace allocation failed");
+  CUDA_TRY(cudaMemset(w.counters, 0, (size_t)b * KVH * 4));
+  const uint32_t bn = b <= 64 ? 64 : b <= 128 ? 128 : 256;
+  if (qgemm_make_xmap(&w.mxn, w.Xn, d, b, bn) || qgemm_make_xmap(&w.moh, w.Oh, qd, b, bn) ||
+      qgemm_make_xmap(&w.mhb, w.Hb, F, b, bn))
+    return fail(FA_ERR_CUDA, "tensor map encoding failed");
+  bws = w;
+  return FA_OK;
+}
+
+int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams &sp, uint32_t *hist,
+                              uint32_t max_steps) {
+  const uint32_t d = cfg.n_embd, hd = cfg.head_dim, Hq = cfg.n_heads, Hkv = cfg.n_kv_heads, qd = Hq * hd;
+  const uint32_t F = layers[0].down.K, qkv_n = layers[0].qkv.n_out, gu_n = layers[0].gateup.n_out;
+  const KvView kvv = kv.view();
+  int rc;
+  uint32_t *tok = sp.ids;  // the sampler's ids are the next step's input tokens
+  if (launch_embed_rows(emb, emb_type, tok, b, d, cfg.vocab_size, bws.X, bws.err, stream))
+    return fail(FA_ERR_CUDA, "embed launch failed");
+  for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+    const LayerW &lw = layers[l];
+    if (launch_norm_rows_h(bws.X, lw.attn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
+      return fail(FA_ERR_CUDA, "norm launch failed");
+    if ((rc = run_qgemm(lw.qkv, bws.mxn, b, bws.QKV, qkv_n, kQgStore))) return rc;
+    if (launch_rope_kv_batch(bws.QKV, b, Hq, Hkv, hd, rope_tab, rope_max, bws.states, kvv, 0, l, bws.Qf, bws.err,
+                             stream))
+      return fail(FA_ERR_CUDA, "rope launch failed");
+    AttnParams ap{};
+    ap.q = bws.Qf;
+    ap.q_rows = b;
+    ap.kv = kvv;
+    ap.layer = l;
+    ap.n_heads = Hq;
+    ap.splits = bws.splits;
+    ap.scale = attn_scale;
+    ap.part = bws.part;
+    ap.counters = bws.counters;
+    ap.out = bws.Of;
+    ap.state = bws.states;
+    ap.row_states = bws.states;
+    ap.row_seq0 = 0;
+    if (launch_attention(ap, false, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
+    if (launch_to_half(bws.Of, (uint64_t)b * qd, bws.Oh, bws.err, stream)) return fail(FA_ERR_CUDA, "convert failed");
+    if ((rc = run_qgemm(lw.o, bws.moh, b, bws.X, d, kQgResid))) return rc;
+    if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
+      return fail(FA_ERR_CUDA, "norm launch failed");
+    if ((rc = run_qgemm(lw.gateup, bws.mxn, b, bws.GU, gu_n, kQgStore))) return rc;
+    if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream))
+      return fail(FA_ERR_CUDA, "swiglu launch failed");
+    if ((rc = run_qgemm(lw.down, bws.mhb, b, bws.X, d, kQgResid))) return rc;
+  }
+  if (launch_norm_rows_h(bws.X, out_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
+    return fail(FA_ERR_CUDA, "norm launch failed");
+  if ((rc = run_qgemm(head, bws.mxn, b, bws.logits, cfg.vocab_size, kQgStore))) return rc;
+  if (launch_sample(sp, b, stream)) return fail(FA_ERR_CUDA, "sampler launch failed");
+  if (launch_batch_step_end(bws.states, b, tok, hist, max_steps, bws.step, stream))
+    return fail(FA_ERR_CUDA, "step end launch failed");
+  return FA_OK;
+}
+
+int Model::decode_batch(KvCache &kv, uint32_t b, const uint32_t *tok, const uint32_t *pos, SamplerParams sp,
+                        uint32_t steps, uint32_t *ids_host, float *logits_host) {
+  if (!tc_ok || tied || !head.mma)
+    return fail(FA_ERR_UNSUPPORTED, "batched decode needs every projection and the output head in the MMA layout");
+  if (!b || b > kv.n_seq) return fail(FA_ERR_INVALID, "batched decode: sequence count out of range");
+  uint32_t max_pos = 0;
+  for (uint32_t r = 0; r < b; ++r) {
+    if (tok[r] >= cfg.vocab_size) return fail(FA_ERR_INVALID, "token id out of range");
+    if ((uint64_t)kv.len[r] + steps > kv.max_ctx) return fail(FA_ERR_CONTEXT, "KV cache capacity exceeded");
+    max_pos = std::max(max_pos, pos[r] + steps);
+  }
+  int rc;
+  if ((rc = ensure_rope(max_pos + 1)) || (rc = ensure_batch_ws(b))) return rc;
+  std::vector<SeqState> st(b);
+  for (uint32_t r = 0; r < b; ++r) {
+    st[r] = SeqState{};
+    st[r].pos = pos[r];
+    st[r].len = kv.len[r];
+    st[r].token = tok[r];
+  }
+  uint32_t *hist = nullptr;
+  CUDA_TRY(cudaMalloc(&hist, (size_t)steps * b * 4));
+  struct Free {
+    void *p;
+    ~Free() { cudaFree(p); }
+  } free_hist{hist};
+  CUDA_TRY(cudaMemcpyAsync(bws.states, st.data(), b * sizeof(SeqState), cudaMemcpyHostToDevice, stream));
+  CUDA_TRY(cudaMemcpyAsync(sp.ids, tok, (size_t)b * 4, cudaMemcpyHostToDevice, stream));
+  CUDA_TRY(cudaMemsetAsync(bws.step, 0, 4, stream));
+  CUDA_TRY(cudaMemsetAsync(bws.err, 0, 4, stream));
+  sp.logits = bws.logits;
+  sp.ld = cfg.vocab_size;
+  sp.n = cfg.vocab_size;
+  sp.row0 = 0;
+  sp.state = nullptr;
+  sp.observe = 1;
+  if (logits_host) {  // per-step logits requested: plain launches, a copy after each step
+    for (uint32_t s = 0; s < steps; ++s) {
+      if ((rc = enqueue_batch_step(kv, b, sp, hist, steps))) return rc;
+      CUDA_TRY(cudaMemcpyAsync(logits_host + (size_t)s * b * cfg.vocab_size, bws.logits,
+                               (size_t)b * cfg.vocab_size * 4, cudaMemcpyDeviceToHost, stream));
+    }
+  } else {
+    cudaGraph_t gr = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    rc = enqueue_batch_step(kv, b, sp, hist, steps);
+    const cudaError_t ce = cudaStreamEndCapture(stream, &gr);
+    if (rc) {
+      if (gr) cudaGraphDestroy(gr);
+      return rc;
+    }
+    if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(ce));
+    const cudaError_t ie = cudaGraphInstantiate(&ge, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ie != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(ie));
+    cudaError_t le = cudaSuccess;
+    for (uint32_t s = 0; s < steps && le == cudaSuccess; ++s) le = cudaGraphLaunch(ge, stream);
+    cudaGraphExecDestroy(ge);
+    if (le != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph launch failed: ") + cudaGetErrorString(le));
+  }
+  uint32_t e = 0;
+  CUDA_TRY(cudaMemcpyAsync(ids_host, hist, (size_t)steps * b * 4, cudaMemcpyDeviceToHost, stream));
+  CUDA_TRY(cudaMemcpyAsync(&e, bws.err, 4, cudaMemcpyDeviceToHost, stream));
+  CUDA_TRY(cudaStreamSynchronize(stream));
+  if (e & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "batched decode: a bounded device wait gave up");
+  if (e & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
+  if (e & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");
+  if (e & kErrRange) return fail(FA_ERR_UNSUPPORTED, "an activation exceeds the f16 range of the tensor-core path");
+  for (uint32_t r = 0; r < b; ++r) kv.len[r] += steps;
+  return FA_OK;
+}
+
 }  // namespace fa
 

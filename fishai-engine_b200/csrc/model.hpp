@@ -59,6 +59,16 @@ struct PrefillWs {
   QgXMap mxn[3], mob[3], mhb[3];  // TMA maps of Xn, Ob, Hb for 64, 128, 256 tokens per tile
 };
 
+// buffers of the batched decode step, `cap` sequences
+struct BatchWs {
+  uint32_t cap = 0, splits = 1;
+  float *X = nullptr, *QKV = nullptr, *Qf = nullptr, *Of = nullptr, *GU = nullptr, *logits = nullptr, *part = nullptr;
+  void *Xn = nullptr, *Oh = nullptr, *Hb = nullptr;
+  uint32_t *counters = nullptr, *err = nullptr, *step = nullptr;
+  SeqState *states = nullptr;
+  QgXMap mxn, moh, mhb;
+};
+
 struct Model {
   fa_config cfg{};
   int device = 0;
@@ -104,6 +114,16 @@ struct Model {
   // current length; leaves the last token's logits in ws.logits and the
   // argmax in ws.state->argmax_key
   int prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t start_pos);
+  // batched decode (f16 tensor-core GEMMs at T = b)
+  BatchWs bws;
+  int ensure_batch_ws(uint32_t b);
+  int enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams &sp, uint32_t *hist, uint32_t max_steps);
+  // `steps` decode steps of sequences 0..b-1 of kv: row r starts from token
+  // tok[r] at RoPE position pos[r] after its cached positions; every step
+  // samples each row with sp (row r = sampler row r) and observes the id.
+  // ids_host [steps][b]; logits_host (optional) [steps][b][vocab]
+  int decode_batch(KvCache &kv, uint32_t b, const uint32_t *tok, const uint32_t *pos, SamplerParams sp, uint32_t steps,
+                   uint32_t *ids_host, float *logits_host);
   // decode-step graph cache
   cudaGraphExec_t graph = nullptr;
   const KvCache *graph_kv = nullptr;

@@ -14,6 +14,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "fa_dequant.cuh"
 #include "fa_device.cuh"
 #include "fa_kernels.hpp"
@@ -307,6 +309,63 @@ __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, f
   for (uint32_t i = threadIdx.x; i < n_ssq; i += blockDim.x) ssq[i] = i == 0 ? s : 0.0f;
 }
 
+// ---- batched decode: row r is cache sequence seq0 + r at its own position ----
+__global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                                uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
+                                float *qf, uint32_t *err) {
+  const uint32_t r = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
+  const float *row = qkv + (size_t)r * (qd + 2 * kd);
+  const uint32_t pos = st[r].pos, slot = st[r].len;
+  if (pos >= rope_max || slot / 16 >= kv.max_pages) {
+    if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
+    return;
+  }
+  const float *cs = rope + (size_t)pos * hd;
+  const uint32_t page = kv.page_table[(seq0 + r) * kv.max_pages + slot / 16];
+  const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
+  for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) {
+    float v = row[j];
+    const bool is_q = j < qd, is_k = !is_q && j < qd + kd;
+    if (is_q || is_k) {
+      const uint32_t base = is_q ? 0 : qd, dd = (j - base) % hd, hb = j - dd;
+      const float cth = cs[2 * (dd % half)], sth = cs[2 * (dd % half) + 1];
+      const float pv = dd < half ? row[hb + dd + half] : row[hb + dd - half];
+      v = dd < half ? __fsub_rn(__fmul_rn(v, cth), __fmul_rn(pv, sth)) : __fadd_rn(__fmul_rn(pv, sth), __fmul_rn(v, cth));
+    }
+    if (is_q) {
+      qf[(size_t)r * qd + j] = v;
+    } else {
+      const uint32_t kc = is_k ? j - qd : j - qd - kd;
+      const uint64_t idx = lbase + kv_index(page, is_k ? 0 : 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
+      if (kv.f16) reinterpret_cast<__half *>(kv.base)[idx] = __float2half_rn(v);
+      else reinterpret_cast<float *>(kv.base)[idx] = v;
+    }
+  }
+}
+
+__global__ void k_to_half(const float *x, uint64_t n, __half *y, uint32_t *err) {
+  bool bad = false;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    bad |= !(fabsf(x[i]) <= kHalfMax);
+    y[i] = __float2half_rn(x[i]);
+  }
+  if (bad && err) atomicOr(err, kErrRange);
+}
+
+// after the sampler: positions advance, the sampled ids (already the next
+// step's input tokens) go to the history
+__global__ void k_batch_step_end(SeqState *st, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
+                                 uint32_t *step) {
+  const uint32_t s = *step;
+  for (uint32_t r = threadIdx.x; r < b; r += blockDim.x) {
+    st[r].pos += 1;
+    st[r].len += 1;
+    if (s < max_steps) hist[(size_t)s * b + r] = ids[r];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *step = s + 1;
+}
+
 template <uint32_t HD, bool F16>
 int launch_attn_hd(const AttnRowsParams &p, cudaStream_t st) {
   const uint32_t smem = 2 * kAK * HD * 2;  // K and V tiles: 32 KB at head_dim 128
@@ -342,6 +401,22 @@ int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
 }
 int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
   k_swiglu_rows<<<dim3((F + 255) / 256, T), 256, 0, st>>>(gu, F, CW, (__half *)h, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                         uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
+                         float *qf, uint32_t *err, cudaStream_t st) {
+  k_rope_kv_batch<<<b, 256, 0, st>>>(qkv, Hq, Hkv, hd, rope, rope_max, states, kv, seq0, layer, qf, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st) {
+  const uint32_t grid = (uint32_t)std::min<uint64_t>((n + 255) / 256, 4096);
+  k_to_half<<<grid ? grid : 1, 256, 0, st>>>(x, n, (__half *)y, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+int launch_batch_step_end(SeqState *states, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
+                          uint32_t *step, cudaStream_t st) {
+  k_batch_step_end<<<1, 256, 0, st>>>(states, b, ids, hist, max_steps, step);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st) {

@@ -104,6 +104,7 @@ SIGNATURES = {
     "fa_sampler_freq": ([_vp, _u32, _u32, _pu32], _i),
     "fa_gemm_tokens": ([_vp, C.c_int32, _u32, _pf, _u32, _pf, _pu32], _i),
     "fa_profile_gemm": ([_vp, C.c_int32, _u32, _u32, _u32, _pf, C.POINTER(C.c_double)], _i),
+    "fa_decode_batch": ([_vp, _vp, _u32, _pu32, _pu32, _vp, _u32, _pu32, _pf], _i),
     "fa_generate": ([_vp, C.POINTER(fa_gen_config), _pu32, _u32, _pu32, _u32, _pu32], _i),
     "fa_decode_greedy": ([_vp, _vp, _u32, _u32, _u32, _u32, _pu32], _i),
     "fa_profile_gemv": ([_vp, C.c_int32, _u32, _pf, _pu64], _i),

@@ -129,6 +129,20 @@ class ModelWeights:
                                    L.f32_ptr(logits) if want_logits else None, C.byref(am)))
         return logits, am.value
 
+    def decode_batch(self, kv_cache: KVCache, tokens, positions, sampler, steps: int, want_logits: bool = False):
+        """Sequences 0..b-1 advance `steps` tokens together (f16 tensor-core
+        projections, per-row attention, device sampling).  Returns ids
+        [steps][b] (and logits [steps][b][vocab] when asked)."""
+        tk, tp = L.u32_array(tokens)
+        ps, pp = L.u32_array(positions)
+        b = tk.size
+        ids = np.zeros((steps, b), dtype=np.uint32)
+        lg = np.zeros((steps, b, self.config.vocab_size), dtype=np.float32) if want_logits else None
+        L.check(L.lib().fa_decode_batch(self._h, kv_cache._h, b, tp, pp, sampler._h, steps,
+                                        ids.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                        L.f32_ptr(lg) if want_logits else None))
+        return (ids, lg) if want_logits else ids
+
     def decode_greedy(self, kv_cache: KVCache, first_token: int, pos: int, steps: int, seq: int = 0):
         ids = np.zeros(steps, dtype=np.uint32)
         L.check(L.lib().fa_decode_greedy(self._h, kv_cache._h, seq, first_token, pos, steps,

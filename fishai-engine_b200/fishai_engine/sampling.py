@@ -41,12 +41,15 @@ class Sampler:
     Categorical draws use Philox4x32-10 keyed by `seed` with the sample index
     as counter (the reference uses the unseeded rand::rng())."""
 
-    def __init__(self, config: SamplerConfig = None, vocab: int = 0, seed: int = 0):
+    def __init__(self, config: SamplerConfig = None, vocab: int = 0, seed: int = 0, seeds=None):
+        """seeds: one Philox key per sequence row (batched decode); else one row keyed by seed"""
         self.config = config or SamplerConfig()
         self.vocab = vocab
-        seeds = (C.c_uint64 * 1)(seed)
+        keys = list(seeds) if seeds is not None else [seed]
+        self.n_seq = len(keys)
+        arr = (C.c_uint64 * self.n_seq)(*keys)
         h = C.c_void_p()
-        L.check(L.lib().fa_sampler_create(C.byref(self.config._c()), 1, vocab, seeds, C.byref(h)))
+        L.check(L.lib().fa_sampler_create(C.byref(self.config._c()), self.n_seq, vocab, arr, C.byref(h)))
         self._h = h
 
     def __del__(self):

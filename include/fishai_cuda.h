@@ -236,6 +236,16 @@ int fa_gemm_tokens(fa_model *m, int32_t proj, uint32_t layer, const float *x_hos
 int fa_profile_gemm(fa_model *m, int32_t proj, uint32_t layer, uint32_t T, uint32_t reps, float *avg_ms,
                     double *flop);
 
+/* Batched decode: sequences 0..b-1 of kv advance `steps` tokens together.
+ * Row r starts from tokens[r] at RoPE position pos[r], appended after its
+ * cached positions; every step forwards all rows (f16 tensor-core GEMMs at
+ * T = b, attention per row over its own cache), samples row r with sampler
+ * row r (Sampler::sample, then observe_token) and feeds the id back.
+ * ids_out [steps][b]; logits_out (NULL or [steps][b][vocab]) also returns
+ * every step's logits.  Only ids cross PCIe when logits_out is NULL. */
+int fa_decode_batch(fa_model *m, fa_kv *kv, uint32_t b, const uint32_t *tokens, const uint32_t *pos, fa_sampler *s,
+                    uint32_t steps, uint32_t *ids_out, float *logits_out);
+
 /* ----------------------------------------------------------- generation */
 typedef struct {
   uint32_t max_tokens;          /* includes the prompt, as in src/model.rs:683-686 */
