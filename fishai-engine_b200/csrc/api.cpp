@@ -993,7 +993,9 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   const uint32_t K = P->K, N = P->n_out;
   std::vector<uint16_t> xb((size_t)T * K);
   for (size_t i = 0; i < xb.size(); ++i) xb[i] = f32_to_f16(x_host[i]);
-  DevBuf x, y, err;
+  DevBuf x, y, err, part;
+  const uint64_t part_floats = std::min<uint64_t>((uint64_t)8 * T * N, 1ull << 24);
+  API_CUDA(cudaMalloc(&part.p, part_floats * 4));
   API_CUDA(cudaMalloc(&x.p, xb.size() * 2));
   API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
   API_CUDA(cudaMalloc(&err.p, 4));
@@ -1014,6 +1016,8 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   p.ldo = N;
   p.epi = kQgStore;
   p.err = (uint32_t *)err.p;
+  p.part = (float *)part.p;
+  p.part_floats = part_floats;
   if (launch_qgemm(p, map, (uint32_t)m.n_sm, m.stream)) return fail(FA_ERR_CUDA, "token GEMM launch failed");
   uint32_t e = 0;
   API_CUDA(cudaMemcpyAsync(y_host, y.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, m.stream));
@@ -1034,7 +1038,9 @@ extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint3
   if (!P || !P->mma || P->qg_tiles.empty() || !T || !reps) return fail(FA_ERR_INVALID, "fa_profile_gemm: bad arguments");
   API_CUDA(cudaSetDevice(m.device));
   const uint32_t K = P->K, N = P->n_out;
-  DevBuf x, y;
+  DevBuf x, y, part;
+  const uint64_t part_floats = std::min<uint64_t>((uint64_t)8 * T * N, 1ull << 24);
+  API_CUDA(cudaMalloc(&part.p, part_floats * 4));
   API_CUDA(cudaMalloc(&x.p, (size_t)T * K * 2));
   API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
   API_CUDA(cudaMemsetAsync(x.p, 0x1C, (size_t)T * K * 2, m.stream));  // f16 0x1C1C ~ 0.0041
@@ -1050,6 +1056,8 @@ extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint3
   p.out = (float *)y.p;
   p.ldo = N;
   p.epi = kQgStore;
+  p.part = (float *)part.p;
+  p.part_floats = part_floats;
   cudaEvent_t e0, e1;
   API_CUDA(cudaEventCreate(&e0));
   API_CUDA(cudaEventCreate(&e1));

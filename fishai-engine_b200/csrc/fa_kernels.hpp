@@ -202,6 +202,9 @@ struct QgParams {
   uint32_t ldo;
   int epi;                   // kQgStore: Y = X W; kQgResid: Y += X W
   uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
+  float *part;               // split-K partials [splits][T][ldo] (null: no K split)
+  uint64_t part_floats;      // capacity of part
+  uint32_t splits;           // set by launch_qgemm
 };
 struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
   alignas(64) unsigned char bytes[128];

@@ -867,11 +867,22 @@ int Model::ensure_prefill_ws(uint32_t cap) {
         qgemm_make_xmap(&w.mhb[b], w.Hb, F, cap, bns[b]))
       return fail(FA_ERR_CUDA, "tensor map encoding failed");
   pws = w;  // the previous buffers stay owned by `allocs` until teardown
+  return ensure_qg_part((uint64_t)8 * std::min<uint32_t>(cap, 512) * std::max(d, qkv_n));
+}
+
+int Model::ensure_qg_part(uint64_t floats) {
+  if (floats <= qg_part_floats) return FA_OK;
+  float *q = (float *)dmalloc(floats * 4);
+  if (!q) return fail(FA_ERR_OOM, "GEMM split-K workspace allocation failed");
+  qg_part = q;
+  qg_part_floats = floats;
   return FA_OK;
 }
 
 int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi) {
   QgParams p{};
+  p.part = qg_part;
+  p.part_floats = qg_part_floats;
   p.w = P.w;
   p.chunks = P.d_chunks;
   p.tiles = P.d_qg_tiles;
@@ -985,7 +996,7 @@ int Model::ensure_batch_ws(uint32_t b) {
       qgemm_make_xmap(&w.mhb, w.Hb, F, b, bn))
     return fail(FA_ERR_CUDA, "tensor map encoding failed");
   bws = w;
-  return FA_OK;
+  return ensure_qg_part((uint64_t)8 * b * std::max(d, qkv_n));
 }
 
 int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams &sp, uint32_t *hist,

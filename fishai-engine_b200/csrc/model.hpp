@@ -114,6 +114,10 @@ struct Model {
   // current length; leaves the last token's logits in ws.logits and the
   // argmax in ws.state->argmax_key
   int prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *tokens_host, uint32_t n, uint32_t start_pos);
+  // split-K partials of the token GEMMs (shared by prefill and batched decode)
+  float *qg_part = nullptr;
+  uint64_t qg_part_floats = 0;
+  int ensure_qg_part(uint64_t floats);
   // batched decode (f16 tensor-core GEMMs at T = b)
   BatchWs bws;
   int ensure_batch_ws(uint32_t b);

@@ -16,7 +16,9 @@
 //       tile overlaps the MMAs of the next)
 // Roles per CTA (one persistent CTA per SM): warp 0 TMA for X, warp 1 MMA
 // issue (one elected lane) and TMEM owner, warps 2-9 dequantisation, warps
-// 10-13 epilogue (tcgen05.ld, optional residual add, f32 stores).
+// 10-13 epilogue (tcgen05.ld, optional residual add, f32 stores).  Output
+// tiles that cannot fill the SMs split K; the split partials are summed in a
+// fixed order by a second kernel.
 // Every mbarrier wait is bounded; on expiry the CTA raises p.err, the other
 // roles stop at their next wait, the MMA warp drains its last commit and the
 // tensor memory is always released.
@@ -24,6 +26,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "fa_device.cuh"
 #include "fa_kernels.hpp"
@@ -61,7 +65,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
@@ -262,6 +266,21 @@ __device__ __forceinline__ void zero_unit(uint32_t w, uint32_t i, uint32_t lane,
       for (int col = 0; col < 2; ++col) put_pair(a, n0 + 16 * t + g + 8 * col, k0 + 2 * c + 8 * half, 0.0f, 0.0f);
 }
 
+// work item wk: K part kp of output tile (nt, tt); k-steps [ks0, ks1)
+struct Work {
+  uint32_t nt, tt, kp, ks0, ks1;
+};
+__device__ __forceinline__ Work work_of(uint32_t wk, uint32_t t_tiles, uint32_t splits, uint32_t ksteps) {
+  Work r;
+  r.kp = wk % splits;
+  const uint32_t rest = wk / splits;
+  r.tt = rest % t_tiles;
+  r.nt = rest / t_tiles;
+  r.ks0 = r.kp * ksteps / splits;
+  r.ks1 = (r.kp + 1) * ksteps / splits;
+  return r;
+}
+
 template <uint32_t BN>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
   using C = QCfg<BN>;
@@ -272,7 +291,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
   QBars &b = *reinterpret_cast<QBars *>(base + C::kBarOff);
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t G16 = p.K / 16, ksteps = (G16 + 3) / 4, t_tiles = (p.T + BN - 1) / BN;
-  const uint32_t n_work = p.n_tiles * t_tiles;
+  const uint32_t splits = p.splits ? p.splits : 1, n_work = p.n_tiles * t_tiles * splits;
   if (tid == 0) {
     for (uint32_t s = 0; s < C::kStages; ++s) {
       mbar_init(&b.full_a[s], kDeq);
@@ -302,8 +321,9 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     if (lane == 0) {
       uint32_t s = 0, ph = 1, pending = 0, last_ph = 0;  // pending: stages with a load issued (bit mask)
       for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
-        const uint32_t tt = wk % t_tiles;
-        for (uint32_t ks = 0; ks < ksteps; ++ks) {
+        const Work wo = work_of(wk, t_tiles, splits, ksteps);
+        const uint32_t tt = wo.tt;
+        for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
           if (!qwait(&b.empty[s], ph, b)) goto tma_out;
           mbar_arrive_expect_tx(&b.full_b[s], C::kBTile);
           tma_load_2d(base + s * C::kStage + kATile, &xmap, (int32_t)(ks * kBK), (int32_t)(tt * BN), &b.full_b[s]);
@@ -326,11 +346,12 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     uint32_t s = 0, ph = 0, acc = 0, aph = 1;
     bool issued = false;
     for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+      const Work wo = work_of(wk, t_tiles, splits, ksteps);
       if (!qwait_warp(&b.acc_empty[acc], aph, b)) break;
       tc_fence_after();
       const uint32_t dt = tmem + acc * BN;
       bool ok = true;
-      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+      for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
         if (!qwait_warp(&b.full_a[s], ph, b) || !qwait_warp(&b.full_b[s], ph, b)) {
           ok = false;
           break;
@@ -340,7 +361,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           const uint32_t a0 = sbase + s * C::kStage, b0 = a0 + kATile;
 #pragma unroll
           for (uint32_t kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16(dt, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + 32 * kk), C::kIdesc, (ks | kk) != 0);
+            umma_f16(dt, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + 32 * kk), C::kIdesc, (ks != wo.ks0) || kk);
           umma_commit(&b.empty[s]);
         }
         __syncwarp();
@@ -369,12 +390,13 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     const uint32_t d = warp - 2, gi = d >> 1, si = d & 1;
     uint32_t s = 0, ph = 1;
     for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
-      const QgTile tl = p.tiles[wk / t_tiles];
+      const Work wo = work_of(wk, t_tiles, splits, ksteps);
+      const QgTile tl = p.tiles[wo.nt];
       const ChunkDesc cd = p.chunks[tl.chunk];
       const uint32_t i = tl.col0 / 64 + si, n0 = 64 * si;
       const bool active = n0 < tl.ncols;
       bool ok = true;
-      for (uint32_t ks = 0; ks < ksteps; ++ks) {
+      for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
         const uint32_t grp = 4 * ks + gi;
         if (!qwait_warp(&b.empty[s], ph, b)) {
           ok = false;
@@ -411,9 +433,12 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
       if (!qwait_warp(&b.acc_full[acc], aph, b)) break;
       tc_fence_after();
-      const QgTile tl = p.tiles[wk / t_tiles];
-      const uint32_t t0 = (wk % t_tiles) * BN, col_out = p.chunks[tl.chunk].out_col + tl.col0;
+      const Work wo = work_of(wk, t_tiles, splits, ksteps);
+      const QgTile tl = p.tiles[wo.nt];
+      const uint32_t t0 = wo.tt * BN, col_out = p.chunks[tl.chunk].out_col + tl.col0;
       const bool mine = m < tl.ncols;
+      float *dst = splits > 1 ? p.part + (size_t)wo.kp * p.T * p.ldo : p.out;
+      const bool add = splits == 1 && p.epi == kQgResid;
       for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((32 * q4) << 16) + acc * BN + c0, v);
@@ -422,9 +447,9 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           for (int j = 0; j < 32; ++j) {
             const uint32_t t = t0 + c0 + j;
             if (t < p.T) {
-              float *o = p.out + (size_t)t * p.ldo + col_out + m;
+              float *o = dst + (size_t)t * p.ldo + col_out + m;
               const float y = __uint_as_float(v[j]);
-              if (p.epi == kQgResid) *o += y;
+              if (add) *o += y;
               else *o = y;
             }
           }
@@ -444,6 +469,15 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+// split partials summed in a fixed order: out (=|+=) sum_s part[s]
+__global__ void k_qg_reduce(const float *part, uint32_t splits, uint64_t n, float *out, int resid) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float v = resid ? out[i] : 0.0f;
+    for (uint32_t s = 0; s < splits; ++s) v += part[(size_t)s * n + i];
+    out[i] = v;
   }
 }
 
@@ -491,16 +525,33 @@ int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows,
   return r == CUDA_SUCCESS ? 0 : -1;
 }
 
-int launch_qgemm(const QgParams &p, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
-  if (!p.T || !p.n_tiles || p.K % 16 || !p.w || !p.out) return -1;
+// K splits when the output tiles leave SMs idle and the partials fit in p.part
+uint32_t qgemm_splits(const QgParams &p, uint32_t bn, uint32_t n_sm) {
+  const uint32_t t_tiles = (p.T + bn - 1) / bn, tiles = p.n_tiles * t_tiles, ksteps = (p.K / 16 + 3) / 4;
+  if (!p.part || tiles >= n_sm) return 1;
+  uint32_t s = std::min<uint32_t>((n_sm + tiles - 1) / tiles, std::max<uint32_t>(1, ksteps / 4));
+  while (s > 1 && (uint64_t)s * p.T * p.ldo > p.part_floats) --s;
+  return s;
+}
+
+int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
+  if (!p0.T || !p0.n_tiles || p0.K % 16 || !p0.w || !p0.out) return -1;
+  QgParams p = p0;
+  p.splits = qgemm_splits(p0, map.bn, n_sm);
   const uint32_t t_tiles = (p.T + map.bn - 1) / map.bn;
-  const uint32_t work = p.n_tiles * t_tiles, grid = work < n_sm ? work : n_sm;
+  const uint32_t work = p.n_tiles * t_tiles * p.splits, grid = work < n_sm ? work : n_sm;
+  int rc;
   switch (map.bn) {
-    case 64: return launch_bn<64>(p, map.bytes, grid, st);
-    case 128: return launch_bn<128>(p, map.bytes, grid, st);
-    case 256: return launch_bn<256>(p, map.bytes, grid, st);
+    case 64: rc = launch_bn<64>(p, map.bytes, grid, st); break;
+    case 128: rc = launch_bn<128>(p, map.bytes, grid, st); break;
+    case 256: rc = launch_bn<256>(p, map.bytes, grid, st); break;
     default: return -1;
   }
+  if (rc || p.splits == 1) return rc;
+  const uint64_t n = (uint64_t)p.T * p.ldo;
+  k_qg_reduce<<<(unsigned)std::min<uint64_t>((n + 255) / 256, 4096), 256, 0, st>>>(p.part, p.splits, n, p.out,
+                                                                                     p.epi == kQgResid);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace fa
