@@ -371,7 +371,7 @@ def main():
         batch = {"value": B * Kb / (b_ms / 1000.0), "unit": "tok/s", "batch": B, "prompt": Pb, "steps": Kb,
                  "warmup": warm, "ms_per_step": b_ms / Kb, "kv_cache": "f16",
                  "sampler": "T 0.8, top-k 40, top-p 0.9, Philox4x32-10 seed 1000+i per sequence",
-                 "path": "f16 tcgen05 GEMMs at T=64, split-K decode attention per row, device sampler",
+                 "path": "f16 tcgen05 GEMMs at T=64 (split K), mma.sync split-K decode attention per row, device sampler",
                  "prefill_s": pf_b,
                  "roofline": {"bound": "hbm", "bytes_per_step": b_step_bytes, "achieved_gbs": b_gbs, "peak": peak,
                               "unit": "GB/s", "frac": b_gbs / peak}}

@@ -241,6 +241,11 @@ int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st);
 int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st);
+// batched decode attention on the tensor cores (mma.sync): grid (splits,
+// kv heads, q_rows), row r of AttnParams uses row_states[r] and cache
+// sequence row_seq0 + r; p.scale as in launch_attention
+int attn_rows_init();
+int launch_attn_decode_rows(const AttnParams &p, cudaStream_t st);
 int launch_batch_step_end(SeqState *states, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
                           uint32_t *step, cudaStream_t st);
 

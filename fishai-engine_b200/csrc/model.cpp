@@ -301,7 +301,8 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   want_tc_prefill = o.use_tc_prefill != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-  if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init() || qgemm_init())
+  if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init() || qgemm_init() ||
+      attn_rows_init())
     return fail(FA_ERR_CUDA, "kernel attribute setup failed");
   CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, device));
   int code = FA_OK;
@@ -1030,7 +1031,7 @@ int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams
     ap.state = bws.states;
     ap.row_states = bws.states;
     ap.row_seq0 = 0;
-    if (launch_attention(ap, false, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
+    if (launch_attn_decode_rows(ap, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
     if (launch_to_half(bws.Of, (uint64_t)b * qd, bws.Oh, bws.err, stream)) return fail(FA_ERR_CUDA, "convert failed");
     if ((rc = run_qgemm(lw.o, bws.moh, b, bws.X, d, kQgResid))) return rc;
     if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))

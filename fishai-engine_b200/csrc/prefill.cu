@@ -283,6 +283,207 @@ __global__ void __launch_bounds__(128) k_attn_causal(const __half *qh, uint32_t 
   }
 }
 
+// ---- batched decode attention on the tensor cores: one query token per row,
+// the REP query heads of a kv head as the MMA rows (padded to 16); grid
+// (splits, kv heads, rows), 4 warps each streaming 32-position K/V tiles of
+// the split (cp.async into private swizzled tiles), S = Q K^T and O += P V by
+// mma.sync, online softmax in base 2; warps merge in shared memory, the last
+// split of a (row, kv head) combines all splits in a fixed order ----
+constexpr uint32_t kDT = 32;
+
+template <uint32_t HD, bool F16>
+__device__ __forceinline__ void stage_rows(const KvView &kv, uint64_t lbase, const uint32_t *pt, uint32_t kvh,
+                                           int is_v, uint32_t s0, uint32_t s_end, uint32_t tile, uint32_t lane) {
+  constexpr uint32_t CH = HD / 8;
+  for (uint32_t i = lane; i < kDT * CH; i += 32) {
+    const uint32_t r = i / CH, c = i % CH, s = s0 + r;
+    const uint32_t dst = tile + sw_off(r, c, HD * 2);
+    if (s >= s_end) {
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
+      continue;
+    }
+    const uint64_t idx = lbase + kv_index(pt[s / 16], is_v, kvh, s % 16, 8 * c, kv.n_kv, HD);
+    if (F16) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(reinterpret_cast<const __half *>(kv.base) + idx)
+                   : "memory");
+    } else {
+      const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(kv.base) + idx);
+      const float4 a = __ldcg(src), b = __ldcg(src + 1);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(pack_h2(a.x, a.y)), "r"(pack_h2(a.z, a.w)),
+                   "r"(pack_h2(b.x, b.y)), "r"(pack_h2(b.z, b.w))
+                   : "memory");
+    }
+  }
+}
+
+template <uint32_t HD, bool F16, uint32_t REP>
+__global__ void __launch_bounds__(128) k_attn_decode_rows(const AttnParams p, float scale_log2) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  constexpr uint32_t RB = HD * 2, KT = HD / 16, NT = kDT / 8, OT = HD / 8, W = 2 + HD;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const uint32_t split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z, KVH = p.kv.n_kv, H = p.n_heads;
+  const uint32_t T = p.row_states[row].len + 1, seq = p.row_seq0 + row;
+  uint32_t Ls = (T + p.splits - 1) / p.splits;
+  Ls = (Ls + kDT - 1) / kDT * kDT;
+  const uint32_t t0 = min(T, split * Ls), t1 = min(T, t0 + Ls);
+  const uint32_t ktile = smem_u32(dsm) + warp * 2 * kDT * RB, vtile = ktile + kDT * RB;
+  const uint64_t lbase = (uint64_t)p.layer * p.kv.layer_stride;
+  const uint32_t *pt = p.kv.page_table + (size_t)seq * p.kv.max_pages;
+  // Q fragments: MMA rows = the query heads of this kv head (rows >= REP are zero)
+  const float *qr = p.q + (size_t)row * H * HD + (size_t)kvh * REP * HD;
+  uint32_t qa[KT][4];
+#pragma unroll
+  for (uint32_t kt = 0; kt < KT; ++kt) {
+    const uint32_t d0 = 16 * kt + 2 * c;
+    auto ld = [&](uint32_t r, uint32_t d) -> uint32_t {
+      return r < REP ? pack_h2(qr[r * HD + d], qr[r * HD + d + 1]) : 0u;
+    };
+    qa[kt][0] = ld(g, d0);
+    qa[kt][1] = ld(g + 8, d0);
+    qa[kt][2] = ld(g, d0 + 8);
+    qa[kt][3] = ld(g + 8, d0 + 8);
+  }
+  float o[OT][4];
+#pragma unroll
+  for (uint32_t j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  for (uint32_t s0 = t0 + warp * kDT; s0 < t1; s0 += 4 * kDT) {
+    stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 0, s0, t1, ktile, lane);
+    stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 1, s0, t1, vtile, lane);
+    if (F16) asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+    float s[NT][4];
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+    for (uint32_t kt = 0; kt < KT; ++kt)
+#pragma unroll
+      for (uint32_t j = 0; j < NT; j += 2) {
+        const uint32_t mi = lane >> 3, r = 8 * j + 8 * (mi >> 1) + (lane & 7), ch = 2 * kt + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(ktile + sw_off(r, ch, RB), b0, b1, b2, b3);
+        mma_f16(s[j], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b0, b1);
+        mma_f16(s[j + 1], qa[kt][0], qa[kt][1], qa[kt][2], qa[kt][3], b2, b3);
+      }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j)
+#pragma unroll
+      for (uint32_t e = 0; e < 2; ++e) {
+        const bool ok = s0 + 8 * j + 2 * c + e < t1;
+        s[j][e] = ok ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][2 + e] = ok ? s[j][2 + e] * scale_log2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[j][e]);
+        mx1 = fmaxf(mx1, s[j][2 + e]);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, off));
+    }
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float a0 = n0 == -INFINITY ? 1.0f : exp2f(m0 - n0), a1 = n1 == -INFINITY ? 1.0f : exp2f(m1 - n1);
+    float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < NT; ++j)
+#pragma unroll
+      for (uint32_t e = 0; e < 2; ++e) {
+        s[j][e] = n0 == -INFINITY ? 0.0f : exp2f(s[j][e] - n0);
+        s[j][2 + e] = n1 == -INFINITY ? 0.0f : exp2f(s[j][2 + e] - n1);
+        ls0 += s[j][e];
+        ls1 += s[j][2 + e];
+      }
+    l0 = fmaf(l0, a0, ls0);
+    l1 = fmaf(l1, a1, ls1);
+    m0 = n0;
+    m1 = n1;
+#pragma unroll
+    for (uint32_t j = 0; j < OT; ++j) {
+      o[j][0] *= a0;
+      o[j][1] *= a0;
+      o[j][2] *= a1;
+      o[j][3] *= a1;
+    }
+#pragma unroll
+    for (uint32_t kt = 0; kt < kDT / 16; ++kt) {
+      const uint32_t pa0 = pack_h2(s[2 * kt][0], s[2 * kt][1]), pa1 = pack_h2(s[2 * kt][2], s[2 * kt][3]);
+      const uint32_t pa2 = pack_h2(s[2 * kt + 1][0], s[2 * kt + 1][1]), pa3 = pack_h2(s[2 * kt + 1][2], s[2 * kt + 1][3]);
+#pragma unroll
+      for (uint32_t j = 0; j < OT; j += 2) {
+        const uint32_t mi = lane >> 3, r = 16 * kt + 8 * (mi & 1) + (lane & 7), ch = j + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vtile + sw_off(r, ch, RB), b0, b1, b2, b3);
+        mma_f16(o[j], pa0, pa1, pa2, pa3, b0, b1);
+        mma_f16(o[j + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+    __syncwarp();  // the next tile overwrites this warp's K/V tiles
+  }
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, off);
+    l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, off);
+  }
+  // merge the 4 warps (the tile memory becomes scratch [warp][16 rows][W])
+  __syncthreads();
+  float *scr = reinterpret_cast<float *>(dsm);
+  float *sw = scr + (size_t)warp * 16 * W;
+  if (c == 0) {
+    sw[g * W] = m0;
+    sw[g * W + 1] = l0;
+    sw[(g + 8) * W] = m1;
+    sw[(g + 8) * W + 1] = l1;
+  }
+#pragma unroll
+  for (uint32_t j = 0; j < OT; ++j)
+#pragma unroll
+    for (uint32_t e = 0; e < 2; ++e) {
+      sw[g * W + 2 + 8 * j + 2 * c + e] = o[j][e];
+      sw[(g + 8) * W + 2 + 8 * j + 2 * c + e] = o[j][2 + e];
+    }
+  __syncthreads();
+  float *part = p.part + (size_t)row * H * p.splits * W;
+  for (uint32_t idx = tid; idx < REP * W; idx += 128) {
+    const uint32_t r = idx / W, cc = idx % W;
+    float M = -INFINITY;
+    for (uint32_t w = 0; w < 4; ++w) M = fmaxf(M, scr[(w * 16 + r) * W]);
+    float v = M;
+    if (cc) {
+      v = 0.0f;
+      for (uint32_t w = 0; w < 4; ++w) {
+        const float mw = scr[(w * 16 + r) * W];
+        if (mw != -INFINITY) v = fmaf(scr[(w * 16 + r) * W + cc], exp2f(mw - M), v);
+      }
+    }
+    part[((kvh * REP + r) * p.splits + split) * W + cc] = v;
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ uint32_t last;
+  uint32_t *cnt = p.counters + (size_t)row * KVH + kvh;
+  if (tid == 0) last = atomicAdd(cnt, 1u) + 1 == p.splits ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // combine the splits of (row, kv head) in split order
+  for (uint32_t idx = tid; idx < REP * HD; idx += 128) {
+    const uint32_t r = idx / HD, d = idx % HD;
+    const float *P = part + (size_t)(kvh * REP + r) * p.splits * W;
+    float M = -INFINITY;
+    for (uint32_t sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(P + sp * W));
+    float L = 0.0f, acc = 0.0f;
+    for (uint32_t sp = 0; sp < p.splits; ++sp) {
+      const float ms = __ldcg(P + sp * W);
+      if (ms == -INFINITY) continue;
+      const float e = exp2f(ms - M);
+      L = fmaf(__ldcg(P + sp * W + 1), e, L);
+      acc = fmaf(__ldcg(P + sp * W + 2 + d), e, acc);
+    }
+    p.out[(size_t)row * H * HD + (size_t)(kvh * REP + r) * HD + d] = L > 0.0f ? acc / L : 0.0f;
+  }
+  if (tid == 0) *cnt = 0u;
+}
+
 // gate/up launch space: chunk c (width w_c) holds gate f in [c*CW/2, +w_c/2)
 // at c*CW + local, then the same up columns
 __global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
@@ -376,6 +577,49 @@ int launch_attn_hd(const AttnRowsParams &p, cudaStream_t st) {
 }
 
 }  // namespace
+
+namespace {
+template <uint32_t HD, bool F16, uint32_t REP>
+void *decode_rows_fn() {
+  return (void *)k_attn_decode_rows<HD, F16, REP>;
+}
+template <uint32_t HD, bool F16>
+void *decode_rows_rep(uint32_t rep) {
+  switch (rep) {
+    case 1: return decode_rows_fn<HD, F16, 1>();
+    case 2: return decode_rows_fn<HD, F16, 2>();
+    case 4: return decode_rows_fn<HD, F16, 4>();
+    case 8: return decode_rows_fn<HD, F16, 8>();
+    default: return nullptr;
+  }
+}
+void *pick_decode_rows(uint32_t hd, bool f16, uint32_t rep) {
+  if (hd == 128) return f16 ? decode_rows_rep<128, true>(rep) : decode_rows_rep<128, false>(rep);
+  if (hd == 64) return f16 ? decode_rows_rep<64, true>(rep) : decode_rows_rep<64, false>(rep);
+  return nullptr;
+}
+}  // namespace
+
+int attn_rows_init() {
+  for (uint32_t hd : {64u, 128u})
+    for (bool f16 : {false, true})
+      for (uint32_t rep : {1u, 2u, 4u, 8u})
+        if (cudaFuncSetAttribute(pick_decode_rows(hd, f16, rep), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(4 * 2 * kDT * hd * 2)))
+          return -1;
+  return 0;
+}
+
+int launch_attn_decode_rows(const AttnParams &p, cudaStream_t st) {
+  const uint32_t hd = p.kv.head_dim, rep = p.n_heads / p.kv.n_kv;
+  if (!p.row_states || p.n_heads % p.kv.n_kv || !p.splits) return -1;
+  void *fn = pick_decode_rows(hd, p.kv.f16 != 0, rep);
+  if (!fn) return -1;
+  const float scale_log2 = p.scale * 1.4426950408889634f;
+  void *args[] = {(void *)&p, (void *)&scale_log2};
+  const dim3 grid(p.splits, p.kv.n_kv, p.q_rows);
+  return cudaLaunchKernel(fn, grid, dim3(128), args, (size_t)4 * 2 * kDT * hd * 2, st) == cudaSuccess ? 0 : -1;
+}
 
 int launch_embed_rows(const void *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab, float *x,
                       uint32_t *err, cudaStream_t st) {

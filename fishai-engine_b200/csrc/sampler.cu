@@ -101,15 +101,23 @@ struct SortedTerm {  // p[index of rank i] / total
 };
 
 // s = fl(..fl(fl(s + t(0)) + t(1)).. + t(n-1)) for terms >= 0, by one warp;
-// with stop > 0 the scan ends at the first i where s > stop and *at = i
+// with stop > 0 the scan ends at the first i where s > stop and *at = i.
+// The terms of the next 256 are loaded while the current 256 are added.
 template <class Term>
 __device__ float warp_seq_sum(Term t, uint32_t n, float s, uint32_t lane, float stop, uint32_t *at) {
+  float nx[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const uint32_t i = 32 * b + lane;
+    nx[b] = i < n ? t(i) : 0.0f;
+  }
   for (uint32_t c0 = 0; c0 < n; c0 += 256) {
     float x[8];
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      const uint32_t i = c0 + 32 * b + lane;
-      x[b] = i < n ? t(i) : 0.0f;
+      x[b] = nx[b];
+      const uint32_t i = c0 + 256 + 32 * b + lane;
+      nx[b] = i < n ? t(i) : 0.0f;
     }
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
@@ -132,12 +140,19 @@ __device__ float warp_seq_sum(Term t, uint32_t n, float s, uint32_t lane, float 
 // categorical_sample's walk: first i with fl(r - p0 - .. - pi) <= 0 (in
 // order), n if none; r > 0
 __device__ uint32_t warp_seq_categorical(const float *v, uint32_t n, float r, uint32_t lane) {
+  float nx[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const uint32_t i = 32 * b + lane;
+    nx[b] = i < n ? __ldcg(v + i) : 0.0f;
+  }
   for (uint32_t c0 = 0; c0 < n; c0 += 256) {
     float x[8];
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      const uint32_t i = c0 + 32 * b + lane;
-      x[b] = i < n ? __ldcg(v + i) : 0.0f;
+      x[b] = nx[b];
+      const uint32_t i = c0 + 256 + 32 * b + lane;
+      nx[b] = i < n ? __ldcg(v + i) : 0.0f;
     }
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
