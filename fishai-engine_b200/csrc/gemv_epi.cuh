@@ -16,44 +16,56 @@ __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" 
 
 __device__ __forceinline__ float silu_ref(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
-// sum of the chunk's published partials in contributor order (deterministic);
-// the partial loads are issued eight at a time so their latencies overlap
-__device__ __forceinline__ float chunk_sum(const GemvParams &p, const ChunkDesc &cd, uint32_t c, uint32_t col) {
-  const uint32_t *sl = p.contrib + cd.contrib_off, n = cd.n_contrib;
-  const float *part = p.part + col;
-  float v = 0.0f;
-  uint32_t t = 0;
-  for (; t + 8 <= n; t += 8) {
-    float a[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = __ldcg(part + (size_t)__ldg(sl + t + j) * p.CW);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v += a[j];
-  }
-  for (; t < n; ++t) v += __ldcg(part + (size_t)__ldg(sl + t) * p.CW);
-  return v;
-}
-
-// fused epilogue for chunk c, run by the NW*32 consumer threads of the CTA that
-// completed the chunk
+// Fused epilogue for chunk c, run by the NW*32 consumer threads of the CTA
+// that completed the chunk.  Phase 1 sums the chunk's published partials into
+// `sums` (shared memory, >= width floats): thread pair (2q, 2q+1) takes
+// column quad q, one the first half of the contributor list and one the
+// second, each in list order, 8 float4 loads in flight; the pair adds its two
+// halves (a fixed order, so results are deterministic).  Phase 2 applies the
+// launch's epilogue mode to the sums.
 template <int NW>
-__device__ void epilogue(const GemvParams &p, float *red, const ChunkDesc &cd, uint32_t c, uint32_t tid, uint32_t warp,
-                         uint32_t lane) {
-  const uint32_t w = cd.width;
+__device__ void epilogue(const GemvParams &p, float *red, float *sums, const ChunkDesc &cd, uint32_t c, uint32_t tid,
+                         uint32_t warp, uint32_t lane) {
+  constexpr uint32_t NT = NW * 32;
+  const uint32_t w = cd.width, n = cd.n_contrib, nq = w / 4;
+  const uint32_t *sl = p.contrib + cd.contrib_off;
+  for (uint32_t i0 = 0; i0 < 2 * nq; i0 += NT) {  // uniform trip count: pairs stay together for the shuffle
+    const uint32_t i = i0 + tid, q = i >> 1, h = i & 1;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (i < 2 * nq) {
+      const uint32_t lo = h ? n / 2 : 0, hi = h ? n : n / 2;
+      const float4 *base = reinterpret_cast<const float4 *>(p.part) + q;
+      for (uint32_t t = lo; t < hi; t += 8) {
+        float4 a[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          a[j] = t + j < hi ? __ldcg(base + (size_t)__ldg(sl + t + j) * (p.CW / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc.x += a[j].x;
+          acc.y += a[j].y;
+          acc.z += a[j].z;
+          acc.w += a[j].w;
+        }
+      }
+    }
+    const float ox = __shfl_xor_sync(0xFFFFFFFFu, acc.x, 1), oy = __shfl_xor_sync(0xFFFFFFFFu, acc.y, 1);
+    const float oz = __shfl_xor_sync(0xFFFFFFFFu, acc.z, 1), ow = __shfl_xor_sync(0xFFFFFFFFu, acc.w, 1);
+    if (i < 2 * nq && h == 0)
+      reinterpret_cast<float4 *>(sums)[q] = make_float4(acc.x + ox, acc.y + oy, acc.z + oz, acc.w + ow);
+  }
+  consumer_bar<NW>();
   float local = 0.0f;
   unsigned long long best = 0ull;
   if (p.epi == kEpiSwiglu) {
     const uint32_t half = w / 2;
-    for (uint32_t i = tid; i < half; i += NW * 32) {
-      const float gsum = chunk_sum(p, cd, c, i), usum = chunk_sum(p, cd, c, i + half);
-      p.out[cd.out_col / 2 + i] = __fmul_rn(silu_ref(gsum), usum);
-    }
+    for (uint32_t i = tid; i < half; i += NT) p.out[cd.out_col / 2 + i] = __fmul_rn(silu_ref(sums[i]), sums[i + half]);
   } else {
     const uint32_t pos = (p.epi == kEpiQkv) ? p.state->pos : 0;   // RoPE position
     const uint32_t wpos = (p.epi == kEpiQkv) ? p.state->len : 0;  // cache slot written
     if (p.epi == kEpiQkv && pos >= p.rope_max && tid == 0) atomicOr(&p.state->err, kErrContext);
-    for (uint32_t i = tid; i < w; i += NW * 32) {
-      const float v = chunk_sum(p, cd, c, i);
+    for (uint32_t i = tid; i < w; i += NT) {
+      const float v = sums[i];
       const uint32_t col = cd.out_col + i;
       if (p.epi == kEpiStore) {
         p.out[col] = v;
@@ -71,8 +83,7 @@ __device__ void epilogue(const GemvParams &p, float *red, const ChunkDesc &cd, u
         float outv = v;
         if ((is_q || is_k) && pos < p.rope_max) {
           const uint32_t dd = (is_q ? col : col - p.q_dim) % hd;
-          const uint32_t ip = dd < half ? i + half : i - half;  // partner column (same chunk)
-          const float pv = chunk_sum(p, cd, c, ip);
+          const float pv = sums[dd < half ? i + half : i - half];  // partner column (same chunk)
           const float *cs = p.rope_tab + (uint64_t)pos * hd + 2 * (dd % half);
           const float cth = cs[0], sth = cs[1];
           outv = dd < half ? __fsub_rn(__fmul_rn(v, cth), __fmul_rn(pv, sth))
@@ -119,6 +130,7 @@ __device__ void epilogue(const GemvParams &p, float *red, const ChunkDesc &cd, u
       else if (p.state && b) atomicMax(&p.state->argmax_key, b);
     }
   }
+  consumer_bar<NW>();  // sums is reused by the caller
 }
 
 }  // namespace epi

@@ -484,7 +484,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     epi::consumer_bar<kWarps>();
     if (*sm.flag) {
       __threadfence();
-      epi::epilogue<kWarps>(p, sm.red, cd, c, tid, warp, lane);
+      epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), cd, c, tid, warp, lane);
       if (tid == 0) p.counters[c] = 0;  // ready for the next use of the chunk counters
       if (p.done) {  // chunk complete: count it for the launches that wait on this one
         __threadfence();
