@@ -155,6 +155,26 @@ def profile_one(args):
     return 0
 
 
+def profile_gemm(args):
+    """One tcgen05 token GEMM (the prefill / batched-decode projection) of a
+    reduced-depth model with the benchmark's shapes: device time and TFLOP/s."""
+    import ctypes as C
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights
+
+    path = synth.cached_preset(PRESET, n_layers=args.layers)
+    m = ModelWeights.load_from_gguf(path)
+    ms, fl = C.c_float(), C.c_double()
+    L.check(L.lib().fa_profile_gemm(m._h, PROFILE_KINDS[args.profile_gemm], 0, args.tokens, args.reps, C.byref(ms),
+                                    C.byref(fl)))
+    print(json.dumps({"profile_gemm": args.profile_gemm, "tokens": args.tokens, "layers": args.layers,
+                      "reps": args.reps, "avg_launch_us": ms.value * 1000.0, "flops": fl.value,
+                      "tflops": fl.value / (ms.value / 1000.0) / 1e12}), flush=True)
+    m.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -173,11 +193,18 @@ def main():
                     help="1: each decode step is one persistent kernel launch")
     ap.add_argument("--profile", choices=list(PROFILE_KINDS), default=None,
                     help="time one GEMV kind only, on a model with --layers layers")
+    ap.add_argument("--profile-gemm", choices=list(PROFILE_KINDS), default=None,
+                    help="time one tcgen05 token GEMM of a reduced-depth model (--layers) for --tokens tokens")
+    ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--model-layers", type=int, default=0,
+                    help="reduced-depth model of the same shapes for the whole run (0: the full 32 layers)")
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
     if args.profile:
         return profile_one(args)
+    if args.profile_gemm:
+        return profile_gemm(args)
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3
@@ -212,11 +239,12 @@ def main():
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(minutes=10))
         pg = dist
     # the synthetic model: rank 0 writes it once, others wait
+    ml = {"n_layers": args.model_layers} if args.model_layers else {}
     if rank == 0:
-        path = synth.cached_preset(PRESET)
+        path = synth.cached_preset(PRESET, **ml)
     if pg:
         pg.barrier()
-    path = synth.cached_preset(PRESET)
+    path = synth.cached_preset(PRESET, **ml)
 
     from fishai_engine.model import ModelWeights
 
