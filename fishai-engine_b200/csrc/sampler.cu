@@ -52,6 +52,9 @@ struct SSmem {
   unsigned long long tile[kTile];
   float redf[kSW];
   unsigned long long redk[kSW];
+  unsigned long long seq_tot[2][kSW], seq_qex[2][kSW];  // ordered scans (double-buffered)
+  uint32_t seq_first[2][kSW];
+  float seq_t[2][kSW];
   uint32_t wcnt[3][kSW];
   float sum, total;
   uint32_t prefix, remaining, cut, tok;
@@ -77,16 +80,7 @@ __device__ __forceinline__ float philox_uniform(uint64_t seed, uint64_t step) {
   return (float)(c0 >> 8) * (1.0f / 16777216.0f);
 }
 
-// half the gap from s >= 0 to the next float above / from r > 0 to the next
-// float below (NaN for inf; 0 where the half gap underflows)
-__device__ __forceinline__ float half_gap_up(float s) {
-  return __fmul_rn(__fsub_rn(__int_as_float(__float_as_int(s) + 1), s), 0.5f);
-}
-__device__ __forceinline__ float half_gap_down(float r) {
-  return __fmul_rn(__fsub_rn(r, __int_as_float(__float_as_int(r) - 1)), 0.5f);
-}
-
-// term t of a sequence handed to the warp scans below
+// term t of a sequence handed to the ordered scans below
 struct RowTerm {
   const float *v;
   __device__ float operator()(uint32_t i) const { return __ldcg(v + i); }
@@ -100,73 +94,164 @@ struct SortedTerm {  // p[index of rank i] / total
   }
 };
 
-// s = fl(..fl(fl(s + t(0)) + t(1)).. + t(n-1)) for terms >= 0, by one warp;
-// with stop > 0 the scan ends at the first i where s > stop and *at = i.
-// The terms of the next 256 are loaded while the current 256 are added.
-template <class Term>
-__device__ float warp_seq_sum(Term t, uint32_t n, float s, uint32_t lane, float stop, uint32_t *at) {
-  float nx[8];
-#pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    const uint32_t i = 32 * b + lane;
-    nx[b] = i < n ? t(i) : 0.0f;
-  }
-  for (uint32_t c0 = 0; c0 < n; c0 += 256) {
-    float x[8];
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      x[b] = nx[b];
-      const uint32_t i = c0 + 256 + 32 * b + lane;
-      nx[b] = i < n ? t(i) : 0.0f;
-    }
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      if (c0 + 32 * b >= n) break;
-      const float h = half_gap_up(s);
-      if (__any_sync(kFull, !(x[b] < h))) {
-        for (int j = 0; j < 32; ++j) {
-          s = __fadd_rn(s, __shfl_sync(kFull, x[b], j));
-          if (stop > 0.0f && s > stop) {
-            *at = c0 + 32 * b + j;
-            return s;
-          }
-        }
-      }
-    }
-  }
-  return s;
+// ---- ordered f32 scans, block-parallel and bit-exact ----
+// The reference accumulates in index order, s(i+1) = fl(s(i) + t(i)).  While
+// s stays inside one binade [2^e, 2^(e+1)) every partial sum is a multiple of
+// that binade's spacing g, and fl(s + t) = s + g * rn(t / g) exactly unless
+// t / g lies exactly halfway between integers (the tie goes to the even
+// multiple, which depends on s) or the rounded sum leaves the binade.  So the
+// scan runs as an integer prefix sum of q(i) = rn(t(i) / g) over a tile of
+// the sequence; at the first index where the prefix would leave the binade,
+// where a tie occurs, or where t is not a finite non-negative float, the
+// partial sum is formed exactly (its bit pattern plus the integer prefix) and
+// that one step is taken in f32 as the reference does; the scan then resumes
+// after it with the new binade.  The walk mode runs the reference's
+// categorical draw r(i+1) = fl(r(i) - p(i)) the same way, downwards.
+enum : int { kSeqSum = 0, kSeqStop = 1, kSeqWalk = 2 };
+constexpr uint32_t kSeqPer = 8;  // terms per thread per tile
+
+// q = rn(t / g) for g = 2^(ue - 150) (ue = max(biased exponent, 1) of the
+// accumulator), t finite and >= 0; tie: t / g is exactly halfway
+__device__ __forceinline__ uint32_t grid_units(uint32_t tb, uint32_t ue, bool &tie) {
+  const uint32_t et = tb >> 23;
+  const uint32_t m = et ? (tb & 0x7FFFFFu) | 0x800000u : tb;
+  const uint32_t e = et ? et : 1u;
+  tie = false;
+  if (e >= ue) return e - ue >= 8 ? 0x80000000u : m << (e - ue);  // >= 2^31 ends the binade anyway
+  const uint32_t sh = ue - e;
+  if (sh >= 32) return 0u;
+  const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+  tie = rem == half;
+  return (m >> sh) + (rem > half ? 1u : 0u);
 }
 
-// categorical_sample's walk: first i with fl(r - p0 - .. - pi) <= 0 (in
-// order), n if none; r > 0
-__device__ uint32_t warp_seq_categorical(const float *v, uint32_t n, float r, uint32_t lane) {
-  float nx[8];
+struct SeqOut {
+  float s;      // final accumulator (kSeqWalk: r)
+  uint32_t at;  // kSeqStop: first i with s > stop; kSeqWalk: first i with r <= 0; n if none
+};
+
+// Whole block.  kSeqSum: s = fl(..fl(s0 + t(0)).. + t(n-1)); kSeqStop: the
+// same scan ended at the first i where s > stop; kSeqWalk: r = s0 > 0 minus
+// the terms in order, ended at the first i where r <= 0.
+template <int MODE, class Term>
+__device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &sm) {
+  constexpr uint32_t TILE = kST * kSeqPer;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float s = s0;
+  uint32_t par = 0;
+  for (uint32_t t0 = 0; t0 < n; t0 += TILE) {
+    const uint32_t tend = min(n, t0 + TILE), j0 = t0 + tid * kSeqPer;
+    float x[kSeqPer];
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    const uint32_t i = 32 * b + lane;
-    nx[b] = i < n ? __ldcg(v + i) : 0.0f;
-  }
-  for (uint32_t c0 = 0; c0 < n; c0 += 256) {
-    float x[8];
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      x[b] = nx[b];
-      const uint32_t i = c0 + 256 + 32 * b + lane;
-      nx[b] = i < n ? __ldcg(v + i) : 0.0f;
-    }
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      if (c0 + 32 * b >= n) break;
-      const float h = half_gap_down(r);
-      if (__any_sync(kFull, !(x[b] < h))) {
-        for (int j = 0; j < 32; ++j) {
-          r = __fsub_rn(r, __shfl_sync(kFull, x[b], j));
-          if (r <= 0.0f) return c0 + 32 * b + j;
-        }
+    for (uint32_t e = 0; e < kSeqPer; ++e) x[e] = j0 + e < tend ? term(j0 + e) : 0.0f;
+    uint32_t i = t0;
+    while (i < tend) {
+      const uint32_t sb = __float_as_uint(s);
+      if (s != s) return {s, n};  // NaN stays NaN (and is never > stop or <= 0)
+      // kind 0: on the binade grid; 1: s == 0 (next step at the first nonzero
+      // term); 2: s == +inf (next step at the first NaN term)
+      int kind = 0;
+      uint32_t ue = 1, room = 0;
+      if (MODE != kSeqWalk && s == 0.0f) {
+        kind = 1;
+      } else if (MODE != kSeqWalk && sb == 0x7F800000u) {
+        kind = 2;
+      } else {
+        const uint32_t es = sb >> 23, m = es ? (sb & 0x7FFFFFu) | 0x800000u : sb;
+        ue = es ? es : 1u;
+        room = MODE == kSeqWalk ? (es >= 2 ? m - 0x800000u : m) : 0x1000000u - m;
       }
+      uint32_t q[kSeqPer];
+      bool st[kSeqPer];
+      unsigned long long tot = 0;
+#pragma unroll
+      for (uint32_t e = 0; e < kSeqPer; ++e) {
+        const uint32_t j = j0 + e, tb = __float_as_uint(x[e]);
+        const bool valid = j >= i && j < tend;
+        q[e] = 0u;
+        st[e] = false;
+        if (valid) {
+          if (kind == 1) {
+            st[e] = x[e] != 0.0f;
+          } else if (kind == 2) {
+            st[e] = x[e] != x[e];
+          } else if ((tb >> 23) >= 255u) {  // negative, inf or NaN: the f32 step decides
+            st[e] = true;
+          } else {
+            bool tie;
+            q[e] = grid_units(tb, ue, tie);
+            st[e] = tie;
+          }
+        }
+        tot += q[e];
+      }
+      // block exclusive prefix of the per-thread totals
+      unsigned long long inc = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long u = __shfl_up_sync(kFull, inc, o);
+        if ((int)lane >= o) inc += u;
+      }
+      if (lane == 31) sm.seq_tot[par][warp] = inc;
+      __syncthreads();
+      unsigned long long winc = sm.seq_tot[par][lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long u = __shfl_up_sync(kFull, winc, o);
+        if ((int)lane >= o) winc += u;
+      }
+      const unsigned long long block_tot = __shfl_sync(kFull, winc, 31);
+      const unsigned long long wexcl = __shfl_sync(kFull, winc - sm.seq_tot[par][lane], warp);
+      unsigned long long Q = wexcl + inc - tot;  // exclusive prefix at this thread's first term
+      uint32_t first = ~0u;
+      unsigned long long qex = 0;
+      float tf = 0.0f;
+#pragma unroll
+      for (uint32_t e = 0; e < kSeqPer; ++e) {
+        const unsigned long long Qi = Q + q[e];
+        bool stp = st[e];
+        if (kind == 0 && !stp && (j0 + e) >= i && (j0 + e) < tend) {
+          stp = Qi >= room;
+          if (MODE == kSeqStop && !stp) stp = __uint_as_float(sb + (uint32_t)Qi) > stop;
+        }
+        if (stp && first == ~0u) {
+          first = j0 + e;
+          qex = Q;
+          tf = x[e];
+        }
+        Q = Qi;
+      }
+      const uint32_t bal = __ballot_sync(kFull, first != ~0u);
+      if (bal) {
+        if (lane == (uint32_t)(__ffs(bal) - 1)) {
+          sm.seq_first[par][warp] = first;
+          sm.seq_qex[par][warp] = qex;
+          sm.seq_t[par][warp] = tf;
+        }
+      } else if (lane == 0) {
+        sm.seq_first[par][warp] = ~0u;
+      }
+      __syncthreads();
+      const uint32_t f = sm.seq_first[par][lane];
+      const uint32_t fmin = __reduce_min_sync(kFull, f);
+      if (fmin == ~0u) {  // no step of its own in the rest of the tile
+        if (kind == 0) s = __uint_as_float(MODE == kSeqWalk ? sb - (uint32_t)block_tot : sb + (uint32_t)block_tot);
+        i = tend;
+      } else {
+        const uint32_t w = __ffs(__ballot_sync(kFull, f == fmin)) - 1;
+        const unsigned long long qx = sm.seq_qex[par][w];
+        const float t = sm.seq_t[par][w];
+        float base = s;
+        if (kind == 0) base = __uint_as_float(MODE == kSeqWalk ? sb - (uint32_t)qx : sb + (uint32_t)qx);
+        s = MODE == kSeqWalk ? __fsub_rn(base, t) : __fadd_rn(base, t);
+        if (MODE == kSeqStop && s > stop) return {s, fmin};
+        if (MODE == kSeqWalk && s <= 0.0f) return {s, fmin};
+        i = fmin + 1;
+      }
+      par ^= 1u;
     }
   }
-  return n;
+  return {s, n};
 }
 
 __device__ __forceinline__ void cmpx(unsigned long long &a, unsigned long long &b, bool up) {
@@ -376,13 +461,7 @@ __global__ void __launch_bounds__(kST, 1) k_sample(const SamplerParams p) {
   // 4: softmax
   for (uint32_t i = tid; i < n; i += kST) __stcg(pr + i, __double2float_rn(exp((double)__fsub_rn(__ldcg(pr + i), mx))));
   __syncthreads();
-  if (warp == 0) {
-    uint32_t at = 0;
-    const float s = warp_seq_sum(RowTerm{pr}, n, 0.0f, lane, 0.0f, &at);
-    if (lane == 0) sm.sum = s;
-  }
-  __syncthreads();
-  const float sum = sm.sum;
+  const float sum = block_seq<kSeqSum>(RowTerm{pr}, n, 0.0f, 0.0f, sm).s;
   if (sum != 0.0f)
     for (uint32_t i = tid; i < n; i += kST) __stcg(pr + i, __fdiv_rn(__ldcg(pr + i), sum));
   __syncthreads();
@@ -463,15 +542,9 @@ __global__ void __launch_bounds__(kST, 1) k_sample(const SamplerParams p) {
         for (uint32_t r = p.top_k + tid; r < n; r += kST) __stcg(pr + (uint32_t)(__ldcg(keys + r) & 0xFFFFFFFFull), 0.0f);
       __syncthreads();
       if (topp) {
-        if (warp == 0) {
-          uint32_t at = 0;
-          const float t = warp_seq_sum(RowTerm{pr}, n, 0.0f, lane, 0.0f, &at);
-          uint32_t cut = n;
-          if (t > 0.0f) warp_seq_sum(SortedTerm{pr, keys, t}, n, 0.0f, lane, 0.999f, &cut);
-          if (lane == 0) sm.cut = t > 0.0f ? cut : n;
-        }
-        __syncthreads();
-        for (uint32_t r = sm.cut + tid; r < n; r += kST) __stcg(pr + (uint32_t)(__ldcg(keys + r) & 0xFFFFFFFFull), 0.0f);
+        const float t = block_seq<kSeqSum>(RowTerm{pr}, n, 0.0f, 0.0f, sm).s;
+        const uint32_t cut = t > 0.0f ? block_seq<kSeqStop>(SortedTerm{pr, keys, t}, n, 0.0f, 0.999f, sm).at : n;
+        for (uint32_t r = cut + tid; r < n; r += kST) __stcg(pr + (uint32_t)(__ldcg(keys + r) & 0xFFFFFFFFull), 0.0f);
         __syncthreads();
       }
     }
@@ -486,11 +559,11 @@ __global__ void __launch_bounds__(kST, 1) k_sample(const SamplerParams p) {
     const bool all_zero = !(key_float((uint32_t)(best >> 32)) > 0.0f);
     if (greedy || all_zero) {
       if (tid == 0) sm.tok = amax;
-    } else if (warp == 0) {
+    } else {
       const float r = philox_uniform(p.seeds[row], p.counters[row]);
-      uint32_t t = r > 0.0f ? warp_seq_categorical(pr, n, r, lane) : 0u;
+      uint32_t t = r > 0.0f ? block_seq<kSeqWalk>(RowTerm{pr}, n, r, 0.0f, sm).at : 0u;
       if (t >= n) t = amax;
-      if (lane == 0) sm.tok = t;
+      if (tid == 0) sm.tok = t;
     }
   }
   __syncthreads();
