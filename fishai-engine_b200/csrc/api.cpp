@@ -919,7 +919,7 @@ int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, ui
         p.in = kind == 1 ? m.ws.attn_out : kind == 2 ? m.ws.x : m.ws.h;
         p.norm_w = lw.ffn_norm;
         p.ssq = m.ws.ssq_o;
-        p.n_ssq = (uint32_t)lw.o.chunks.size();
+        p.n_ssq = lw.o.parts();
         p.eps = m.cfg.norm_eps;
         p.epi = kind == 2 ? kEpiSwiglu : kEpiStore;
         p.out = kind == 2 ? m.ws.h : m.ws.logits;  // scratch destination

@@ -335,6 +335,7 @@ int attention_init() {
       if (cudaFuncSetAttribute(pick_kernel(rep, f16), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)attn_smem(rep, 128, f16)) != cudaSuccess)
         return -1;
+  if (attn_paged_init()) return -1;
   done.fetch_or(1ull << dev);
   return 0;
 }
@@ -343,9 +344,10 @@ int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st) {
   const uint32_t rep = p.n_heads / p.kv.n_kv, hd = p.kv.head_dim;
   const bool f16 = p.kv.f16 != 0;
   if (hd > 128 || rep > kMaxRep || p.n_heads % p.kv.n_kv || !p.splits || p.splits > kMaxSplits) return -1;
+  if (attention_init()) return -1;
+  if (attn_paged_supported(p)) return launch_attn_paged(p, pdl, st);  // batch-1 decode: bulk-copy tiles
   void *fn = pick_kernel(rep, f16);
   if (!fn) return -1;
-  if (attention_init()) return -1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.kv.n_kv, p.q_rows ? p.q_rows : 1);
   cfg.blockDim = dim3(kWarps * 32);

@@ -60,6 +60,10 @@ __host__ __device__ inline uint64_t kv_index(uint32_t page, int is_v, uint32_t h
   return ((((uint64_t)page * 2 + (uint64_t)is_v) * n_kv + h) * 16 + slot) * hd + d;
 }
 
+// most CTAs contributing to one GEMV chunk (the MMA path's last arriver
+// keeps their partial slots in shared memory)
+constexpr uint32_t kGemvMaxContrib = 256;
+
 struct GemvParams {
   const uint8_t *w;
   const ChunkDesc *chunks;
@@ -136,6 +140,11 @@ struct AttnParams {
 // of a stream capture; launch_attention calls it as well
 int attention_init();
 int launch_attention(const AttnParams &p, bool pdl, cudaStream_t st);
+// batch-1 paged decode attention with bulk-copy tiles (attn_paged.cu); the
+// launcher above routes to it when attn_paged_supported holds
+bool attn_paged_supported(const AttnParams &p);
+int attn_paged_init();
+int launch_attn_paged(const AttnParams &p, bool pdl, cudaStream_t st);
 
 struct EmbedParams {
   const uint8_t *emb;      // native [V][d] blocks

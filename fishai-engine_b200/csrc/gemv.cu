@@ -332,7 +332,7 @@ __device__ __forceinline__ void flush(const GemvParams &p, const Smem &sm, const
   consumer_bar();
   if (*sm.flag) {
     __threadfence();
-    epi::epilogue<kConsumerWarps>(p, sm.red, sm.warp_part, cd, c, tid, warp, lane);
+    epi::epilogue<kConsumerWarps>(p, sm.red, sm.warp_part, p.contrib + cd.contrib_off, cd, c, tid, warp, lane);
     if (tid == 0) p.counters[c] = 0;  // ready for the next launch
   }
   consumer_bar();

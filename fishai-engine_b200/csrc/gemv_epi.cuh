@@ -20,28 +20,29 @@ __device__ __forceinline__ float silu_ref(float g) { return g * (1.0f / (1.0f + 
 // that completed the chunk.  Phase 1 sums the chunk's published partials into
 // `sums` (shared memory, >= width floats): thread pair (2q, 2q+1) takes
 // column quad q, one the first half of the contributor list and one the
-// second, each in list order, 8 float4 loads in flight; the pair adds its two
-// halves (a fixed order, so results are deterministic).  Phase 2 applies the
-// launch's epilogue mode to the sums.
+// second, each in list order, 12 float4 loads in flight; the pair adds its
+// two halves (a fixed order, so results are deterministic).  `sl` lists the
+// contributors' partial slots (shared memory on the MMA path).  Phase 2
+// applies the launch's epilogue mode to the sums.
 template <int NW>
-__device__ void epilogue(const GemvParams &p, float *red, float *sums, const ChunkDesc &cd, uint32_t c, uint32_t tid,
-                         uint32_t warp, uint32_t lane) {
+__device__ void epilogue(const GemvParams &p, float *red, float *sums, const uint32_t *sl, const ChunkDesc &cd,
+                         uint32_t c, uint32_t tid, uint32_t warp, uint32_t lane) {
   constexpr uint32_t NT = NW * 32;
+  constexpr uint32_t kInFlight = 12;
   const uint32_t w = cd.width, n = cd.n_contrib, nq = w / 4;
-  const uint32_t *sl = p.contrib + cd.contrib_off;
   for (uint32_t i0 = 0; i0 < 2 * nq; i0 += NT) {  // uniform trip count: pairs stay together for the shuffle
     const uint32_t i = i0 + tid, q = i >> 1, h = i & 1;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (i < 2 * nq) {
       const uint32_t lo = h ? n / 2 : 0, hi = h ? n : n / 2;
       const float4 *base = reinterpret_cast<const float4 *>(p.part) + q;
-      for (uint32_t t = lo; t < hi; t += 8) {
-        float4 a[8];
+      for (uint32_t t = lo; t < hi; t += kInFlight) {
+        float4 a[kInFlight];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          a[j] = t + j < hi ? __ldcg(base + (size_t)__ldg(sl + t + j) * (p.CW / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t j = 0; j < kInFlight; ++j)
+          a[j] = t + j < hi ? __ldcg(base + (size_t)sl[t + j] * (p.CW / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (uint32_t j = 0; j < kInFlight; ++j) {
           acc.x += a[j].x;
           acc.y += a[j].y;
           acc.z += a[j].z;

@@ -24,6 +24,7 @@ constexpr uint32_t kMaxStageGroups = 4;     // row groups per stage
 constexpr uint32_t kStageTarget = 36 * 1024;
 constexpr uint32_t kTblWords = 8 * 24;      // one table: (groups x blocks <= 8) x (3 splits x 4 lanes x 2 words)
 constexpr uint32_t kZeroWords = 256;        // B fragment source of the lanes whose column is unused
+constexpr uint32_t kSlotWord = kWarps * kTblWords - kGemvMaxContrib;  // epilogue: contributor slots at the table end
 // shared memory: mbarriers + flag | reduction scratch | zero area | tables | x | ring
 constexpr uint32_t kOffRed = 256, kOffZero = kOffRed + 512, kOffTbl = kOffZero + 4 * kZeroWords,
                    kOffX = kOffTbl + 4 * kWarps * kTblWords;
@@ -420,24 +421,53 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
   const uint32_t G = p.K / 16, start = R.c0 * G + R.g0, end = R.c1 * G + R.g1;
   const uint32_t n_units = end > start ? end - start : 0;
   if (!n_units) return;
+  // the CTA's rows of x, in unit order: xs[16u + r] = x[16 g(u) + r]; the
+  // first batch of x and norm weights is loaded together with the sum-of-
+  // squares partials (one round trip), then normalised once inv is known
+  constexpr uint32_t kPre = 8, NT = kWarps * 32;
+  const uint32_t nx = n_units * 16;
+  float xr[kPre], wr[kPre];
+  auto load_batch = [&](uint32_t base) {
+#pragma unroll
+    for (uint32_t j = 0; j < kPre; ++j) {
+      const uint32_t i = base + j * NT + tid;
+      if (i < nx) {
+        const uint32_t k = 16 * ((start + i / 16) % G) + (i & 15);
+        xr[j] = __ldcg(p.in + k);
+        wr[j] = norm ? __ldg(p.norm_w + k) : 1.0f;
+      }
+    }
+  };
+  load_batch(0);
   if (norm) {
-    if (warp == 0) {
+    if (warp == 0) {  // lane-strided partial sums in index order, every load in flight
       float s = 0.0f;
-      for (uint32_t i = lane; i < p.n_ssq; i += 32) s += __ldcg(p.ssq + i);
+      for (uint32_t i0 = 0; i0 < p.n_ssq; i0 += 32 * kPre) {
+        float v[kPre];
+#pragma unroll
+        for (uint32_t j = 0; j < kPre; ++j) {
+          const uint32_t i = i0 + 32 * j + lane;
+          v[j] = i < p.n_ssq ? __ldcg(p.ssq + i) : 0.0f;
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kPre; ++j) s += v[j];
+      }
 #pragma unroll
       for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
       if (lane == 0) sm.red[96] = 1.0f / sqrtf(s / (float)p.K + p.eps);
     }
     epi::consumer_bar<kWarps>();
   }
-  // the CTA's rows of x, in unit order: xs[16u + r] = x[16 g(u) + r]
   {
     const float inv = norm ? sm.red[96] : 1.0f;
-    for (uint32_t i = tid; i < n_units * 16; i += kWarps * 32) {
-      const uint32_t k = 16 * ((start + i / 16) % G) + (i & 15);
-      float v = __ldcg(p.in + k);
-      if (norm) v = __fmul_rn(__fmul_rn(v, inv), p.norm_w[k]);  // rms_norm (src/tensor.rs:280-290)
-      sm.xs[i] = v;
+    for (uint32_t base = 0; base < nx; base += kPre * NT) {
+      if (base) load_batch(base);
+#pragma unroll
+      for (uint32_t j = 0; j < kPre; ++j) {
+        const uint32_t i = base + j * NT + tid;
+        // rms_norm (src/tensor.rs:280-290): (x * inv) * w
+        if (i < nx) sm.xs[i] = norm ? __fmul_rn(__fmul_rn(xr[j], inv), wr[j]) : xr[j];
+      }
     }
   }
   epi::consumer_bar<kWarps>();
@@ -459,8 +489,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       default: segment<kQ4_0>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
     }
     u += seg;
-    // the CTA's rows of chunk c are done: publish the partial; the last
-    // contributing CTA sums the partials and runs the epilogue
+    // the CTA's rows of chunk c are done: its partial into its slot
     const uint32_t slot_p = cta * p.max_chunks_per_cta + (c - R.c0);
     if (ok && 64 * warp < cd.width) {
       switch (cd.type) {
@@ -475,16 +504,25 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
 #pragma unroll
       for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
     corr[0] = corr[1] = 0.0f;
-    __threadfence();
+    // publish: the last contributing CTA to arrive sums the partials and runs
+    // the epilogue.  The contributors' partial slots are fetched while the
+    // arrival atomic is in flight (only the last arriver uses them).
+    const uint32_t n = cd.n_contrib;
+    uint32_t slot_k = 0;
+    if (tid < n) slot_k = __ldg(p.contrib + cd.contrib_off + tid);
     epi::consumer_bar<kWarps>();
     if (tid == 0) {
+      __threadfence();  // the CTA's partial (ordered before by the barrier) is visible first
       const uint32_t old = atomicAdd(p.counters + c, 1u);
-      *sm.flag = (old + 1 == cd.n_contrib) ? 1u : 0u;
+      sm.flag[0] = (old + 1 == n) ? 1u : 0u;
     }
     epi::consumer_bar<kWarps>();
-    if (*sm.flag) {
+    if (sm.flag[0]) {
       __threadfence();
-      epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), cd, c, tid, warp, lane);
+      uint32_t *slots = sm.tbl + kSlotWord;
+      if (tid < n) slots[tid] = slot_k;
+      epi::consumer_bar<kWarps>();
+      epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), slots, cd, c, tid, warp, lane);
       if (tid == 0) p.counters[c] = 0;  // ready for the next use of the chunk counters
       if (p.done) {  // chunk complete: count it for the launches that wait on this one
         __threadfence();

@@ -245,6 +245,7 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     if (who[c].empty() || P.n_ctas > 65535) return fail(FA_ERR_INVALID, "GEMV split failed");
     P.chunks[c].contrib_off = (uint32_t)P.contrib.size();
     P.chunks[c].n_contrib = (uint32_t)who[c].size();
+    if (mma && who[c].size() > kGemvMaxContrib) return fail(FA_ERR_UNSUPPORTED, "GEMV chunk has too many contributors");
     for (uint16_t i : who[c]) P.contrib.push_back(i * P.max_chunks_per_cta + (c - P.ranges[i].c0));
   }
   P.d_chunks = (ChunkDesc *)m.dmalloc(P.chunks.size() * sizeof(ChunkDesc));
@@ -494,7 +495,7 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
   p.in = w.x;
   p.norm_w = lw.attn_norm;
   p.ssq = l == 0 ? w.ssq_e : w.ssq_d;
-  p.n_ssq = l == 0 ? embed_ctas : (uint32_t)layers[l - 1].down.chunks.size();
+  p.n_ssq = l == 0 ? embed_ctas : layers[l - 1].down.parts();
   p.eps = cfg.norm_eps;
   p.epi = kEpiQkv;
   p.out = w.q;
@@ -541,7 +542,7 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.in = w.x;
   p.norm_w = lw.ffn_norm;
   p.ssq = w.ssq_o;
-  p.n_ssq = (uint32_t)lw.o.chunks.size();
+  p.n_ssq = lw.o.parts();
   p.eps = cfg.norm_eps;
   p.epi = kEpiSwiglu;
   p.out = w.h;
@@ -563,7 +564,7 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
 int Model::enqueue_head(Workspace &w, SeqState *st) {
   const uint32_t L = cfg.n_layers;
   const float *ssq_in = L ? w.ssq_d : w.ssq_e;
-  const uint32_t n_ssq = L ? (uint32_t)layers[L - 1].down.chunks.size() : embed_ctas;
+  const uint32_t n_ssq = L ? layers[L - 1].down.parts() : embed_ctas;
   if (!tied) {
     GemvParams p = gemv_base(head);
     p.pro = kProRmsNorm;
@@ -607,7 +608,6 @@ int Model::enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hi
 
 int Model::alloc_workspace(Workspace &w) {
   const uint32_t d = cfg.n_embd, qd = cfg.n_heads * cfg.head_dim;
-  const uint32_t L = cfg.n_layers;
   w.x = (float *)dmalloc(((size_t)d + 8) * 4);  // +8: inputs are read in whole 8-row groups
   w.q = (float *)dmalloc(qd * 4);
   w.h = (float *)dmalloc(((size_t)cfg.n_ff_used + 8) * 4);
@@ -616,8 +616,13 @@ int Model::alloc_workspace(Workspace &w) {
   w.attn_out = (float *)dmalloc(((size_t)qd + 8) * 4);
   w.attn_cnt = (uint32_t *)dmalloc(cfg.n_kv_heads * 4);
   w.ssq_e = (float *)dmalloc((size_t)std::max<uint32_t>(embed_ctas, (uint32_t)n_sm) * 4);
-  w.ssq_o = (float *)dmalloc((L ? layers[0].o.chunks.size() : 1) * 4);
-  w.ssq_d = (float *)dmalloc((L ? layers[0].down.chunks.size() : 1) * 4);
+  uint32_t n_ssq_o = 1, n_ssq_d = 1;  // sum-of-squares partials of the residual launches
+  for (const LayerW &lw : layers) {
+    n_ssq_o = std::max(n_ssq_o, lw.o.parts());
+    n_ssq_d = std::max(n_ssq_d, lw.down.parts());
+  }
+  w.ssq_o = (float *)dmalloc((size_t)n_ssq_o * 4);
+  w.ssq_d = (float *)dmalloc((size_t)n_ssq_d * 4);
   w.state = (SeqState *)dmalloc(sizeof(SeqState));
   if (!w.x || !w.q || !w.h || !w.logits || !w.attn_part || !w.attn_out || !w.attn_cnt || !w.ssq_e || !w.ssq_o ||
       !w.ssq_d || !w.state)
@@ -733,7 +738,7 @@ int Model::prepare_step(const KvCache &kv, uint32_t seq) {
     p.in = ws.x;
     p.norm_w = lw.attn_norm;
     p.ssq = l == 0 ? ws.ssq_e : ws.ssq_d;
-    p.n_ssq = l == 0 ? grid : (uint32_t)layers[l - 1].down.chunks.size();
+    p.n_ssq = l == 0 ? grid : layers[l - 1].down.parts();
     p.eps = cfg.norm_eps;
     p.epi = kEpiQkv;
     p.out = ws.q;
@@ -748,7 +753,7 @@ int Model::prepare_step(const KvCache &kv, uint32_t seq) {
     const uint32_t q_qkv = (uint32_t)ph.size();
     add_gemv(p, prev, prev_count);
     const uint32_t q_attn = (uint32_t)ph.size();
-    ph.push_back({kPhAttn, l, q_qkv, (uint32_t)lw.qkv.chunks.size()});
+    ph.push_back({kPhAttn, l, q_qkv, lw.qkv.parts()});
     p = gemv_base(lw.o);
     p.pro = kProPlain;
     p.in = ws.attn_out;
@@ -763,13 +768,13 @@ int Model::prepare_step(const KvCache &kv, uint32_t seq) {
     p.in = ws.x;
     p.norm_w = lw.ffn_norm;
     p.ssq = ws.ssq_o;
-    p.n_ssq = (uint32_t)lw.o.chunks.size();
+    p.n_ssq = lw.o.parts();
     p.eps = cfg.norm_eps;
     p.epi = kEpiSwiglu;
     p.out = ws.h;
     p.state = ws.state;
     const uint32_t q_gu = (uint32_t)ph.size();
-    add_gemv(p, q_o, (uint32_t)lw.o.chunks.size());
+    add_gemv(p, q_o, lw.o.parts());
     p = gemv_base(lw.down);
     p.pro = kProPlain;
     p.in = ws.h;
@@ -778,15 +783,15 @@ int Model::prepare_step(const KvCache &kv, uint32_t seq) {
     p.ssq_out = ws.ssq_d;
     p.state = ws.state;
     prev = (uint32_t)ph.size();
-    prev_count = (uint32_t)lw.down.chunks.size();
-    add_gemv(p, q_gu, (uint32_t)lw.gateup.chunks.size());
+    prev_count = lw.down.parts();
+    add_gemv(p, q_gu, lw.gateup.parts());
   }
   GemvParams p = gemv_base(head);
   p.pro = kProRmsNorm;
   p.in = ws.x;
   p.norm_w = out_norm;
   p.ssq = ws.ssq_d;
-  p.n_ssq = (uint32_t)layers[L - 1].down.chunks.size();
+  p.n_ssq = layers[L - 1].down.parts();
   p.eps = cfg.norm_eps;
   p.epi = kEpiLogits;
   p.out = ws.logits;
@@ -945,7 +950,7 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
     }
   }
   // the last token through the decode head: logits + argmax
-  const uint32_t n_ssq = (uint32_t)layers[cfg.n_layers - 1].down.chunks.size();
+  const uint32_t n_ssq = layers[cfg.n_layers - 1].down.parts();
   if (launch_last_row(pws.X, T - 1, d, ws.x, ws.ssq_d, n_ssq, stream)) return fail(FA_ERR_CUDA, "last row launch failed");
   SeqState st{};
   st.pos = start_pos + n - 1;

@@ -29,6 +29,10 @@ struct GemvPlan {
   std::vector<QgTile> qg_tiles;  // token-parallel GEMM output tiles (MMA layout only)
   QgTile *d_qg_tiles = nullptr;
   uint32_t n_out = 0;            // width of the launch output space
+  // epilogue completions of one launch: one per chunk (its last arriving
+  // CTA), each leaving one sum-of-squares partial (residual launches) and
+  // one `done` count
+  uint32_t parts() const { return (uint32_t)chunks.size(); }
 };
 
 struct LayerW {
