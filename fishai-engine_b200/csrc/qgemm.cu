@@ -173,8 +173,8 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
         const uint32_t bit = 12 * (f0 + b);
         const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
                                       : (h.w >> (bit - 64));
-        sa[j][b] = d * (float)(fld & 63u);
-        sb[j][b] = dm * (float)((fld >> 6) & 63u);
+        sa[j][b] = d * u2f_small(fld & 63u);
+        sb[j][b] = dm * u2f_small((fld >> 6) & 63u);
       }
     }
   } else if (T == kQ6_K) {
@@ -218,7 +218,8 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
     if (T == kQ6_K) {  // value = d * sc * (q - 32), sc per (row, 16-column sub-block 4i + t)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float sc = (float)(int8_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]);
+        // the int8 sub-scale s as (s + 128) - 128: exact, without the slow I2F path
+        const float sc = u2f_small((uint32_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]) ^ 0x80u) - 128.0f;
         A[j] = A[j] * sc;
         B[j] = A[j] * 32.0f;
       }
@@ -248,9 +249,12 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
       for (int col = 0; col < 2; ++col) {      // column g then g+8
         const int x0 = 4 * half + 2 * col, x1 = x0 + 1;
         const int j0 = 2 * half, j1 = 2 * half + 1;
-        const float v0 = fmaf(A[j0], (float)e[x0], -B[j0]);
-        const float v1 = fmaf(A[j1], (float)e[x1], -B[j1]);
-        put_pair(a, n + 8 * col, k0 + rr[j0], v0, v1);
+        // codes to floats by the exponent trick (exact, full-rate adds), then
+        // value = A * code - B with one rounding, two lanes per instruction
+        const float2 ef = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | e[x0]), __uint_as_float(0x4B000000u | e[x1])),
+                                     make_float2(-8388608.0f, -8388608.0f));
+        const float2 v = __ffma2_rn(make_float2(A[j0], A[j1]), ef, make_float2(-B[j0], -B[j1]));
+        put_pair(a, n + 8 * col, k0 + rr[j0], v.x, v.y);
       }
     }
   }
