@@ -17,8 +17,9 @@
 // reduce-scatter across the lanes leaves every (position, head) total on one
 // lane (a fixed summation tree).  Online softmax per warp and head, PV in
 // registers; the warps merge in a fixed order, the split partial (max, sum,
-// unnormalised o) goes to global memory and the last split CTA of the kv
-// head combines the splits in split order.
+// unnormalised o) goes to global memory; either the consumer combines the
+// splits (the o projection's kProAttn prologue, partials_only) or the last
+// split CTA of the kv head does, in split order.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -267,27 +268,40 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
 #pragma unroll
     for (uint32_t d = 0; d < DPL; ++d) mg[(warp * REP + h) * (HD + 2) + 2 + lane * DPL + d] = o[h][d];
   __syncthreads();
+  // per head: the maximum over the warps and each warp's weight exp(m_w - M)
+  // (0 for a warp that saw no position), once
+  float *ew = sc;                 // [kPW][REP]
+  float *Mh = sc + kPW * REP;     // [REP]
+  if (tid < REP) {
+    float M = -INFINITY;
+#pragma unroll
+    for (uint32_t w = 0; w < kPW; ++w) M = fmaxf(M, mg[(w * REP + tid) * (HD + 2)]);
+#pragma unroll
+    for (uint32_t w = 0; w < kPW; ++w) {
+      const float mw = mg[(w * REP + tid) * (HD + 2)];
+      ew[w * REP + tid] = mw == -INFINITY ? 0.0f : expf(mw - M);
+    }
+    Mh[tid] = M;
+  }
+  __syncthreads();
   float *part = p.part;
   for (uint32_t idx = tid; idx < REP * (HD + 2); idx += kPW * 32) {
     const uint32_t r = idx / (HD + 2), c = idx % (HD + 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (uint32_t w = 0; w < kPW; ++w) M = fmaxf(M, mg[(w * REP + r) * (HD + 2)]);
     float out;
     if (c == 0) {
-      out = M;
+      out = Mh[r];
     } else {
       float acc = 0.0f;
 #pragma unroll
       for (uint32_t w = 0; w < kPW; ++w) {
-        const float mw = mg[(w * REP + r) * (HD + 2)];
-        if (mw == -INFINITY) continue;
-        acc = fmaf(mg[(w * REP + r) * (HD + 2) + c], expf(mw - M), acc);
+        const float e = ew[w * REP + r];
+        if (e != 0.0f) acc = fmaf(mg[(w * REP + r) * (HD + 2) + c], e, acc);
       }
       out = acc;
     }
     part[((uint64_t)(kvh * REP + r) * p.splits + split) * (HD + 2) + c] = out;
   }
+  if (p.partials_only) return;  // the o projection's prologue combines the splits
   // the last split CTA of this kv head combines all splits (fixed order)
   __threadfence();
   __syncthreads();

@@ -37,6 +37,8 @@ struct SeqState {
 enum : int {
   kProPlain = 0,    // x = in[k]
   kProRmsNorm = 1,  // x = in[k] * (1/sqrt(sum(ssq)/n + eps)) * norm_w[k]      (src/tensor.rs:280-290)
+  kProAttn = 2,     // x = decode attention output combined from its split partials:
+                    //   x[h*hd + d] = sum_s o_s[d] e_s / sum_s l_s e_s, e_s = exp(m_s - max_s m_s)
 };
 enum : int {
   kEpiStore = 0,    // y[col] = v
@@ -92,6 +94,8 @@ struct GemvParams {
   // epilogue
   int epi;
   float *out;              // store / swiglu / logits / qkv(q part)
+  const float *attn_part;  // kProAttn: [K / attn_hd heads][attn_splits][2 + attn_hd] (max, sum, o)
+  uint32_t attn_splits, attn_hd;
   float *resid;            // kEpiResid
   float *ssq_out;          // kEpiResid: [n_chunks]
   // qkv
@@ -116,6 +120,7 @@ uint32_t gemv_mma_stages(uint32_t stage_bytes, uint32_t max_units, size_t smem_b
 // shared-memory offsets of the GEMV layout: the coefficient tables, and the
 // ring after the x slice of max_units row groups
 uint32_t gemv_mma_table_offset();
+uint32_t gemv_mma_table_words();  // 32-bit words of the table area (kProAttn's head weights live there)
 uint32_t gemv_mma_ring_offset(uint32_t max_units);
 // row groups per pipeline stage for chunks of this type and group size
 uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type);
@@ -133,6 +138,7 @@ struct AttnParams {
   uint32_t *counters;      // [n_kv] arrival counters (zero between launches)
   float *out;              // [H*hd] combined attention output
   SeqState *state;         // T = len + 1
+  int partials_only;       // batch-1 paged kernel: leave the split partials for the consumer (kProAttn)
   const SeqState *row_states;  // batched decode: per query row state (T = len + 1), cache sequence row_seq0 + row
   uint32_t row_seq0;
 };

@@ -64,6 +64,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
 
 uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type) { return stage_groups(gbytes, type); }
 uint32_t gemv_mma_table_offset() { return kOffTbl; }
+uint32_t gemv_mma_table_words() { return kWarps * kTblWords; }
 uint32_t gemv_mma_ring_offset(uint32_t max_units) { return ring_offset(max_units); }
 
 size_t gemv_mma_smem_bytes(const GemvParams &p) {

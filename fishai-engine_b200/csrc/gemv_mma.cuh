@@ -409,10 +409,73 @@ __device__ __forceinline__ uint32_t cta_units(const GemvParams &p, uint32_t cta)
   return end > start ? end - start : 0;
 }
 
+// kProAttn prologue: the CTA's rows of x are decode-attention outputs, made
+// here from the attention's split partials (max m_s, sum l_s, unnormalised
+// o_s per query head and split).  Each warp computes the weights of some
+// heads (lane = split: M = max m_s, e_s = exp(m_s - M), L = sum l_s e_s by a
+// butterfly) into the table area while every thread's split values of its
+// first row are already in flight; then x = (sum_s o_s e_s in split order) /
+// L.  One round trip replaces the attention's own split combine.
+__device__ __forceinline__ void attn_prologue(const GemvParams &p, const Smem &sm, uint32_t start, uint32_t G,
+                                              uint32_t nx, uint32_t tid, uint32_t warp, uint32_t lane) {
+  constexpr uint32_t NT = kWarps * 32, kB = 32;
+  const uint32_t S = p.attn_splits, hd = p.attn_hd, NH = p.K / hd, stride = hd + 2;
+  float *ecoef = reinterpret_cast<float *>(sm.tbl);  // [NH][S], then the sums [NH]
+  float *lsum = ecoef + NH * S;
+  float ov[kB];
+  auto row_of = [&](uint32_t i) { return 16 * ((start + i / 16) % G) + (i & 15); };
+  auto load = [&](uint32_t k, uint32_t s0) {
+    const float *P = p.attn_part + (size_t)(k / hd) * S * stride + 2 + k % hd;
+#pragma unroll
+    for (uint32_t s = 0; s < kB; ++s) ov[s] = s0 + s < S ? __ldcg(P + (size_t)(s0 + s) * stride) : 0.0f;
+  };
+  if (tid < nx) load(row_of(tid), 0);
+  for (uint32_t h = warp; h < NH; h += kWarps) {
+    const float *P = p.attn_part + (size_t)h * S * stride;
+    float mv[2], lv[2];
+#pragma unroll
+    for (uint32_t j = 0; j < 2; ++j) {
+      const uint32_t s = lane + 32 * j;
+      mv[j] = s < S ? __ldcg(P + (size_t)s * stride) : -INFINITY;
+      lv[j] = s < S ? __ldcg(P + (size_t)s * stride + 1) : 0.0f;
+    }
+    float M = fmaxf(mv[0], mv[1]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    float Ls = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < 2; ++j) {
+      const uint32_t s = lane + 32 * j;
+      const float e = mv[j] == -INFINITY ? 0.0f : expf(mv[j] - M);
+      if (s < S) ecoef[h * S + s] = e;
+      Ls = fmaf(lv[j], e, Ls);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) Ls += __shfl_xor_sync(0xFFFFFFFFu, Ls, o);
+    if (lane == 0) lsum[h] = Ls;
+  }
+  epi::consumer_bar<kWarps>();
+  for (uint32_t i = tid; i < nx; i += NT) {
+    const uint32_t k = row_of(i), h = k / hd;
+    const float *e = ecoef + h * S;
+    float acc = 0.0f;
+    for (uint32_t s0 = 0; s0 < S; s0 += kB) {
+      if (i != tid || s0) load(k, s0);
+#pragma unroll
+      for (uint32_t s = 0; s < kB; ++s)
+        if (s0 + s < S) acc = fmaf(ov[s], e[s0 + s], acc);
+    }
+    sm.xs[i] = acc / lsum[h];
+  }
+}
+
 // Consumers (kWarps warps): the CTA's rows of x (normalised when the launch
 // has an RMSNorm prologue), then its stages; at the end of each chunk segment
 // the partial is published and the last contributing CTA runs the epilogue.
 // slot / phase continue through the ring across launches.
+// ATTN_PRO: the build that can run the kProAttn prologue (the persistent
+// step kernel combines attention itself and leaves it out).
+template <bool ATTN_PRO = true>
 __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const Smem &sm, uint32_t tid,
                                         uint32_t warp, uint32_t lane, uint32_t &slot, uint32_t &phase, bool &ok) {
   if (cta >= p.n_ctas) return;
@@ -426,6 +489,9 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
   // squares partials (one round trip), then normalised once inv is known
   constexpr uint32_t kPre = 8, NT = kWarps * 32;
   const uint32_t nx = n_units * 16;
+  if (ATTN_PRO && p.pro == kProAttn) {
+    attn_prologue(p, sm, start, G, nx, tid, warp, lane);
+  } else {
   float xr[kPre], wr[kPre];
   auto load_batch = [&](uint32_t base) {
 #pragma unroll
@@ -469,6 +535,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
         if (i < nx) sm.xs[i] = norm ? __fmul_rn(__fmul_rn(xr[j], inv), wr[j]) : xr[j];
       }
     }
+  }
   }
   epi::consumer_bar<kWarps>();
   const uint32_t tbl = smem_u32(sm.tbl + warp * kTblWords);

@@ -510,6 +510,20 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
   return launch_gemv(p, pdl, stream) ? fail(FA_ERR_CUDA, "qkv gemv launch failed") : FA_OK;
 }
 
+bool Model::attn_fused(uint32_t l) const {
+  AttnParams ap{};
+  SeqState dummy{};  // the support test only asks that a state exists
+  ap.q_rows = 1;
+  ap.state = &dummy;
+  ap.kv.head_dim = cfg.head_dim;
+  ap.kv.n_kv = cfg.n_kv_heads;
+  ap.n_heads = cfg.n_heads;
+  ap.splits = attn_splits;
+  const GemvPlan &o = layers[l].o;
+  return attn_paged_supported(ap) && o.mma && o.K == cfg.n_heads * cfg.head_dim &&
+         (uint64_t)cfg.n_heads * (attn_splits + 1) <= gemv_mma_table_words();
+}
+
 int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
   AttnParams ap{};
   ap.q = w.q;
@@ -524,6 +538,7 @@ int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t se
   ap.counters = w.attn_cnt;
   ap.out = w.attn_out;
   ap.state = st;
+  ap.partials_only = attn_fused(l) ? 1 : 0;
   return launch_attention(ap, pdl, stream) ? fail(FA_ERR_CUDA, "attention launch failed") : FA_OK;
 }
 
@@ -532,6 +547,12 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   GemvParams p = gemv_base(lw.o);
   p.pro = kProPlain;
   p.in = w.attn_out;
+  if (attn_fused(l)) {
+    p.pro = kProAttn;
+    p.attn_part = w.attn_part;
+    p.attn_splits = attn_splits;
+    p.attn_hd = cfg.head_dim;
+  }
   p.epi = kEpiResid;
   p.resid = w.x;
   p.ssq_out = w.ssq_o;

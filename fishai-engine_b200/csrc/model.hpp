@@ -146,6 +146,9 @@ struct Model {
   int enqueue_embed(Workspace &w, SeqState *st);
   int enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
   int enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
+  // layer l's o projection combines the batch-1 attention's split partials
+  // in its prologue (the attention then leaves them uncombined)
+  bool attn_fused(uint32_t l) const;
   int enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump);
   int enqueue_head(Workspace &w, SeqState *st);
   int enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump);

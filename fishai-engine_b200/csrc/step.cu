@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams sp) {
         const GemvParams &p = sp.gemv[ph.idx];
         if (!cta_units(p, blockIdx.x)) continue;
         if (!wait_phase(sp, ph, epoch, sm, tid)) ok = false;
-        consume(p, blockIdx.x, sm, tid, warp, lane, slot, phase, ok);
+        consume<false>(p, blockIdx.x, sm, tid, warp, lane, slot, phase, ok);
       } else {  // attention of layer ph.idx: items (split, kv head) over (CTA, group)
         const uint32_t n_items = sp.attn.splits * sp.attn.kv.n_kv, slots = gridDim.x * sp.attn_groups;
         if (blockIdx.x * sp.attn_groups >= n_items) continue;
