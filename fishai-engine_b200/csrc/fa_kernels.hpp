@@ -217,9 +217,8 @@ struct QgParams {
   uint32_t ldo;
   int epi;                   // kQgStore: Y = X W; kQgResid: Y += X W
   uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
-  float *part;               // split-K partials [splits][T][ldo] (null: no K split)
-  uint64_t part_floats;      // capacity of part
-  uint32_t splits;           // set by launch_qgemm
+  float *part;               // stream-K partial tiles: 2 slots per CTA of 128 x BN floats
+  uint64_t part_floats;      // capacity of part (>= qgemm_part_floats(bn, n_sm))
 };
 struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
   alignas(64) unsigned char bytes[128];
@@ -228,6 +227,8 @@ struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_r
 int qgemm_init();
 int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows, uint32_t bn);
 int launch_qgemm(const QgParams &p, const QgXMap &map, uint32_t n_sm, cudaStream_t st);
+// floats of the partial-tile buffer a launch with tiles of bn tokens needs
+uint64_t qgemm_part_floats(uint32_t bn, uint32_t n_sm);
 
 // ---- token-parallel forward pieces (prefill.cu) ----
 struct AttnRowsParams {

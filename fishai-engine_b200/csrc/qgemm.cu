@@ -6,8 +6,8 @@
 // f16 operands (11 mantissa bits: 8x less rounding than bf16 at the same
 // tensor throughput; the activation producers flag values beyond the f16
 // range), f32 accumulation in tensor memory:
-//   A = W^T tile: 128 weight columns x 64 rows, dequantised by 8 producer
-//       warps from the packed codes straight into the K-major 128-byte
+//   A = W^T tile: 128 weight columns x 64 rows, dequantised by 16 producer
+//       warps (one 16-row x 32-column block each) from the packed codes straight into the K-major 128-byte
 //       swizzled shared-memory layout the MMA reads (d*sc*q - dmin*m etc. in
 //       f32, rounded once to f16)
 //   B = X tile: BN tokens x 64 rows of f16 activations, loaded by a TMA
@@ -15,10 +15,10 @@
 //   D = 128 x BN f32 accumulator in TMEM (two buffers: the epilogue of one
 //       tile overlaps the MMAs of the next)
 // Roles per CTA (one persistent CTA per SM): warp 0 TMA for X, warp 1 MMA
-// issue (one elected lane) and TMEM owner, warps 2-9 dequantisation, warps
-// 10-13 epilogue (tcgen05.ld, optional residual add, f32 stores).  Output
-// tiles that cannot fill the SMs split K; the split partials are summed in a
-// fixed order by a second kernel.
+// issue (one elected lane) and TMEM owner, warps 2-17 dequantisation, warps
+// 18-21 epilogue (tcgen05.ld, optional residual add, f32 stores).  Work is
+// split stream-K (below); the pieces of tiles split between CTAs are summed
+// in a fixed order by a second kernel.
 // Every mbarrier wait is bounded; on expiry the CTA raises p.err, the other
 // roles stop at their next wait, the MMA warp drains its last commit and the
 // tensor memory is always released.
@@ -36,9 +36,9 @@ namespace fa {
 namespace {
 
 constexpr uint32_t kBM = 128, kBK = 64;          // weight columns (MMA M) and rows per k-step
-constexpr uint32_t kDeq = 8;                     // dequant warps: one (16-row group, 64-column slice) each
+constexpr uint32_t kDeq = 16;                    // dequant warps: one (16-row group, 32-column block) each
 constexpr uint32_t kEpi0 = 2 + kDeq;             // first epilogue warp
-constexpr uint32_t kQThreads = (kEpi0 + 4) * 32; // 448
+constexpr uint32_t kQThreads = (kEpi0 + 4) * 32; // 704
 constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB
 
 template <uint32_t BN>
@@ -126,94 +126,109 @@ __device__ __forceinline__ bool qwait_warp(uint64_t *bar, uint32_t parity, QBars
   return __all_sync(0xFFFFFFFFu, qwait(bar, parity, b));
 }
 
-// One (16-row group, 64-column slice) unit of the A tile: lane l = 4g + c
-// owns, per 16x16 tile t, the weight columns g and g+8 and the rows 2c,
+// Q4_K unit of one warp of a pair: all four tiles of the 64-column slice i,
+// rows 2c, 2c+1 (th = 0) or 2c+8, 2c+9 (th = 1) of lane l = 4g + c, so each
+// warp reads the scale headers of its own two rows only.
+__device__ __forceinline__ void deq_unit_q4k_rows(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th,
+                                                  uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3;
+  const uint4 qv = ldg128(G + 512 * i + 16 * lane);  // Q4_K slices are whole (4 tiles): one word per tile
+  const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
+  const uint32_t r0 = 2 * c + 8 * th, s = i >> 2, f0 = 2 * (i & 3);
+  float sa[2][2], sb[2][2];  // [row][32-column block]
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const uint4 h = ldg128(G + 8 * w + (16 * s + r0 + jj) * 16);
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t bit = 12 * (f0 + b);
+      const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
+                                    : (h.w >> (bit - 64));
+      sa[jj][b] = d * u2f_small(fld & 63u);
+      sb[jj][b] = dm * u2f_small((fld >> 6) & 63u);
+    }
+  }
+#pragma unroll
+  for (uint32_t t = 0; t < 4; ++t) {
+    const uint32_t b = t >> 1, W = q[t] >> (8 * th);  // this row half's codes in nibbles 0, 4, 1, 5 of W
+    const uint32_t n = n0 + 16 * t + g;
+#pragma unroll
+    for (int col = 0; col < 2; ++col) {  // column g then g+8
+      const uint32_t e0 = (W >> (4 * col)) & 0xFu, e1 = (W >> (16 + 4 * col)) & 0xFu;
+      const float2 ef = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | e0), __uint_as_float(0x4B000000u | e1)),
+                                   make_float2(-8388608.0f, -8388608.0f));
+      const float2 v = __ffma2_rn(make_float2(sa[0][b], sa[1][b]), ef, make_float2(-sb[0][b], -sb[1][b]));
+      put_pair(a, n + 8 * col, k0 + r0, v.x, v.y);
+    }
+  }
+}
+
+// One (16-row group, 32-column block) unit of the A tile: block th (0 or 1)
+// of the 64-column slice i.  Lane l = 4g + c owns, per 16x16 tile t of the
+// block (t = 2th, 2th + 1), the weight columns g and g+8 and the rows 2c,
 // 2c+1, 2c+8, 2c+9 of the group (the mma.sync fragment order the layout
-// stores).  `rows` = group rows at k offset 16*gi of the tile.
+// stores); k0 = the group's first row in the tile.  The caller skips a
+// block past the slice's last tile (2th >= nt).
 template <int T>
-__device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t i, uint32_t lane, uint32_t a,
-                                         uint32_t n0, uint32_t k0) {
+__device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
+                                         uint32_t a, uint32_t n0, uint32_t k0) {
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t nt = min(64u, w - 64 * i) / 16;
   const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-  // code words: Q4 types one u32 per tile, Q8_0 two
-  uint32_t q[8];
+  // code words of the block's two tiles: Q4 types one u32 per tile, Q8_0 two
+  uint32_t q[4];
   if (T == kQ8_0) {
-    const uint8_t *p = G + 1024 * i + 8 * nt * lane;
-    const uint4 v0 = ldg128(p);
-    q[0] = v0.x; q[1] = v0.y; q[2] = v0.z; q[3] = v0.w;
-    if (nt == 4) {
-      const uint4 v1 = ldg128(p + 16);
-      q[4] = v1.x; q[5] = v1.y; q[6] = v1.z; q[7] = v1.w;
-    } else {
-      q[4] = q[5] = q[6] = q[7] = 0u;
-    }
+    const uint4 v = ldg128(G + 1024 * i + 8 * nt * lane + 16 * th);
+    q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
   } else {
-    const uint8_t *p = G + 512 * i + 4 * nt * lane;
-    if (nt == 4) {
-      const uint4 v = ldg128(p);
-      q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
-    } else {
-      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
-      q[0] = v.x; q[1] = v.y; q[2] = q[3] = 0u;
-    }
+    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(G + 512 * i + 4 * nt * lane + 8 * th));
+    q[0] = v.x; q[1] = v.y; q[2] = q[3] = 0u;
   }
-  // per (row, 32-column block) scale and offset: value = A * code - B
-  float sa[4][2], sb[4][2];
+  // per row scale and offset of the block: value = A * code - B
+  float sa[4], sb[4];
   if (T == kQ4_K) {
-    const uint32_t s = i >> 2, f0 = 2 * (i & 3);
+    const uint32_t s = i >> 2, bit = 12 * (2 * (i & 3) + th);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint4 h = ldg128(G + 8 * w + (16 * s + rr[j]) * 16);
       const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
       const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
       const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        const uint32_t bit = 12 * (f0 + b);
-        const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
-                                      : (h.w >> (bit - 64));
-        sa[j][b] = d * u2f_small(fld & 63u);
-        sb[j][b] = dm * u2f_small((fld >> 6) & 63u);
-      }
+      const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
+                                    : (h.w >> (bit - 64));
+      sa[j] = d * u2f_small(fld & 63u);
+      sb[j] = dm * u2f_small((fld >> 6) & 63u);
     }
   } else if (T == kQ6_K) {
     const uint32_t s = i >> 2;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float d = ldg_h(G + 13 * w + (16 * s + rr[j]) * 2);
-      sa[j][0] = d;  // the int8 sub-scale varies per tile: applied below
-      sb[j][0] = 0.0f;
-      sa[j][1] = d;
-      sb[j][1] = 0.0f;
+      sa[j] = ldg_h(G + 13 * w + (16 * s + rr[j]) * 2);  // the int8 sub-scale varies per tile: applied below
+      sb[j] = 0.0f;
     }
   } else {
     const uint32_t dreg = (T == kQ8_0) ? 16 : 8;
     const float off = (T == kQ8_0) ? 128.0f : 8.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        const float d = ldg_h(G + dreg * w + (16 * (2 * i + b) + rr[j]) * 2);
-        sa[j][b] = d;
-        sb[j][b] = d * off;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float d = ldg_h(G + dreg * w + (16 * (2 * i + th) + rr[j]) * 2);
+      sa[j] = d;
+      sb[j] = d * off;
+    }
   }
-  uint32_t hw[2] = {0u, 0u};
-  if (T == kQ6_K) {
-    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(G + 8 * w + 256 * i + 8 * lane));
-    hw[0] = v.x;
-    hw[1] = v.y;
-  }
+  uint32_t hw = 0u;
+  if (T == kQ6_K) hw = __ldg(reinterpret_cast<const uint32_t *>(G + 8 * w + 256 * i + 8 * lane + 4 * th));
 #pragma unroll
-  for (uint32_t t = 0; t < 4; ++t) {
-    if (t >= nt) break;
-    const uint32_t b = t >> 1;
+  for (uint32_t tt = 0; tt < 2; ++tt) {
+    const uint32_t t = 2 * th + tt;
     float A[4], B[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      A[j] = sa[j][b];
-      B[j] = sb[j][b];
+      A[j] = sa[j];
+      B[j] = sb[j];
     }
     if (T == kQ6_K) {  // value = d * sc * (q - 32), sc per (row, 16-column sub-block 4i + t)
 #pragma unroll
@@ -227,15 +242,15 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
     // codes of the 8 fragment elements: (col g | g+8) x (rows 2c, 2c+1 | 2c+8, 2c+9)
     uint32_t e[8];
     if (T == kQ8_0) {
-      const uint32_t P = q[2 * t], Q = q[2 * t + 1];
+      const uint32_t P = q[2 * tt], Q = q[2 * tt + 1];
       e[0] = P & 0xFFu; e[1] = (P >> 16) & 0xFFu; e[2] = (P >> 8) & 0xFFu; e[3] = P >> 24;
       e[4] = Q & 0xFFu; e[5] = (Q >> 16) & 0xFFu; e[6] = (Q >> 8) & 0xFFu; e[7] = Q >> 24;
     } else {
-      const uint32_t W = q[t];
+      const uint32_t W = q[tt];
       e[0] = W & 0xFu; e[1] = (W >> 16) & 0xFu; e[2] = (W >> 4) & 0xFu; e[3] = (W >> 20) & 0xFu;
       e[4] = (W >> 8) & 0xFu; e[5] = (W >> 24) & 0xFu; e[6] = (W >> 12) & 0xFu; e[7] = W >> 28;
       if (T == kQ6_K) {
-        const uint32_t H = hw[b] >> (2 * (t & 1));
+        const uint32_t H = hw >> (2 * tt);
         const uint32_t pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
 #pragma unroll
         for (int x = 0; x < 8; ++x) e[x] |= ((H >> pos[x]) & 3u) << 4;
@@ -260,30 +275,56 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
   }
 }
 
-__device__ __forceinline__ void zero_unit(uint32_t w, uint32_t i, uint32_t lane, uint32_t a, uint32_t n0,
-                                          uint32_t k0) {
-  const uint32_t g = lane >> 2, c = lane & 3, nt = min(64u, w - 64 * i) / 16;
-  for (uint32_t t = 0; t < nt; ++t)
+__device__ __forceinline__ void zero_unit(uint32_t th, uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3;
+  for (uint32_t t = 2 * th; t < 2 * th + 2; ++t)
 #pragma unroll
     for (int half = 0; half < 2; ++half)
 #pragma unroll
       for (int col = 0; col < 2; ++col) put_pair(a, n0 + 16 * t + g + 8 * col, k0 + 2 * c + 8 * half, 0.0f, 0.0f);
 }
 
-// work item wk: K part kp of output tile (nt, tt); k-steps [ks0, ks1)
-struct Work {
-  uint32_t nt, tt, kp, ks0, ks1;
-};
-__device__ __forceinline__ Work work_of(uint32_t wk, uint32_t t_tiles, uint32_t splits, uint32_t ksteps) {
-  Work r;
-  r.kp = wk % splits;
-  const uint32_t rest = wk / splits;
-  r.tt = rest % t_tiles;
-  r.nt = rest / t_tiles;
-  r.ks0 = r.kp * ksteps / splits;
-  r.ks1 = (r.kp + 1) * ksteps / splits;
-  return r;
+// Stream-K work split: the sequence of (output tile, k-step) pairs, tiles in
+// order (token tile fastest) and each tile's k-steps in order, is cut into
+// gridDim.x equal contiguous ranges of at least kMinSk k-steps; CTA c takes
+// [sk_start(c), sk_start(c + 1)).  A range covers whole tiles except possibly
+// a piece of a tile at each end: the pieces go to partial slots 2c (the
+// range's first segment) and 2c + 1 (its last), and k_qg_fixup adds the
+// pieces of each split tile in CTA order.  (Measured against whole tiles in
+// strided waves with only the last wave split: that order shares weight
+// tiles better in L2 but loses more to the partial wave, and pure stream-K
+// gave the faster prefill and batched decode.)
+constexpr uint32_t kMinSk = 8;
+__host__ __device__ __forceinline__ uint32_t sk_start(uint32_t c, uint64_t W, uint32_t G) {
+  return (uint32_t)((uint64_t)c * W / G);
 }
+struct Seg {
+  uint32_t nt, tt, ks0, ks1;
+  bool first, whole;
+};
+struct SegIter {
+  uint32_t k, end, KS, t_tiles;
+  bool first;
+  __device__ SegIter(uint32_t cta, uint32_t G, uint32_t n_tiles, uint32_t t_tiles_, uint32_t ksteps)
+      : KS(ksteps), t_tiles(t_tiles_), first(true) {
+    const uint64_t W = (uint64_t)n_tiles * t_tiles_ * ksteps;
+    k = sk_start(cta, W, G);
+    end = sk_start(cta + 1, W, G);
+  }
+  __device__ bool next(Seg &sg) {
+    if (k >= end) return false;
+    const uint32_t x = k / KS;
+    sg.tt = x % t_tiles;
+    sg.nt = x / t_tiles;
+    sg.ks0 = k % KS;
+    sg.ks1 = min(KS, sg.ks0 + (end - k));
+    sg.whole = sg.ks0 == 0 && sg.ks1 == KS;
+    sg.first = first;
+    first = false;
+    k += sg.ks1 - sg.ks0;
+    return true;
+  }
+};
 
 template <uint32_t BN>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
@@ -295,7 +336,6 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
   QBars &b = *reinterpret_cast<QBars *>(base + C::kBarOff);
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t G16 = p.K / 16, ksteps = (G16 + 3) / 4, t_tiles = (p.T + BN - 1) / BN;
-  const uint32_t splits = p.splits ? p.splits : 1, n_work = p.n_tiles * t_tiles * splits;
   if (tid == 0) {
     for (uint32_t s = 0; s < C::kStages; ++s) {
       mbar_init(&b.full_a[s], kDeq);
@@ -324,10 +364,11 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- X tiles by TMA ----
     if (lane == 0) {
       uint32_t s = 0, ph = 1, pending = 0, last_ph = 0;  // pending: stages with a load issued (bit mask)
-      for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
-        const Work wo = work_of(wk, t_tiles, splits, ksteps);
-        const uint32_t tt = wo.tt;
-        for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
+      SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
+      Seg sg;
+      while (it.next(sg)) {
+        const uint32_t tt = sg.tt;
+        for (uint32_t ks = sg.ks0; ks < sg.ks1; ++ks) {
           if (!qwait(&b.empty[s], ph, b)) goto tma_out;
           mbar_arrive_expect_tx(&b.full_b[s], C::kBTile);
           tma_load_2d(base + s * C::kStage + kATile, &xmap, (int32_t)(ks * kBK), (int32_t)(tt * BN), &b.full_b[s]);
@@ -349,8 +390,9 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- MMA issue ----
     uint32_t s = 0, ph = 0, acc = 0, aph = 1;
     bool issued = false;
-    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
-      const Work wo = work_of(wk, t_tiles, splits, ksteps);
+    SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
+    Seg wo;
+    while (it.next(wo)) {
       if (!qwait_warp(&b.acc_empty[acc], aph, b)) break;
       tc_fence_after();
       const uint32_t dt = tmem + acc * BN;
@@ -390,15 +432,17 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       if (!mbar_wait_sleep(&b.done, 0)) atomicExch(&b.abort, 1u);
     }
   } else if (warp < kEpi0) {
-    // ---- dequantisation: unit (group gi, slice si) of every stage ----
-    const uint32_t d = warp - 2, gi = d >> 1, si = d & 1;
+    // ---- dequantisation: unit (group gi, slice si, block th) of every stage ----
+    const uint32_t d = warp - 2, gi = d >> 2, si = (d >> 1) & 1, th = d & 1;
     uint32_t s = 0, ph = 1;
-    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
-      const Work wo = work_of(wk, t_tiles, splits, ksteps);
+    SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
+    Seg wo;
+    while (it.next(wo)) {
       const QgTile tl = p.tiles[wo.nt];
       const ChunkDesc cd = p.chunks[tl.chunk];
       const uint32_t i = tl.col0 / 64 + si, n0 = 64 * si;
-      const bool active = n0 < tl.ncols;
+      // the block exists: inside the tile's columns and the slice's tiles
+      const bool active = n0 < tl.ncols && 2 * th < min(64u, cd.width - 64 * i) / 16;
       bool ok = true;
       for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
         const uint32_t grp = 4 * ks + gi;
@@ -411,13 +455,13 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           if (grp < G16) {
             const uint8_t *G = p.w + cd.offset + (uint64_t)grp * cd.gbytes;
             switch (cd.type) {
-              case kQ4_K: deq_unit<kQ4_K>(G, cd.width, i, lane, a, n0, 16 * gi); break;
-              case kQ6_K: deq_unit<kQ6_K>(G, cd.width, i, lane, a, n0, 16 * gi); break;
-              case kQ8_0: deq_unit<kQ8_0>(G, cd.width, i, lane, a, n0, 16 * gi); break;
-              default: deq_unit<kQ4_0>(G, cd.width, i, lane, a, n0, 16 * gi); break;
+              case kQ4_K: deq_unit_q4k_rows(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+              case kQ6_K: deq_unit<kQ6_K>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+              case kQ8_0: deq_unit<kQ8_0>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+              default: deq_unit<kQ4_0>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
             }
           } else {
-            zero_unit(cd.width, i, lane, a, n0, 16 * gi);
+            zero_unit(th, lane, a, n0, 16 * gi);
           }
         }
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
@@ -434,15 +478,18 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- epilogue warpgroup: TMEM lanes 32*(warp%4) .. +32 ----
     const uint32_t q4 = warp & 3, m = 32 * q4 + lane;
     uint32_t acc = 0, aph = 0;
-    for (uint32_t wk = blockIdx.x; wk < n_work; wk += gridDim.x) {
+    SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
+    Seg wo;
+    while (it.next(wo)) {
       if (!qwait_warp(&b.acc_full[acc], aph, b)) break;
       tc_fence_after();
-      const Work wo = work_of(wk, t_tiles, splits, ksteps);
       const QgTile tl = p.tiles[wo.nt];
       const uint32_t t0 = wo.tt * BN, col_out = p.chunks[tl.chunk].out_col + tl.col0;
       const bool mine = m < tl.ncols;
-      float *dst = splits > 1 ? p.part + (size_t)wo.kp * p.T * p.ldo : p.out;
-      const bool add = splits == 1 && p.epi == kQgResid;
+      // a whole tile goes to the output; a piece of a split tile to the
+      // CTA's partial slot ([token][column] within the tile)
+      const bool add = wo.whole && p.epi == kQgResid;
+      float *slot = p.part + (size_t)(2 * blockIdx.x + (wo.first ? 0 : 1)) * kBM * BN;
       for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((32 * q4) << 16) + acc * BN + c0, v);
@@ -451,7 +498,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           for (int j = 0; j < 32; ++j) {
             const uint32_t t = t0 + c0 + j;
             if (t < p.T) {
-              float *o = dst + (size_t)t * p.ldo + col_out + m;
+              float *o = wo.whole ? p.out + (size_t)t * p.ldo + col_out + m : slot + (size_t)(c0 + j) * kBM + m;
               const float y = __uint_as_float(v[j]);
               if (add) *o += y;
               else *o = y;
@@ -476,13 +523,49 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
   }
 }
 
-// split partials summed in a fixed order: out (=|+=) sum_s part[s]
-__global__ void k_qg_reduce(const float *part, uint32_t splits, uint64_t n, float *out, int resid) {
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-    float v = resid ? out[i] : 0.0f;
-    for (uint32_t s = 0; s < splits; ++s) v += part[(size_t)s * n + i];
-    out[i] = v;
+// Stream-K fixup: blocks (b - 1, y) look at the range boundary sk_start(b);
+// the first boundary inside a tile adds that tile's pieces (the CTA that
+// reached into it from its start or earlier, then each CTA starting inside
+// it) in CTA order and writes (or, for a residual launch, adds) the output.
+constexpr uint32_t kFixupSlots = 512;  // pieces of one tile: at most k-steps per tile + 1 (the host checks)
+
+__global__ void k_qg_fixup(const QgParams p, uint32_t BN, uint32_t G) {
+  const uint32_t KS = (p.K / 16 + 3) / 4, t_tiles = (p.T + BN - 1) / BN;
+  const uint64_t W = (uint64_t)p.n_tiles * t_tiles * KS;
+  const uint32_t bnd = blockIdx.x + 1;  // blockIdx.y: which 1024 elements of the tile
+  auto kstart = [&](uint32_t c) { return (uint64_t)sk_start(c, W, G); };
+  const uint64_t kb = kstart(bnd);
+  if (kb % KS == 0) return;  // a tile edge: no tile is split here
+  const uint32_t x = (uint32_t)(kb / KS);
+  const uint64_t x0 = (uint64_t)x * KS;
+  if (kstart(bnd - 1) > x0) return;  // an earlier boundary inside this tile does it
+  const uint32_t tt = x % t_tiles, nt = x / t_tiles;
+  const QgTile tl = p.tiles[nt];
+  const uint32_t col_out = p.chunks[tl.chunk].out_col + tl.col0;
+  // the pieces' slots, in CTA order, once per block
+  __shared__ uint32_t slots[kFixupSlots];
+  __shared__ uint32_t n_slots;
+  if (threadIdx.x == 0) {
+    uint32_t n = 0;
+    slots[n++] = 2 * (bnd - 1) + (kstart(bnd - 1) < x0 ? 1 : 0);
+    for (uint32_t c = bnd; c < G && kstart(c) < x0 + KS && n < kFixupSlots; ++c) slots[n++] = 2 * c;
+    n_slots = n;
   }
+  __syncthreads();
+  const uint32_t n = n_slots;
+  // this block's 1024 elements of the tile, four consecutive columns per thread
+  const uint32_t idx = blockIdx.y * 1024 + 4 * threadIdx.x, t = idx / kBM, m = idx % kBM;
+  if (idx >= BN * kBM || m >= tl.ncols || tt * BN + t >= p.T) return;
+  float4 *o = reinterpret_cast<float4 *>(p.out + (size_t)(tt * BN + t) * p.ldo + col_out + m);
+  float4 v = p.epi == kQgResid ? *o : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (uint32_t j = 0; j < n; ++j) {
+    const float4 a = __ldcg(reinterpret_cast<const float4 *>(p.part + (size_t)slots[j] * kBM * BN + idx));
+    v.x += a.x;
+    v.y += a.y;
+    v.z += a.z;
+    v.w += a.w;
+  }
+  *o = v;
 }
 
 template <uint32_t BN>
@@ -529,32 +612,23 @@ int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows,
   return r == CUDA_SUCCESS ? 0 : -1;
 }
 
-// K splits when the output tiles leave SMs idle and the partials fit in p.part
-uint32_t qgemm_splits(const QgParams &p, uint32_t bn, uint32_t n_sm) {
-  const uint32_t t_tiles = (p.T + bn - 1) / bn, tiles = p.n_tiles * t_tiles, ksteps = (p.K / 16 + 3) / 4;
-  if (!p.part || tiles >= n_sm) return 1;
-  uint32_t s = std::min<uint32_t>((n_sm + tiles - 1) / tiles, std::max<uint32_t>(1, ksteps / 4));
-  while (s > 1 && (uint64_t)s * p.T * p.ldo > p.part_floats) --s;
-  return s;
-}
+uint64_t qgemm_part_floats(uint32_t bn, uint32_t n_sm) { return (uint64_t)2 * n_sm * kBM * bn; }
 
 int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
-  if (!p0.T || !p0.n_tiles || p0.K % 16 || !p0.w || !p0.out) return -1;
-  QgParams p = p0;
-  p.splits = qgemm_splits(p0, map.bn, n_sm);
-  const uint32_t t_tiles = (p.T + map.bn - 1) / map.bn;
-  const uint32_t work = p.n_tiles * t_tiles * p.splits, grid = work < n_sm ? work : n_sm;
+  if (!p0.T || !p0.n_tiles || p0.K % 16 || !p0.w || !p0.out || p0.ldo % 4) return -1;  // fixup: float4 rows
+  const uint32_t t_tiles = (p0.T + map.bn - 1) / map.bn, ksteps = (p0.K / 16 + 3) / 4;
+  const uint64_t W = (uint64_t)p0.n_tiles * t_tiles * ksteps;
+  const uint32_t grid = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(n_sm, W / kMinSk));
+  if (!p0.part || p0.part_floats < qgemm_part_floats(map.bn, grid) || ksteps + 1 > kFixupSlots) return -1;
   int rc;
   switch (map.bn) {
-    case 64: rc = launch_bn<64>(p, map.bytes, grid, st); break;
-    case 128: rc = launch_bn<128>(p, map.bytes, grid, st); break;
-    case 256: rc = launch_bn<256>(p, map.bytes, grid, st); break;
+    case 64: rc = launch_bn<64>(p0, map.bytes, grid, st); break;
+    case 128: rc = launch_bn<128>(p0, map.bytes, grid, st); break;
+    case 256: rc = launch_bn<256>(p0, map.bytes, grid, st); break;
     default: return -1;
   }
-  if (rc || p.splits == 1) return rc;
-  const uint64_t n = (uint64_t)p.T * p.ldo;
-  k_qg_reduce<<<(unsigned)std::min<uint64_t>((n + 255) / 256, 4096), 256, 0, st>>>(p.part, p.splits, n, p.out,
-                                                                                     p.epi == kQgResid);
+  if (rc || grid < 2) return rc;
+  k_qg_fixup<<<dim3(grid - 1, map.bn * kBM / 1024), 256, 0, st>>>(p0, map.bn, grid);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
