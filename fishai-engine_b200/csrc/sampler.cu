@@ -108,7 +108,7 @@ struct SortedTerm {  // p[index of rank i] / total
 // after it with the new binade.  The walk mode runs the reference's
 // categorical draw r(i+1) = fl(r(i) - p(i)) the same way, downwards.
 enum : int { kSeqSum = 0, kSeqStop = 1, kSeqWalk = 2 };
-constexpr uint32_t kSeqPer = 8;  // terms per thread per tile
+constexpr uint32_t kSeqPer = 8;  // terms per thread per tile (after the first tile)
 
 // q = rn(t / g) for g = 2^(ue - 150) (ue = max(biased exponent, 1) of the
 // accumulator), t finite and >= 0; tie: t / g is exactly halfway
@@ -135,15 +135,17 @@ struct SeqOut {
 // the terms in order, ended at the first i where r <= 0.
 template <int MODE, class Term>
 __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &sm) {
-  constexpr uint32_t TILE = kST * kSeqPer;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float s = s0;
   uint32_t par = 0;
-  for (uint32_t t0 = 0; t0 < n; t0 += TILE) {
-    const uint32_t tend = min(n, t0 + TILE), j0 = t0 + tid * kSeqPer;
+  // the first tile holds one term per thread: early on the running sum is
+  // small against the terms, so binade crossings and ties (each a rescan of
+  // the rest of its tile) are frequent there and cheap in a short tile
+  for (uint32_t t0 = 0, per = 1; t0 < n; t0 += kST * per, per = kSeqPer) {
+    const uint32_t tend = min(n, t0 + kST * per), j0 = t0 + tid * per;
     float x[kSeqPer];
 #pragma unroll
-    for (uint32_t e = 0; e < kSeqPer; ++e) x[e] = j0 + e < tend ? term(j0 + e) : 0.0f;
+    for (uint32_t e = 0; e < kSeqPer; ++e) x[e] = e < per && j0 + e < tend ? term(j0 + e) : 0.0f;
     uint32_t i = t0;
     while (i < tend) {
       const uint32_t sb = __float_as_uint(s);
@@ -167,7 +169,7 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
 #pragma unroll
       for (uint32_t e = 0; e < kSeqPer; ++e) {
         const uint32_t j = j0 + e, tb = __float_as_uint(x[e]);
-        const bool valid = j >= i && j < tend;
+        const bool valid = e < per && j >= i && j < tend;
         q[e] = 0u;
         st[e] = false;
         if (valid) {
@@ -210,7 +212,7 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
       for (uint32_t e = 0; e < kSeqPer; ++e) {
         const unsigned long long Qi = Q + q[e];
         bool stp = st[e];
-        if (kind == 0 && !stp && (j0 + e) >= i && (j0 + e) < tend) {
+        if (kind == 0 && !stp && e < per && (j0 + e) >= i && (j0 + e) < tend) {
           stp = Qi >= room;
           if (MODE == kSeqStop && !stp) stp = __uint_as_float(sb + (uint32_t)Qi) > stop;
         }
@@ -358,6 +360,7 @@ __device__ void select_top_k(const float *pr, uint32_t n, uint32_t k, SSmem &sm)
       const uint32_t i = base + lane;
       const uint32_t key = i < n ? float_key(__ldcg(pr + i)) : 0u;
       const bool in = i < n && (key & mask) == prefix;
+      if (!__any_sync(kFull, in)) continue;  // after the first pass most warps hold no candidate
       const uint32_t b = (key >> (8 * d)) & 255u;
       const uint32_t peers = __match_any_sync(kFull, in ? b : 256u + lane);
       if (in && lane == (uint32_t)(__ffs(peers) - 1)) sm.whist[warp][b] += __popc(peers);
