@@ -93,6 +93,31 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // Programmatic dependent launch (no-ops when the launch has no PDL attribute).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+// first statement of a kernel launched by launch_pdl: let the next kernel's
+// CTAs be scheduled, then wait for the previous kernels' completion (and
+// their memory) before touching anything they write or read
+__device__ __forceinline__ void pdl_enter() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
+
+// Launch with programmatic dependent launch: the kernel's CTAs may start
+// while the previous kernel on the stream finishes, so the kernel must call
+// pdl_wait() (pdl_enter()) before it uses memory earlier kernels write or read.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...) == cudaSuccess ? 0 : -1;
+}
 
 // ---- clusters / DSMEM ----
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -25,6 +25,7 @@ namespace {
 
 __global__ void k_embed_rows(const uint8_t *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab,
                              float *x, uint32_t *err) {
+  pdl_enter();
   const uint32_t t = blockIdx.x;
   if (t >= T) return;
   uint32_t id = tok[t];
@@ -51,6 +52,7 @@ __device__ float block_sum(float v, float *red) {
 constexpr float kHalfMax = 65504.0f;
 
 __global__ void k_norm_rows_h(const float *x, const float *w, float eps, uint32_t d, __half *out, uint32_t *err) {
+  pdl_enter();
   __shared__ float red[32];
   const float *r = x + (size_t)blockIdx.x * d;
   float s = 0.0f;
@@ -70,6 +72,7 @@ __global__ void k_norm_rows_h(const float *x, const float *w, float eps, uint32_
 __global__ void k_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                uint32_t rope_max, uint32_t pos0, uint32_t len0, KvView kv, uint32_t seq, uint32_t layer,
                                __half *qh, uint32_t *err) {
+  pdl_enter();
   const uint32_t t = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
   const float *row = qkv + (size_t)t * (qd + 2 * kd);
   const uint32_t pos = pos0 + t, slot = len0 + t;
@@ -159,6 +162,7 @@ template <uint32_t HD, bool F16>
 __global__ void __launch_bounds__(128) k_attn_causal(const __half *qh, uint32_t T, uint32_t Hq, uint32_t Hkv,
                                                      uint32_t len0, KvView kv, uint32_t seq, uint32_t layer,
                                                      float scale_log2, __half *out) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t asm_raw[];
   constexpr uint32_t RB = HD * 2, KT = HD / 16, NT = kAK / 8, OT = HD / 8;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
@@ -318,6 +322,7 @@ __device__ __forceinline__ void stage_rows(const KvView &kv, uint64_t lbase, con
 
 template <uint32_t HD, bool F16, uint32_t REP>
 __global__ void __launch_bounds__(128) k_attn_decode_rows(const AttnParams p, float scale_log2) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t dsm[];
   constexpr uint32_t RB = HD * 2, KT = HD / 16, NT = kDT / 8, OT = HD / 8, W = 2 + HD;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
@@ -487,6 +492,7 @@ __global__ void __launch_bounds__(128) k_attn_decode_rows(const AttnParams p, fl
 // gate/up launch space: chunk c (width w_c) holds gate f in [c*CW/2, +w_c/2)
 // at c*CW + local, then the same up columns
 __global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
+  pdl_enter();
   const uint32_t t = blockIdx.y, f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= F) return;
   const uint32_t c = f / (CW / 2), local = f - c * (CW / 2), wc = min(CW, 2 * F - c * CW);
@@ -499,6 +505,7 @@ __global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *
 
 // last token's row -> x, its sum of squares -> ssq[0] (the rest zero)
 __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq) {
+  pdl_enter();
   __shared__ float red[32];
   float s = 0.0f;
   for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
@@ -514,6 +521,7 @@ __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, f
 __global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                 uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
                                 float *qf, uint32_t *err) {
+  pdl_enter();
   const uint32_t r = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
   const float *row = qkv + (size_t)r * (qd + 2 * kd);
   const uint32_t pos = st[r].pos, slot = st[r].len;
@@ -545,6 +553,7 @@ __global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uin
 }
 
 __global__ void k_to_half(const float *x, uint64_t n, __half *y, uint32_t *err) {
+  pdl_enter();
   bool bad = false;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
     bad |= !(fabsf(x[i]) <= kHalfMax);
@@ -557,6 +566,7 @@ __global__ void k_to_half(const float *x, uint64_t n, __half *y, uint32_t *err) 
 // step's input tokens) go to the history
 __global__ void k_batch_step_end(SeqState *st, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
                                  uint32_t *step) {
+  pdl_enter();
   const uint32_t s = *step;
   for (uint32_t r = threadIdx.x; r < b; r += blockDim.x) {
     st[r].pos += 1;
@@ -571,9 +581,8 @@ template <uint32_t HD, bool F16>
 int launch_attn_hd(const AttnRowsParams &p, cudaStream_t st) {
   const uint32_t smem = 2 * kAK * HD * 2;  // K and V tiles: 32 KB at head_dim 128
   const dim3 grid((p.T + kAQ - 1) / kAQ, p.Hq);
-  k_attn_causal<HD, F16><<<grid, 128, smem, st>>>((const __half *)p.qh, p.T, p.Hq, p.Hkv, p.len0, p.kv, p.seq,
-                                                  p.layer, p.scale_log2, (__half *)p.out);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_attn_causal<HD, F16>, grid, dim3(128), smem, st, (const __half *)p.qh, p.T, p.Hq, p.Hkv,
+                    p.len0, p.kv, p.seq, p.layer, p.scale_log2, (__half *)p.out);
 }
 
 }  // namespace
@@ -618,24 +627,32 @@ int launch_attn_decode_rows(const AttnParams &p, cudaStream_t st) {
   const float scale_log2 = p.scale * 1.4426950408889634f;
   void *args[] = {(void *)&p, (void *)&scale_log2};
   const dim3 grid(p.splits, p.kv.n_kv, p.q_rows);
-  return cudaLaunchKernel(fn, grid, dim3(128), args, (size_t)4 * 2 * kDT * hd * 2, st) == cudaSuccess ? 0 : -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = (size_t)4 * 2 * kDT * hd * 2;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? 0 : -1;
 }
 
 int launch_embed_rows(const void *emb, int type, const uint32_t *tok, uint32_t T, uint32_t d, uint32_t vocab, float *x,
                       uint32_t *err, cudaStream_t st) {
-  k_embed_rows<<<T, 256, 0, st>>>((const uint8_t *)emb, type, tok, T, d, vocab, x, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_embed_rows, dim3(T), dim3(256), 0, st, (const uint8_t *)emb, type, tok, T, d, vocab, x, err);
 }
 int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, uint32_t d, void *out, uint32_t *err,
                        cudaStream_t st) {
-  k_norm_rows_h<<<T, 256, 0, st>>>(x, w, eps, d, (__half *)out, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_norm_rows_h, dim3(T), dim3(256), 0, st, x, w, eps, d, (__half *)out, err);
 }
 int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                         uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
                         void *qh, uint32_t *err, cudaStream_t st) {
-  k_rope_kv_rows<<<T, 256, 0, st>>>(qkv, T, Hq, Hkv, hd, rope, rope_max, pos0, len0, kv, seq, layer, (__half *)qh, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_rope_kv_rows, dim3(T), dim3(256), 0, st, qkv, T, Hq, Hkv, hd, rope, rope_max, pos0, len0, kv, seq,
+                    layer, (__half *)qh, err);
 }
 int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
   if (p.Hq % p.Hkv) return -1;
@@ -644,28 +661,24 @@ int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
   return -1;
 }
 int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
-  k_swiglu_rows<<<dim3((F + 255) / 256, T), 256, 0, st>>>(gu, F, CW, (__half *)h, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
 }
 int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st) {
-  k_rope_kv_batch<<<b, 256, 0, st>>>(qkv, Hq, Hkv, hd, rope, rope_max, states, kv, seq0, layer, qf, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_rope_kv_batch, dim3(b), dim3(256), 0, st, qkv, Hq, Hkv, hd, rope, rope_max, states, kv, seq0, layer,
+                    qf, err);
 }
 int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st) {
   const uint32_t grid = (uint32_t)std::min<uint64_t>((n + 255) / 256, 4096);
-  k_to_half<<<grid ? grid : 1, 256, 0, st>>>(x, n, (__half *)y, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_to_half, dim3(grid ? grid : 1), dim3(256), 0, st, x, n, (__half *)y, err);
 }
 int launch_batch_step_end(SeqState *states, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
                           uint32_t *step, cudaStream_t st) {
-  k_batch_step_end<<<1, 256, 0, st>>>(states, b, ids, hist, max_steps, step);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_batch_step_end, dim3(1), dim3(256), 0, st, states, b, ids, hist, max_steps, step);
 }
 int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st) {
-  k_last_row<<<1, 256, 0, st>>>(X, row, d, x, ssq, n_ssq);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_last_row, dim3(1), dim3(256), 0, st, X, row, d, x, ssq, n_ssq);
 }
 
 }  // namespace fa

@@ -359,9 +359,14 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = b.tmem;
+  // programmatic dependent launch: the weight dequantisation (static data)
+  // may start while the previous kernel finishes; the X loads and the output
+  // stores wait for it (warp 0 and the epilogue warps call pdl_wait)
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ---- X tiles by TMA ----
+    pdl_wait();
     if (lane == 0) {
       uint32_t s = 0, ph = 1, pending = 0, last_ph = 0;  // pending: stages with a load issued (bit mask)
       SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
@@ -478,6 +483,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- epilogue warpgroup: TMEM lanes 32*(warp%4) .. +32 ----
     const uint32_t q4 = warp & 3, m = 32 * q4 + lane;
     uint32_t acc = 0, aph = 0;
+    pdl_wait();
     SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
     Seg wo;
     while (it.next(wo)) {
@@ -530,6 +536,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
 constexpr uint32_t kFixupSlots = 512;  // pieces of one tile: at most k-steps per tile + 1 (the host checks)
 
 __global__ void k_qg_fixup(const QgParams p, uint32_t BN, uint32_t G) {
+  pdl_enter();
   const uint32_t KS = (p.K / 16 + 3) / 4, t_tiles = (p.T + BN - 1) / BN;
   const uint64_t W = (uint64_t)p.n_tiles * t_tiles * KS;
   const uint32_t bnd = blockIdx.x + 1;  // blockIdx.y: which 1024 elements of the tile
@@ -571,8 +578,7 @@ __global__ void k_qg_fixup(const QgParams p, uint32_t BN, uint32_t G) {
 template <uint32_t BN>
 int launch_bn(const QgParams &p, const void *tmap, uint32_t grid, cudaStream_t st) {
   const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(tmap);
-  k_qgemm<BN><<<grid, kQThreads, QCfg<BN>::kSmem, st>>>(p, *m);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_qgemm<BN>, dim3(grid), dim3(kQThreads), QCfg<BN>::kSmem, st, p, *m);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -628,8 +634,7 @@ int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStrea
     default: return -1;
   }
   if (rc || grid < 2) return rc;
-  k_qg_fixup<<<dim3(grid - 1, map.bn * kBM / 1024), 256, 0, st>>>(p0, map.bn, grid);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_qg_fixup, dim3(grid - 1, map.bn * kBM / 1024), dim3(256), 0, st, p0, map.bn, grid);
 }
 
 }  // namespace fa

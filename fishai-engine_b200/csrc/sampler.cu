@@ -432,6 +432,7 @@ __device__ void select_top_k(const float *pr, uint32_t n, uint32_t k, SSmem &sm)
 }
 
 __global__ void __launch_bounds__(kST, 1) k_sample(const SamplerParams p) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SSmem &sm = *reinterpret_cast<SSmem *>(smem_raw);
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -598,8 +599,7 @@ int sampler_init() {
 int launch_sample(const SamplerParams &p, uint32_t rows, cudaStream_t st) {
   if (!rows || !p.n || p.n > p.vocab) return -1;
   if (sample_needs_sort(p) && (!p.keys || p.pow2 < p.n)) return -1;
-  k_sample<<<rows, kST, sizeof(SSmem), st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_sample, dim3(rows), dim3(kST), sizeof(SSmem), st, p);
 }
 
 int launch_sampler_observe(uint32_t *freq, uint32_t vocab, uint32_t seq, uint32_t token, cudaStream_t st) {
