@@ -52,7 +52,9 @@ struct SSmem {
   unsigned long long tile[kTile];
   float redf[kSW];
   unsigned long long redk[kSW];
-  unsigned long long seq_tot[2][kSW], seq_qex[2][kSW];  // ordered scans (double-buffered)
+  uint32_t seq_tot[2][kSW], seq_qex[2][kSW];  // ordered scans (double-buffered)
+  float seq_s;
+  uint32_t seq_at;
   uint32_t seq_first[2][kSW];
   float seq_t[2][kSW];
   uint32_t wcnt[3][kSW];
@@ -108,7 +110,12 @@ struct SortedTerm {  // p[index of rank i] / total
 // after it with the new binade.  The walk mode runs the reference's
 // categorical draw r(i+1) = fl(r(i) - p(i)) the same way, downwards.
 enum : int { kSeqSum = 0, kSeqStop = 1, kSeqWalk = 2 };
-constexpr uint32_t kSeqPer = 8;  // terms per thread per tile (after the first tile)
+constexpr uint32_t kMlp = 8;     // loads in flight per thread in the streaming passes
+constexpr uint32_t kMlpW = 4;    // warp-wide iterations loaded ahead in the top-k passes
+constexpr uint32_t kSeqPer = 8;
+constexpr uint32_t kSeqSat = 1u << 30;  // saturation of the scan's integer prefixes
+constexpr uint32_t kSeqHead = 2048;     // leading terms one lane adds in order
+__device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min(a + b, kSeqSat); }  // terms per thread per tile (after the first tile)
 
 // q = rn(t / g) for g = 2^(ue - 150) (ue = max(biased exponent, 1) of the
 // accumulator), t finite and >= 0; tie: t / g is exactly halfway
@@ -138,10 +145,35 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float s = s0;
   uint32_t par = 0;
-  // the first tile holds one term per thread: early on the running sum is
-  // small against the terms, so binade crossings and ties (each a rescan of
-  // the rest of its tile) are frequent there and cheap in a short tile
-  for (uint32_t t0 = 0, per = 1; t0 < n; t0 += kST * per, per = kSeqPer) {
+  // The first kSeqHead terms are added in order by one lane from shared
+  // memory: early on the running sum is small against the terms, so binade
+  // crossings and ties (each a rescan of the rest of a tile) come every few
+  // terms there, while a plain f32 chain costs a few cycles per term.
+  const uint32_t hn = min(n, kSeqHead);
+  if (hn) {
+    float *hs = reinterpret_cast<float *>(sm.tile);
+    for (uint32_t i = tid; i < hn; i += kST) hs[i] = term(i);
+    __syncthreads();
+    if (tid == 0) {
+      float r = s0;
+      uint32_t at = n;
+      for (uint32_t i = 0; i < hn; ++i) {
+        r = MODE == kSeqWalk ? __fsub_rn(r, hs[i]) : __fadd_rn(r, hs[i]);
+        if ((MODE == kSeqStop && r > stop) || (MODE == kSeqWalk && r <= 0.0f)) {
+          at = i;
+          break;
+        }
+      }
+      sm.seq_s = r;
+      sm.seq_at = at;
+    }
+    __syncthreads();
+    s = sm.seq_s;
+    const uint32_t at = sm.seq_at;
+    __syncthreads();  // the staging area and seq_s/seq_at are free again
+    if (at != n) return {s, at};
+  }
+  for (uint32_t t0 = hn, per = kSeqPer; t0 < n; t0 += kST * per) {
     const uint32_t tend = min(n, t0 + kST * per), j0 = t0 + tid * per;
     float x[kSeqPer];
 #pragma unroll
@@ -165,7 +197,7 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
       }
       uint32_t q[kSeqPer];
       bool st[kSeqPer];
-      unsigned long long tot = 0;
+      uint32_t tot = 0;
 #pragma unroll
       for (uint32_t e = 0; e < kSeqPer; ++e) {
         const uint32_t j = j0 + e, tb = __float_as_uint(x[e]);
@@ -185,32 +217,37 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
             st[e] = tie;
           }
         }
-        tot += q[e];
+        q[e] = min(q[e], kSeqSat);
+        tot = sat_add(tot, q[e]);
       }
-      // block exclusive prefix of the per-thread totals
-      unsigned long long inc = tot;
+      // block exclusive prefix of the per-thread totals, saturating at
+      // kSeqSat: a saturated prefix is only ever compared with room (< 2^25),
+      // and min(prefix, kSeqSat) keeps every such comparison exact
+      uint32_t inc = tot;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long u = __shfl_up_sync(kFull, inc, o);
-        if ((int)lane >= o) inc += u;
+        const uint32_t u = __shfl_up_sync(kFull, inc, o);
+        if ((int)lane >= o) inc = sat_add(inc, u);
       }
+      const uint32_t t_ex = __shfl_up_sync(kFull, inc, 1);
       if (lane == 31) sm.seq_tot[par][warp] = inc;
       __syncthreads();
-      unsigned long long winc = sm.seq_tot[par][lane];
+      uint32_t winc = sm.seq_tot[par][lane];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long u = __shfl_up_sync(kFull, winc, o);
-        if ((int)lane >= o) winc += u;
+        const uint32_t u = __shfl_up_sync(kFull, winc, o);
+        if ((int)lane >= o) winc = sat_add(winc, u);
       }
-      const unsigned long long block_tot = __shfl_sync(kFull, winc, 31);
-      const unsigned long long wexcl = __shfl_sync(kFull, winc - sm.seq_tot[par][lane], warp);
-      unsigned long long Q = wexcl + inc - tot;  // exclusive prefix at this thread's first term
+      const uint32_t block_tot = __shfl_sync(kFull, winc, 31);
+      const uint32_t w_ex = __shfl_up_sync(kFull, winc, 1);
+      const uint32_t wexcl = __shfl_sync(kFull, lane ? w_ex : 0u, warp);
+      uint32_t Q = sat_add(wexcl, lane ? t_ex : 0u);  // exclusive prefix at this thread's first term
       uint32_t first = ~0u;
-      unsigned long long qex = 0;
+      uint32_t qex = 0;
       float tf = 0.0f;
 #pragma unroll
       for (uint32_t e = 0; e < kSeqPer; ++e) {
-        const unsigned long long Qi = Q + q[e];
+        const uint32_t Qi = sat_add(Q, q[e]);
         bool stp = st[e];
         if (kind == 0 && !stp && e < per && (j0 + e) >= i && (j0 + e) < tend) {
           stp = Qi >= room;
@@ -241,7 +278,7 @@ __device__ SeqOut block_seq(Term term, uint32_t n, float s0, float stop, SSmem &
         i = tend;
       } else {
         const uint32_t w = __ffs(__ballot_sync(kFull, f == fmin)) - 1;
-        const unsigned long long qx = sm.seq_qex[par][w];
+        const uint32_t qx = sm.seq_qex[par][w];
         const float t = sm.seq_t[par][w];
         float base = s;
         if (kind == 0) base = __uint_as_float(MODE == kSeqWalk ? sb - (uint32_t)qx : sb + (uint32_t)qx);
@@ -356,14 +393,22 @@ __device__ void select_top_k(const float *pr, uint32_t n, uint32_t k, SSmem &sm)
   for (int d = 3; d >= 0; --d) {
     for (uint32_t i = tid; i < kSW * 256; i += kST) (&sm.whist[0][0])[i] = 0u;
     __syncthreads();
-    for (uint32_t base = warp * 32; base < n; base += kST) {
-      const uint32_t i = base + lane;
-      const uint32_t key = i < n ? float_key(__ldcg(pr + i)) : 0u;
-      const bool in = i < n && (key & mask) == prefix;
-      if (!__any_sync(kFull, in)) continue;  // after the first pass most warps hold no candidate
-      const uint32_t b = (key >> (8 * d)) & 255u;
-      const uint32_t peers = __match_any_sync(kFull, in ? b : 256u + lane);
-      if (in && lane == (uint32_t)(__ffs(peers) - 1)) sm.whist[warp][b] += __popc(peers);
+    for (uint32_t base0 = warp * 32; base0 < n; base0 += kST * kMlpW) {
+      uint32_t keys[kMlpW];  // kMlpW iterations' loads in flight
+#pragma unroll
+      for (uint32_t u = 0; u < kMlpW; ++u) {
+        const uint32_t i = base0 + u * kST + lane;
+        keys[u] = i < n ? float_key(__ldcg(pr + i)) : 0u;
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < kMlpW; ++u) {
+        const uint32_t i = base0 + u * kST + lane, key = keys[u];
+        const bool in = i < n && (key & mask) == prefix;
+        if (!__any_sync(kFull, in)) continue;  // after the first pass most warps hold no candidate
+        const uint32_t b = (key >> (8 * d)) & 255u;
+        const uint32_t peers = __match_any_sync(kFull, in ? b : 256u + lane);
+        if (in && lane == (uint32_t)(__ffs(peers) - 1)) sm.whist[warp][b] += __popc(peers);
+      }
     }
     __syncthreads();
     if (tid < 256) {
@@ -392,11 +437,19 @@ __device__ void select_top_k(const float *pr, uint32_t n, uint32_t k, SSmem &sm)
   // warp w owns indices [lo, hi): counts of keys above / equal to thr
   const uint32_t R = (n + kST - 1) / kST * 32, lo = min(n, warp * R), hi = min(n, lo + R);
   uint32_t gt = 0, eq = 0;
-  for (uint32_t base = lo; base < hi; base += 32) {
-    const uint32_t i = base + lane;
-    const uint32_t key = i < hi ? float_key(__ldcg(pr + i)) : 0u;
-    gt += __popc(__ballot_sync(kFull, i < hi && key > thr));
-    eq += __popc(__ballot_sync(kFull, i < hi && key == thr));
+  for (uint32_t base0 = lo; base0 < hi; base0 += 32 * kMlpW) {
+    uint32_t keys[kMlpW];
+#pragma unroll
+    for (uint32_t u = 0; u < kMlpW; ++u) {
+      const uint32_t i = base0 + 32 * u + lane;
+      keys[u] = i < hi ? float_key(__ldcg(pr + i)) : 0u;
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < kMlpW; ++u) {
+      const uint32_t i = base0 + 32 * u + lane;
+      gt += __popc(__ballot_sync(kFull, i < hi && keys[u] > thr));
+      eq += __popc(__ballot_sync(kFull, i < hi && keys[u] == thr));
+    }
   }
   if (lane == 0) {
     sm.wcnt[0][warp] = gt;
@@ -413,20 +466,29 @@ __device__ void select_top_k(const float *pr, uint32_t n, uint32_t k, SSmem &sm)
   __syncthreads();
   uint32_t out = sm.wcnt[2][warp], eq_seen = 0;
   const uint32_t lt = (1u << lane) - 1u;
-  for (uint32_t base = lo; base < hi; base += 32) {
-    const uint32_t i = base + lane;
-    const float pv = i < hi ? __ldcg(pr + i) : 0.0f;
-    const uint32_t key = float_key(pv);
-    const uint32_t beq = __ballot_sync(kFull, i < hi && key == thr);
-    const bool keep = i < hi && (key > thr || (key == thr && eq_seen + __popc(beq & lt) < take));
-    const uint32_t bk = __ballot_sync(kFull, keep);
-    if (keep) {
-      const uint32_t o = out + __popc(bk & lt);
-      sm.cidx[o] = i;
-      sm.cp[o] = pv;
+  for (uint32_t base0 = lo; base0 < hi; base0 += 32 * kMlpW) {
+    float pvs[kMlpW];
+#pragma unroll
+    for (uint32_t u = 0; u < kMlpW; ++u) {
+      const uint32_t i = base0 + 32 * u + lane;
+      pvs[u] = i < hi ? __ldcg(pr + i) : 0.0f;
     }
-    out += __popc(bk);
-    eq_seen += __popc(beq);
+#pragma unroll
+    for (uint32_t u = 0; u < kMlpW; ++u) {  // in index order: ties are taken lowest index first
+      const uint32_t i = base0 + 32 * u + lane;
+      const float pv = pvs[u];
+      const uint32_t key = float_key(pv);
+      const uint32_t beq = __ballot_sync(kFull, i < hi && key == thr);
+      const bool keep = i < hi && (key > thr || (key == thr && eq_seen + __popc(beq & lt) < take));
+      const uint32_t bk = __ballot_sync(kFull, keep);
+      if (keep) {
+        const uint32_t o = out + __popc(bk & lt);
+        sm.cidx[o] = i;
+        sm.cp[o] = pv;
+      }
+      out += __popc(bk);
+      eq_seen += __popc(beq);
+    }
   }
   __syncthreads();
 }
@@ -447,27 +509,57 @@ __global__ void __launch_bounds__(kST, 1) k_sample(const SamplerParams p) {
   const uint32_t *fq = p.freq + (size_t)row * p.vocab;
   const bool rep = p.rep != 1.0f, fpp = !(p.freq_pen == 0.0f && p.pres_pen == 0.0f);
   const bool temp = p.temperature > 0.0f && p.temperature != 1.0f;
+  // The elementwise passes stream the row through L2 with kMlp independent
+  // loads in flight per thread (one CTA per row would otherwise wait a full
+  // memory latency per element it handles).
   // 1-3: adjusted logits and their maximum
   float mx = -INFINITY;
-  for (uint32_t i = tid; i < n; i += kST) {
-    float l = lg[i];
-    const uint32_t f = (rep || fpp) ? fq[i] : 0u;
-    if (rep && f) l = l > 0.0f ? __fdiv_rn(l, p.rep) : __fmul_rn(l, p.rep);
-    if (fpp && f) {
-      l = __fsub_rn(l, __fmul_rn(p.freq_pen, (float)f));
-      l = __fsub_rn(l, p.pres_pen);
+  for (uint32_t i0 = tid; i0 < n; i0 += kST * kMlp) {
+    float lv[kMlp];
+    uint32_t fv[kMlp];
+#pragma unroll
+    for (uint32_t j = 0; j < kMlp; ++j) {
+      const uint32_t i = i0 + j * kST;
+      lv[j] = i < n ? lg[i] : 0.0f;
+      fv[j] = (rep || fpp) && i < n ? fq[i] : 0u;
     }
-    if (temp) l = __fdiv_rn(l, p.temperature);
-    __stcg(pr + i, l);
-    mx = fmaxf(mx, l);
+#pragma unroll
+    for (uint32_t j = 0; j < kMlp; ++j) {
+      const uint32_t i = i0 + j * kST;
+      if (i >= n) break;
+      float l = lv[j];
+      const uint32_t f = fv[j];
+      if (rep && f) l = l > 0.0f ? __fdiv_rn(l, p.rep) : __fmul_rn(l, p.rep);
+      if (fpp && f) {
+        l = __fsub_rn(l, __fmul_rn(p.freq_pen, (float)f));
+        l = __fsub_rn(l, p.pres_pen);
+      }
+      if (temp) l = __fdiv_rn(l, p.temperature);
+      __stcg(pr + i, l);
+      mx = fmaxf(mx, l);
+    }
   }
   mx = block_max(mx, sm);
   // 4: softmax
-  for (uint32_t i = tid; i < n; i += kST) __stcg(pr + i, __double2float_rn(exp((double)__fsub_rn(__ldcg(pr + i), mx))));
+  for (uint32_t i0 = tid; i0 < n; i0 += kST * kMlp) {
+    float v[kMlp];
+#pragma unroll
+    for (uint32_t j = 0; j < kMlp; ++j) v[j] = i0 + j * kST < n ? __ldcg(pr + i0 + j * kST) : 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < kMlp; ++j)
+      if (i0 + j * kST < n) __stcg(pr + i0 + j * kST, __double2float_rn(exp((double)__fsub_rn(v[j], mx))));
+  }
   __syncthreads();
   const float sum = block_seq<kSeqSum>(RowTerm{pr}, n, 0.0f, 0.0f, sm).s;
   if (sum != 0.0f)
-    for (uint32_t i = tid; i < n; i += kST) __stcg(pr + i, __fdiv_rn(__ldcg(pr + i), sum));
+    for (uint32_t i0 = tid; i0 < n; i0 += kST * kMlp) {
+      float v[kMlp];
+#pragma unroll
+      for (uint32_t j = 0; j < kMlp; ++j) v[j] = i0 + j * kST < n ? __ldcg(pr + i0 + j * kST) : 0.0f;
+#pragma unroll
+      for (uint32_t j = 0; j < kMlp; ++j)
+        if (i0 + j * kST < n) __stcg(pr + i0 + j * kST, __fdiv_rn(v[j], sum));
+    }
   __syncthreads();
   const bool topk = p.top_k > 0 && p.top_k < n, topp = p.top_p > 0.0f && p.top_p < 1.0f;
   const bool greedy = p.temperature == 0.0f;
