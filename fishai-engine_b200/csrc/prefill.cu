@@ -55,6 +55,42 @@ __global__ void k_norm_rows_h(const float *x, const float *w, float eps, uint32_
   pdl_enter();
   __shared__ float red[32];
   const float *r = x + (size_t)blockIdx.x * d;
+  constexpr uint32_t kV = 8;  // float4 of the row per thread held in registers (rows up to 8192 wide)
+  if (d % (4 * blockDim.x) == 0 && d <= 4 * kV * blockDim.x) {
+    // the thread's slice of the row and of the norm weights in one round trip
+    const uint32_t nv = d / (4 * blockDim.x);
+    float4 xv[kV], wv[kV];
+#pragma unroll
+    for (uint32_t j = 0; j < kV; ++j)
+      if (j < nv) {
+        xv[j] = __ldcg(reinterpret_cast<const float4 *>(r) + j * blockDim.x + threadIdx.x);
+        wv[j] = __ldg(reinterpret_cast<const float4 *>(w) + j * blockDim.x + threadIdx.x);
+      }
+    float s = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < kV; ++j)
+      if (j < nv) {
+        s = fmaf(xv[j].x, xv[j].x, s);
+        s = fmaf(xv[j].y, xv[j].y, s);
+        s = fmaf(xv[j].z, xv[j].z, s);
+        s = fmaf(xv[j].w, xv[j].w, s);
+      }
+    s = block_sum(s, red);
+    const float inv = 1.0f / sqrtf(s / (float)d + eps);
+    bool bad = false;
+#pragma unroll
+    for (uint32_t j = 0; j < kV; ++j)
+      if (j < nv) {
+        const float a = __fmul_rn(__fmul_rn(xv[j].x, inv), wv[j].x), b = __fmul_rn(__fmul_rn(xv[j].y, inv), wv[j].y);
+        const float c = __fmul_rn(__fmul_rn(xv[j].z, inv), wv[j].z), e = __fmul_rn(__fmul_rn(xv[j].w, inv), wv[j].w);
+        bad |= !(fabsf(a) <= kHalfMax) || !(fabsf(b) <= kHalfMax) || !(fabsf(c) <= kHalfMax) || !(fabsf(e) <= kHalfMax);
+        __half2 *o = reinterpret_cast<__half2 *>(out + (size_t)blockIdx.x * d) + 2 * (j * blockDim.x + threadIdx.x);
+        o[0] = __floats2half2_rn(a, b);
+        o[1] = __floats2half2_rn(c, e);
+      }
+    if (bad && err) atomicOr(err, kErrRange);
+    return;
+  }
   float s = 0.0f;
   for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) s = fmaf(r[i], r[i], s);
   s = block_sum(s, red);
@@ -532,22 +568,43 @@ __global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uin
   const float *cs = rope + (size_t)pos * hd;
   const uint32_t page = kv.page_table[(seq0 + r) * kv.max_pages + slot / 16];
   const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
-  for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) {
-    float v = row[j];
-    const bool is_q = j < qd, is_k = !is_q && j < qd + kd;
-    if (is_q || is_k) {
-      const uint32_t base = is_q ? 0 : qd, dd = (j - base) % hd, hb = j - dd;
-      const float cth = cs[2 * (dd % half)], sth = cs[2 * (dd % half) + 1];
-      const float pv = dd < half ? row[hb + dd + half] : row[hb + dd - half];
-      v = dd < half ? __fsub_rn(__fmul_rn(v, cth), __fmul_rn(pv, sth)) : __fadd_rn(__fmul_rn(pv, sth), __fmul_rn(v, cth));
+  const uint32_t n = qd + 2 * kd;
+  constexpr uint32_t kU = 8;  // elements per thread per round, their loads issued together
+  for (uint32_t j0 = threadIdx.x; j0 < n; j0 += kU * blockDim.x) {
+    float v[kU], pv[kU], cth[kU], sth[kU];
+#pragma unroll
+    for (uint32_t u = 0; u < kU; ++u) {
+      const uint32_t j = j0 + u * blockDim.x;
+      v[u] = pv[u] = cth[u] = sth[u] = 0.0f;
+      if (j < n) {
+        v[u] = row[j];
+        if (j < qd + kd) {  // q and k are rotated
+          const uint32_t base = j < qd ? 0 : qd, dd = (j - base) % hd, hb = j - dd;
+          cth[u] = cs[2 * (dd % half)];
+          sth[u] = cs[2 * (dd % half) + 1];
+          pv[u] = dd < half ? row[hb + dd + half] : row[hb + dd - half];
+        }
+      }
     }
-    if (is_q) {
-      qf[(size_t)r * qd + j] = v;
-    } else {
-      const uint32_t kc = is_k ? j - qd : j - qd - kd;
-      const uint64_t idx = lbase + kv_index(page, is_k ? 0 : 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
-      if (kv.f16) reinterpret_cast<__half *>(kv.base)[idx] = __float2half_rn(v);
-      else reinterpret_cast<float *>(kv.base)[idx] = v;
+#pragma unroll
+    for (uint32_t u = 0; u < kU; ++u) {
+      const uint32_t j = j0 + u * blockDim.x;
+      if (j >= n) break;
+      float x = v[u];
+      const bool is_q = j < qd, is_k = !is_q && j < qd + kd;
+      if (is_q || is_k) {
+        const uint32_t dd = (j - (is_q ? 0 : qd)) % hd;
+        x = dd < half ? __fsub_rn(__fmul_rn(x, cth[u]), __fmul_rn(pv[u], sth[u]))
+                      : __fadd_rn(__fmul_rn(pv[u], sth[u]), __fmul_rn(x, cth[u]));
+      }
+      if (is_q) {
+        qf[(size_t)r * qd + j] = x;
+      } else {
+        const uint32_t kc = is_k ? j - qd : j - qd - kd;
+        const uint64_t idx = lbase + kv_index(page, is_k ? 0 : 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
+        if (kv.f16) reinterpret_cast<__half *>(kv.base)[idx] = __float2half_rn(x);
+        else reinterpret_cast<float *>(kv.base)[idx] = x;
+      }
     }
   }
 }
