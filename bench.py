@@ -165,12 +165,13 @@ def profile_gemm(args):
     from fishai_engine import synth, _lib as L
     from fishai_engine.model import ModelWeights
 
-    path = synth.cached_preset(PRESET, n_layers=args.layers)
+    path = synth.cached_preset(BATCH_PRESET if args.batch_weights else PRESET, n_layers=args.layers)
     m = ModelWeights.load_from_gguf(path)
     ms, fl = C.c_float(), C.c_double()
     L.check(L.lib().fa_profile_gemm(m._h, PROFILE_KINDS[args.profile_gemm], 0, args.tokens, args.reps, C.byref(ms),
                                     C.byref(fl)))
-    print(json.dumps({"profile_gemm": args.profile_gemm, "tokens": args.tokens, "layers": args.layers,
+    print(json.dumps({"profile_gemm": args.profile_gemm, "weights": BATCH_PRESET if args.batch_weights else PRESET,
+                      "tokens": args.tokens, "layers": args.layers,
                       "reps": args.reps, "avg_launch_us": ms.value * 1000.0, "flops": fl.value,
                       "tflops": fl.value / (ms.value / 1000.0) / 1e12}), flush=True)
     m.close()
@@ -198,6 +199,8 @@ def main():
     ap.add_argument("--profile-gemm", choices=list(PROFILE_KINDS), default=None,
                     help="time one tcgen05 token GEMM of a reduced-depth model (--layers) for --tokens tokens")
     ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--batch-weights", action="store_true",
+                    help="--profile-gemm on the Q8_0 model of the batched-decode workload")
     ap.add_argument("--model-layers", type=int, default=0,
                     help="reduced-depth model of the same shapes for the whole run (0: the full 32 layers)")
     ap.add_argument("--layers", type=int, default=2)

@@ -41,13 +41,25 @@ constexpr uint32_t kEpi0 = 2 + kDeq;             // first epilogue warp
 constexpr uint32_t kQThreads = (kEpi0 + 4) * 32; // 704
 constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB
 
-template <uint32_t BN>
+// Shared memory of one weight prefetch slot of a dequant warp (codes + scales)
+constexpr uint32_t kPfWarp = 544;
+
+// PF: the launch stages its weight bytes through the prefetch ring (every
+// chunk Q8_0 or Q4_0); otherwise the dequant warps load them directly.
+template <uint32_t BN, bool PF>
 struct QCfg {
   static constexpr uint32_t kBTile = BN * kBK * 2;
   static constexpr uint32_t kStage = kATile + kBTile;
-  static constexpr uint32_t kStages = (192 * 1024) / kStage > 8 ? 8 : (192 * 1024) / kStage;
-  static constexpr uint32_t kBarOff = kStages * kStage;
+  // A/B stages (without the ring: as many as 192 KB holds, at most 8) and
+  // the ring's depth in k-steps
+  static constexpr uint32_t kFit = (192 * 1024) / kStage > 8 ? 8 : (192 * 1024) / kStage;
+  static constexpr uint32_t kStages = PF ? (BN == 64 ? 6 : (BN == 128 ? 5 : 3)) : kFit;
+  static constexpr uint32_t kPf = PF ? 4 : 0;
+  static constexpr uint32_t kPfStage = kDeq * kPfWarp;  // one region per dequant warp
+  static constexpr uint32_t kPfOff = kStages * kStage;
+  static constexpr uint32_t kBarOff = kPfOff + kPf * kPfStage;
   static constexpr uint32_t kSmem = 1024 + kBarOff + 256;   // 1 KB alignment slack, barriers
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static constexpr uint32_t kTmemCols = 2 * BN;
   // tcgen05 instruction descriptor: f32 D, f16 A and B (format 0), both K-major, M = 128, N = BN
   static constexpr uint32_t kIdesc = (1u << 4) | ((BN >> 3) << 17) | ((kBM >> 4) << 24);
@@ -109,10 +121,6 @@ __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void put_pair(uint32_t a, uint32_t n, uint32_t k, float lo, float hi) {
   sts32(a + n * 128 + ((((k >> 3) ^ (n & 7)) << 4) | ((k & 7) << 1)), pack_f16(lo, hi));
 }
-__device__ __forceinline__ uint4 ldg128(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
-__device__ __forceinline__ float ldg_h(const uint8_t *p) {
-  return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(p))));
-}
 
 // bounded wait that also gives up once another role has aborted
 __device__ __forceinline__ bool qwait(uint64_t *bar, uint32_t parity, QBars &b) {
@@ -125,6 +133,19 @@ __device__ __forceinline__ bool qwait(uint64_t *bar, uint32_t parity, QBars &b) 
 __device__ __forceinline__ bool qwait_warp(uint64_t *bar, uint32_t parity, QBars &b) {
   return __all_sync(0xFFFFFFFFu, qwait(bar, parity, b));
 }
+
+__device__ __forceinline__ uint4 ldg128(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+__device__ __forceinline__ uint2 ldg64(const uint8_t *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+__device__ __forceinline__ uint32_t ldg32(const uint8_t *p) { return __ldg(reinterpret_cast<const uint32_t *>(p)); }
+__device__ __forceinline__ __half2 u32_h2(uint32_t v) { return *reinterpret_cast<const __half2 *>(&v); }
+__device__ __forceinline__ uint32_t h2_u32(__half2 v) { return *reinterpret_cast<const uint32_t *>(&v); }
+
+// Dequant units.  A unit is one (16-row group, 32-column block) piece of
+// the A tile: block th (0 or 1) of the 64-column slice i.  Lane l = 4g + c
+// owns, per 16x16 tile t of the block (t = 2th, 2th + 1), the weight
+// columns g and g+8 and the rows 2c, 2c+1, 2c+8, 2c+9 of the group (the
+// mma.sync fragment order the layout stores); k0 = the group's first row in
+// the tile.  The caller skips a block past the slice's last tile (2th >= nt).
 
 // Q4_K unit of one warp of a pair: all four tiles of the 64-column slice i,
 // rows 2c, 2c+1 (th = 0) or 2c+8, 2c+9 (th = 1) of lane l = 4g + c, so each
@@ -166,96 +187,36 @@ __device__ __forceinline__ void deq_unit_q4k_rows(const uint8_t *G, uint32_t w, 
   }
 }
 
-// One (16-row group, 32-column block) unit of the A tile: block th (0 or 1)
-// of the 64-column slice i.  Lane l = 4g + c owns, per 16x16 tile t of the
-// block (t = 2th, 2th + 1), the weight columns g and g+8 and the rows 2c,
-// 2c+1, 2c+8, 2c+9 of the group (the mma.sync fragment order the layout
-// stores); k0 = the group's first row in the tile.  The caller skips a
-// block past the slice's last tile (2th >= nt).
-template <int T>
-__device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
-                                         uint32_t a, uint32_t n0, uint32_t k0) {
-  const uint32_t g = lane >> 2, c = lane & 3;
+// Q6_K unit: value = d * sc * (q - 32), sc per (row, 16-column sub-block
+// 4i + t), computed in f32 and rounded once to f16.
+__device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
+                                             uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3, s = i >> 2;
   const uint32_t nt = min(64u, w - 64 * i) / 16;
   const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-  // code words of the block's two tiles: Q4 types one u32 per tile, Q8_0 two
-  uint32_t q[4];
-  if (T == kQ8_0) {
-    const uint4 v = ldg128(G + 1024 * i + 8 * nt * lane + 16 * th);
-    q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
-  } else {
-    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(G + 512 * i + 4 * nt * lane + 8 * th));
-    q[0] = v.x; q[1] = v.y; q[2] = q[3] = 0u;
-  }
-  // per row scale and offset of the block: value = A * code - B
-  float sa[4], sb[4];
-  if (T == kQ4_K) {
-    const uint32_t s = i >> 2, bit = 12 * (2 * (i & 3) + th);
+  const uint2 qv = ldg64(G + 512 * i + 4 * nt * lane + 8 * th);  // low nibbles: a word per tile
+  const uint32_t hw = ldg32(G + 8 * w + 256 * i + 8 * lane + 4 * th);  // high bit pairs
+  float sa[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 h = ldg128(G + 8 * w + (16 * s + rr[j]) * 16);
-      const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
-      const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-      const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
-      const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
-                                    : (h.w >> (bit - 64));
-      sa[j] = d * u2f_small(fld & 63u);
-      sb[j] = dm * u2f_small((fld >> 6) & 63u);
-    }
-  } else if (T == kQ6_K) {
-    const uint32_t s = i >> 2;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      sa[j] = ldg_h(G + 13 * w + (16 * s + rr[j]) * 2);  // the int8 sub-scale varies per tile: applied below
-      sb[j] = 0.0f;
-    }
-  } else {
-    const uint32_t dreg = (T == kQ8_0) ? 16 : 8;
-    const float off = (T == kQ8_0) ? 128.0f : 8.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float d = ldg_h(G + dreg * w + (16 * (2 * i + th) + rr[j]) * 2);
-      sa[j] = d;
-      sb[j] = d * off;
-    }
-  }
-  uint32_t hw = 0u;
-  if (T == kQ6_K) hw = __ldg(reinterpret_cast<const uint32_t *>(G + 8 * w + 256 * i + 8 * lane + 4 * th));
+  for (int j = 0; j < 4; ++j) sa[j] = h2f(__ldg(reinterpret_cast<const uint16_t *>(G + 13 * w + (16 * s + rr[j]) * 2)));
 #pragma unroll
   for (uint32_t tt = 0; tt < 2; ++tt) {
     const uint32_t t = 2 * th + tt;
     float A[4], B[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      A[j] = sa[j];
-      B[j] = sb[j];
-    }
-    if (T == kQ6_K) {  // value = d * sc * (q - 32), sc per (row, 16-column sub-block 4i + t)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        // the int8 sub-scale s as (s + 128) - 128: exact, without the slow I2F path
-        const float sc = u2f_small((uint32_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]) ^ 0x80u) - 128.0f;
-        A[j] = A[j] * sc;
-        B[j] = A[j] * 32.0f;
-      }
+      // the int8 sub-scale s as (s + 128) - 128: exact, without the slow I2F path
+      const float sc = u2f_small((uint32_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]) ^ 0x80u) - 128.0f;
+      A[j] = sa[j] * sc;
+      B[j] = A[j] * 32.0f;
     }
     // codes of the 8 fragment elements: (col g | g+8) x (rows 2c, 2c+1 | 2c+8, 2c+9)
-    uint32_t e[8];
-    if (T == kQ8_0) {
-      const uint32_t P = q[2 * tt], Q = q[2 * tt + 1];
-      e[0] = P & 0xFFu; e[1] = (P >> 16) & 0xFFu; e[2] = (P >> 8) & 0xFFu; e[3] = P >> 24;
-      e[4] = Q & 0xFFu; e[5] = (Q >> 16) & 0xFFu; e[6] = (Q >> 8) & 0xFFu; e[7] = Q >> 24;
-    } else {
-      const uint32_t W = q[tt];
-      e[0] = W & 0xFu; e[1] = (W >> 16) & 0xFu; e[2] = (W >> 4) & 0xFu; e[3] = (W >> 20) & 0xFu;
-      e[4] = (W >> 8) & 0xFu; e[5] = (W >> 24) & 0xFu; e[6] = (W >> 12) & 0xFu; e[7] = W >> 28;
-      if (T == kQ6_K) {
-        const uint32_t H = hw >> (2 * tt);
-        const uint32_t pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+    const uint32_t W = tt ? qv.y : qv.x, H = hw >> (2 * tt);
+    uint32_t e[8] = {W & 0xFu, (W >> 16) & 0xFu, (W >> 4) & 0xFu, (W >> 20) & 0xFu,
+                     (W >> 8) & 0xFu, (W >> 24) & 0xFu, (W >> 12) & 0xFu, W >> 28};
+    const uint32_t pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
 #pragma unroll
-        for (int x = 0; x < 8; ++x) e[x] |= ((H >> pos[x]) & 3u) << 4;
-      }
-    }
+    for (int x = 0; x < 8; ++x) e[x] |= ((H >> pos[x]) & 3u) << 4;
     // element x: col g + 8*((x>>1)&1), row index j = (x&1) + 2*(x>>2)
     const uint32_t n = n0 + 16 * t + g;
 #pragma unroll
@@ -272,6 +233,112 @@ __device__ __forceinline__ void deq_unit(const uint8_t *G, uint32_t w, uint32_t 
         put_pair(a, n + 8 * col, k0 + rr[j0], v.x, v.y);
       }
     }
+  }
+}
+
+// Q8_0 / Q4_0 unit from its code words q (Q8_0: two words per tile; Q4_0:
+// one, in q.x and q.y) and the f16 scales of rows 2c, 2c+1 (d01) and 2c+8,
+// 2c+9 (d23).  value = d * (code - z), z = 128 (Q8_0) or 8 (Q4_0), in
+// packed f16: a byte permute (or mask) puts two codes into the mantissas of
+// 1024.0 (f16 0x6400 | code = 1024 + code, exact), one subtraction of
+// 1024 + z leaves the integer code - z (exact), and one multiplication by
+// the row scales rounds d * (code - z) once: the same f16 values as the
+// exact f32 product rounded to f16.  Pairs are stored to the swizzled
+// layout at the lane's two row-chunk addresses (the 128-byte swizzle XORs
+// the 16-byte chunk index with n & 7 = g).
+template <int T>
+__device__ __forceinline__ void deq_unit_q0(uint4 q, uint32_t d01, uint32_t d23, uint32_t th, uint32_t lane,
+                                            uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3;
+  const uint32_t base = a + (n0 + g) * 128 + 4 * c;
+  const uint32_t s0 = base + (((k0 >> 3) ^ g) << 4), s1 = base + ((((k0 >> 3) + 1) ^ g) << 4);
+  const __half2 dlo = u32_h2(d01), dhi = u32_h2(d23);
+  const __half2 zp = __float2half2_rn(T == kQ8_0 ? 1152.0f : 1032.0f);
+#pragma unroll
+  for (uint32_t tt = 0; tt < 2; ++tt) {
+    const uint32_t o = (2 * th + tt) * 16 * 128;  // tile t: columns n0 + 16t ..
+    // pairs (column g | g+8) x (rows 2c, 2c+1 | 2c+8, 2c+9)
+    uint32_t pr[4];
+    if (T == kQ8_0) {
+      const uint32_t P = tt ? q.z : q.x, Q = tt ? q.w : q.y;
+      pr[0] = __byte_perm(P, 0x64646464u, 0x4240);
+      pr[1] = __byte_perm(P, 0x64646464u, 0x4341);
+      pr[2] = __byte_perm(Q, 0x64646464u, 0x4240);
+      pr[3] = __byte_perm(Q, 0x64646464u, 0x4341);
+    } else {
+      const uint32_t W = tt ? q.y : q.x;
+      pr[0] = (W & 0x000F000Fu) | 0x64006400u;
+      pr[1] = ((W >> 4) & 0x000F000Fu) | 0x64006400u;
+      pr[2] = ((W >> 8) & 0x000F000Fu) | 0x64006400u;
+      pr[3] = ((W >> 12) & 0x000F000Fu) | 0x64006400u;
+    }
+    sts32(s0 + o, h2_u32(__hmul2(__hsub2(u32_h2(pr[0]), zp), dlo)));
+    sts32(s0 + o + 8 * 128, h2_u32(__hmul2(__hsub2(u32_h2(pr[1]), zp), dlo)));
+    sts32(s1 + o, h2_u32(__hmul2(__hsub2(u32_h2(pr[2]), zp), dhi)));
+    sts32(s1 + o + 8 * 128, h2_u32(__hmul2(__hsub2(u32_h2(pr[3]), zp), dhi)));
+  }
+}
+
+// the Q8_0 / Q4_0 unit's code words and row scales from global memory
+template <int T>
+__device__ __forceinline__ void load_q0(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
+                                        uint4 &q, uint32_t &d01, uint32_t &d23) {
+  const uint32_t nt = min(64u, w - 64 * i) / 16, c = lane & 3;
+  const uint8_t *sc = G + (T == kQ8_0 ? 16 : 8) * w + 32 * (2 * i + th) + 4 * c;
+  if (T == kQ8_0) {
+    q = ldg128(G + 1024 * i + 8 * nt * lane + 16 * th);
+  } else {
+    const uint2 v = ldg64(G + 512 * i + 4 * nt * lane + 8 * th);
+    q = make_uint4(v.x, v.y, 0u, 0u);
+  }
+  d01 = ldg32(sc);
+  d23 = ldg32(sc + 16);
+}
+
+// ---- weight prefetch ring (launches whose chunks are all Q8_0 / Q4_0) ----
+// Each dequant warp copies the code words and scales of its unit for the
+// next kPf - 1 k-steps into its own shared-memory region with cp.async
+// (commit groups, one per k-step), so a warp keeps several k-steps of weight
+// loads in flight instead of one.  Every byte is copied once per warp (the
+// 32-byte scale vector by lanes 0 and 1), so the lanes read each other's
+// copies after the group's wait and a __syncwarp.  Region of one warp and
+// slot: [0, 512) codes (uint4 or uint2 per lane), [512, 544) the f16 scales
+// of the block's 16 rows.
+__device__ __forceinline__ void cpa16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa8(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fetch_q0(int type, const uint8_t *G, uint32_t w, uint32_t i, uint32_t th,
+                                         uint32_t lane, uint32_t R) {
+  const uint32_t nt = min(64u, w - 64 * i) / 16;
+  if (type == kQ8_0) {
+    cpa16(R + 16 * lane, G + 1024 * i + 8 * nt * lane + 16 * th);
+    if (lane < 2) cpa16(R + 512 + 16 * lane, G + 16 * w + 32 * (2 * i + th) + 16 * lane);
+  } else {
+    cpa8(R + 8 * lane, G + 512 * i + 4 * nt * lane + 8 * th);
+    if (lane < 2) cpa16(R + 512 + 16 * lane, G + 8 * w + 32 * (2 * i + th) + 16 * lane);
   }
 }
 
@@ -326,9 +393,48 @@ struct SegIter {
   }
 };
 
-template <uint32_t BN>
+// The (weight tile, k-step) sequence of a CTA's range one k-step at a time,
+// with the dequant unit's chunk data of the current tile: a dequant warp
+// keeps two, one for the prefetch and one for the dequantisation.
+struct DqCursor {
+  const uint8_t *base;  // the chunk's first row group
+  uint32_t k, ks, tt, nt, gbytes, w, i;
+  int type;
+  bool active;  // this warp's block exists in the tile
+  __device__ void tile(const QgParams &p, uint32_t si, uint32_t th) {
+    if (nt >= p.n_tiles) return;
+    const QgTile tl = p.tiles[nt];
+    const ChunkDesc cd = p.chunks[tl.chunk];
+    base = p.w + cd.offset;
+    gbytes = cd.gbytes;
+    w = cd.width;
+    type = cd.type;
+    i = tl.col0 / 64 + si;
+    active = 64 * si < tl.ncols && 2 * th < min(64u, cd.width - 64 * i) / 16;
+  }
+  __device__ DqCursor(const QgParams &p, uint32_t k0, uint32_t KS, uint32_t t_tiles, uint32_t si, uint32_t th) {
+    const uint32_t x = k0 / KS;
+    k = k0;
+    ks = k0 % KS;
+    tt = x % t_tiles;
+    nt = x / t_tiles;
+    active = false;
+    tile(p, si, th);
+  }
+  __device__ void next(const QgParams &p, uint32_t KS, uint32_t t_tiles, uint32_t si, uint32_t th) {
+    ++k;
+    if (++ks < KS) return;
+    ks = 0;
+    if (++tt < t_tiles) return;
+    tt = 0;
+    ++nt;
+    tile(p, si, th);
+  }
+};
+
+template <uint32_t BN, bool PF>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
-  using C = QCfg<BN>;
+  using C = QCfg<BN, PF>;
   extern __shared__ __align__(1024) uint8_t qsm_raw[];
   const uint32_t raw = smem_u32(qsm_raw), pad = (1024u - (raw & 1023u)) & 1023u;
   uint8_t *base = qsm_raw + pad;
@@ -440,33 +546,46 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- dequantisation: unit (group gi, slice si, block th) of every stage ----
     const uint32_t d = warp - 2, gi = d >> 2, si = (d >> 1) & 1, th = d & 1;
     uint32_t s = 0, ph = 1;
-    SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
-    Seg wo;
-    while (it.next(wo)) {
-      const QgTile tl = p.tiles[wo.nt];
-      const ChunkDesc cd = p.chunks[tl.chunk];
-      const uint32_t i = tl.col0 / 64 + si, n0 = 64 * si;
-      // the block exists: inside the tile's columns and the slice's tiles
-      const bool active = n0 < tl.ncols && 2 * th < min(64u, cd.width - 64 * i) / 16;
-      bool ok = true;
-      for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
-        const uint32_t grp = 4 * ks + gi;
-        if (!qwait_warp(&b.empty[s], ph, b)) {
-          ok = false;
-          break;
+    if constexpr (PF) {
+      // The weight bytes of k-step j + kPf - 1 are copied while k-step j is
+      // dequantised (one cp.async group per k-step, empty where the unit has
+      // no weights), so each warp has kPf - 1 k-steps of loads in flight.
+      const uint32_t pf0 = sbase + C::kPfOff + d * kPfWarp;
+      const uint64_t Wk = (uint64_t)p.n_tiles * t_tiles * ksteps;
+      const uint32_t kend = sk_start(blockIdx.x + 1, Wk, gridDim.x);
+      DqCursor fc(p, sk_start(blockIdx.x, Wk, gridDim.x), ksteps, t_tiles, si, th);
+      DqCursor cc = fc;
+      uint32_t fslot = 0, cslot = 0;
+      auto fetch = [&]() {
+        const uint32_t grp = 4 * fc.ks + gi;
+        if (fc.k < kend) {
+          if (fc.active && grp < G16)
+            fetch_q0(fc.type, fc.base + (uint64_t)grp * fc.gbytes, fc.w, fc.i, th, lane, pf0 + fslot * C::kPfStage);
+          fc.next(p, ksteps, t_tiles, si, th);
         }
-        const uint32_t a = sbase + s * C::kStage;
-        if (active) {
+        cpa_commit();
+        if (++fslot == C::kPf) fslot = 0;
+      };
+#pragma unroll 1
+      for (uint32_t j = 0; j + 1 < C::kPf; ++j) fetch();
+      for (; cc.k < kend; cc.next(p, ksteps, t_tiles, si, th)) {
+        fetch();
+        cpa_wait<C::kPf - 1>();  // this lane's copies for k-step cc.k have landed
+        __syncwarp();            // ... and every other lane's
+        if (!qwait_warp(&b.empty[s], ph, b)) break;
+        const uint32_t a = sbase + s * C::kStage, grp = 4 * cc.ks + gi, R = pf0 + cslot * C::kPfStage;
+        if (cc.active) {
           if (grp < G16) {
-            const uint8_t *G = p.w + cd.offset + (uint64_t)grp * cd.gbytes;
-            switch (cd.type) {
-              case kQ4_K: deq_unit_q4k_rows(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
-              case kQ6_K: deq_unit<kQ6_K>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
-              case kQ8_0: deq_unit<kQ8_0>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
-              default: deq_unit<kQ4_0>(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+            const uint32_t c4 = 4 * (lane & 3);
+            const uint32_t d01 = lds32(R + 512 + c4), d23 = lds32(R + 528 + c4);
+            if (cc.type == kQ8_0) {
+              deq_unit_q0<kQ8_0>(lds128(R + 16 * lane), d01, d23, th, lane, a, 64 * si, 16 * gi);
+            } else {
+              const uint2 v = lds64(R + 8 * lane);
+              deq_unit_q0<kQ4_0>(make_uint4(v.x, v.y, 0u, 0u), d01, d23, th, lane, a, 64 * si, 16 * gi);
             }
           } else {
-            zero_unit(th, lane, a, n0, 16 * gi);
+            zero_unit(th, lane, a, 64 * si, 16 * gi);
           }
         }
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
@@ -476,8 +595,57 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           s = 0;
           ph ^= 1u;
         }
+        if (++cslot == C::kPf) cslot = 0;
       }
-      if (!ok) break;
+      cpa_wait<0>();  // no copy may still be writing shared memory when the CTA exits
+    } else {
+      SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
+      Seg wo;
+      while (it.next(wo)) {
+        const QgTile tl = p.tiles[wo.nt];
+        const ChunkDesc cd = p.chunks[tl.chunk];
+        const uint32_t i = tl.col0 / 64 + si, n0 = 64 * si;
+        // the block exists: inside the tile's columns and the slice's tiles
+        const bool active = n0 < tl.ncols && 2 * th < min(64u, cd.width - 64 * i) / 16;
+        bool ok = true;
+        for (uint32_t ks = wo.ks0; ks < wo.ks1; ++ks) {
+          const uint32_t grp = 4 * ks + gi;
+          if (!qwait_warp(&b.empty[s], ph, b)) {
+            ok = false;
+            break;
+          }
+          const uint32_t a = sbase + s * C::kStage;
+          if (active) {
+            if (grp < G16) {
+              const uint8_t *G = p.w + cd.offset + (uint64_t)grp * cd.gbytes;
+              uint4 q;
+              uint32_t d01, d23;
+              switch (cd.type) {
+                case kQ4_K: deq_unit_q4k_rows(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+                case kQ6_K: deq_unit_q6k(G, cd.width, i, th, lane, a, n0, 16 * gi); break;
+                case kQ8_0:
+                  load_q0<kQ8_0>(G, cd.width, i, th, lane, q, d01, d23);
+                  deq_unit_q0<kQ8_0>(q, d01, d23, th, lane, a, n0, 16 * gi);
+                  break;
+                default:
+                  load_q0<kQ4_0>(G, cd.width, i, th, lane, q, d01, d23);
+                  deq_unit_q0<kQ4_0>(q, d01, d23, th, lane, a, n0, 16 * gi);
+                  break;
+              }
+            } else {
+              zero_unit(th, lane, a, n0, 16 * gi);
+            }
+          }
+          fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b.full_a[s]);
+          if (++s == C::kStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
     }
   } else {
     // ---- epilogue warpgroup: TMEM lanes 32*(warp%4) .. +32 ----
@@ -578,7 +746,13 @@ __global__ void k_qg_fixup(const QgParams p, uint32_t BN, uint32_t G) {
 template <uint32_t BN>
 int launch_bn(const QgParams &p, const void *tmap, uint32_t grid, cudaStream_t st) {
   const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(tmap);
-  return launch_pdl(k_qgemm<BN>, dim3(grid), dim3(kQThreads), QCfg<BN>::kSmem, st, p, *m);
+  if (p.prefetch) return launch_pdl(k_qgemm<BN, true>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
+  return launch_pdl(k_qgemm<BN, false>, dim3(grid), dim3(kQThreads), QCfg<BN, false>::kSmem, st, p, *m);
+}
+template <uint32_t BN, bool PF>
+bool set_smem() {
+  return cudaFuncSetAttribute(k_qgemm<BN, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<BN, PF>::kSmem) ==
+         cudaSuccess;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -586,9 +760,8 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 }  // namespace
 
 int qgemm_init() {
-  if (cudaFuncSetAttribute(k_qgemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<64>::kSmem) ||
-      cudaFuncSetAttribute(k_qgemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<128>::kSmem) ||
-      cudaFuncSetAttribute(k_qgemm<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<256>::kSmem))
+  if (!set_smem<64, false>() || !set_smem<128, false>() || !set_smem<256, false>() || !set_smem<64, true>() ||
+      !set_smem<128, true>() || !set_smem<256, true>())
     return -1;
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;

@@ -66,6 +66,10 @@ MODELS = {
     "q4k_q6k": _kq_spec(),
     "q4_0": _kq_spec(type_embd=O.Q4_0, type_q=O.Q4_0, type_k=O.Q4_0, type_v=O.Q4_0, type_o=O.Q4_0,
                      type_gate=O.Q4_0, type_up=O.Q4_0, type_down=O.Q4_0, type_out=O.Q6_K, n_kv_heads=8),
+    # mixed-type launches (qkv: Q8_0, Q4_0 and Q6_K chunks) load the weights
+    # directly; single-type Q8_0 / Q4_0 launches go through the prefetch ring
+    "mixed": _kq_spec(type_q=O.Q8_0, type_k=O.Q4_0, type_v=O.Q6_K, type_o=O.Q8_0, type_gate=O.Q4_0,
+                      type_up=O.Q4_0, type_down=O.Q8_0, type_out=O.Q8_0),
 }
 
 
