@@ -356,8 +356,44 @@ __device__ __forceinline__ void stage_rows(const KvView &kv, uint64_t lbase, con
   }
 }
 
+// The same for an f16 cache, K and V at once, s0 a multiple of 32: the tile
+// is two whole pages, so lane l's chunks are (row 2j + l / 16, chunk l % 16)
+// for j = 0..15, in page j / 8 at a fixed offset from the lane's base, and
+// the swizzled destination is a per-lane base plus a constant (row bit 0 is
+// the lane's, rows differ by multiples of 2 in the XOR).
+template <uint32_t HD>
+__device__ __forceinline__ void stage_kv_f16(const KvView &kv, uint64_t lbase, const uint32_t *pt, uint32_t kvh,
+                                             uint32_t s0, uint32_t s_end, uint32_t ktile, uint32_t vtile,
+                                             uint32_t lane) {
+  static_assert(HD == 128, "two rows of 16 chunks per warp-wide copy");
+  const uint32_t c = lane & 15, r0 = lane >> 4;
+  const __half *base = reinterpret_cast<const __half *>(kv.base) + lbase;
+  const uint64_t vofs = (uint64_t)kv.n_kv * 16 * HD;  // V block of (page, kv head) after the K blocks
+  const __half *kp[2];
+#pragma unroll
+  for (uint32_t q = 0; q < 2; ++q)  // pages past the sequence's end are not read
+    kp[q] = s0 + 16 * q < s_end ? base + kv_index(pt[s0 / 16 + q], 0, kvh, r0, 8 * c, kv.n_kv, HD) : base;
+  uint32_t xo[4];
+#pragma unroll
+  for (uint32_t m = 0; m < 4; ++m) xo[m] = ((c ^ r0) ^ (2 * m)) << 4;
+  const uint32_t row0 = r0 * HD * 2;
+  const bool full = s0 + kDT <= s_end;
+#pragma unroll
+  for (uint32_t j = 0; j < 16; ++j) {
+    const uint32_t off = row0 + 2 * j * HD * 2 + xo[j & 3];
+    const __half *src = kp[j >> 3] + 2 * (j & 7) * HD;
+    if (full || s0 + 2 * j + r0 < s_end) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ktile + off), "l"(src) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(vtile + off), "l"(src + vofs) : "memory");
+    } else {
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(ktile + off), "r"(0u) : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vtile + off), "r"(0u) : "memory");
+    }
+  }
+}
+
 template <uint32_t HD, bool F16, uint32_t REP>
-__global__ void __launch_bounds__(128) k_attn_decode_rows(const AttnParams p, float scale_log2) {
+__global__ void __launch_bounds__(128, 3) k_attn_decode_rows(const AttnParams p, float scale_log2) {
   pdl_enter();
   extern __shared__ __align__(128) uint8_t dsm[];
   constexpr uint32_t RB = HD * 2, KT = HD / 16, NT = kDT / 8, OT = HD / 8, W = 2 + HD;
@@ -389,8 +425,12 @@ __global__ void __launch_bounds__(128) k_attn_decode_rows(const AttnParams p, fl
   for (uint32_t j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   for (uint32_t s0 = t0 + warp * kDT; s0 < t1; s0 += 4 * kDT) {
-    stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 0, s0, t1, ktile, lane);
-    stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 1, s0, t1, vtile, lane);
+    if constexpr (F16 && HD == 128) {
+      stage_kv_f16<HD>(p.kv, lbase, pt, kvh, s0, t1, ktile, vtile, lane);
+    } else {
+      stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 0, s0, t1, ktile, lane);
+      stage_rows<HD, F16>(p.kv, lbase, pt, kvh, 1, s0, t1, vtile, lane);
+    }
     if (F16) asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
     float s[NT][4];
