@@ -193,6 +193,47 @@ __device__ __forceinline__ void load_kv_tile(const KvView &kv, uint64_t lbase, c
   }
 }
 
+// The same for an f16 cache, K and V at once, 128 threads, s0 a multiple
+// of 64 (four whole pages): thread i copies chunk i % 16 of rows i / 16 + 8j
+// (j = 0..7: page j / 2, slot i / 16 + 8 (j & 1)); the row's swizzle term
+// is the thread's own (rows differ by multiples of 8), so the destination
+// is a per-thread base plus 2048 j.
+template <uint32_t HD>
+__device__ __forceinline__ void load_kv_tiles_f16(const KvView &kv, uint64_t lbase, const uint32_t *pt, uint32_t kvh,
+                                                  uint32_t s0, uint32_t s_end, uint32_t ktile, uint32_t vtile) {
+  static_assert(HD == 128 && kAK == 64, "64 rows of 16 chunks over 128 threads");
+  const uint32_t c = threadIdx.x & 15, r0 = threadIdx.x >> 4;
+  const __half *base = reinterpret_cast<const __half *>(kv.base) + lbase;
+  const uint64_t vofs = (uint64_t)kv.n_kv * 16 * HD;  // V block of (page, kv head) after the K blocks
+  const uint32_t dst0 = r0 * HD * 2 + ((c ^ r0) << 4);
+  const bool full = s0 + kAK <= s_end;
+#pragma unroll
+  for (uint32_t q = 0; q < 4; ++q) {
+    if (!(s0 + 16 * q < s_end)) {  // pages past the slots this tile reads are not looked up
+#pragma unroll
+      for (uint32_t jj = 0; jj < 2; ++jj) {
+        const uint32_t off = dst0 + (2 * q + jj) * 8 * HD * 2;
+        asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(ktile + off), "r"(0u) : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vtile + off), "r"(0u) : "memory");
+      }
+      continue;
+    }
+    const __half *src0 = base + kv_index(pt[s0 / 16 + q], 0, kvh, r0, 8 * c, kv.n_kv, HD);
+#pragma unroll
+    for (uint32_t jj = 0; jj < 2; ++jj) {
+      const uint32_t off = dst0 + (2 * q + jj) * 8 * HD * 2;
+      const __half *src = src0 + 8 * jj * HD;
+      if (full || s0 + 16 * q + 8 * jj + r0 < s_end) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ktile + off), "l"(src) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(vtile + off), "l"(src + vofs) : "memory");
+      } else {
+        asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(ktile + off), "r"(0u) : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(vtile + off), "r"(0u) : "memory");
+      }
+    }
+  }
+}
+
 // grid (query tiles, q heads); 4 warps x 16 query rows
 template <uint32_t HD, bool F16>
 __global__ void __launch_bounds__(128) k_attn_causal(const __half *qh, uint32_t T, uint32_t Hq, uint32_t Hkv,
@@ -229,8 +270,12 @@ __global__ void __launch_bounds__(128) k_attn_causal(const __half *qh, uint32_t 
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   const uint32_t q0 = t0 + 16 * warp + g, q1 = q0 + 8;  // query tokens of this lane's rows
   for (uint32_t s0 = 0; s0 < s_end; s0 += kAK) {
-    load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 0, s0, s_end, ks_tile);
-    load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 1, s0, s_end, vs_tile);
+    if constexpr (F16 && HD == 128) {
+      load_kv_tiles_f16<HD>(kv, lbase, pt, kvh, s0, s_end, ks_tile, vs_tile);
+    } else {
+      load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 0, s0, s_end, ks_tile);
+      load_kv_tile<HD, F16>(kv, lbase, pt, kvh, 1, s0, s_end, vs_tile);
+    }
     if (F16) asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     // S = Q K^T for 16 rows x 64 slots
