@@ -1018,7 +1018,7 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   p.err = (uint32_t *)err.p;
   p.part = (float *)part.p;
   p.part_floats = part_floats;
-  p.prefetch = P->qg_prefetch ? 1u : 0u;
+  p.prefetch = P->qg_prefetch;
   if (launch_qgemm(p, map, (uint32_t)m.n_sm, m.stream)) return fail(FA_ERR_CUDA, "token GEMM launch failed");
   uint32_t e = 0;
   API_CUDA(cudaMemcpyAsync(y_host, y.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, m.stream));
@@ -1059,7 +1059,7 @@ extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint3
   p.epi = kQgStore;
   p.part = (float *)part.p;
   p.part_floats = part_floats;
-  p.prefetch = P->qg_prefetch ? 1u : 0u;
+  p.prefetch = P->qg_prefetch;
   cudaEvent_t e0, e1;
   API_CUDA(cudaEventCreate(&e0));
   API_CUDA(cudaEventCreate(&e1));

@@ -219,7 +219,7 @@ struct QgParams {
   uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
   float *part;               // stream-K partial tiles: 2 slots per CTA of 128 x BN floats
   uint64_t part_floats;      // capacity of part (>= qgemm_part_floats(bn, n_sm))
-  uint32_t prefetch;         // 1: every chunk is Q8_0 or Q4_0 (weight bytes through the prefetch ring)
+  uint32_t prefetch;         // kQ8_0 / kQ4_0: every chunk has that type (weights through the prefetch ring); 0: direct loads
 };
 struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
   alignas(64) unsigned char bytes[128];

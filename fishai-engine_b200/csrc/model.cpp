@@ -260,9 +260,9 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     for (uint32_t c = 0; c < nc; ++c)
       for (uint32_t c0 = 0; c0 < P.chunks[c].width; c0 += 128)
         P.qg_tiles.push_back({c, c0, std::min<uint32_t>(128, P.chunks[c].width - c0), 0});
-    P.qg_prefetch = true;
+    P.qg_prefetch = nc && (P.chunks[0].type == kQ8_0 || P.chunks[0].type == kQ4_0) ? P.chunks[0].type : 0u;
     for (uint32_t c = 0; c < nc; ++c)
-      P.qg_prefetch = P.qg_prefetch && (P.chunks[c].type == kQ8_0 || P.chunks[c].type == kQ4_0);
+      if (P.chunks[c].type != P.qg_prefetch) P.qg_prefetch = 0;
     P.d_qg_tiles = (QgTile *)m.dmalloc(P.qg_tiles.size() * sizeof(QgTile));
     if (!P.d_qg_tiles) return fail(FA_ERR_OOM, "GEMM tile table allocation failed");
     CUDA_TRY(cudaMemcpy(P.d_qg_tiles, P.qg_tiles.data(), P.qg_tiles.size() * sizeof(QgTile), cudaMemcpyHostToDevice));
@@ -924,7 +924,7 @@ int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *ou
   p.ldo = ldo;
   p.epi = epi;
   p.err = pws.err;
-  p.prefetch = P.qg_prefetch ? 1u : 0u;
+  p.prefetch = P.qg_prefetch;
   return launch_qgemm(p, map, (uint32_t)n_sm, stream) ? fail(FA_ERR_CUDA, "token GEMM launch failed") : FA_OK;
 }
 

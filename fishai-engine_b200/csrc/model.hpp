@@ -28,7 +28,7 @@ struct GemvPlan {
   uint64_t native_bytes = 0;  // algorithmic bytes (native GGML blocks)
   std::vector<QgTile> qg_tiles;  // token-parallel GEMM output tiles (MMA layout only)
   QgTile *d_qg_tiles = nullptr;
-  bool qg_prefetch = false;      // every chunk Q8_0 / Q4_0: the GEMM's weight prefetch ring applies
+  uint32_t qg_prefetch = 0;      // kQ8_0 / kQ4_0 when every chunk has that type (the GEMM's prefetch ring), else 0
   uint32_t n_out = 0;            // width of the launch output space
   // epilogue completions of one launch: one per chunk (its last arriving
   // CTA), each leaving one sum-of-squares partial (residual launches) and

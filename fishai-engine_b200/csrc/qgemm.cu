@@ -246,12 +246,11 @@ __device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint3
 // exact f32 product rounded to f16.  Pairs are stored to the swizzled
 // layout at the lane's two row-chunk addresses (the 128-byte swizzle XORs
 // the 16-byte chunk index with n & 7 = g).
+// s0, s1: the lane's store addresses of rows 2c, 2c+1 and 2c+8, 2c+9 of
+// column n0 + g (q0_store_offsets).
 template <int T>
-__device__ __forceinline__ void deq_unit_q0(uint4 q, uint32_t d01, uint32_t d23, uint32_t th, uint32_t lane,
-                                            uint32_t a, uint32_t n0, uint32_t k0) {
-  const uint32_t g = lane >> 2, c = lane & 3;
-  const uint32_t base = a + (n0 + g) * 128 + 4 * c;
-  const uint32_t s0 = base + (((k0 >> 3) ^ g) << 4), s1 = base + ((((k0 >> 3) + 1) ^ g) << 4);
+__device__ __forceinline__ void deq_pairs_q0(uint4 q, uint32_t d01, uint32_t d23, uint32_t th, uint32_t s0,
+                                             uint32_t s1) {
   const __half2 dlo = u32_h2(d01), dhi = u32_h2(d23);
   const __half2 zp = __float2half2_rn(T == kQ8_0 ? 1152.0f : 1032.0f);
 #pragma unroll
@@ -277,6 +276,21 @@ __device__ __forceinline__ void deq_unit_q0(uint4 q, uint32_t d01, uint32_t d23,
     sts32(s1 + o, h2_u32(__hmul2(__hsub2(u32_h2(pr[2]), zp), dhi)));
     sts32(s1 + o + 8 * 128, h2_u32(__hmul2(__hsub2(u32_h2(pr[3]), zp), dhi)));
   }
+}
+
+// byte offsets in the A tile of the lane's two row chunks of column n0 + g
+// (k0 = 16 gi: chunks 2gi and 2gi + 1, XOR-swizzled with n & 7 = g)
+__device__ __forceinline__ void q0_store_offsets(uint32_t lane, uint32_t n0, uint32_t k0, uint32_t &o0, uint32_t &o1) {
+  const uint32_t g = lane >> 2, c = lane & 3, base = (n0 + g) * 128 + 4 * c;
+  o0 = base + (((k0 >> 3) ^ g) << 4);
+  o1 = base + ((((k0 >> 3) + 1) ^ g) << 4);
+}
+template <int T>
+__device__ __forceinline__ void deq_unit_q0(uint4 q, uint32_t d01, uint32_t d23, uint32_t th, uint32_t lane,
+                                            uint32_t a, uint32_t n0, uint32_t k0) {
+  uint32_t o0, o1;
+  q0_store_offsets(lane, n0, k0, o0, o1);
+  deq_pairs_q0<T>(q, d01, d23, th, a + o0, a + o1);
 }
 
 // the Q8_0 / Q4_0 unit's code words and row scales from global memory
@@ -330,17 +344,6 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
   return v;
 }
-__device__ __forceinline__ void fetch_q0(int type, const uint8_t *G, uint32_t w, uint32_t i, uint32_t th,
-                                         uint32_t lane, uint32_t R) {
-  const uint32_t nt = min(64u, w - 64 * i) / 16;
-  if (type == kQ8_0) {
-    cpa16(R + 16 * lane, G + 1024 * i + 8 * nt * lane + 16 * th);
-    if (lane < 2) cpa16(R + 512 + 16 * lane, G + 16 * w + 32 * (2 * i + th) + 16 * lane);
-  } else {
-    cpa8(R + 8 * lane, G + 512 * i + 4 * nt * lane + 8 * th);
-    if (lane < 2) cpa16(R + 512 + 16 * lane, G + 8 * w + 32 * (2 * i + th) + 16 * lane);
-  }
-}
 
 __device__ __forceinline__ void zero_unit(uint32_t th, uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
   const uint32_t g = lane >> 2, c = lane & 3;
@@ -393,47 +396,59 @@ struct SegIter {
   }
 };
 
-// The (weight tile, k-step) sequence of a CTA's range one k-step at a time,
-// with the dequant unit's chunk data of the current tile: a dequant warp
-// keeps two, one for the prefetch and one for the dequantisation.
-struct DqCursor {
-  const uint8_t *base;  // the chunk's first row group
-  uint32_t k, ks, tt, nt, gbytes, w, i;
-  int type;
+// The prefetch side of a dequant warp: the (weight tile, k-step) sequence
+// of the CTA's range one k-step at a time, with the source addresses of
+// the warp's unit (code words of lane l, the 32-byte scale vector for lanes
+// 0 and 1) in the current k-step's row group; within a tile they advance by
+// four row groups per k-step.
+template <int PT>
+struct PfCursor {
+  const uint8_t *code, *sc;
+  uint64_t step;
+  uint32_t k, ks, tt, nt, gi, si, th, lane;
   bool active;  // this warp's block exists in the tile
-  __device__ void tile(const QgParams &p, uint32_t si, uint32_t th) {
+  __device__ void tile(const QgParams &p) {
     if (nt >= p.n_tiles) return;
     const QgTile tl = p.tiles[nt];
     const ChunkDesc cd = p.chunks[tl.chunk];
-    base = p.w + cd.offset;
-    gbytes = cd.gbytes;
-    w = cd.width;
-    type = cd.type;
-    i = tl.col0 / 64 + si;
-    active = 64 * si < tl.ncols && 2 * th < min(64u, cd.width - 64 * i) / 16;
+    const uint32_t i = tl.col0 / 64 + si, w = cd.width, nt16 = min(64u, w - 64 * i) / 16;
+    active = 64 * si < tl.ncols && 2 * th < nt16;
+    const uint8_t *G = p.w + cd.offset + (uint64_t)(4 * ks + gi) * cd.gbytes;
+    code = G + (PT == kQ8_0 ? 1024 * i + 8 * nt16 * lane + 16 * th : 512 * i + 4 * nt16 * lane + 8 * th);
+    sc = G + (PT == kQ8_0 ? 16 : 8) * w + 32 * (2 * i + th) + 16 * lane;
+    step = 4ull * cd.gbytes;
   }
-  __device__ DqCursor(const QgParams &p, uint32_t k0, uint32_t KS, uint32_t t_tiles, uint32_t si, uint32_t th) {
+  __device__ PfCursor(const QgParams &p, uint32_t k0, uint32_t KS, uint32_t t_tiles, uint32_t gi_, uint32_t si_,
+                      uint32_t th_, uint32_t lane_)
+      : gi(gi_), si(si_), th(th_), lane(lane_), active(false) {
     const uint32_t x = k0 / KS;
     k = k0;
     ks = k0 % KS;
     tt = x % t_tiles;
     nt = x / t_tiles;
-    active = false;
-    tile(p, si, th);
+    tile(p);
   }
-  __device__ void next(const QgParams &p, uint32_t KS, uint32_t t_tiles, uint32_t si, uint32_t th) {
+  __device__ void next(const QgParams &p, uint32_t KS, uint32_t t_tiles) {
     ++k;
-    if (++ks < KS) return;
+    if (++ks < KS) {
+      code += step;
+      sc += step;
+      return;
+    }
     ks = 0;
-    if (++tt < t_tiles) return;
-    tt = 0;
-    ++nt;
-    tile(p, si, th);
+    if (++tt == t_tiles) {
+      tt = 0;
+      ++nt;
+    }
+    tile(p);
   }
 };
 
-template <uint32_t BN, bool PF>
+// PT: 0 = the dequant warps load the weights directly; kQ8_0 / kQ4_0 = every
+// chunk has that type and the weights go through the prefetch ring
+template <uint32_t BN, int PT>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
+  constexpr bool PF = PT != 0;
   using C = QCfg<BN, PF>;
   extern __shared__ __align__(1024) uint8_t qsm_raw[];
   const uint32_t raw = smem_u32(qsm_raw), pad = (1024u - (raw & 1023u)) & 1023u;
@@ -550,43 +565,59 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       // The weight bytes of k-step j + kPf - 1 are copied while k-step j is
       // dequantised (one cp.async group per k-step, empty where the unit has
       // no weights), so each warp has kPf - 1 k-steps of loads in flight.
-      const uint32_t pf0 = sbase + C::kPfOff + d * kPfWarp;
+      // The fetch records per slot what the k-step needs: 1 dequantise, 2
+      // zero rows past K, 0 nothing (block outside the tile).
+      static_assert((C::kPf & (C::kPf - 1)) == 0, "ring depth a power of two");
+      constexpr bool Q8 = PT == kQ8_0;
       const uint64_t Wk = (uint64_t)p.n_tiles * t_tiles * ksteps;
-      const uint32_t kend = sk_start(blockIdx.x + 1, Wk, gridDim.x);
-      DqCursor fc(p, sk_start(blockIdx.x, Wk, gridDim.x), ksteps, t_tiles, si, th);
-      DqCursor cc = fc;
-      uint32_t fslot = 0, cslot = 0;
+      const uint32_t k0 = sk_start(blockIdx.x, Wk, gridDim.x), kend = sk_start(blockIdx.x + 1, Wk, gridDim.x);
+      const uint32_t pf0 = sbase + C::kPfOff + d * kPfWarp;
+      const uint32_t rq = pf0 + (Q8 ? 16 : 8) * lane, rs = pf0 + 512 + 4 * (lane & 3);  // this lane's reads
+      uint32_t o0, o1;
+      q0_store_offsets(lane, 64 * si, 16 * gi, o0, o1);
+      PfCursor<PT> fc(p, k0, ksteps, t_tiles, gi, si, th, lane);
+      uint32_t fslot = 0, cslot = 0, flags = 0;
       auto fetch = [&]() {
-        const uint32_t grp = 4 * fc.ks + gi;
+        uint32_t f = 0;
         if (fc.k < kend) {
-          if (fc.active && grp < G16)
-            fetch_q0(fc.type, fc.base + (uint64_t)grp * fc.gbytes, fc.w, fc.i, th, lane, pf0 + fslot * C::kPfStage);
-          fc.next(p, ksteps, t_tiles, si, th);
+          if (fc.active) {
+            if (4 * fc.ks + gi < G16) {
+              const uint32_t R = pf0 + fslot * C::kPfStage;
+              if (Q8) cpa16(R + 16 * lane, fc.code);
+              else cpa8(R + 8 * lane, fc.code);
+              if (lane < 2) cpa16(R + 512 + 16 * lane, fc.sc);
+              f = 1;
+            } else {
+              f = 2;
+            }
+          }
+          fc.next(p, ksteps, t_tiles);
         }
         cpa_commit();
-        if (++fslot == C::kPf) fslot = 0;
+        flags = (flags & ~(3u << (2 * fslot))) | (f << (2 * fslot));
+        fslot = (fslot + 1) & (C::kPf - 1);
       };
 #pragma unroll 1
       for (uint32_t j = 0; j + 1 < C::kPf; ++j) fetch();
-      for (; cc.k < kend; cc.next(p, ksteps, t_tiles, si, th)) {
+      for (uint32_t n = kend - k0; n; --n) {
         fetch();
-        cpa_wait<C::kPf - 1>();  // this lane's copies for k-step cc.k have landed
+        cpa_wait<C::kPf - 1>();  // this lane's copies for the k-step have landed
         __syncwarp();            // ... and every other lane's
         if (!qwait_warp(&b.empty[s], ph, b)) break;
-        const uint32_t a = sbase + s * C::kStage, grp = 4 * cc.ks + gi, R = pf0 + cslot * C::kPfStage;
-        if (cc.active) {
-          if (grp < G16) {
-            const uint32_t c4 = 4 * (lane & 3);
-            const uint32_t d01 = lds32(R + 512 + c4), d23 = lds32(R + 528 + c4);
-            if (cc.type == kQ8_0) {
-              deq_unit_q0<kQ8_0>(lds128(R + 16 * lane), d01, d23, th, lane, a, 64 * si, 16 * gi);
-            } else {
-              const uint2 v = lds64(R + 8 * lane);
-              deq_unit_q0<kQ4_0>(make_uint4(v.x, v.y, 0u, 0u), d01, d23, th, lane, a, 64 * si, 16 * gi);
-            }
+        const uint32_t f = (flags >> (2 * cslot)) & 3u, a = sbase + s * C::kStage;
+        if (f == 1u) {
+          const uint32_t so = cslot * C::kPfStage;
+          const uint32_t d01 = lds32(rs + so), d23 = lds32(rs + so + 16);
+          uint4 q;
+          if (Q8) {
+            q = lds128(rq + so);
           } else {
-            zero_unit(th, lane, a, 64 * si, 16 * gi);
+            const uint2 v = lds64(rq + so);
+            q = make_uint4(v.x, v.y, 0u, 0u);
           }
+          deq_pairs_q0<PT>(q, d01, d23, th, a + o0, a + o1);
+        } else if (f == 2u) {
+          zero_unit(th, lane, a, 64 * si, 16 * gi);
         }
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
         __syncwarp();
@@ -595,7 +626,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           s = 0;
           ph ^= 1u;
         }
-        if (++cslot == C::kPf) cslot = 0;
+        cslot = (cslot + 1) & (C::kPf - 1);
       }
       cpa_wait<0>();  // no copy may still be writing shared memory when the CTA exits
     } else {
@@ -746,13 +777,16 @@ __global__ void k_qg_fixup(const QgParams p, uint32_t BN, uint32_t G) {
 template <uint32_t BN>
 int launch_bn(const QgParams &p, const void *tmap, uint32_t grid, cudaStream_t st) {
   const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(tmap);
-  if (p.prefetch) return launch_pdl(k_qgemm<BN, true>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
-  return launch_pdl(k_qgemm<BN, false>, dim3(grid), dim3(kQThreads), QCfg<BN, false>::kSmem, st, p, *m);
+  if (p.prefetch == kQ8_0)
+    return launch_pdl(k_qgemm<BN, kQ8_0>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
+  if (p.prefetch == kQ4_0)
+    return launch_pdl(k_qgemm<BN, kQ4_0>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
+  return launch_pdl(k_qgemm<BN, 0>, dim3(grid), dim3(kQThreads), QCfg<BN, false>::kSmem, st, p, *m);
 }
-template <uint32_t BN, bool PF>
+template <uint32_t BN, int PT>
 bool set_smem() {
-  return cudaFuncSetAttribute(k_qgemm<BN, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<BN, PF>::kSmem) ==
-         cudaSuccess;
+  return cudaFuncSetAttribute(k_qgemm<BN, PT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              QCfg<BN, PT != 0>::kSmem) == cudaSuccess;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -760,8 +794,9 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 }  // namespace
 
 int qgemm_init() {
-  if (!set_smem<64, false>() || !set_smem<128, false>() || !set_smem<256, false>() || !set_smem<64, true>() ||
-      !set_smem<128, true>() || !set_smem<256, true>())
+  if (!set_smem<64, 0>() || !set_smem<128, 0>() || !set_smem<256, 0>() || !set_smem<64, kQ8_0>() ||
+      !set_smem<128, kQ8_0>() || !set_smem<256, kQ8_0>() || !set_smem<64, kQ4_0>() || !set_smem<128, kQ4_0>() ||
+      !set_smem<256, kQ4_0>())
     return -1;
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;
