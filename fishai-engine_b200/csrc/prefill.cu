@@ -139,6 +139,58 @@ __global__ void k_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32
   }
 }
 
+// The same with four elements per work unit (hd % 4 == 0): a q or k head's
+// unit is dims (d, d + 1) and their rotation partners (d + hd/2, d + hd/2 + 1)
+// for d even < hd/2 (one float4 of cos/sin), a v unit four consecutive dims;
+// paired loads and stores, the same per-element rounding.
+__global__ void k_rope_kv_rows4(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd,
+                                const float *rope, uint32_t rope_max, uint32_t pos0, uint32_t len0, KvView kv,
+                                uint32_t seq, uint32_t layer, __half *qh, uint32_t *err) {
+  pdl_enter();
+  const uint32_t t = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
+  const float *row = qkv + (size_t)t * (qd + 2 * kd);
+  const uint32_t pos = pos0 + t, slot = len0 + t;
+  if (pos >= rope_max || slot / 16 >= kv.max_pages) {
+    if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
+    return;
+  }
+  const float *cs = rope + (size_t)pos * hd;
+  const uint32_t page = kv.page_table[seq * kv.max_pages + slot / 16];
+  const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
+  const uint32_t upr = half / 2, n_rot = (Hq + Hkv) * upr, n_units = n_rot + kd / 4;
+  auto put2 = [&](uint64_t idx, float a, float b) {  // two consecutive cache elements
+    if (kv.f16) *reinterpret_cast<__half2 *>(reinterpret_cast<__half *>(kv.base) + idx) = __floats2half2_rn(a, b);
+    else *reinterpret_cast<float2 *>(reinterpret_cast<float *>(kv.base) + idx) = make_float2(a, b);
+  };
+  for (uint32_t u = threadIdx.x; u < n_units; u += blockDim.x) {
+    if (u < n_rot) {
+      const uint32_t head = u / upr, dd = 2 * (u % upr), hb = head * hd;
+      const float2 x = *reinterpret_cast<const float2 *>(row + hb + dd);
+      const float2 y = *reinterpret_cast<const float2 *>(row + hb + dd + half);
+      const float4 c = *reinterpret_cast<const float4 *>(cs + 2 * dd);  // cos, sin of dd and dd + 1
+      const float a0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(y.x, c.y));
+      const float a1 = __fsub_rn(__fmul_rn(x.y, c.z), __fmul_rn(y.y, c.w));
+      const float b0 = __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(y.x, c.x));
+      const float b1 = __fadd_rn(__fmul_rn(x.y, c.w), __fmul_rn(y.y, c.z));
+      if (head < Hq) {
+        __half *q = qh + (size_t)t * qd + hb + dd;
+        *reinterpret_cast<__half2 *>(q) = __floats2half2_rn(a0, a1);
+        *reinterpret_cast<__half2 *>(q + half) = __floats2half2_rn(b0, b1);
+      } else {
+        const uint64_t idx = lbase + kv_index(page, 0, head - Hq, slot % 16, dd, kv.n_kv, hd);
+        put2(idx, a0, a1);
+        put2(idx + half, b0, b1);
+      }
+    } else {
+      const uint32_t kc = 4 * (u - n_rot);
+      const float4 v = *reinterpret_cast<const float4 *>(row + qd + kd + kc);
+      const uint64_t idx = lbase + kv_index(page, 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
+      put2(idx, v.x, v.y);
+      put2(idx + 2, v.z, v.w);
+    }
+  }
+}
+
 // ---- causal flash attention (mma.sync m16n8k16 f16, f32 accumulation) ----
 constexpr uint32_t kAQ = 64, kAK = 64;  // query rows and cache slots per tile
 
@@ -624,6 +676,33 @@ __global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *
   h[(size_t)t * F + f] = __float2half_rn(v);
 }
 
+// The same, four consecutive columns per thread (F % 4 == 0, CW % 32 == 0:
+// the four stay inside one chunk half and the loads are float4-aligned),
+// streaming loads, one 8-byte store; the same per-element arithmetic.
+__global__ void k_swiglu_rows4(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
+  pdl_enter();
+  const uint32_t t = blockIdx.y, f = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (f >= F) return;
+  const uint32_t hw = CW / 2, c = f / hw, local = f - c * hw, wc = min(CW, 2 * F - c * CW);
+  const float *row = gu + (size_t)t * 2 * F + (size_t)c * CW + local;
+  const float4 g4 = __ldcs(reinterpret_cast<const float4 *>(row));
+  const float4 u4 = __ldcs(reinterpret_cast<const float4 *>(row + wc / 2));
+  const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+  float v[4];
+  bool bad = false;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[e] = gv[e] * (1.0f / (1.0f + expf(-gv[e]))) * uv[e];
+    bad |= !(fabsf(v[e]) <= kHalfMax);
+  }
+  if (bad && err) atomicOr(err, kErrRange);
+  const __half2 lo = __floats2half2_rn(v[0], v[1]), hi = __floats2half2_rn(v[2], v[3]);
+  uint2 o;
+  o.x = *reinterpret_cast<const uint32_t *>(&lo);
+  o.y = *reinterpret_cast<const uint32_t *>(&hi);
+  *reinterpret_cast<uint2 *>(h + (size_t)t * F + f) = o;
+}
+
 // last token's row -> x, its sum of squares -> ssq[0] (the rest zero)
 __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq) {
   pdl_enter();
@@ -793,6 +872,10 @@ int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, ui
 int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                         uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
                         void *qh, uint32_t *err, cudaStream_t st) {
+  const auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (hd % 4 == 0 && a16(qkv) && a16(rope) && a16(kv.base) && kv.layer_stride % 4 == 0 && reinterpret_cast<uintptr_t>(qh) % 4 == 0)
+    return launch_pdl(k_rope_kv_rows4, dim3(T), dim3(256), 0, st, qkv, T, Hq, Hkv, hd, rope, rope_max, pos0, len0, kv,
+                      seq, layer, (__half *)qh, err);
   return launch_pdl(k_rope_kv_rows, dim3(T), dim3(256), 0, st, qkv, T, Hq, Hkv, hd, rope, rope_max, pos0, len0, kv, seq,
                     layer, (__half *)qh, err);
 }
@@ -803,6 +886,8 @@ int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
   return -1;
 }
 int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
+  if (F % 4 == 0 && CW % 32 == 0 && reinterpret_cast<uintptr_t>(gu) % 16 == 0 && reinterpret_cast<uintptr_t>(h) % 8 == 0)
+    return launch_pdl(k_swiglu_rows4, dim3((F / 4 + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
   return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
 }
 int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
