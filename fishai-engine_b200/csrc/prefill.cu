@@ -718,6 +718,55 @@ __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, f
 }
 
 // ---- batched decode: row r is cache sequence seq0 + r at its own position ----
+// The same with the four-element units of k_rope_kv_rows4 (hd % 4 == 0),
+// grid (rows, unit blocks): one unit per thread, q kept in f32.
+__global__ void k_rope_kv_batch4(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+                                 uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
+                                 float *qf, uint32_t *err) {
+  pdl_enter();
+  const uint32_t r = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
+  const uint32_t upr = half / 2, n_rot = (Hq + Hkv) * upr, n_units = n_rot + kd / 4;
+  const uint32_t u = blockIdx.y * blockDim.x + threadIdx.x;
+  const float *row = qkv + (size_t)r * (qd + 2 * kd);
+  const uint32_t pos = st[r].pos, slot = st[r].len;
+  if (pos >= rope_max || slot / 16 >= kv.max_pages) {
+    if (u == 0 && err) atomicOr(err, kErrContext);
+    return;
+  }
+  if (u >= n_units) return;
+  const uint32_t page = kv.page_table[(seq0 + r) * kv.max_pages + slot / 16];
+  const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
+  auto put2 = [&](uint64_t idx, float a, float b) {  // two consecutive cache elements
+    if (kv.f16) *reinterpret_cast<__half2 *>(reinterpret_cast<__half *>(kv.base) + idx) = __floats2half2_rn(a, b);
+    else *reinterpret_cast<float2 *>(reinterpret_cast<float *>(kv.base) + idx) = make_float2(a, b);
+  };
+  if (u < n_rot) {
+    const uint32_t head = u / upr, dd = 2 * (u % upr), hb = head * hd;
+    const float2 x = *reinterpret_cast<const float2 *>(row + hb + dd);
+    const float2 y = *reinterpret_cast<const float2 *>(row + hb + dd + half);
+    const float4 c = *reinterpret_cast<const float4 *>(rope + (size_t)pos * hd + 2 * dd);  // cos, sin of dd, dd + 1
+    const float a0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(y.x, c.y));
+    const float a1 = __fsub_rn(__fmul_rn(x.y, c.z), __fmul_rn(y.y, c.w));
+    const float b0 = __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(y.x, c.x));
+    const float b1 = __fadd_rn(__fmul_rn(x.y, c.w), __fmul_rn(y.y, c.z));
+    if (head < Hq) {
+      float *q = qf + (size_t)r * qd + hb + dd;
+      *reinterpret_cast<float2 *>(q) = make_float2(a0, a1);
+      *reinterpret_cast<float2 *>(q + half) = make_float2(b0, b1);
+    } else {
+      const uint64_t idx = lbase + kv_index(page, 0, head - Hq, slot % 16, dd, kv.n_kv, hd);
+      put2(idx, a0, a1);
+      put2(idx + half, b0, b1);
+    }
+  } else {
+    const uint32_t kc = 4 * (u - n_rot);
+    const float4 v = *reinterpret_cast<const float4 *>(row + qd + kd + kc);
+    const uint64_t idx = lbase + kv_index(page, 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
+    put2(idx, v.x, v.y);
+    put2(idx + 2, v.z, v.w);
+  }
+}
+
 __global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                 uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
                                 float *qf, uint32_t *err) {
@@ -893,6 +942,12 @@ int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, voi
 int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st) {
+  const auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (hd % 4 == 0 && a16(qkv) && a16(rope) && a16(kv.base) && kv.layer_stride % 4 == 0 && reinterpret_cast<uintptr_t>(qf) % 8 == 0) {
+    const uint32_t units = (Hq + Hkv) * (hd / 4) + Hkv * hd / 4;
+    return launch_pdl(k_rope_kv_batch4, dim3(b, (units + 255) / 256), dim3(256), 0, st, qkv, Hq, Hkv, hd, rope, rope_max,
+                      states, kv, seq0, layer, qf, err);
+  }
   return launch_pdl(k_rope_kv_batch, dim3(b), dim3(256), 0, st, qkv, Hq, Hkv, hd, rope, rope_max, states, kv, seq0, layer,
                     qf, err);
 }
