@@ -141,6 +141,9 @@ struct AttnParams {
   int partials_only;       // batch-1 paged kernel: leave the split partials for the consumer (kProAttn)
   const SeqState *row_states;  // batched decode: per query row state (T = len + 1), cache sequence row_seq0 + row
   uint32_t row_seq0;
+  void *out_h;             // batched decode: non-null -> the combined output as f16 [rows][H*hd] here
+                           // instead of out (values beyond the f16 range flag kErrRange in err)
+  uint32_t *err;
 };
 // attention_init: once per device (current), before the first launch_attention
 // of a stream capture; launch_attention calls it as well

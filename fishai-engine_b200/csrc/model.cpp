@@ -1033,7 +1033,7 @@ int Model::ensure_batch_ws(uint32_t b) {
 
 int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams &sp, uint32_t *hist,
                               uint32_t max_steps) {
-  const uint32_t d = cfg.n_embd, hd = cfg.head_dim, Hq = cfg.n_heads, Hkv = cfg.n_kv_heads, qd = Hq * hd;
+  const uint32_t d = cfg.n_embd, hd = cfg.head_dim, Hq = cfg.n_heads, Hkv = cfg.n_kv_heads;
   const uint32_t F = layers[0].down.K, qkv_n = layers[0].qkv.n_out, gu_n = layers[0].gateup.n_out;
   const KvView kvv = kv.view();
   int rc;
@@ -1059,11 +1059,12 @@ int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams
     ap.part = bws.part;
     ap.counters = bws.counters;
     ap.out = bws.Of;
+    ap.out_h = bws.Oh;  // the combine writes the o GEMM's f16 operand directly
+    ap.err = bws.err;
     ap.state = bws.states;
     ap.row_states = bws.states;
     ap.row_seq0 = 0;
     if (launch_attn_decode_rows(ap, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
-    if (launch_to_half(bws.Of, (uint64_t)b * qd, bws.Oh, bws.err, stream)) return fail(FA_ERR_CUDA, "convert failed");
     if ((rc = run_qgemm(lw.o, bws.moh, b, bws.X, d, kQgResid))) return rc;
     if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
       return fail(FA_ERR_CUDA, "norm launch failed");

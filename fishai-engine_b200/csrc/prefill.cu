@@ -657,7 +657,14 @@ __global__ void __launch_bounds__(128, 3) k_attn_decode_rows(const AttnParams p,
       L = fmaf(__ldcg(P + sp * W + 1), e, L);
       acc = fmaf(__ldcg(P + sp * W + 2 + d), e, acc);
     }
-    p.out[(size_t)row * H * HD + (size_t)(kvh * REP + r) * HD + d] = L > 0.0f ? acc / L : 0.0f;
+    const float y = L > 0.0f ? acc / L : 0.0f;
+    const size_t o = (size_t)row * H * HD + (size_t)(kvh * REP + r) * HD + d;
+    if (p.out_h) {  // straight to the f16 operand of the o GEMM
+      if (!(fabsf(y) <= kHalfMax) && p.err) atomicOr(p.err, kErrRange);
+      reinterpret_cast<__half *>(p.out_h)[o] = __float2half_rn(y);
+    } else {
+      p.out[o] = y;
+    }
   }
   if (tid == 0) *cnt = 0u;
 }
