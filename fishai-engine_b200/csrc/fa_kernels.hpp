@@ -260,7 +260,6 @@ int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *s
 int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st);
-int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st);
 // batched decode attention on the tensor cores (mma.sync): grid (splits,
 // kv heads, q_rows), row r of AttnParams uses row_states[r] and cache
 // sequence row_seq0 + r; p.scale as in launch_attention

@@ -829,16 +829,6 @@ __global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uin
   }
 }
 
-__global__ void k_to_half(const float *x, uint64_t n, __half *y, uint32_t *err) {
-  pdl_enter();
-  bool bad = false;
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-    bad |= !(fabsf(x[i]) <= kHalfMax);
-    y[i] = __float2half_rn(x[i]);
-  }
-  if (bad && err) atomicOr(err, kErrRange);
-}
-
 // after the sampler: positions advance, the sampled ids (already the next
 // step's input tokens) go to the history
 __global__ void k_batch_step_end(SeqState *st, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
@@ -957,10 +947,6 @@ int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv
   }
   return launch_pdl(k_rope_kv_batch, dim3(b), dim3(256), 0, st, qkv, Hq, Hkv, hd, rope, rope_max, states, kv, seq0, layer,
                     qf, err);
-}
-int launch_to_half(const float *x, uint64_t n, void *y, uint32_t *err, cudaStream_t st) {
-  const uint32_t grid = (uint32_t)std::min<uint64_t>((n + 255) / 256, 4096);
-  return launch_pdl(k_to_half, dim3(grid ? grid : 1), dim3(256), 0, st, x, n, (__half *)y, err);
 }
 int launch_batch_step_end(SeqState *states, uint32_t b, const uint32_t *ids, uint32_t *hist, uint32_t max_steps,
                           uint32_t *step, cudaStream_t st) {
