@@ -7,9 +7,13 @@
 // tensor throughput; the activation producers flag values beyond the f16
 // range), f32 accumulation in tensor memory:
 //   A = W^T tile: 128 weight columns x 64 rows, dequantised by 16 producer
-//       warps (one 16-row x 32-column block each) from the packed codes straight into the K-major 128-byte
-//       swizzled shared-memory layout the MMA reads (d*sc*q - dmin*m etc. in
-//       f32, rounded once to f16)
+//       warps (one 16-row x 32-column unit each) into the K-major 128-byte
+//       swizzled shared-memory layout the MMA reads, every value rounded once
+//       to f16: Q4_K / Q6_K in f32 (d*sc*q - dmin*m), Q8_0 / Q4_0 in packed
+//       f16 (exact code - z, one rounding multiply by d).  Launches whose
+//       chunks all have one of the last two types stage the weight bytes
+//       through a per-warp cp.async ring a few k-steps ahead; the others load
+//       them directly.
 //   B = X tile: BN tokens x 64 rows of f16 activations, loaded by a TMA
 //       tensor copy with the same 128-byte swizzle (no multicast)
 //   D = 128 x BN f32 accumulator in TMEM (two buffers: the epilogue of one
