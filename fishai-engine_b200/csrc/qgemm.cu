@@ -247,7 +247,7 @@ __device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint3
 // 1024.0 (f16 0x6400 | code = 1024 + code, exact), one subtraction of
 // 1024 + z leaves the integer code - z (exact), and one multiplication by
 // the row scales rounds d * (code - z) once: the same f16 values as the
-// exact f32 product rounded to f16.  Pairs are stored to the swizzled
+// exact f32 product rounded to f16 (a zero may carry the scale's sign).  Pairs are stored to the swizzled
 // layout at the lane's two row-chunk addresses (the 128-byte swizzle XORs
 // the 16-byte chunk index with n & 7 = g).
 // s0, s1: the lane's store addresses of rows 2c, 2c+1 and 2c+8, 2c+9 of
