@@ -9,7 +9,7 @@ and rounds that to f16.  These tests check, for every code and a wide range
 of f16 scales (subnormals included), that both give the same f16 bits (up
 to the sign of a zero), i.e. that the packed path equals the exact product
 d * (code - z) rounded once to f16 (the Q8_0 value of src/quant.rs:261-290
-and its Q4_0 counterpart, with the stored code offset by z).
+and the Q4_0 value of src/quant.rs:123-157, the stored code offset by z).
 
 numpy evaluates float16 arithmetic in float32 and rounds the result once to
 float16; a product or difference of two f16 values is exact in float32, so
