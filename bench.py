@@ -5,12 +5,17 @@ Q4_K with Q6_K attn_v / ffn_down / output, weights N(0, 0.02) from seed 2):
 batch 1, a 2048-token prompt, then greedy decode.  One step = one decode
 token (one forward pass through the model + argmax, a CUDA-graph replay).
 
+Generation follows GenerationState::generate (src/model.rs:638-705): the
+prompt is prefilled, the last prompt token is fed again at position P, and
+the greedy ids that follow are checked against the committed 64-id golden
+before the timed steps continue the same sequence.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --profile gateup --layers 2 --reps 3   # one GEMV kind on a
       reduced-depth model of the same shapes (small cases for ncu captures)
 
-With N > 1 (torchrun) every rank runs an independent replica (the decode
-path at batch 1 does not shard); value = all ranks' tokens / max rank time.
+With N > 1 (torchrun) every rank runs an independent replica of the b=1
+decode (it does not shard); value = all ranks' tokens / max rank time.
 Prints one JSON line (rank 0)."""
 from __future__ import annotations
 
@@ -31,8 +36,17 @@ PRESET = "llama3-8b-q4_k_m"
 BATCH_PRESET = "llama3-8b-q8_0"
 BATCH_WORKLOAD = "llama3-8b-shaped Q8_0 synthetic GGUF (seed 3), 64 sequences x 4096-token prompts, 128 sampled steps"
 WORKLOAD = "llama3-8b-shaped Q4_K_M synthetic GGUF, batch 1, 2048-token prompt, greedy decode"
+DATA = "synthetic (seeded N(0,0.02) weights, uniform prompt ids)"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+GOLDEN_DIR = os.path.join(ROOT, "tests", "golden")
+# the other workload shapes, each reported at one GPU beside the headline:
+# name -> (preset, override, prompt seed, prompt, greedy tokens, golden file)
+EXTRA = {
+    "tiny": ("tiny-q8_0", {}, 0, 32, 128, "tiny_greedy.json"),
+    "7b": ("llama2-7b-q4_0", {}, 1, 512, 256, "7b_greedy.json"),
+    "70b": ("llama3-70b-q4_k", {}, 4, 4096, 256, None),
+}
 
 
 def measured_peaks():
@@ -114,25 +128,88 @@ def dist_env():
     return world, rank, local
 
 
-def cpu_baseline_sample(path: str, n_layers_total: int, layers: int):
-    """Reference-algorithm CPU timing (oracle port, i-j-p matmul, one thread,
-    the reference has no threads): one token's matmuls of `layers` layers,
-    scaled by multiply-adds to a whole token (layers + output head)."""
+def load_golden(name):
+    p = os.path.join(GOLDEN_DIR, name) if name else None
+    if not p or not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f)
+
+
+def golden_check(golden, prompt, ids):
+    """{match, checked, first_mismatch} of generated ids against a committed
+    golden (None when the golden does not cover this prompt)"""
+    if not golden or golden["prompt"] != list(prompt):
+        return None
+    want = golden["greedy_ids"]
+    n = min(len(want), len(ids))
+    bad = [i for i in range(n) if int(ids[i]) != int(want[i])]
+    return {"match": not bad and n == len(want), "checked": n, "first_mismatch": bad[0] if bad else None}
+
+
+def cpu_token_sample(path, prompt_len, layers, threads):
+    """Reference-order CPU timing (the oracle port; one thread, as the
+    reference runs): one decode token at context prompt_len through the first
+    `layers` layers (all when 0) -- matmuls in i-j-p order, RoPE, the K/V head
+    expansion copy, attention over the whole cache -- plus the output head and
+    the greedy pick.  Returns (seconds per whole token, layer seconds, head
+    seconds, layers timed, model layers)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
-    m = O.Model(path, resident=False, threads=1)
-    cfg = m.cfg
-    secs, macs = 0.0, 0.0
-    for layer in range(layers):
-        s, mc = m.time_layer(layer % n_layers_total)
-        secs += s
-        macs += mc
-    per_layer_macs = macs / layers
-    token_macs = per_layer_macs * n_layers_total + cfg["n_embd"] * cfg["vocab_size"]
-    sec_per_token = secs / macs * token_macs
+    m = O.Model(path, resident=False, threads=threads)
+    L = m.cfg["n_layers"]
+    n = layers if 0 < layers < L else L
+    kv = m.kv(prompt_len + 2)
+    kv.fill_synthetic(prompt_len)
+    ls, hs, _ = m.time_token(kv, 5, prompt_len, n)
+    del kv
     m.close()
-    return 1.0 / sec_per_token, secs, layers
+    return hs + ls * L / n, ls, hs, n, L
+
+
+def reference_arm(args, world, rank):
+    """The reference's own CPU algorithm for the headline workload, timed on
+    this host: the oracle (the reference crate cannot be built: no Rust
+    toolchain) runs whole decode tokens of the 8B Q4_K_M model at context
+    2048 in the reference's loop order on one thread.  The input file is
+    written by the oracle's copy of the synthetic writer, so this arm never
+    loads the CUDA library."""
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+
+    from fishai_engine import synth
+
+    path = synth.cached_preset(PRESET, writer=O.write_gguf)
+    m = O.Model(path, resident=False, threads=os.cpu_count() or 1)
+    P, n_tok = args.prompt, max(1, args.ref_tokens)
+    kv = m.kv(P + n_tok + 2)
+    kv.fill_synthetic(P)
+    tok = int(np.random.default_rng(2).integers(3, m.cfg["vocab_size"], P)[-1])
+    t_layers = t_head = 0.0
+    for i in range(n_tok):
+        ls, hs, tok = m.time_token(kv, tok, P + i, 0)
+        t_layers += ls
+        t_head += hs
+    total = t_layers + t_head
+    value = n_tok / total
+    sample = (f"{n_tok} whole decode token(s) at context {P}: all {m.cfg['n_layers']} layers (i-j-p f32 matmuls, "
+              f"RoPE, expand_kv_heads copy, attention) {t_layers:.1f}s + output head and greedy pick {t_head:.1f}s, "
+              f"one thread (host has {os.cpu_count()} cores); weights dequantised to f32 outside the timed region, "
+              f"as the reference does at load; cache rows before position {P} hold synthetic values")
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": n_tok,
+            "steps_requested": args.steps, "warmup": 0, "ms_per_step": 1000.0 * total / n_tok,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "config": {"workload": WORKLOAD, "batch": 1, "prompt": P}, "impl": "reference",
+            "timed": "every step is one whole decode token; nothing is extrapolated",
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    m.close()
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 PROFILE_KINDS = {"qkv": 0, "o": 1, "gateup": 2, "down": 3, "head": 4}
@@ -178,6 +255,54 @@ def profile_gemm(args):
     return 0
 
 
+def kv_read_bytes(cfg, kv_elem, ctx):
+    return 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * kv_elem * ctx
+
+
+def greedy_config(name, args, local, peak):
+    """One more workload shape at one GPU: prefill, re-feed of the last
+    prompt token at position P, then G greedy steps timed with CUDA events;
+    the ids are checked against the shape's golden where one is committed."""
+    import numpy as np
+    import torch
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights
+
+    preset, override, seed, P, G, gname = EXTRA[name]
+    path = synth.cached_preset(preset, **override)
+    m = ModelWeights.load_from_gguf(path, device=local, use_tc_prefill=args.decode_prefill == "tc")
+    cfg = m.config
+    _, wbytes = m.weight_bytes()
+    prompt = np.random.default_rng(seed).integers(3, cfg.vocab_size, P).tolist()
+    kv_dtype = L.KV_F16 if args.kv == "f16" else L.KV_F32
+    kv = m.new_kv_cache(P + G + 8, dtype=kv_dtype)
+    stream = torch.cuda.ExternalStream(L.lib().fa_model_stream(m._h))
+    t0 = time.perf_counter()
+    m.prefill(prompt, 0, kv, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    m.decode_greedy(m.new_kv_cache(8, dtype=kv_dtype), prompt[-1], 0, 4)  # graph capture outside the timing
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ids = m.decode_greedy(kv, prompt[-1], P, G)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    mean_ctx = P + (G + 1) / 2.0
+    step_bytes = wbytes + kv_read_bytes(cfg, 2 if args.kv == "f16" else 4, mean_ctx)
+    gbs = step_bytes * G / (ms / 1000.0) / 1e9
+    out = {"value": G / (ms / 1000.0), "unit": "tok/s", "model": f"{preset} synthetic GGUF (seed {seed})",
+           "batch": 1, "prompt": P, "steps": G, "ms_per_step": ms / G, "kv_cache": args.kv,
+           "prefill": args.decode_prefill, "prefill_wall_s": prefill_s,
+           "greedy_ids_match_golden": golden_check(load_golden(gname), prompt, ids),
+           "roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved_gbs": gbs, "peak": peak,
+                        "unit": "GB/s", "frac": gbs / peak}}
+    del kv
+    m.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -186,9 +311,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
-    ap.add_argument("--cpu-layers", type=int, default=4)
-    ap.add_argument("--prefill", choices=["tc", "exact"], default="tc",
-                    help="tc: f16 tensor-core prefill (tcgen05 GEMMs, flash attention); exact: f32 token steps")
+    ap.add_argument("--decode-prefill", choices=["tc", "exact"], default="exact",
+                    help="how the prompt of the timed decode is prefilled: exact (f32 token steps, the reference's "
+                         "values) or tc (f16 tensor cores)")
+    ap.add_argument("--cpu-layers", type=int, default=8,
+                    help="layers of the whole-token CPU sample beside our figure (0: skip)")
+    ap.add_argument("--ref-tokens", type=int, default=1, help="whole decode tokens the reference arm times")
+    ap.add_argument("--configs", default="tiny,7b",
+                    help="other workload shapes reported at one GPU (tiny, 7b, 70b; empty: none)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode figure (0: skip)")
     ap.add_argument("--batch-prompt", type=int, default=4096)
     ap.add_argument("--batch-steps", type=int, default=128)
@@ -213,28 +343,16 @@ def main():
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3
-
-    from fishai_engine import synth, _lib as L
-
     if args.impl == "reference":
-        if rank != 0:
-            return 0
-        path = synth.cached_preset(PRESET)
-        samples = max(1, min(args.steps, args.cpu_layers))
-        value, secs, layers = cpu_baseline_sample(path, 32, samples)
-        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
-                "config": {"workload": WORKLOAD}, "impl": "reference",
-                "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": "port",
-                                 "sample": f"{layers} layers x one token of reference-order (i-j-p) f32 matmuls, "
-                                           f"{secs:.1f}s, scaled by multiply-adds to 32 layers + output head"},
-                "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return 0
+        return reference_arm(args, world, rank)
+
+    import ctypes as C
 
     import numpy as np
     import torch
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights
 
     torch.cuda.set_device(local)
     pg = None
@@ -251,36 +369,48 @@ def main():
         pg.barrier()
     path = synth.cached_preset(PRESET, **ml)
 
-    from fishai_engine.model import ModelWeights
-
     m = ModelWeights.load_from_gguf(path, device=local, use_step_kernel=bool(args.step_kernel),
-                                    use_tc_prefill=args.prefill == "tc")
+                                    use_tc_prefill=True)
     cfg = m.config
+    step_kernel = m.step_kernel_active
     dev_bytes, step_weight_bytes = m.weight_bytes()
     P, K, W = args.prompt, args.steps, args.warmup
+    G = 64  # greedy ids checked against the golden before the warm-up
     E = min(K, 128)  # end-to-end steps
     kv_dtype = L.KV_F16 if args.kv == "f16" else L.KV_F32
-    kv = m.new_kv_cache(P + W + K + E + 8, dtype=kv_dtype)
     prompt = np.random.default_rng(2 + rank).integers(3, cfg.vocab_size, P).tolist()
     stream = torch.cuda.ExternalStream(L.lib().fa_model_stream(m._h))
+    peak, peak_src = measured_peaks()
 
-    # prefill: one untimed run into a scratch cache (workspace, tensor maps),
-    # then the timed prefill of the prompt (host ids in, last logits out)
-    if args.prefill == "tc":
-        kv_w = m.new_kv_cache(P + 8, dtype=kv_dtype)
-        m.prefill(prompt, 0, kv_w)
-        del kv_w
+    # prefill throughput on the tensor-core path (scratch caches: one warm-up
+    # run for the workspace and tensor maps, then the timed run)
+    kv_w = m.new_kv_cache(P + 8, dtype=kv_dtype)
+    m.prefill(prompt, 0, kv_w, want_logits=False)
+    del kv_w
+    kv_p = m.new_kv_cache(P + 8, dtype=kv_dtype)
     torch.cuda.synchronize()
     pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pe0.record(stream)
     t0 = time.perf_counter()
-    _, tok = m.prefill(prompt, 0, kv)
+    m.prefill(prompt, 0, kv_p)
     prefill_s = time.perf_counter() - t0
     pe1.record(stream)
     pe1.synchronize()
     prefill_dev_s = pe0.elapsed_time(pe1) / 1000.0
-    pos = P
-    ids = m.decode_greedy(kv, tok, pos, W)  # warm-up (graph capture + steady state)
+    del kv_p
+
+    # the decode sequence: prompt prefilled (--decode-prefill), the last
+    # prompt token fed again at position P (src/model.rs:656-657), greedy ids
+    # checked against the golden, then warm-up and timed steps continue it
+    m.set_tc_prefill(args.decode_prefill == "tc")
+    kv = m.new_kv_cache(P + G + W + K + E + 8, dtype=kv_dtype)
+    t0 = time.perf_counter()
+    m.prefill(prompt, 0, kv, want_logits=False)
+    decode_prefill_s = time.perf_counter() - t0
+    ids = m.decode_greedy(kv, prompt[-1], P, G)
+    parity = golden_check(load_golden("8b_greedy.json") if not ml else None, prompt, ids)
+    pos = P + G
+    ids = m.decode_greedy(kv, int(ids[-1]), pos, W)  # warm-up (steady state)
     pos += W
     tok = int(ids[-1])
 
@@ -299,6 +429,7 @@ def main():
     if pg:
         pg.barrier()
     ms = ev0.elapsed_time(ev1)
+    launches = m.step_launches()
     pos += K
     tok = int(ids[-1])
     t_max = ms
@@ -308,13 +439,15 @@ def main():
         t_max = float(t.item())
     value = world * K / (t_max / 1000.0)
 
-    # end to end through the public API: host token in, host argmax out, per step
+    # end to end through the public API: per step one token id in and the
+    # argmax id out (fa_forward with no logits buffer; the library moves the
+    # 40-byte step state each way through a pinned staging buffer)
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
     t0 = time.perf_counter()
     for _ in range(E):
-        _, am = m.forward([tok], pos, kv, return_argmax=True)
+        _, am = m.forward([tok], pos, kv, return_argmax=True, want_logits=False)
         tok = int(am[0])
         pos += 1
     e2e_s = time.perf_counter() - t0
@@ -325,11 +458,8 @@ def main():
 
     # roofline of the dominant kernel: the fused FFN gate+up GEMV
     # (33% of a step's bytes), timed with CUDA events over all 32 layers
-    import ctypes as C
-
     avg, nbytes = C.c_float(), C.c_uint64()
     L.check(L.lib().fa_profile_gemv(m._h, 2, 64, C.byref(avg), C.byref(nbytes)))
-    peak, peak_src = measured_peaks()
     achieved = nbytes.value / (avg.value / 1000.0) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "gemv_gateup_8b_traffic.json")
@@ -341,10 +471,9 @@ def main():
 
     # whole-step bytes: weights + embedding row + KV read at the mean context
     kv_elem = 2 if args.kv == "f16" else 4
-    ctx0 = P + W
+    ctx0 = P + G + W
     mean_ctx = ctx0 + (K + 1) / 2.0
-    kv_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * kv_elem * mean_ctx
-    step_bytes = step_weight_bytes + kv_bytes
+    step_bytes = step_weight_bytes + kv_read_bytes(cfg, kv_elem, mean_ctx)
     step_gbs = step_bytes * (K / (ms / 1000.0)) / 1e9
 
     # prefill roofline: tensor-bound; linear flops 2 x (layer weights) per token
@@ -354,20 +483,18 @@ def main():
     pf_flops = 2.0 * lin * P + 4.0 * cfg.n_layers * cfg.n_heads * hd * P * (P + 1) / 2 + 2.0 * d * cfg.vocab_size
     tpeak, tpeak_src = measured_tensor_peak()
     gemm_ms, gemm_fl = C.c_float(), C.c_double()
-    gemm = None
-    if args.prefill == "tc":
-        L.check(L.lib().fa_profile_gemm(m._h, 2, 0, P, 5, C.byref(gemm_ms), C.byref(gemm_fl)))
-        gemm = {"kernel": "k_qgemm (gate+up, Q4_K, tcgen05 f16)", "tokens": P, "avg_launch_us": gemm_ms.value * 1e3,
-                "achieved": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
-                "frac": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12 / tpeak}
+    L.check(L.lib().fa_profile_gemm(m._h, 2, 0, P, 5, C.byref(gemm_ms), C.byref(gemm_fl)))
+    gemm = {"kernel": "k_qgemm (gate+up, Q4_K, tcgen05 f16)", "tokens": P, "avg_launch_us": gemm_ms.value * 1e3,
+            "achieved": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
+            "frac": gemm_fl.value / (gemm_ms.value / 1000.0) / 1e12 / tpeak}
     prefill = {"value": P / prefill_s, "unit": "tok/s", "tokens": P,
-               "path": ("f16 tensor cores: tcgen05 dequant-GEMMs, causal flash attention (mma.sync), chunks of 2048"
-                        if args.prefill == "tc" else "causal token-by-token steps (f32 path)"),
+               "path": "f16 tensor cores: tcgen05 dequant-GEMMs, causal flash attention (mma.sync), chunks of 2048",
                "device_s": prefill_dev_s,
                "roofline": {"bound": "tensor", "flops": pf_flops, "achieved": pf_flops / prefill_dev_s / 1e12,
                             "peak": tpeak, "unit": "TFLOP/s", "frac": pf_flops / prefill_dev_s / 1e12 / tpeak,
                             "peak_source": tpeak_src},
                "gemm": gemm}
+    m.close()
 
     # batched decode on the 8B Q8_0 model (seed 3): 64 sequences with
     # 4096-token prompts prefilled into the paged f16 cache, then 128 steps
@@ -406,7 +533,7 @@ def main():
         be1.synchronize()
         b_ms = be0.elapsed_time(be1)
         mean_ctx_b = Pb + warm + (Kb + 1) / 2.0
-        kvb_bytes = 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * mean_ctx_b * B
+        kvb_bytes = kv_read_bytes(cfg, 2, mean_ctx_b) * B
         b_step_bytes = b_weight_bytes + kvb_bytes
         b_gbs = b_step_bytes * Kb / (b_ms / 1000.0) / 1e9
         batch = {"value": B * Kb / (b_ms / 1000.0), "unit": "tok/s", "model": BATCH_WORKLOAD, "batch": B,
@@ -420,25 +547,31 @@ def main():
         del kvb, smp
         mb.close()
 
+    extra = {}
+    if not ml:
+        for name in [c for c in args.configs.split(",") if c]:
+            extra[name] = greedy_config(name, args, local, peak)
+
     cpu = None
     if rank == 0 and world == 1 and args.cpu_layers > 0:
-        v, secs, layers = cpu_baseline_sample(path, cfg.n_layers, args.cpu_layers)
-        cpu = {"value": v, "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": f"{layers} layers x one token of reference-order (i-j-p) f32 matmuls on one core "
-                         f"({secs:.1f}s), scaled by multiply-adds to 32 layers + output head; host has "
+        per_tok, ls, hs, n, nl = cpu_token_sample(path, P, args.cpu_layers, os.cpu_count() or 1)
+        cpu = {"value": 1.0 / per_tok, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"one decode token at context {P} in the reference's order on one core: {n} of {nl} layers "
+                         f"(i-j-p f32 matmuls, RoPE, expand_kv_heads copy, attention) {ls:.1f}s + output head and "
+                         f"greedy pick {hs:.1f}s; per-token time = head + layers x {nl}/{n}; host has "
                          f"{os.cpu_count()} cores"}
 
-    launches_per_step = 1 + 5 * cfg.n_layers + 2
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": t_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 activations, Q4_K/Q6_K weights, f16 KV" if args.kv == "f16" else "f32",
-        "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
+        "data": DATA,
         "config": {"workload": WORKLOAD, "batch": 1, "prompt": P, "kv_cache": args.kv,
-                   "step_kernel": m.step_kernel_active,
+                   "decode_prefill": args.decode_prefill, "step_kernel": step_kernel,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (4.9 GB of weights streamed per step)"},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv (fused ffn gate+up, Q4_K)", "achieved": achieved,
+        "greedy_ids_match_golden": parity,
+        "roofline": {"bound": "hbm", "kernel": "k_gemv_mma (fused ffn gate+up, Q4_K)", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "bytes_per_launch": nbytes.value, "avg_launch_us": avg.value * 1000.0,
                      "peak_source": peak_src,
@@ -447,15 +580,19 @@ def main():
                               "achieved_gbs": head_bytes.value / (head_avg.value / 1000.0) / 1e9}},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 40, "d2h_bytes_per_step": 40,
-                "api": "fa_forward (one token id in, argmax id out per step)"},
+                "api": "fa_forward with no logits buffer: the step state (token id, position) in and the argmax "
+                       "id out, 40 bytes each way through the library's pinned staging buffer"},
         "prefill": prefill,
         "decode_b64": batch,
-        "gpu_launches": launches_per_step * K,
+        "configs": extra,
+        "gpu_launches": launches * K,
+        "launches_per_step": launches,
         "clocks": clocks,
+        "decode_prefill_wall_s": decode_prefill_s,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del kv, m
+    del kv
     if pg:
         pg.destroy_process_group()
     return 0

@@ -15,6 +15,7 @@
 #include "fa_kernels.hpp"
 #include "gguf.hpp"
 #include "model.hpp"
+#include "sdpa.hpp"
 
 namespace fa {
 int synth_write(const char *path, const fa_synth_spec *s, uint64_t seed);
@@ -126,11 +127,19 @@ int create_kv(Model &m, uint32_t n_seq, uint32_t max_ctx, int dtype, KvCache *kv
   const uint64_t pages = (uint64_t)n_seq * kv->max_pages;
   kv->layer_stride = pages * 2 * m.cfg.n_kv_heads * 16 * m.cfg.head_dim;
   const uint64_t bytes = kv->layer_stride * m.cfg.n_layers * (kv->f16 ? 2 : 4);
-  if (cudaMalloc(&kv->base, bytes) != cudaSuccess) return fail(FA_ERR_OOM, "KV cache allocation failed");
+  if (cudaMalloc(&kv->base, bytes) != cudaSuccess) {
+    cudaGetLastError();  // not sticky: later launch checks must not see it
+    kv->base = nullptr;
+    return fail(FA_ERR_OOM, "KV cache allocation of " + std::to_string(bytes) + " bytes failed");
+  }
   API_CUDA(cudaMemset(kv->base, 0, bytes));
   std::vector<uint32_t> pt(pages);
   for (uint64_t i = 0; i < pages; ++i) pt[i] = (uint32_t)i;  // static page assignment per sequence
-  if (cudaMalloc(&kv->page_table, pages * 4) != cudaSuccess) return fail(FA_ERR_OOM, "page table allocation failed");
+  if (cudaMalloc(&kv->page_table, pages * 4) != cudaSuccess) {
+    cudaGetLastError();
+    kv->page_table = nullptr;
+    return fail(FA_ERR_OOM, "page table allocation failed");
+  }
   API_CUDA(cudaMemcpy(kv->page_table, pt.data(), pages * 4, cudaMemcpyHostToDevice));
   return m.ensure_rope(max_ctx + 1);
 }
@@ -502,6 +511,27 @@ int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *s
 }
 void *fa_model_stream(fa_model *m) { return m ? (void *)m->m.stream : nullptr; }
 int fa_model_step_kernel_active(const fa_model *m) { return m && m->m.step_ok ? 1 : 0; }
+int fa_model_set_tc_prefill(fa_model *m, int32_t on) {
+  API_NULL(m);
+  if (on && !m->m.tc_ok) return fail(FA_ERR_UNSUPPORTED, "tensor-core prefill needs every projection in the MMA layout");
+  m->m.want_tc_prefill = on != 0;
+  return FA_OK;
+}
+int fa_debug_set(fa_model *fm, int32_t key, uint64_t value) {
+  API_NULL(fm);
+  Model &m = fm->m;
+  if (key == FA_DEBUG_WAIT_LIMIT_NS) m.dbg_wait_ns = value;
+  else if (key == FA_DEBUG_WITHHOLD_WEIGHTS) m.dbg_withhold = value ? 1u : 0u;
+  else return fail(FA_ERR_INVALID, "fa_debug_set: unknown key");
+  drop_graph(m);  // captured launches hold the old parameters
+  return FA_OK;
+}
+int fa_model_step_launches(const fa_model *m, uint32_t *n) {
+  API_NULL(m);
+  API_NULL(n);
+  *n = m->m.graph ? m->m.graph_kernels : 0;
+  return FA_OK;
+}
 
 // ------------------------------------------------------------ KV cache
 int fa_kv_create(fa_model *m, uint32_t n_seq, uint32_t max_ctx, int32_t dtype, fa_kv **out) {
@@ -587,7 +617,14 @@ int fa_forward(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
     void *p;
     ~F() { cudaFree(p); }
   } free_hid{hid_dev};
-  if ((rc = set_state(m, m.ws.state, tokens[0], pos, kv->kv.len[seq], 0))) return rc;
+  // the step's state crosses PCIe through the model's pinned staging
+  // buffer: one 40-byte upload, one 40-byte read-back (plus the logits row
+  // when asked for)
+  *m.h_state = SeqState{};
+  m.h_state->pos = pos;
+  m.h_state->len = kv->kv.len[seq];
+  m.h_state->token = tokens[0];
+  API_CUDA(cudaMemcpyAsync(m.ws.state, m.h_state, sizeof(SeqState), cudaMemcpyHostToDevice, m.stream));
   if (hidden) {
     if ((rc = m.enqueue_step(kv->kv, seq, m.ws, hid_dev))) return rc;
   } else {
@@ -597,9 +634,9 @@ int fa_forward(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
     API_CUDA(cudaMemcpyAsync(logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
   if (hidden)
     API_CUDA(cudaMemcpyAsync(hidden, hid_dev, (size_t)m.cfg.n_layers * m.cfg.n_embd * 4, cudaMemcpyDeviceToHost, m.stream));
-  SeqState st;
-  API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
+  API_CUDA(cudaMemcpyAsync(m.h_state, m.ws.state, sizeof(SeqState), cudaMemcpyDeviceToHost, m.stream));
   API_CUDA(cudaStreamSynchronize(m.stream));
+  const SeqState st = *m.h_state;
   if (st.err) return check_err_flags(m, m.ws.state);
   if (argmax) argmax[0] = st.token;
   kv->kv.len[seq] += 1;
@@ -827,15 +864,15 @@ int fa_sampler_freq(fa_sampler *s, uint32_t seq, uint32_t token, uint32_t *count
 }
 
 // ------------------------------------------------------------ attention
-namespace {
-constexpr uint32_t kSdpaSplits = 32;
-
-int sdpa_check(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H,
-               uint32_t KVH, uint32_t hd, const float *out) {
-  if (!q || !k || !v || !out) return fail(FA_ERR_INVALID, "fa_sdpa: null buffer");
-  if (!q_len || !kv_len || !H || !KVH || !hd) return fail(FA_ERR_INVALID, "fa_sdpa: zero size");
+}  // extern "C"
+namespace fa {
+int sdpa_check(const char *who, const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len,
+               uint32_t H, uint32_t KVH, uint32_t hd, const float *out) {
+  const std::string w(who);
+  if (!q || !k || !v || !out) return fail(FA_ERR_INVALID, w + ": null buffer");
+  if (!q_len || !kv_len || !H || !KVH || !hd) return fail(FA_ERR_INVALID, w + ": zero size");
   if (hd > 128 || H % KVH || (H / KVH != 1 && H / KVH != 2 && H / KVH != 4 && H / KVH != 8))
-    return fail(FA_ERR_UNSUPPORTED, "fa_sdpa: head_dim <= 128 and n_heads/n_kv_heads in {1,2,4,8}");
+    return fail(FA_ERR_UNSUPPORTED, w + ": head_dim <= 128 and n_heads/n_kv_heads in {1,2,4,8}");
   return FA_OK;
 }
 
@@ -858,7 +895,9 @@ AttnParams sdpa_params(const float *q, const float *k, const float *v, uint32_t 
   ap.out = out;
   return ap;
 }
+}  // namespace fa
 
+namespace {
 std::mutex g_sdpa_mu;
 struct SdpaScratch {
   void *buf = nullptr;
@@ -866,16 +905,17 @@ struct SdpaScratch {
 };
 SdpaScratch g_sdpa[64];  // per device
 }  // namespace
+extern "C" {
 
 int fa_sdpa(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H, uint32_t KVH,
             uint32_t hd, float *out, void *stream) {
-  int rc = sdpa_check(q, k, v, q_len, kv_len, H, KVH, hd, out);
+  int rc = sdpa_check("fa_sdpa", q, k, v, q_len, kv_len, H, KVH, hd, out);
   if (rc) return rc;
   int dev = 0;
   API_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(FA_ERR_INVALID, "fa_sdpa: device ordinal out of range");
-  const size_t part_floats = (size_t)q_len * H * kSdpaSplits * (2 + hd);
-  const size_t need = part_floats * 4 + (size_t)q_len * KVH * 4;
+  const size_t part_floats = sdpa_part_floats(q_len, H, hd);
+  const size_t need = part_floats * 4 + sdpa_counters(q_len, KVH) * 4;
   std::lock_guard<std::mutex> lock(g_sdpa_mu);
   SdpaScratch &s = g_sdpa[dev];
   if (s.bytes < need) {
@@ -887,9 +927,32 @@ int fa_sdpa(const float *q, const float *k, const float *v, uint32_t q_len, uint
   }
   float *part = (float *)s.buf;
   uint32_t *counters = (uint32_t *)(part + part_floats);
-  API_CUDA(cudaMemsetAsync(counters, 0, (size_t)q_len * KVH * 4, (cudaStream_t)stream));
+  API_CUDA(cudaMemsetAsync(counters, 0, sdpa_counters(q_len, KVH) * 4, (cudaStream_t)stream));
   AttnParams ap = sdpa_params(q, k, v, q_len, kv_len, H, KVH, hd, out, part, counters);
   if (launch_attention(ap, false, (cudaStream_t)stream)) return fail(FA_ERR_CUDA, "fa_sdpa: launch failed");
+  return FA_OK;
+}
+
+int fa_sdpa_host(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len, uint32_t H,
+                 uint32_t KVH, uint32_t hd, float *out) {
+  int rc = sdpa_check("fa_sdpa_host", q, k, v, q_len, kv_len, H, KVH, hd, out);
+  if (rc) return rc;
+  const size_t nq = (size_t)q_len * H * hd, nkv = (size_t)kv_len * KVH * hd;
+  float *buf = nullptr;
+  if (cudaMalloc(&buf, (2 * nq + 2 * nkv) * 4) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA_ERR_OOM, "fa_sdpa_host: device buffers");
+  }
+  struct F {
+    void *p;
+    ~F() { cudaFree(p); }
+  } free_buf{buf};
+  float *dq = buf, *dk = dq + nq, *dv = dk + nkv, *dout = dv + nkv;
+  API_CUDA(cudaMemcpy(dq, q, nq * 4, cudaMemcpyHostToDevice));
+  API_CUDA(cudaMemcpy(dk, k, nkv * 4, cudaMemcpyHostToDevice));
+  API_CUDA(cudaMemcpy(dv, v, nkv * 4, cudaMemcpyHostToDevice));
+  if ((rc = fa_sdpa(dq, dk, dv, q_len, kv_len, H, KVH, hd, dout, nullptr))) return rc;
+  API_CUDA(cudaMemcpy(out, dout, nq * 4, cudaMemcpyDeviceToHost));
   return FA_OK;
 }
 

@@ -105,6 +105,10 @@ struct GemvParams {
   KvView kv;
   uint32_t seq, layer;
   SeqState *state;         // pos / argmax
+  // failure-path testing (k_gemv_mma): the producer issues no weight copies,
+  // so every consumer wait runs out; wait limit in ns (0: kWaitLimitNs)
+  uint32_t withhold_weights;
+  uint64_t wait_limit_ns;
 };
 
 // one-time per-device kernel attributes (dynamic smem)

@@ -338,7 +338,7 @@ __device__ __forceinline__ void segment(const GemvParams &p, const Smem &sm, con
     const uint32_t ng = min(sg, seg - done);
     // after a timed-out wait the warp keeps the loop structure but skips the
     // work; the error flag tells the host the result is void
-    if (ok && !mbar_wait_sleep(&sm.full[slot], phase)) ok = false;
+    if (ok && !mbar_wait_sleep(&sm.full[slot], phase, p.wait_limit_ns ? p.wait_limit_ns : kWaitLimitNs)) ok = false;
     if (active && ok) {
       const uint32_t base = ring + slot * p.stage_bytes;
       build<T>(base, gbytes, w, warp, nblk, ng, xs0 + 64 * (u + done), lane, tbl, corr);
@@ -376,7 +376,7 @@ __device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc
 // the ring.  s counts stages through the ring across launches (slot s % NS,
 // a slot is refilled once its consumers released it).
 __device__ __forceinline__ void produce(const GemvParams &p, uint32_t cta, const Smem &sm, uint32_t &s, bool &ok) {
-  if (cta >= p.n_ctas) return;
+  if (cta >= p.n_ctas || p.withhold_weights) return;
   const CtaRange R = p.ranges[cta];
   const uint32_t G = p.K / 16, start = R.c0 * G + R.g0, end = R.c1 * G + R.g1;
   const uint32_t n_units = end > start ? end - start : 0;

@@ -67,7 +67,10 @@ int config_from_gguf(const Gguf &g, fa_config *c) {
 
 void *Model::dmalloc(size_t bytes) {
   void *p = nullptr;
-  if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) {
+    cudaGetLastError();  // an allocation failure is not sticky: keep it out of later launch checks
+    return nullptr;
+  }
   allocs.push_back(p);
   device_bytes += bytes;
   return p;
@@ -77,6 +80,7 @@ Model::~Model() {
   for (KvCache *kv : live_kv) kv->m = nullptr;  // caches may outlive the model
   if (graph) cudaGraphExecDestroy(graph);
   if (device >= 0) cudaSetDevice(device);
+  if (h_state) cudaFreeHost(h_state);
   for (void *p : allocs) cudaFree(p);
   if (stream) cudaStreamDestroy(stream);
 }
@@ -305,6 +309,7 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   want_tc_prefill = o.use_tc_prefill != 0;
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  CUDA_TRY(cudaMallocHost(&h_state, sizeof(SeqState)));
   if (gemv_init() || gemv_mma_init() || attention_init() || step_init() || sampler_init() || qgemm_init() ||
       attn_rows_init())
     return fail(FA_ERR_CUDA, "kernel attribute setup failed");
@@ -474,6 +479,8 @@ GemvParams Model::gemv_base(const GemvPlan &P) const {
   p.x_slot = P.x_slot;
   p.part = part;
   p.counters = counters;
+  p.withhold_weights = dbg_withhold;
+  p.wait_limit_ns = dbg_wait_ns;
   return p;
 }
 
@@ -659,6 +666,20 @@ int Model::alloc_workspace(Workspace &w) {
   return FA_OK;
 }
 
+// kernel launches one replay of a captured graph performs
+static uint32_t count_kernel_nodes(cudaGraph_t g) {
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || !n) return 0;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return 0;
+  uint32_t k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+  }
+  return k;
+}
+
 int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
   int rc;
   if (step_ok && (rc = prepare_step(kv, seq))) return rc;
@@ -694,6 +715,7 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
       return rc;
     }
     if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph capture failed: ") + cudaGetErrorString(ce));
+    graph_kernels = count_kernel_nodes(gr);
     ce = cudaGraphInstantiate(&graph, gr, 0);
     cudaGraphDestroy(gr);
     if (ce != cudaSuccess) return fail(FA_ERR_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(ce));

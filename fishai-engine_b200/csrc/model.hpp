@@ -99,6 +99,11 @@ struct Model {
   Workspace ws;                 // single-sequence decode workspace
   std::vector<void *> allocs;   // every device allocation, freed at teardown
   std::set<KvCache *> live_kv;  // caches created on this model (detached at teardown)
+  SeqState *h_state = nullptr;  // pinned host staging of the single-token forward's state
+  // failure-path testing (fa_debug_set): GEMV launches withhold their weight
+  // copies / use a shorter wait limit
+  uint32_t dbg_withhold = 0;
+  uint64_t dbg_wait_ns = 0;
   uint64_t device_bytes = 0, step_bytes = 0;
   // persistent decode-step kernel (all GEMVs in the MMA layout, untied head)
   bool want_step = false;            // requested by the load options
@@ -135,6 +140,7 @@ struct Model {
                    uint32_t *ids_host, float *logits_host);
   // decode-step graph cache
   cudaGraphExec_t graph = nullptr;
+  uint32_t graph_kernels = 0;   // kernel nodes of the captured step graph
   const KvCache *graph_kv = nullptr;
   uint32_t graph_seq = 0;
   // device sampler run after every step of a generation (null: argmax only)

@@ -9,17 +9,16 @@
 // cudaFree or an allocating library routine.
 #include <cuda_runtime.h>
 
-#include <cmath>
 #include <mutex>
 #include <string>
 
 #include "../../include/fishai_cuda.h"
 #include "fa_host.hpp"
 #include "fa_kernels.hpp"
+#include "sdpa.hpp"
 
 namespace {
 
-constexpr uint32_t kSplits = 32;               // same split count as fa_sdpa
 constexpr size_t kMaxPartFloats = 1u << 19;    // 2 MiB of split partials
 constexpr size_t kMaxCounters = 1024;          // q_len * n_kv_heads arrival counters
 constexpr size_t kScratchFloats = kMaxPartFloats + kMaxCounters;
@@ -35,16 +34,17 @@ float *g_addr[64];  // device address of g_noalloc_scratch per device ordinal
 extern "C" int fa_sdpa_noalloc(const float *q, const float *k, const float *v, uint32_t q_len, uint32_t kv_len,
                                uint32_t H, uint32_t KVH, uint32_t hd, float *out, void *stream) {
   using namespace fa;
-  if (!q || !k || !v || !out) return fail(FA_ERR_INVALID, "fa_sdpa_noalloc: null buffer");
-  if (!q_len || !kv_len || !H || !KVH || !hd) return fail(FA_ERR_INVALID, "fa_sdpa_noalloc: zero size");
-  if (hd > 128 || H % KVH || (H / KVH != 1 && H / KVH != 2 && H / KVH != 4 && H / KVH != 8))
-    return fail(FA_ERR_UNSUPPORTED, "fa_sdpa_noalloc: head_dim <= 128 and n_heads/n_kv_heads in {1,2,4,8}");
-  const size_t part_floats = (size_t)q_len * H * kSplits * (2 + hd);
-  const size_t counters = (size_t)q_len * KVH;
+  int rc = sdpa_check("fa_sdpa_noalloc", q, k, v, q_len, kv_len, H, KVH, hd, out);
+  if (rc) return rc;
+  // the limits follow fa_sdpa's split count (kSdpaSplits)
+  const uint64_t part_floats = sdpa_part_floats(q_len, H, hd);
+  const uint64_t counters = sdpa_counters(q_len, KVH);
   if (part_floats > kMaxPartFloats || counters > kMaxCounters)
-    return fail(FA_ERR_INVALID, "fa_sdpa_noalloc: q_len*n_heads*32*(head_dim+2) = " + std::to_string(part_floats) +
+    return fail(FA_ERR_INVALID, "fa_sdpa_noalloc: q_len*n_heads*" + std::to_string(kSdpaSplits) +
+                                    "*(head_dim+2) = " + std::to_string(part_floats) +
                                     " exceeds the fixed scratch of " + std::to_string(kMaxPartFloats) +
-                                    " floats (or q_len*n_kv_heads > " + std::to_string(kMaxCounters) + ")");
+                                    " floats, or q_len*n_kv_heads = " + std::to_string(counters) + " exceeds " +
+                                    std::to_string(kMaxCounters));
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(FA_ERR_CUDA, "fa_sdpa_noalloc: no current CUDA device");
@@ -68,21 +68,7 @@ extern "C" int fa_sdpa_noalloc(const float *q, const float *k, const float *v, u
   // the arrival counters must start at zero; the array keeps the last call's contents
   if (cudaMemsetAsync(cnt, 0, counters * sizeof(uint32_t), (cudaStream_t)stream) != cudaSuccess)
     return fail(FA_ERR_CUDA, "fa_sdpa_noalloc: clearing the counters failed");
-  AttnParams ap{};
-  ap.q = q;
-  ap.kc = k;
-  ap.vc = v;
-  ap.t_fixed = kv_len;
-  ap.q_rows = q_len;
-  ap.kv.n_kv = KVH;
-  ap.kv.head_dim = hd;
-  ap.kv.f16 = 0;
-  ap.n_heads = H;
-  ap.splits = kSplits;
-  ap.scale = 1.0f / std::sqrt((float)hd);  // src/tensor.rs:486
-  ap.part = part;
-  ap.counters = cnt;
-  ap.out = out;
+  const AttnParams ap = sdpa_params(q, k, v, q_len, kv_len, H, KVH, hd, out, part, cnt);
   if (launch_attention(ap, false, (cudaStream_t)stream)) return fail(FA_ERR_CUDA, "fa_sdpa_noalloc: launch failed");
   return FA_OK;
 }

@@ -16,6 +16,7 @@ ERR_INVALID, ERR_GGUF, ERR_UNSUPPORTED, ERR_OOM, ERR_CUDA, ERR_NCCL, ERR_CONTEXT
 
 F32, F16, Q4_0, Q4_1, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 3, 6, 8, 12, 14
 KV_F32, KV_F16 = 0, 1
+DEBUG_WAIT_LIMIT_NS, DEBUG_WITHHOLD_WEIGHTS = 1, 2
 
 
 class FishaiError(RuntimeError):
@@ -88,6 +89,9 @@ SIGNATURES = {
     "fa_model_weight_bytes": ([_vp, _pu64, _pu64], _i),
     "fa_model_stream": ([_vp], _vp),
     "fa_model_step_kernel_active": ([_vp], _i),
+    "fa_model_set_tc_prefill": ([_vp, C.c_int32], _i),
+    "fa_model_step_launches": ([_vp, _pu32], _i),
+    "fa_debug_set": ([_vp, C.c_int32, _u64], _i),
     "fa_kv_create": ([_vp, _u32, _u32, C.c_int32, C.POINTER(_vp)], _i),
     "fa_kv_free": ([_vp], None),
     "fa_kv_clear": ([_vp, C.c_int32], _i),
@@ -110,6 +114,7 @@ SIGNATURES = {
     "fa_profile_gemv": ([_vp, C.c_int32, _u32, _pf, _pu64], _i),
     "fa_sdpa": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp], _i),
     "fa_sdpa_noalloc": ([_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp], _i),
+    "fa_sdpa_host": ([_pf, _pf, _pf, _u32, _u32, _u32, _u32, _u32, _pf], _i),
     "fa_synth_write": ([C.c_char_p, C.POINTER(fa_synth_spec), _u64], _i),
 }
 

@@ -78,6 +78,17 @@ class ModelWeights:
         L.check(L.lib().fa_model_config(h, C.byref(c)))
         return cls(h, ModelConfig._from_c(c))
 
+    def set_tc_prefill(self, on: bool):
+        """prefill() on the f16 tensor-core path (True) or the f32 token steps"""
+        L.check(L.lib().fa_model_set_tc_prefill(self._h, int(on)))
+
+    def step_launches(self) -> int:
+        """kernel launches in one replay of the captured decode step (0 before
+        the first decode)"""
+        n = C.c_uint32()
+        L.check(L.lib().fa_model_step_launches(self._h, C.byref(n)))
+        return n.value
+
     @property
     def step_kernel_active(self) -> bool:
         """True when decode steps run as the persistent step kernel."""
@@ -103,15 +114,17 @@ class ModelWeights:
         return KVCache(self, max_ctx, n_seq, dtype)
 
     def forward(self, token_ids, pos: int, kv_cache: KVCache, seq: int = 0, return_argmax: bool = False,
-                hidden: bool = False):
+                hidden: bool = False, want_logits: bool = True):
         """ModelWeights::forward (src/model.rs:316-455): logits [n * vocab];
-        every token at `pos`, no mask, as in the reference."""
+        every token at `pos`, no mask, as in the reference.  want_logits=False
+        leaves the logits on the device (None is returned in their place):
+        only the argmax ids cross PCIe."""
         toks, tp = L.u32_array(token_ids)
         n, V = toks.size, self.config.vocab_size
-        logits = np.zeros(n * V, dtype=np.float32)
+        logits = np.zeros(n * V, dtype=np.float32) if want_logits else None
         am = np.zeros(n, dtype=np.uint32)
         hid = np.zeros(self.config.n_layers * n * self.config.n_embd, dtype=np.float32) if hidden else None
-        L.check(L.lib().fa_forward(self._h, kv_cache._h, seq, tp, n, pos, L.f32_ptr(logits),
+        L.check(L.lib().fa_forward(self._h, kv_cache._h, seq, tp, n, pos, L.f32_ptr(logits) if want_logits else None,
                                    am.ctypes.data_as(C.POINTER(C.c_uint32)), L.f32_ptr(hid) if hidden else None))
         out = [logits]
         if return_argmax:

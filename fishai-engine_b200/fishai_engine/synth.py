@@ -48,23 +48,35 @@ def write(path: str, seed: int, threads: int = 0, **fields) -> str:
     return str(path)
 
 
-def write_preset(name: str, path: str, threads: int = 0, **override) -> str:
+def preset_fields(name: str, **override):
+    """(spec fields, seed) of a preset with some fields replaced"""
     fields, seed = PRESETS[name]
     f = dict(fields)
     f.update(override)
     seed = f.pop("seed", seed)
-    return write(path, seed, threads, **f)
+    return f, seed
 
 
-def cached_preset(name: str, directory: str = None, **override) -> str:
+def write_preset(name: str, path: str, threads: int = 0, writer=None, **override) -> str:
+    """writer: a function with the signature of write() (default: this
+    library's fa_synth_write)"""
+    f, seed = preset_fields(name, **override)
+    return (writer or write)(path, seed, threads, **f)
+
+
+def cache_path(name: str, directory: str = None, **override) -> str:
+    directory = directory or os.environ.get("FISHAI_SYNTH_DIR", "/tmp/fishai_synth")
+    tag = "-".join(f"{k}{v}" for k, v in sorted(override.items()))
+    return os.path.join(directory, f"{name}{'-' + tag if tag else ''}.gguf")
+
+
+def cached_preset(name: str, directory: str = None, writer=None, **override) -> str:
     """Write the preset once into `directory` (default $FISHAI_SYNTH_DIR or
     /tmp/fishai_synth) and reuse it afterwards."""
-    directory = directory or os.environ.get("FISHAI_SYNTH_DIR", "/tmp/fishai_synth")
-    os.makedirs(directory, exist_ok=True)
-    tag = "-".join(f"{k}{v}" for k, v in sorted(override.items()))
-    path = os.path.join(directory, f"{name}{'-' + tag if tag else ''}.gguf")
+    path = cache_path(name, directory, **override)
+    os.makedirs(os.path.dirname(path), exist_ok=True)
     if not os.path.exists(path):
-        tmp = path + ".tmp"
-        write_preset(name, tmp, **override)
+        tmp = f"{path}.tmp{os.getpid()}"
+        write_preset(name, tmp, writer=writer, **override)
         os.replace(tmp, path)
     return path

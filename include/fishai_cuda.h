@@ -130,6 +130,26 @@ int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *s
 void *fa_model_stream(fa_model *m);
 /* 1 when decode steps run as the persistent step kernel, else 0 */
 int fa_model_step_kernel_active(const fa_model *m);
+/* Routes fa_prefill to the f16 tensor-core path (on = 1) or to the f32 token
+ * steps (on = 0) from now on; the load option use_tc_prefill sets the
+ * initial choice.  FA_ERR_UNSUPPORTED when the model cannot take the
+ * tensor-core path.  (No reference counterpart: the reference prefills token
+ * by token, src/model.rs:644-650.) */
+int fa_model_set_tc_prefill(fa_model *m, int32_t on);
+/* Kernel launches in one replay of the captured single-sequence decode step
+ * (the CUDA graph behind fa_forward / fa_decode_greedy / fa_generate); 0
+ * before the first capture. */
+int fa_model_step_launches(const fa_model *m, uint32_t *n);
+/* Failure-path testing (no reference counterpart; the reference has no
+ * device waits).  FA_DEBUG_WAIT_LIMIT_NS: the bounded waits of the decode
+ * GEMV give up after `value` ns instead of 2 s (0 restores the default).
+ * FA_DEBUG_WITHHOLD_WEIGHTS: value 1 makes the decode GEMV's producer issue
+ * no weight copies, so its consumers' waits run out, the kernel returns and
+ * the call reports FA_ERR_TIMEOUT; 0 restores normal operation.  Nothing
+ * faults or hangs: every wait is bounded and the context stays usable. */
+#define FA_DEBUG_WAIT_LIMIT_NS 1
+#define FA_DEBUG_WITHHOLD_WEIGHTS 2
+int fa_debug_set(fa_model *m, int32_t key, uint64_t value);
 
 /* ------------------------------------------------------------- KV cache */
 typedef struct fa_kv fa_kv;
@@ -173,6 +193,11 @@ int fa_prefill(fa_model *m, fa_kv *kv, uint32_t seq, const uint32_t *tokens_host
  * head_dim <= 128; n_heads / n_kv_heads in {1, 2, 4, 8}. */
 int fa_sdpa(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t q_len, uint32_t kv_len,
             uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_dev, void *stream);
+/* the same on host buffers (tensor::scaled_dot_product_attention's own
+ * calling convention: slices in, a vector out); device buffers are
+ * allocated, filled, and freed inside the call */
+int fa_sdpa_host(const float *q_host, const float *k_host, const float *v_host, uint32_t q_len, uint32_t kv_len,
+                 uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_host);
 
 /* No counterpart in the reference.  fa_sdpa without any device allocation,
  * for callers that must not call cudaMalloc: code whose device memory is
@@ -187,7 +212,10 @@ int fa_sdpa(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t
  *   q_len * n_kv_heads <= 1024,
  * else FA_ERR_INVALID (e.g. head_dim 128 allows q_len * n_heads <= 126).
  * The first call on each device looks up the array's device address with
- * that device current; make that first call before any stream capture.
+ * that device current; make that first call before any stream capture.  The
+ * address is kept for the life of the process: after cudaDeviceReset (or
+ * anything else that destroys and re-creates the device's primary context)
+ * it is stale, so do not call this entry point on that device again.
  * Every call on a device shares the one array: calls that overlap on the GPU
  * (different streams, no ordering between them) race and give wrong output.
  * The counters it needs at zero are cleared on `stream` by every call. */

@@ -1139,6 +1139,13 @@ int or_kv_get(const or_kv *kv, size_t layer, float *k, float *v) {
   memcpy(v, kv->v[layer], kv->len * kv->kvd * sizeof(float));
   return 0;
 }
+int or_kv_set(or_kv *kv, size_t layer, const float *k, const float *v, size_t len) {
+  if (layer >= kv->n_layers || len > kv->max_ctx) return -1;
+  memcpy(kv->k[layer], k, len * kv->kvd * sizeof(float));
+  memcpy(kv->v[layer], v, len * kv->kvd * sizeof(float));
+  kv->len = len;
+  return 0;
+}
 static float kv_round(const or_kv *kv, float x) { return kv->f16 ? or_f16_to_f32(or_f32_to_f16(x)) : x; }
 
 /* ------------------------------------------------------------------------ */
@@ -1308,6 +1315,135 @@ double or_time_layer(or_model *m, size_t layer, double *macs) {
   free(y);
   return (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
 }
+
+/* ---- whole-token timing in the reference's order (CPU baseline) ---- */
+static double now_s(void) {
+  struct timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return (double)t.tv_sec + 1e-9 * (double)t.tv_nsec;
+}
+
+typedef struct { const or_tensor *t; size_t n, chunk; float *out; } dq_ctx;
+static void dq_task(void *vctx, size_t task) {
+  dq_ctx *x = (dq_ctx *)vctx;
+  size_t e0 = task * x->chunk, n = e0 + x->chunk <= x->n ? x->chunk : x->n - e0;
+  tensor_slice(x->t, e0, n, x->out + e0);
+}
+/* the reference holds every weight as f32 after load (src/model.rs:252-298):
+ * this rebuilds that copy of one tensor, with all threads, outside the timed
+ * region */
+static float *dequant_all(const or_model *m, const or_tensor *t, size_t n) {
+  float *w = (float *)malloc(n * sizeof(float));
+  dq_ctx x = {t, n, (size_t)256 * 4096, w};
+  parallel_for(m->threads, (n + x.chunk - 1) / x.chunk, dq_task, &x);
+  return w;
+}
+
+void or_kv_fill_synthetic(or_kv *kv, size_t len, uint64_t seed) {
+  if (len > kv->max_ctx) len = kv->max_ctx;
+  uint64_t s = seed * 6364136223846793005ull + 1442695040888963407ull;
+  for (size_t l = 0; l < kv->n_layers; ++l)
+    for (size_t i = 0; i < len * kv->kvd; ++i) {
+      s = s * 6364136223846793005ull + 1442695040888963407ull;
+      kv->k[l][i] = (float)((s >> 40) & 0xFFFF) * (1.0f / 65536.0f) - 0.5f;
+      kv->v[l][i] = (float)((s >> 24) & 0xFFFF) * (1.0f / 65536.0f) - 0.5f;
+    }
+  kv->len = len;
+}
+
+/* One decode token through ModelWeights::forward in the reference's order and
+ * data movement (src/model.rs:316-455): per layer rms_norm, the q/k/v
+ * matmuls (i-j-p, src/tensor.rs:244-258), RoPE on q and k with the table
+ * rebuilt per call (src/model.rs:469-491), the cache append, expand_kv_heads
+ * copying the whole cache to n_heads heads (src/model.rs:500-526), attention
+ * over the expanded rows (src/tensor.rs:451-551), the o matmul and residual,
+ * rms_norm, gate/up matmuls, SiLU, product, down matmul and residual; then the
+ * output norm, the head matmul and the greedy pick (softmax + first argmax,
+ * src/sampling.rs:110-152).  Only the first n_layers_timed layers run (all
+ * when 0).  Weights are dequantised to f32 before each matmul outside the
+ * timed region (the reference does that once at load).  One thread for all
+ * timed work.  out[0] = seconds in the layers, out[1] = seconds in the head
+ * and the pick.  Returns the picked id, or -1 when the cache is full. */
+long or_time_token(or_model *m, or_kv *kv, uint32_t token, size_t pos, size_t n_layers_timed, double out[2]) {
+  const or_config *c = &m->cfg;
+  const size_t d = c->n_embd, H = c->n_heads, KVH = c->n_kv_heads, hd = c->head_dim;
+  const size_t qd = H * hd, kvd = KVH * hd, F = c->n_ff_used, V = c->vocab_size, rep = H / KVH;
+  if (kv->len + 1 > kv->max_ctx || token >= V) return -1;
+  const size_t NL = n_layers_timed && n_layers_timed < c->n_layers ? n_layers_timed : c->n_layers;
+  const size_t T = kv->len + 1;
+  float *x = (float *)malloc(d * sizeof(float)), *xn = (float *)malloc(d * sizeof(float));
+  float *q = (float *)malloc(qd * sizeof(float)), *k = (float *)malloc(kvd * sizeof(float));
+  float *v = (float *)malloc(kvd * sizeof(float)), *att = (float *)malloc(qd * sizeof(float));
+  float *proj = (float *)malloc(d * sizeof(float)), *g = (float *)malloc(F * sizeof(float));
+  float *u = (float *)malloc(F * sizeof(float)), *sc = (float *)malloc(T * sizeof(float));
+  float *ek = (float *)malloc(T * qd * sizeof(float)), *ev = (float *)malloc(T * qd * sizeof(float));
+  float *wn = (float *)malloc(d * sizeof(float));
+  double t_layers = 0.0, t0;
+  tensor_slice(&m->embd, (size_t)token * d, d, x);
+  for (size_t l = 0; l < NL; ++l) {
+    const or_tensor *L = &m->layers[l * T_PER_LAYER];
+    float *w1 = dequant_all(m, &L[T_NORM1], d), *w2 = dequant_all(m, &L[T_NORM2], d);
+    float *wq = dequant_all(m, &L[T_Q], d * qd), *wk = dequant_all(m, &L[T_K], d * kvd);
+    float *wv = dequant_all(m, &L[T_V], d * kvd), *wo = dequant_all(m, &L[T_O], qd * d);
+    t0 = now_s();
+    or_rms_norm(x, w1, d, c->norm_eps, xn);
+    or_matmul(xn, wq, 1, d, qd, q);
+    or_matmul(xn, wk, 1, d, kvd, k);
+    or_matmul(xn, wv, 1, d, kvd, v);
+    or_apply_rope_to_tensor(q, qd, H, hd, pos, c->rope_base);
+    or_apply_rope_to_tensor(k, kvd, KVH, hd, pos, c->rope_base);
+    memcpy(kv->k[l] + kv->len * kvd, k, kvd * sizeof(float));
+    memcpy(kv->v[l] + kv->len * kvd, v, kvd * sizeof(float));
+    for (size_t s = 0; s < T; ++s)
+      for (size_t h = 0; h < KVH; ++h)
+        for (size_t r = 0; r < rep; ++r) {
+          memcpy(ek + s * qd + (h * rep + r) * hd, kv->k[l] + s * kvd + h * hd, hd * sizeof(float));
+          memcpy(ev + s * qd + (h * rep + r) * hd, kv->v[l] + s * kvd + h * hd, hd * sizeof(float));
+        }
+    sdpa_gqa(q, ek, ev, 1, T, H, H, hd, att, sc);
+    or_matmul(att, wo, 1, qd, d, proj);
+    for (size_t i = 0; i < d; ++i) x[i] = x[i] + proj[i];
+    t_layers += now_s() - t0;
+    free(wq); free(wk); free(wv); free(wo);
+    float *wg = dequant_all(m, &L[T_GATE], d * F), *wu = dequant_all(m, &L[T_UP], d * F);
+    t0 = now_s();
+    or_rms_norm(x, w2, d, c->norm_eps, xn);
+    or_matmul(xn, wg, 1, d, F, g);
+    or_silu(g, F, g);
+    or_matmul(xn, wu, 1, d, F, u);
+    for (size_t i = 0; i < F; ++i) g[i] = g[i] * u[i];
+    t_layers += now_s() - t0;
+    free(wg); free(wu);
+    float *wd = dequant_all(m, &L[T_DOWN], F * d);
+    t0 = now_s();
+    or_matmul(g, wd, 1, F, d, proj);
+    for (size_t i = 0; i < d; ++i) x[i] = x[i] + proj[i];
+    t_layers += now_s() - t0;
+    free(wd); free(w1); free(w2);
+  }
+  kv->len += 1;
+  float *wo_n = dequant_all(m, &m->out_norm, d);
+  float *wh = c->tied_output ? NULL : dequant_all(m, &m->out, d * V);
+  float *logits = (float *)malloc(V * sizeof(float)), *probs = (float *)malloc(V * sizeof(float));
+  t0 = now_s();
+  or_rms_norm(x, wo_n, d, c->norm_eps, wn);
+  if (wh) {
+    or_matmul(wn, wh, 1, d, V, logits);
+  } else {
+    for (size_t j = 0; j < V; ++j) logits[j] = 0.0f;
+    tied_ctx tc = {m, wn, 1, logits};
+    parallel_for(1, (V + 63) / 64, tied_task, &tc);
+  }
+  or_softmax_probs(logits, V, probs);
+  const long id = (long)or_argmax(probs, V);
+  out[1] = now_s() - t0;
+  out[0] = t_layers;
+  free(wo_n); free(wh); free(logits); free(probs);
+  free(x); free(xn); free(q); free(k); free(v); free(att); free(proj); free(g); free(u); free(sc);
+  free(ek); free(ev); free(wn);
+  return id;
+}
+
 
 /* ------------------------------------------------------------------------ */
 /* sampler, src/sampling.rs:95-310                                           */

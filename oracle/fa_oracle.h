@@ -125,6 +125,9 @@ void or_kv_clear(or_kv *kv);
 size_t or_kv_len(const or_kv *kv);
 /* copies layer `layer` K and V rows [0, len) into k/v (len*n_kv*hd floats) */
 int or_kv_get(const or_kv *kv, size_t layer, float *k, float *v);
+/* test helper: layer `layer` rows [0, len) from k/v; the cache length
+ * becomes len (set every layer before a forward) */
+int or_kv_set(or_kv *kv, size_t layer, const float *k, const float *v, size_t len);
 
 /* ModelWeights::forward (src/model.rs:316-455): reference semantics, every
  * token of the batch at the same position, no mask.  logits: n*V floats.
@@ -141,6 +144,15 @@ int or_prefill(or_model *m, const uint32_t *tokens, size_t n, size_t pos0, or_kv
 /* CPU-baseline sample: seconds for one token's matmuls of one layer in the
  * reference's i-j-p order; *macs receives the multiply-add count */
 double or_time_layer(or_model *m, size_t layer, double *macs);
+/* CPU baseline: one decode token in the reference's order and data movement
+ * (all matmuls i-j-p, RoPE, expand_kv_heads, attention, output head, greedy
+ * pick), one thread, weights dequantised outside the timed region; the first
+ * n_layers_timed layers (0: all).  out[0] / out[1]: seconds in the layers /
+ * in the head and pick.  Returns the picked id or -1 (cache full, bad id). */
+long or_time_token(or_model *m, or_kv *kv, uint32_t token, size_t pos, size_t n_layers_timed, double out[2]);
+/* timing only: rows [0, len) of every layer's K/V set to deterministic
+ * pseudo-random values in [-0.5, 0.5), len = the cache length afterwards */
+void or_kv_fill_synthetic(or_kv *kv, size_t len, uint64_t seed);
 
 /* ---- sampler (src/sampling.rs:14-310) ---- */
 typedef struct {

@@ -126,7 +126,46 @@ def lib():
         L.or_argmax.argtypes = [fp, sz]; L.or_argmax.restype = sz
         L.or_generate.argtypes = [vp, C.POINTER(_GenCfg), u32p, sz, u32p, sz, C.c_int]; L.or_generate.restype = C.c_long
         L.or_time_layer.argtypes = [vp, sz, C.POINTER(C.c_double)]; L.or_time_layer.restype = C.c_double
+        L.or_time_token.argtypes = [vp, vp, C.c_uint32, sz, sz, C.POINTER(C.c_double)]
+        L.or_time_token.restype = C.c_long
+        L.or_kv_fill_synthetic.argtypes = [vp, sz, C.c_uint64]
+        L.or_kv_set.argtypes = [vp, sz, fp, fp, sz]; L.or_kv_set.restype = C.c_int
     return _lib
+
+
+class _SynthSpec(C.Structure):  # fa_synth_spec of include/fishai_cuda.h
+    _fields_ = [("n_layers", C.c_uint32), ("n_embd", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+                ("n_ff", C.c_uint32), ("vocab", C.c_uint32), ("context_len", C.c_uint32), ("rope_base", C.c_float),
+                ("norm_eps", C.c_float), ("sigma", C.c_float), ("type_embd", C.c_int32), ("type_q", C.c_int32),
+                ("type_k", C.c_int32), ("type_v", C.c_int32), ("type_o", C.c_int32), ("type_gate", C.c_int32),
+                ("type_up", C.c_int32), ("type_down", C.c_int32), ("type_out", C.c_int32), ("threads", C.c_uint32)]
+
+
+_synth = None
+
+
+def write_gguf(path: str, seed: int, threads: int = 0, **fields) -> str:
+    """The package's synthetic GGUF writer through oracle/build/libsynth.so
+    (host code only; byte-identical to fa_synth_write), for callers that must
+    not load the CUDA library: the CPU reference arm of bench.py."""
+    global _synth
+    if _synth is None:
+        build()
+        _synth = C.CDLL(os.path.join(_HERE, "build", "libsynth.so"))
+        _synth.or_synth_write.argtypes = [C.c_char_p, C.POINTER(_SynthSpec), C.c_uint64]
+        _synth.or_synth_write.restype = C.c_int
+        _synth.or_synth_last_error.argtypes = [C.c_char_p, C.c_size_t]
+        _synth.or_synth_last_error.restype = C.c_size_t
+    s = _SynthSpec()
+    s.threads = threads
+    s.type_out = fields.pop("type_out", -1)
+    for k, v in fields.items():
+        setattr(s, k, v)
+    if _synth.or_synth_write(str(path).encode(), C.byref(s), seed):
+        buf = C.create_string_buffer(512)
+        _synth.or_synth_last_error(buf, 512)
+        raise ValueError(buf.value.decode())
+    return str(path)
 
 
 def _f(a):
@@ -356,6 +395,16 @@ class Model:
         s = lib().or_time_layer(self.h, layer, C.byref(macs))
         return s, macs.value
 
+    def time_token(self, kv, token, pos, layers=0):
+        """One decode token in the reference's order and data movement, one
+        thread (or_time_token): (seconds in the first `layers` layers (0: all),
+        seconds in the output head and greedy pick, picked id)."""
+        out = (C.c_double * 2)()
+        tok = lib().or_time_token(self.h, kv.h, int(token), int(pos), int(layers), out)
+        if tok < 0:
+            raise ValueError("or_time_token: cache full or token out of range")
+        return out[0], out[1], int(tok)
+
     def kv(self, max_ctx, kv_f16=False):
         return KV(self, max_ctx, kv_f16)
 
@@ -408,6 +457,18 @@ class KV:
 
     def __len__(self):
         return lib().or_kv_len(self.h)
+
+    def set(self, layer, k, v):
+        """layer `layer` rows from k, v ([len][n_kv*hd] f32); the cache length
+        becomes len"""
+        k, kp = _f(np.asarray(k).reshape(-1))
+        v, vp = _f(np.asarray(v).reshape(-1))
+        if lib().or_kv_set(self.h, layer, kp, vp, k.size // self.kvd):
+            raise IndexError("or_kv_set: bad layer or length")
+
+    def fill_synthetic(self, length, seed=0):
+        """timing only: `length` cached rows of pseudo-random K/V values"""
+        lib().or_kv_fill_synthetic(self.h, int(length), int(seed))
 
     def clear(self):
         lib().or_kv_clear(self.h)

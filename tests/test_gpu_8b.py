@@ -44,3 +44,26 @@ def test_8b_q4_k_m_first_64_greedy_ids_match_golden(step_kernel):
         assert ids == g["greedy_ids"]
     finally:
         m.close()
+
+
+@pytest.mark.skipif(not os.path.exists(GOLDEN), reason="fixture not generated: python tests/golden/make_golden.py 8b")
+@pytest.mark.parametrize("prefill", ["exact", "tc"])
+def test_8b_benchmark_configuration_greedy_ids(prefill):
+    """The configuration bench.py times: f16 KV cache, the prompt prefilled
+    (exact = f32 token steps; tc = f16 tensor-core GEMMs and flash attention),
+    the last prompt token fed again at position P (src/model.rs:656-657), then
+    greedy steps through the captured decode graph.  The first 64 ids must
+    equal the oracle's (whose cache is f32)."""
+    from fishai_engine import _lib as L
+
+    g = json.load(open(GOLDEN))
+    path = synth.cached_preset(g["preset"])
+    m = ModelWeights.load_from_gguf(path, use_tc_prefill=prefill == "tc")
+    try:
+        prompt = g["prompt"]
+        kv = m.new_kv_cache(len(prompt) + 80, dtype=L.KV_F16)
+        m.prefill(prompt, 0, kv, want_logits=False)
+        ids = m.decode_greedy(kv, prompt[-1], len(prompt), 64).tolist()
+        assert ids == g["greedy_ids"], [i for i in range(64) if ids[i] != g["greedy_ids"][i]][:1]
+    finally:
+        m.close()

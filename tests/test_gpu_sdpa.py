@@ -16,7 +16,7 @@ def mar(a, b):
 def test_reference_known_answers():
     from fishai_engine.tensor import scaled_dot_product_attention as sdpa
 
-    out = sdpa([1.0, 0.0], [1.0, 0.0, 0.0, 1.0], [1.0, 0.0, 0.0, 1.0], 1, 2).cpu().numpy()
+    out = sdpa([1.0, 0.0], [1.0, 0.0, 0.0, 1.0], [1.0, 0.0, 0.0, 1.0], 1, 2).reshape(-1)
     assert abs(out[0] - 0.67) < 0.05 and abs(out[1] - 0.33) < 0.05
 
 
@@ -29,10 +29,28 @@ def test_matches_oracle(q_len, kv_len, H, KVH, hd):
     q = rng.normal(0, 1, (q_len, H * hd)).astype(np.float32)
     k = rng.normal(0, 1, (kv_len, KVH * hd)).astype(np.float32)
     v = rng.normal(0, 1, (kv_len, KVH * hd)).astype(np.float32)
-    got = sdpa(q, k, v, H, hd, KVH).cpu().numpy().reshape(q_len, H * hd)
+    got = sdpa(q, k, v, H, hd, KVH).reshape(q_len, H * hd)
     # the reference expands kv heads (src/model.rs:500-526) then runs SDPA
     rep = H // KVH
     ke = np.repeat(k.reshape(kv_len, KVH, hd), rep, axis=1).reshape(kv_len, H * hd)
     ve = np.repeat(v.reshape(kv_len, KVH, hd), rep, axis=1).reshape(kv_len, H * hd)
     want = O.sdpa(q, ke, ve, H, hd).reshape(q_len, H * hd)
     assert mar(got, want) <= 1e-5
+
+
+def test_device_pointer_form_matches_host_form():
+    import torch
+
+    from fishai_engine.tensor import scaled_dot_product_attention as sdpa
+    from fishai_engine.tensor import scaled_dot_product_attention_device as sdpa_dev
+
+    rng = np.random.default_rng(7)
+    q = rng.normal(0, 1, (2, 8 * 64)).astype(np.float32)
+    k = rng.normal(0, 1, (100, 2 * 64)).astype(np.float32)
+    v = rng.normal(0, 1, (100, 2 * 64)).astype(np.float32)
+    want = sdpa(q, k, v, 8, 64, 2)
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    od = torch.empty_like(qd)
+    sdpa_dev(qd, kd, vd, od, 2, 100, 8, 64, 2, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(od.cpu().numpy(), want)

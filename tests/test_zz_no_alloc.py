@@ -62,3 +62,40 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     rc = _call("fa_sdpa_noalloc", q, k, k, q_len, kv_len, H, KVH, hd, out)
     assert rc == L.ERR_INVALID
     assert "exceeds the fixed scratch" in L.last_error()
+
+
+def test_noalloc_allocates_no_device_memory():
+    """After one warm call, a call with a larger shape than any before it
+    leaves the device's free memory unchanged (fa_sdpa, by contrast, grows its
+    scratch for such a call)."""
+    import torch
+    from fishai_engine import _lib as L
+
+    def run(q_len, kv_len, H, KVH, hd):
+        q = torch.ones(q_len, H * hd, device="cuda")
+        k = torch.ones(kv_len, KVH * hd, device="cuda")
+        out = torch.empty_like(q)
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        L.check(_call("fa_sdpa_noalloc", q, k, k, q_len, kv_len, H, KVH, hd, out))
+        torch.cuda.synchronize()
+        return free0, torch.cuda.mem_get_info()[0]
+
+    run(1, 16, 4, 4, 64)  # warm: symbol lookup, module load
+    before, after = run(3, 4096, 32, 8, 128)  # larger than any call so far
+    assert before == after
+
+
+def test_noalloc_rejects_too_many_query_rows_per_kv_head():
+    """the second limit: q_len * n_kv_heads <= 1024 (here 129 * 8 = 1032
+    while the partials, 129 * 8 * 32 * 4 floats, would still fit)"""
+    import torch
+    from fishai_engine import _lib as L
+
+    q_len, kv_len, H, KVH, hd = 129, 4, 8, 8, 2
+    q = torch.zeros(q_len, H * hd, device="cuda")
+    k = torch.zeros(kv_len, KVH * hd, device="cuda")
+    out = torch.zeros_like(q)
+    rc = _call("fa_sdpa_noalloc", q, k, k, q_len, kv_len, H, KVH, hd, out)
+    assert rc == L.ERR_INVALID
+    assert "q_len*n_kv_heads = 1032" in L.last_error()
