@@ -14,9 +14,11 @@ before the timed steps continue the same sequence.
   python bench.py --profile gateup --layers 2 --reps 3   # one GEMV kind on a
       reduced-depth model of the same shapes (small cases for ncu captures)
 
-With N > 1 (torchrun) every rank runs an independent replica of the b=1
-decode (it does not shard); value = all ranks' tokens / max rank time.
-Prints one JSON line (rank 0)."""
+With N > 1 (torchrun) every rank runs an independent replica of the 8B b=1
+decode (it does not shard); value = all ranks' tokens / max rank time.  The
+"tp70b" key carries the 70B-shaped model tensor-parallel over the same N
+GPUs (NCCL all-reduce after every o and down projection); at N = 1 it is
+that model on one GPU.  Prints one JSON line (rank 0)."""
 from __future__ import annotations
 
 import argparse
@@ -303,6 +305,122 @@ def greedy_config(name, args, local, peak):
     return out
 
 
+TP_PRESET = "llama3-70b-q4_k"
+
+
+def tp70b_leg(args, world, rank, local, pg, peak):
+    """Config 5: the Llama-3-70B-shaped Q4_K model (Q6_K head, seed 4) on
+    all ranks of the job as one tensor-parallel model (TP = world; world 1 is
+    the single-GPU figure): a 4096-token prompt through the tensor-core
+    prefill, the last prompt token fed again, greedy decode timed with CUDA
+    events (max over ranks); then 16 sequences of 2048-token contexts decoding
+    together.  Every rank computes the same ids (replicated head)."""
+    import numpy as np
+    import torch
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights, tp_unique_id
+    from fishai_engine.sampling import Sampler, SamplerConfig
+
+    over = {"n_layers": args.tp_layers} if args.tp_layers else {}
+    if rank == 0:
+        synth.cached_preset(TP_PRESET, **over)
+    if pg:
+        pg.barrier()
+    path = synth.cached_preset(TP_PRESET, **over)
+    uid = None
+    if world > 1:
+        box = [tp_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(box, src=0)
+        uid = box[0]
+    t0 = time.perf_counter()
+    m = ModelWeights.load_from_gguf(path, device=local, tp_rank=rank, tp_world=world, nccl_id=uid,
+                                    use_tc_prefill=True)
+    load_s = time.perf_counter() - t0
+    cfg = m.config
+    _, wbytes = m.weight_bytes()
+    P, G, K = 4096, 8, args.tp_steps
+    prompt = np.random.default_rng(4).integers(3, cfg.vocab_size, P).tolist()
+    kv = m.new_kv_cache(P + G + K + 8, dtype=L.KV_F16)
+    stream = torch.cuda.ExternalStream(L.lib().fa_model_stream(m._h))
+    t0 = time.perf_counter()
+    m.prefill(prompt, 0, kv, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    ids = m.decode_greedy(kv, prompt[-1], P, G)  # warm-up: graph capture, NCCL connections
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ids2 = m.decode_greedy(kv, int(ids[-1]), P + G, K)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    agree = True
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        mine = torch.tensor(ids2.astype(np.int64), device="cuda")
+        first = mine.clone()
+        pg.broadcast(first, src=0)
+        ok = torch.tensor([int(torch.equal(mine, first))], device="cuda")
+        pg.all_reduce(ok, op=pg.ReduceOp.MIN)
+        agree = bool(ok.item())
+    mean_ctx = P + G + (K + 1) / 2.0
+    hd = cfg.head_dim
+    kv_local = 2 * cfg.n_layers * m.local_kv_heads * hd * 2 * mean_ctx
+    gpu_bytes = wbytes + kv_local  # what one GPU streams per token (its shards + replicated head)
+    gbs = gpu_bytes * K / (ms / 1000.0) / 1e9
+    out = {"value": K / (ms / 1000.0), "unit": "tok/s",
+           "model": f"{TP_PRESET} synthetic GGUF (seed 4)" + (f", first {args.tp_layers} layers" if over else ""),
+           "tp": world, "batch": 1, "prompt": P, "steps": K, "ms_per_step": ms / K, "kv_cache": "f16",
+           "prefill": "tc", "prefill_wall_s": prefill_s, "load_s": load_s, "ranks_agree_on_ids": agree,
+           "all_reduces_per_token": 2 * cfg.n_layers if world > 1 else 0,
+           "roofline": {"bound": "hbm", "bytes_per_gpu_per_step": gpu_bytes, "achieved_gbs_per_gpu": gbs,
+                        "peak": peak, "unit": "GB/s", "frac": gbs / peak}}
+    del kv
+    # 16 sequences with 2048-token contexts, greedy, decoding together
+    B, Pb, Kb = 16, 2048, args.tp_batch_steps
+    if Kb > 0:
+        kvb = m.new_kv_cache(Pb + Kb + 16, dtype=L.KV_F16, n_seq=B)
+        rng = np.random.default_rng(4)
+        last = []
+        for r in range(B):
+            pr = rng.integers(3, cfg.vocab_size, Pb).tolist()
+            m.prefill(pr, 0, kvb, seq=r, want_logits=False)
+            last.append(pr[-1])
+        smp = Sampler(SamplerConfig(0.0, 0, 1.0, 1.0, 0.0, 0.0), cfg.vocab_size, seeds=list(range(B)))
+        w = m.decode_batch(kvb, last, [Pb] * B, smp, 2)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        m.decode_batch(kvb, w[-1].tolist(), [Pb + 2] * B, smp, Kb)
+        e1.record(stream)
+        e1.synchronize()
+        bms = e0.elapsed_time(e1)
+        if pg:
+            t = torch.tensor([bms], device="cuda")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            bms = float(t.item())
+        bkv = 2 * cfg.n_layers * m.local_kv_heads * hd * 2 * (Pb + 2 + (Kb + 1) / 2.0) * B
+        bgbs = (wbytes + bkv) * Kb / (bms / 1000.0) / 1e9
+        out["b16"] = {"value": B * Kb / (bms / 1000.0), "unit": "tok/s", "batch": B, "context": Pb, "steps": Kb,
+                      "ms_per_step": bms / Kb, "sampler": "greedy",
+                      "roofline": {"bound": "hbm", "bytes_per_gpu_per_step": wbytes + bkv,
+                                   "achieved_gbs_per_gpu": bgbs, "peak": peak, "unit": "GB/s", "frac": bgbs / peak}}
+        del kvb, smp
+    m.close()
+    if rank == 0 and world == 1 and args.cpu_layers > 0:
+        per_tok, ls, hs, n, nl = cpu_token_sample(path, P, 1, os.cpu_count() or 1)
+        out["cpu_baseline"] = {"value": 1.0 / per_tok, "unit": "tok/s", "cores": 1, "kind": "port",
+                               "sample": f"one decode token at context {P} in the reference's order on one core: "
+                                         f"1 of {nl} layers {ls:.1f}s + output head and greedy pick {hs:.1f}s; "
+                                         f"per-token time = head + layer x {nl}"}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -318,7 +436,13 @@ def main():
                     help="layers of the whole-token CPU sample beside our figure (0: skip)")
     ap.add_argument("--ref-tokens", type=int, default=1, help="whole decode tokens the reference arm times")
     ap.add_argument("--configs", default="tiny,7b",
-                    help="other workload shapes reported at one GPU (tiny, 7b, 70b; empty: none)")
+                    help="other workload shapes reported at one GPU (tiny, 7b; empty: none)")
+    ap.add_argument("--tp70b", type=int, choices=[0, 1], default=1,
+                    help="1: the 70B-shaped model, tensor-parallel over all ranks of the job (one GPU at N=1)")
+    ap.add_argument("--tp-steps", type=int, default=128, help="timed greedy steps of the 70B leg")
+    ap.add_argument("--tp-batch-steps", type=int, default=32, help="timed steps of the 70B b=16 leg (0: skip)")
+    ap.add_argument("--tp-layers", type=int, default=0,
+                    help="reduced-depth 70B-shaped model for quick checks (0: all 80 layers)")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode figure (0: skip)")
     ap.add_argument("--batch-prompt", type=int, default=4096)
     ap.add_argument("--batch-steps", type=int, default=128)
@@ -496,12 +620,14 @@ def main():
                "gemm": gemm}
     m.close()
 
+    tp70b = tp70b_leg(args, world, rank, local, pg, peak) if args.tp70b and not ml else None
+
     # batched decode on the 8B Q8_0 model (seed 3): 64 sequences with
     # 4096-token prompts prefilled into the paged f16 cache, then 128 steps
     # sampled with T 0.8, top-k 40, top-p 0.9 (Philox seed 1000 + i), all
     # sequences one token per step
     batch = None
-    if args.batch > 0:
+    if args.batch > 0 and world == 1:
         from fishai_engine.sampling import Sampler, SamplerConfig
 
         if rank == 0:
@@ -548,7 +674,7 @@ def main():
         mb.close()
 
     extra = {}
-    if not ml:
+    if not ml and world == 1:
         for name in [c for c in args.configs.split(",") if c]:
             extra[name] = greedy_config(name, args, local, peak)
 
@@ -585,6 +711,7 @@ def main():
         "prefill": prefill,
         "decode_b64": batch,
         "configs": extra,
+        "tp70b": tp70b,
         "gpu_launches": launches * K,
         "launches_per_step": launches,
         "clocks": clocks,

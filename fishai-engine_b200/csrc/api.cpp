@@ -16,6 +16,7 @@
 #include "gguf.hpp"
 #include "model.hpp"
 #include "sdpa.hpp"
+#include "tp.hpp"
 
 namespace fa {
 int synth_write(const char *path, const fa_synth_spec *s, uint64_t seed);
@@ -56,7 +57,7 @@ void copy_str(const std::string &s, char *buf, size_t cap) {
 int check_err_flags(Model &m, const SeqState *st_dev) {
   SeqState st;
   API_CUDA(cudaMemcpyAsync(&st, st_dev, sizeof st, cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   if (st.err & kErrWaitTimeout) {
     m.step_kv = nullptr;  // the step kernel's phase counters are void: upload a fresh plan next time
     return fail(FA_ERR_TIMEOUT, "a bounded device wait gave up");
@@ -190,7 +191,7 @@ int forward_compat(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens
                                          cudaMemcpyDeviceToHost, m.stream));
   }
   if (hidden) API_CUDA(cudaMemcpyAsync(hidden, hid_dev, (size_t)m.cfg.n_layers * n * d * 4, cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   for (uint32_t t = 0; t < n; ++t) {
     if ((rc = check_err_flags(m, fm->compat[t].state))) return rc;
     if (argmax) {
@@ -484,7 +485,6 @@ int fa_model_load(const char *path, const fa_model_opts *opts, fa_model **out) {
   fa_model_opts o;
   if (opts) o = *opts;
   else fa_model_opts_default(&o);
-  if (o.tp_world > 1) return fail(FA_ERR_UNSUPPORTED, "tensor parallel load goes through fa_model_load with TP support");
   fa_model *m = new (std::nothrow) fa_model();
   if (!m) return fail(FA_ERR_OOM, "out of memory");
   int rc = m->m.load(path, o);
@@ -500,7 +500,50 @@ void fa_model_free(fa_model *m) { delete m; }
 int fa_model_config(const fa_model *m, fa_config *cfg) {
   API_NULL(m);
   API_NULL(cfg);
-  *cfg = m->m.cfg;
+  *cfg = m->m.gcfg;
+  return FA_OK;
+}
+int fa_model_tp(const fa_model *m, int32_t *rank, int32_t *world, uint32_t *local_heads, uint32_t *local_kv_heads,
+                uint32_t *local_ff) {
+  API_NULL(m);
+  if (rank) *rank = m->m.tp.rank;
+  if (world) *world = m->m.tp.world;
+  if (local_heads) *local_heads = m->m.cfg.n_heads;
+  if (local_kv_heads) *local_kv_heads = m->m.cfg.n_kv_heads;
+  if (local_ff) *local_ff = m->m.cfg.n_ff_used;
+  return FA_OK;
+}
+int fa_tp_unique_id(void *out128) {
+  API_NULL(out128);
+  std::string msg;
+  if (tp_unique_id(out128, &msg)) return fail(FA_ERR_NCCL, "ncclGetUniqueId: " + msg);
+  return FA_OK;
+}
+int fa_tp_shard(int32_t ggml_type, const void *bytes_host, uint32_t K, uint32_t N, int32_t axis, uint32_t rank,
+                uint32_t world, void *out_host, size_t cap, size_t *out_bytes, uint32_t *row_bytes) {
+  API_NULL(bytes_host);
+  API_NULL(out_bytes);
+  if (!world || rank >= world) return fail(FA_ERR_INVALID, "fa_tp_shard: rank out of range");
+  const uint32_t rb = native_row_bytes(ggml_type, N);
+  if (!type_known(ggml_type) || !rb) return fail(FA_ERR_UNSUPPORTED, "fa_tp_shard: unsupported type");
+  const uint8_t *src = (const uint8_t *)bytes_host;
+  if (axis == 0) {  // rows
+    if (K % world) return fail(FA_ERR_INVALID, "fa_tp_shard: rows do not divide by world");
+    const uint32_t nr = K / world;
+    *out_bytes = (size_t)nr * rb;
+    if (row_bytes) *row_bytes = rb;
+    if (out_host) std::memcpy(out_host, tp_rows(src, rb, rank * nr), std::min(cap, *out_bytes));
+    return FA_OK;
+  }
+  if (N % world) return fail(FA_ERR_INVALID, "fa_tp_shard: columns do not divide by world");
+  const uint32_t nc = N / world;
+  std::vector<uint8_t> buf;
+  uint32_t srb = 0;
+  if (tp_shard_columns(ggml_type, src, K, N, rank * nc, (rank + 1) * nc, buf, &srb))
+    return fail(FA_ERR_UNSUPPORTED, "fa_tp_shard: column shard does not fall on block boundaries");
+  *out_bytes = buf.size();
+  if (row_bytes) *row_bytes = srb;
+  if (out_host) std::memcpy(out_host, buf.data(), std::min(cap, buf.size()));
   return FA_OK;
 }
 int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *step_bytes) {
@@ -635,7 +678,7 @@ int fa_forward(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
   if (hidden)
     API_CUDA(cudaMemcpyAsync(hidden, hid_dev, (size_t)m.cfg.n_layers * m.cfg.n_embd * 4, cudaMemcpyDeviceToHost, m.stream));
   API_CUDA(cudaMemcpyAsync(m.h_state, m.ws.state, sizeof(SeqState), cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   const SeqState st = *m.h_state;
   if (st.err) return check_err_flags(m, m.ws.state);
   if (argmax) argmax[0] = st.token;
@@ -662,7 +705,7 @@ int fa_prefill(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
       API_CUDA(cudaMemcpyAsync(last_logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
     SeqState st;
     API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
-    API_CUDA(cudaStreamSynchronize(m.stream));
+    { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
     if (last_argmax) *last_argmax = ~(uint32_t)(st.argmax_key & 0xFFFFFFFFull);
     kv->kv.len[seq] += n;
     return FA_OK;
@@ -675,7 +718,7 @@ int fa_prefill(fa_model *fm, fa_kv *kv, uint32_t seq, const uint32_t *tokens, ui
     API_CUDA(cudaMemcpyAsync(last_logits, m.ws.logits, (size_t)m.cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m.stream));
   SeqState st;
   API_CUDA(cudaMemcpyAsync(&st, m.ws.state, sizeof st, cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   if (st.err) return check_err_flags(m, m.ws.state);
   if (last_argmax) *last_argmax = st.token;
   kv->kv.len[seq] += n;
@@ -696,7 +739,7 @@ int fa_decode_greedy(fa_model *fm, fa_kv *kv, uint32_t seq, uint32_t first_token
   if ((rc = set_state(m, m.ws.state, first_token, pos, kv->kv.len[seq], 0))) return rc;
   if ((rc = m.run_steps(kv->kv, seq, steps))) return rc;
   if (ids_host) API_CUDA(cudaMemcpyAsync(ids_host, m.ws.ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   if ((rc = check_err_flags(m, m.ws.state))) return rc;
   kv->kv.len[seq] += steps;
   return FA_OK;
@@ -754,7 +797,7 @@ int fa_generate(fa_model *fm, const fa_gen_config *cfg, const uint32_t *prompt, 
     const uint32_t chunk = std::min<uint32_t>(steps - done, cfg->n_stop ? 32 : steps);
     if ((rc = m.run_steps(kvh.kv, 0, chunk))) return rc;
     API_CUDA(cudaMemcpyAsync(ids.data() + done, m.ws.ids + done, (size_t)chunk * 4, cudaMemcpyDeviceToHost, m.stream));
-    API_CUDA(cudaStreamSynchronize(m.stream));
+    { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
     for (uint32_t s = done; s < done + chunk; ++s) {
       if (s < P) continue;  // prefill logits are discarded
       const uint32_t t = ids[s];
@@ -1086,7 +1129,7 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   uint32_t e = 0;
   API_CUDA(cudaMemcpyAsync(y_host, y.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, m.stream));
   API_CUDA(cudaMemcpyAsync(&e, err.p, 4, cudaMemcpyDeviceToHost, m.stream));
-  API_CUDA(cudaStreamSynchronize(m.stream));
+  { const int sync_rc = m.sync(); if (sync_rc) return sync_rc; }
   if (e) return fail(FA_ERR_TIMEOUT, "token GEMM: a bounded device wait gave up");
   return FA_OK;
 }

@@ -39,14 +39,17 @@ namespace fa {
 
 enum : int { kF32 = 0, kF16 = 1, kQ4_0 = 2, kQ4_1 = 3, kQ5_0 = 6, kQ8_0 = 8, kQ4_K = 12, kQ6_K = 14 };
 
-// bytes of one row of `w` columns in native GGML blocks
+// bytes of one row of `w` columns in native GGML blocks.  A Q4_K row of
+// w = 256 s + 128 columns (a tensor-parallel shard holding half of a
+// super-block) is stored as s + 1 whole blocks, the half block re-encoded as
+// a block whose upper 128 columns are zero (tp_shard_columns).
 FA_HD inline uint32_t native_row_bytes(int type, uint32_t w) {
   switch (type) {
     case kF32: return 4 * w;
     case kF16: return 2 * w;
     case kQ4_0: return w / 32 * 18;
     case kQ8_0: return w / 32 * 34;
-    case kQ4_K: return w / 256 * 144;
+    case kQ4_K: return (w + 255) / 256 * 144;
     case kQ6_K: return w / 256 * 210;
     default: return 0;
   }
@@ -90,7 +93,11 @@ FA_HD inline bool gemv_type_supported(int type) {
 // stores q+128 in 0..255 (value d(u-128)): the same information, re-encoded.
 // ---------------------------------------------------------------------------
 FA_HD inline bool mma_type(int type) { return type == kQ4_K || type == kQ6_K || type == kQ8_0 || type == kQ4_0; }
-FA_HD inline uint32_t mma_group_bytes(int type, uint32_t w) { return 16 * native_row_bytes(type, w); }
+// a Q4_K group holds 8w code bytes and one 16-byte header per row and
+// super-block (so a half super-block takes 8w + 256 bytes, no padding)
+FA_HD inline uint32_t mma_group_bytes(int type, uint32_t w) {
+  return type == kQ4_K ? 8 * w + 256 * ((w + 255) / 256) : 16 * native_row_bytes(type, w);
+}
 // row m / column k of fragment element e of lane l inside a 16x16 tile
 FA_HD inline uint32_t frag_m(uint32_t l, uint32_t e) { return l / 4 + 8 * ((e >> 1) & 1); }
 FA_HD inline uint32_t frag_k(uint32_t l, uint32_t e) { return 2 * (l % 4) + (e & 1) + 8 * (e >> 2); }

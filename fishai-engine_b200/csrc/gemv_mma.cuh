@@ -505,7 +505,35 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     }
   };
   load_batch(0);
-  if (norm) {
+  if (norm && p.n_ssq == 0) {
+    // no sum-of-squares partials (x is the result of a tensor-parallel
+    // all-reduce): each consumer thread squares its float4 share of x, the
+    // warps' sums are added in warp order (deterministic)
+    const float4 *in4 = reinterpret_cast<const float4 *>(p.in);
+    const uint32_t n4 = p.K / 4;
+    float s = 0.0f;
+    for (uint32_t i0 = tid; i0 < n4; i0 += 4 * NT) {
+      float4 a[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t i = i0 + j * NT;
+        a[j] = i < n4 ? __ldcg(in4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j)
+        s = fmaf(a[j].w, a[j].w, fmaf(a[j].z, a[j].z, fmaf(a[j].y, a[j].y, fmaf(a[j].x, a[j].x, s))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    if (lane == 0) sm.red[warp] = s;
+    epi::consumer_bar<kWarps>();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (uint32_t w = 0; w < (uint32_t)kWarps; ++w) t += sm.red[w];
+      sm.red[96] = 1.0f / sqrtf(t / (float)p.K + p.eps);
+    }
+    epi::consumer_bar<kWarps>();
+  } else if (norm) {
     if (warp == 0) {  // lane-strided partial sums in index order, every load in flight
       float s = 0.0f;
       for (uint32_t i0 = 0; i0 < p.n_ssq; i0 += 32 * kPre) {

@@ -4,8 +4,10 @@
 #include "model.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
+#include <thread>
 
 namespace fa {
 
@@ -93,6 +95,9 @@ struct TensorRef {
   size_t nbytes = 0;
   int type = 0;
   uint64_t nelem = 0;
+  uint32_t row_bytes = 0;   // stride of the rows at `data` (0: native_row_bytes of the width)
+  uint32_t algo_bytes = 0;  // bytes a row contributes to the algorithmic count (0: row_bytes)
+  std::vector<uint8_t> own; // storage of a tensor-parallel column shard
 };
 
 int get_tensor(const Gguf &g, const std::string &name, TensorRef *r) {
@@ -114,6 +119,35 @@ uint32_t pick_cw(int type, uint32_t N, bool paired) {
   else if (N >= 512 * 37) cw = 512;
   if (paired && (type == kQ4_K || type == kQ6_K)) cw = std::max(cw, 512u);
   return cw;
+}
+
+// columns [c0, c1) of every row of `src` ([K][N]) as a tensor of its own
+int shard_cols(const TensorRef &src, const char *what, uint32_t K, uint32_t N, uint32_t c0, uint32_t c1,
+               TensorRef *dst) {
+  dst->t = src.t;
+  dst->type = src.type;
+  uint32_t rb = 0;
+  if (tp_shard_columns(src.type, src.data, K, N, c0, c1, dst->own, &rb))
+    return fail(FA_ERR_UNSUPPORTED, std::string("tensor-parallel shard of ") + what + ": columns [" +
+                                        std::to_string(c0) + ", " + std::to_string(c1) +
+                                        ") do not fall on the type's block boundaries");
+  dst->data = dst->own.data();
+  dst->nbytes = dst->own.size();
+  dst->nelem = (uint64_t)K * (c1 - c0);
+  dst->row_bytes = rb;
+  // a half super-block streams its 64 code bytes and the shared 16-byte header
+  dst->algo_bytes = (src.type == kQ4_K && c1 - c0 == 128) ? 80 : rb;
+  return FA_OK;
+}
+
+// rows [r0, r0 + nr) of `src` ([K][N]): a contiguous range of the mapping
+void shard_rows(const TensorRef &src, uint32_t N, uint32_t r0, uint32_t nr, TensorRef *dst) {
+  const uint32_t rb = native_row_bytes(src.type, N);
+  dst->t = src.t;
+  dst->type = src.type;
+  dst->data = tp_rows(src.data, rb, r0);
+  dst->nbytes = (size_t)nr * rb;
+  dst->nelem = (uint64_t)nr * N;
 }
 
 }  // namespace
@@ -155,15 +189,18 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
   for (size_t i = 0; i < nparts; ++i) {
     const TensorRef &a = parts[i];
     const uint32_t N = widths[i];
-    const uint64_t nb = type_nbytes(a.type, (uint64_t)K * N);
+    const uint32_t rb = a.row_bytes ? a.row_bytes : native_row_bytes(a.type, N);
+    const uint64_t nb = (uint64_t)K * rb, ab = (uint64_t)K * (a.algo_bytes ? a.algo_bytes : rb);
+    if (!mma && rb != native_row_bytes(a.type, N))
+      return fail(FA_ERR_UNSUPPORTED, "a half super-block shard needs the tensor-core layout");
     CUDA_TRY(cudaMemcpyAsync(staging, a.data, nb, cudaMemcpyHostToDevice, m.stream));
-    P.native_bytes += nb;
+    P.native_bytes += ab;
     const void *src_b = nullptr;
     if (paired) {
       const TensorRef &b = parts[1];
       if (b.type != a.type) return fail(FA_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a ggml type");
       CUDA_TRY(cudaMemcpyAsync(staging2, b.data, nb, cudaMemcpyHostToDevice, m.stream));
-      P.native_bytes += nb;
+      P.native_bytes += ab;
       src_b = staging2;
     }
     const int rc = mma ? launch_repack_mma(a.type, staging, src_b, K, N, CW, buf, region[i], m.stream)
@@ -351,6 +388,27 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
         if (widths[j] % type_block(t.type)) return fail(FA_ERR_UNSUPPORTED, "projection width not block aligned");
       }
     }
+  // tensor parallelism: this rank keeps query heads [R*H/W, (R+1)*H/W), the
+  // KV heads they read, FFN columns [R*F/W, (R+1)*F/W) of gate and up, and
+  // the matching rows of attn_output and ffn_down (whose partial sums the
+  // ranks add up with an all-reduce); embedding, norms and the output head
+  // are replicated
+  gcfg = cfg;
+  const uint32_t W = o.tp_world > 1 ? (uint32_t)o.tp_world : 1u;
+  const uint32_t R = W > 1 ? (uint32_t)o.tp_rank : 0u;
+  if (W > 1) {
+    if (o.tp_rank < 0 || R >= W) return fail(FA_ERR_INVALID, "tp_rank out of range");
+    if (H % W || KVH % W || F % W)
+      return fail(FA_ERR_UNSUPPORTED, "heads, KV heads and FFN width must divide by the tensor-parallel world");
+    if (cfg.tied_output) return fail(FA_ERR_UNSUPPORTED, "tensor parallelism needs an untied output head");
+    if (!o.nccl_id) return fail(FA_ERR_INVALID, "tensor parallelism needs the rank-0 NCCL unique id");
+    if ((rc = tp.init((int)R, (int)W, o.nccl_id, device))) return rc;
+    want_step = false;  // the persistent step kernel is single-GPU
+  }
+  const uint32_t Hl = H / W, KVHl = KVH / W, Fl = F / W, qdl = Hl * hd, kvdl = KVHl * hd;
+  cfg.n_heads = Hl;
+  cfg.n_kv_heads = KVHl;
+  cfg.n_ff_used = Fl;
   TensorRef temb, onorm, out;
   if ((rc = get_tensor(g, "token_embd.weight", &temb))) return rc;
   if ((rc = get_tensor(g, "output_norm.weight", &onorm))) return rc;
@@ -392,15 +450,28 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
     auto &T = lt[l];
     if ((rc = upload_f32(T[0], &lw.attn_norm))) return rc;
     if ((rc = upload_f32(T[5], &lw.ffn_norm))) return rc;
-    if ((rc = build_plan(*this, lw.qkv, {T[1], T[2], T[3]}, {0, qd, qd + kvd}, false, d, {qd, kvd, kvd}, 256, staging,
+    TensorRef wq, wk, wv, wo, wg, wu, wd;
+    if (W > 1) {
+      if ((rc = shard_cols(T[1], "attn_q", d, qd, R * qdl, (R + 1) * qdl, &wq)) ||
+          (rc = shard_cols(T[2], "attn_k", d, kvd, R * kvdl, (R + 1) * kvdl, &wk)) ||
+          (rc = shard_cols(T[3], "attn_v", d, kvd, R * kvdl, (R + 1) * kvdl, &wv)) ||
+          (rc = shard_cols(T[6], "ffn_gate", d, F, R * Fl, (R + 1) * Fl, &wg)) ||
+          (rc = shard_cols(T[7], "ffn_up", d, F, R * Fl, (R + 1) * Fl, &wu)))
+        return rc;
+      shard_rows(T[4], d, R * qdl, qdl, &wo);
+      shard_rows(T[8], d, R * Fl, Fl, &wd);
+    } else {
+      wq = T[1], wk = T[2], wv = T[3], wo = T[4], wg = T[6], wu = T[7], wd = T[8];
+    }
+    if ((rc = build_plan(*this, lw.qkv, {wq, wk, wv}, {0, qdl, qdl + kvdl}, false, d, {qdl, kvdl, kvdl}, 256, staging,
                          staging2, hd)))
       return rc;
-    if ((rc = build_plan(*this, lw.o, {T[4]}, {0}, false, qd, {d}, pick_cw(T[4].type, d, false), staging, staging2)))
+    if ((rc = build_plan(*this, lw.o, {wo}, {0}, false, qdl, {d}, pick_cw(wo.type, d, false), staging, staging2)))
       return rc;
-    if ((rc = build_plan(*this, lw.gateup, {T[6], T[7]}, {0}, true, d, {F}, pick_cw(T[6].type, 2 * F, true), staging,
+    if ((rc = build_plan(*this, lw.gateup, {wg, wu}, {0}, true, d, {Fl}, pick_cw(wg.type, 2 * Fl, true), staging,
                          staging2)))
       return rc;
-    if ((rc = build_plan(*this, lw.down, {T[8]}, {0}, false, F, {d}, pick_cw(T[8].type, d, false), staging, staging2)))
+    if ((rc = build_plan(*this, lw.down, {wd}, {0}, false, Fl, {d}, pick_cw(wd.type, d, false), staging, staging2)))
       return rc;
     step_bytes += lw.qkv.native_bytes + lw.o.native_bytes + lw.gateup.native_bytes + lw.down.native_bytes;
     step_bytes += type_nbytes(T[0].type, d) + type_nbytes(T[5].type, d);
@@ -427,6 +498,18 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   if (!part || !counters) return fail(FA_ERR_OOM, "GEMV scratch allocation failed");
   CUDA_TRY(cudaMemset(counters, 0, (size_t)max_chunks * sizeof(uint32_t)));
   if ((rc = alloc_workspace(ws))) return rc;
+  if (W > 1) {
+    // the collective replaces the epilogues' sum-of-squares partials with a
+    // prologue that squares x itself: the tensor-core GEMV's mode only
+    for (const LayerW &lw : layers)
+      if (!lw.qkv.mma || !lw.o.mma || !lw.gateup.mma || !lw.down.mma || !head.mma)
+        return fail(FA_ERR_UNSUPPORTED, "tensor parallelism needs Q4_K / Q6_K / Q8_0 / Q4_0 projections");
+    if (!(ar_send = (float *)dmalloc(((size_t)d + 8) * 4))) return fail(FA_ERR_OOM, "all-reduce buffer");
+    // one all-reduce outside any graph capture: NCCL sets up its peer
+    // connections here rather than inside the first captured step
+    CUDA_TRY(cudaMemsetAsync(ar_send, 0, ((size_t)d + 8) * 4, stream));
+    if ((rc = tp.all_reduce(ar_send, ar_send, d, stream)) || (rc = sync())) return rc;
+  }
   if ((rc = setup_step_kernel())) return rc;
   gguf.reset();  // host mapping no longer needed
   return FA_OK;
@@ -506,6 +589,10 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
   p.norm_w = lw.attn_norm;
   p.ssq = l == 0 ? w.ssq_e : w.ssq_d;
   p.n_ssq = l == 0 ? embed_ctas : layers[l - 1].down.parts();
+  if (l > 0 && tp.world > 1) {  // x came from an all-reduce: the prologue sums its squares itself
+    p.ssq = nullptr;
+    p.n_ssq = 0;
+  }
   p.eps = cfg.norm_eps;
   p.epi = kEpiQkv;
   p.out = w.q;
@@ -567,13 +654,22 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.resid = w.x;
   p.ssq_out = w.ssq_o;
   p.state = st;
+  // tensor parallel: rank 0 adds its partial sums to the residual in place,
+  // the others store theirs; the all-reduce then leaves x + sum on every rank
+  const bool part = tp.world > 1 && tp.rank > 0;
+  if (part) {
+    p.epi = kEpiStore;
+    p.out = ar_send;
+  }
+  int rc;
   if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "o gemv launch failed");
+  if (tp.world > 1 && (rc = tp_reduce(w.x, ar_send, cfg.n_embd))) return rc;
   p = gemv_base(lw.gateup);
   p.pro = kProRmsNorm;
   p.in = w.x;
   p.norm_w = lw.ffn_norm;
-  p.ssq = w.ssq_o;
-  p.n_ssq = lw.o.parts();
+  p.ssq = tp.world > 1 ? nullptr : w.ssq_o;
+  p.n_ssq = tp.world > 1 ? 0 : lw.o.parts();
   p.eps = cfg.norm_eps;
   p.epi = kEpiSwiglu;
   p.out = w.h;
@@ -586,7 +682,12 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.resid = w.x;
   p.ssq_out = w.ssq_d;
   p.state = st;
+  if (part) {
+    p.epi = kEpiStore;
+    p.out = ar_send;
+  }
   if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "down gemv launch failed");
+  if (tp.world > 1 && (rc = tp_reduce(w.x, ar_send, cfg.n_embd))) return rc;
   if (hidden_dump)
     CUDA_TRY(cudaMemcpyAsync(hidden_dump, w.x, cfg.n_embd * 4, cudaMemcpyDeviceToDevice, stream));
   return FA_OK;
@@ -601,8 +702,8 @@ int Model::enqueue_head(Workspace &w, SeqState *st) {
     p.pro = kProRmsNorm;
     p.in = w.x;
     p.norm_w = out_norm;
-    p.ssq = ssq_in;
-    p.n_ssq = n_ssq;
+    p.ssq = tp.world > 1 ? nullptr : ssq_in;
+    p.n_ssq = tp.world > 1 ? 0 : n_ssq;
     p.eps = cfg.norm_eps;
     p.epi = kEpiLogits;
     p.out = w.logits;
@@ -664,6 +765,31 @@ int Model::alloc_workspace(Workspace &w) {
   CUDA_TRY(cudaMemset(w.h, 0, ((size_t)cfg.n_ff_used + 8) * 4));
   CUDA_TRY(cudaMemset(w.attn_out, 0, ((size_t)qd + 8) * 4));
   return FA_OK;
+}
+
+int Model::tp_reduce(float *x, const float *partials, size_t count) {
+  return tp.all_reduce(tp.rank == 0 ? x : partials, x, count, stream);
+}
+
+int Model::sync() {
+  if (tp.world <= 1) {
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? FA_OK : fail(FA_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
+  }
+  // a peer that died leaves our collectives waiting: poll with a bound
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(stream);
+    if (e == cudaSuccess) return FA_OK;
+    if (e != cudaErrorNotReady) return fail(FA_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
+    std::string msg;
+    if (tp.check_async(&msg)) return fail(FA_ERR_NCCL, "collective failed: " + msg);
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60)) {
+      tp.abort();
+      return fail(FA_ERR_TIMEOUT, "tensor-parallel step did not finish within 60 s (a peer rank stopped?)");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
 }
 
 // kernel launches one replay of a captured graph performs
@@ -911,7 +1037,8 @@ int Model::ensure_prefill_ws(uint32_t cap) {
   w.Qh = dmalloc((size_t)cap * qd * 2);
   w.Ob = dmalloc((size_t)cap * qd * 2);
   w.Hb = dmalloc((size_t)cap * F * 2);
-  if (!w.tok || !w.err || !w.X || !w.QKV || !w.GU || !w.Xn || !w.Qh || !w.Ob || !w.Hb)
+  if (tp.rank > 0) w.Y = (float *)dmalloc((size_t)cap * d * 4);
+  if (!w.tok || !w.err || !w.X || !w.QKV || !w.GU || !w.Xn || !w.Qh || !w.Ob || !w.Hb || (tp.rank > 0 && !w.Y))
     return fail(FA_ERR_OOM, "prefill workspace allocation failed");
   const uint32_t bns[3] = {64, 128, 256};
   for (int b = 0; b < 3; ++b)
@@ -988,13 +1115,19 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
       ap.scale_log2 = scale_log2;
       ap.out = pws.Ob;
       if (launch_attn_rows(ap, stream)) return fail(FA_ERR_CUDA, "prefill attention launch failed");
-      if ((rc = run_qgemm(lw.o, pws.mob[b], T, pws.X, d, kQgResid))) return rc;
+      // tensor parallel: rank 0 adds its partial sums to X, the others store
+      // theirs in Y; the all-reduce leaves X + sum on every rank
+      float *o_dst = tp.rank > 0 ? pws.Y : pws.X;
+      const int o_epi = tp.rank > 0 ? kQgStore : kQgResid;
+      if ((rc = run_qgemm(lw.o, pws.mob[b], T, o_dst, d, o_epi))) return rc;
+      if (tp.world > 1 && (rc = tp_reduce(pws.X, pws.Y, (size_t)T * d))) return rc;
       if (launch_norm_rows_h(pws.X, lw.ffn_norm, cfg.norm_eps, T, d, pws.Xn, pws.err, stream))
         return fail(FA_ERR_CUDA, "norm launch failed");
       if ((rc = run_qgemm(lw.gateup, pws.mxn[b], T, pws.GU, gu_n, kQgStore))) return rc;
       if (launch_swiglu_rows(pws.GU, T, F, lw.gateup.CW, pws.Hb, pws.err, stream))
         return fail(FA_ERR_CUDA, "swiglu launch failed");
-      if ((rc = run_qgemm(lw.down, pws.mhb[b], T, pws.X, d, kQgResid))) return rc;
+      if ((rc = run_qgemm(lw.down, pws.mhb[b], T, o_dst, d, o_epi))) return rc;
+      if (tp.world > 1 && (rc = tp_reduce(pws.X, pws.Y, (size_t)T * d))) return rc;
     }
   }
   // the last token through the decode head: logits + argmax
@@ -1007,7 +1140,7 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
   if ((rc = enqueue_head(ws, ws.state))) return rc;
   uint32_t e = 0;
   CUDA_TRY(cudaMemcpyAsync(&e, pws.err, 4, cudaMemcpyDeviceToHost, stream));
-  CUDA_TRY(cudaStreamSynchronize(stream));
+  if ((rc = sync())) return rc;
   if (e & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "prefill: a bounded device wait gave up");
   if (e & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
   if (e & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");
@@ -1041,6 +1174,8 @@ int Model::ensure_batch_ws(uint32_t b) {
   w.err = (uint32_t *)dmalloc(4);
   w.step = (uint32_t *)dmalloc(4);
   w.states = (SeqState *)dmalloc((size_t)b * sizeof(SeqState));
+  if (tp.rank > 0 && !(w.Y = (float *)dmalloc((size_t)b * d * 4)))
+    return fail(FA_ERR_OOM, "batched decode workspace allocation failed");
   if (!w.X || !w.QKV || !w.Qf || !w.Of || !w.GU || !w.logits || !w.part || !w.Xn || !w.Oh || !w.Hb || !w.counters ||
       !w.err || !w.step || !w.states)
     return fail(FA_ERR_OOM, "batched decode workspace allocation failed");
@@ -1087,13 +1222,17 @@ int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams
     ap.row_states = bws.states;
     ap.row_seq0 = 0;
     if (launch_attn_decode_rows(ap, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
-    if ((rc = run_qgemm(lw.o, bws.moh, b, bws.X, d, kQgResid))) return rc;
+    float *o_dst = tp.rank > 0 ? bws.Y : bws.X;  // as in prefill_tc
+    const int o_epi = tp.rank > 0 ? kQgStore : kQgResid;
+    if ((rc = run_qgemm(lw.o, bws.moh, b, o_dst, d, o_epi))) return rc;
+    if (tp.world > 1 && (rc = tp_reduce(bws.X, bws.Y, (size_t)b * d))) return rc;
     if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
       return fail(FA_ERR_CUDA, "norm launch failed");
     if ((rc = run_qgemm(lw.gateup, bws.mxn, b, bws.GU, gu_n, kQgStore))) return rc;
     if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream))
       return fail(FA_ERR_CUDA, "swiglu launch failed");
-    if ((rc = run_qgemm(lw.down, bws.mhb, b, bws.X, d, kQgResid))) return rc;
+    if ((rc = run_qgemm(lw.down, bws.mhb, b, o_dst, d, o_epi))) return rc;
+    if (tp.world > 1 && (rc = tp_reduce(bws.X, bws.Y, (size_t)b * d))) return rc;
   }
   if (launch_norm_rows_h(bws.X, out_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
     return fail(FA_ERR_CUDA, "norm launch failed");
@@ -1168,7 +1307,7 @@ int Model::decode_batch(KvCache &kv, uint32_t b, const uint32_t *tok, const uint
   uint32_t e = 0;
   CUDA_TRY(cudaMemcpyAsync(ids_host, hist, (size_t)steps * b * 4, cudaMemcpyDeviceToHost, stream));
   CUDA_TRY(cudaMemcpyAsync(&e, bws.err, 4, cudaMemcpyDeviceToHost, stream));
-  CUDA_TRY(cudaStreamSynchronize(stream));
+  if ((rc = sync())) return rc;
   if (e & kErrWaitTimeout) return fail(FA_ERR_TIMEOUT, "batched decode: a bounded device wait gave up");
   if (e & kErrBadToken) return fail(FA_ERR_INVALID, "token id out of range");
   if (e & kErrContext) return fail(FA_ERR_CONTEXT, "position or KV capacity exceeded");

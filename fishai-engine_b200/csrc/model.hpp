@@ -11,6 +11,7 @@
 #include "fa_host.hpp"
 #include "fa_kernels.hpp"
 #include "gguf.hpp"
+#include "tp.hpp"
 
 namespace fa {
 
@@ -60,6 +61,7 @@ struct PrefillWs {
   uint32_t cap = 0;
   uint32_t *tok = nullptr, *err = nullptr;
   float *X = nullptr, *QKV = nullptr, *GU = nullptr;
+  float *Y = nullptr;  // tensor parallel, ranks > 0: this rank's o / down partial sums [cap][d]
   void *Xn = nullptr, *Qh = nullptr, *Ob = nullptr, *Hb = nullptr;
   QgXMap mxn[3], mob[3], mhb[3];  // TMA maps of Xn, Ob, Hb for 64, 128, 256 tokens per tile
 };
@@ -68,6 +70,7 @@ struct PrefillWs {
 struct BatchWs {
   uint32_t cap = 0, splits = 1;
   float *X = nullptr, *QKV = nullptr, *Qf = nullptr, *Of = nullptr, *GU = nullptr, *logits = nullptr, *part = nullptr;
+  float *Y = nullptr;  // tensor parallel, ranks > 0: o / down partial sums [cap][d]
   void *Xn = nullptr, *Oh = nullptr, *Hb = nullptr;
   uint32_t *counters = nullptr, *err = nullptr, *step = nullptr;
   SeqState *states = nullptr;
@@ -75,7 +78,13 @@ struct BatchWs {
 };
 
 struct Model {
+  // this rank's configuration: with tensor parallelism n_heads, n_kv_heads and
+  // n_ff_used are the rank's shares (the attention heads, KV heads and FFN
+  // columns it holds); gcfg is the model's own configuration
   fa_config cfg{};
+  fa_config gcfg{};
+  TpComm tp;                     // world 1: no communicator
+  float *ar_send = nullptr;      // decode step, ranks > 0: o / down partial sums [d]
   int device = 0;
   bool pdl = true, graphs = true;
   cudaStream_t stream = nullptr;
@@ -164,6 +173,13 @@ struct Model {
   int alloc_workspace(Workspace &w);
   // run `n` steps (graph replays when enabled)
   int run_steps(const KvCache &kv, uint32_t seq, uint32_t n);
+  // tensor parallel: the all-reduce that completes a row-sharded projection
+  // (rank 0 added the residual itself): send = x on rank 0, own partials
+  // elsewhere; recv = x on every rank
+  int tp_reduce(float *x, const float *partials, size_t count);
+  // wait for the model stream; under tensor parallelism bounded (60 s) and
+  // watching the communicator's asynchronous error
+  int sync();
   void *dmalloc(size_t bytes);
   GemvParams gemv_base(const GemvPlan &P) const;
 };

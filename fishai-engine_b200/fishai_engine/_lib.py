@@ -92,6 +92,9 @@ SIGNATURES = {
     "fa_model_set_tc_prefill": ([_vp, C.c_int32], _i),
     "fa_model_step_launches": ([_vp, _pu32], _i),
     "fa_debug_set": ([_vp, C.c_int32, _u64], _i),
+    "fa_model_tp": ([_vp, _pi, _pi, _pu32, _pu32, _pu32], _i),
+    "fa_tp_unique_id": ([_vp], _i),
+    "fa_tp_shard": ([C.c_int32, _vp, _u32, _u32, C.c_int32, _u32, _u32, _vp, _sz, C.POINTER(_sz), _pu32], _i),
     "fa_kv_create": ([_vp, _u32, _u32, C.c_int32, C.POINTER(_vp)], _i),
     "fa_kv_free": ([_vp], None),
     "fa_kv_clear": ([_vp, C.c_int32], _i),

@@ -18,7 +18,8 @@ class KVCache:
         self.n_seq = n_seq
         self.dtype = dtype
         self._n_layers = cfg.n_layers
-        self.kv_dim = cfg.n_kv_heads * cfg.head_dim
+        # a tensor-parallel rank caches only the KV heads it holds
+        self.kv_dim = getattr(model, "local_kv_heads", cfg.n_kv_heads) * cfg.head_dim
         h = C.c_void_p()
         L.check(L.lib().fa_kv_create(model._h, n_seq, self.max_ctx, dtype, C.byref(h)))
         self._h = h

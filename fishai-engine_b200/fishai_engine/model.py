@@ -61,17 +61,32 @@ class ModelWeights:
     def __init__(self, handle, config: ModelConfig):
         self._h = handle
         self.config = config
+        r, w = C.c_int(), C.c_int()
+        hl, kvl, fl = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        L.check(L.lib().fa_model_tp(handle, C.byref(r), C.byref(w), C.byref(hl), C.byref(kvl), C.byref(fl)))
+        self.tp_rank, self.tp_world = r.value, w.value
+        self.local_heads, self.local_kv_heads, self.local_ff = hl.value, kvl.value, fl.value
 
     @classmethod
     def load_from_gguf(cls, gguf, config: Optional[ModelConfig] = None, device: int = 0, use_graphs: bool = True,
-                       use_pdl: bool = True, use_step_kernel: bool = False,
-                       use_tc_prefill: bool = False) -> "ModelWeights":
+                       use_pdl: bool = True, use_step_kernel: bool = False, use_tc_prefill: bool = False,
+                       tp_rank: int = 0, tp_world: int = 1, nccl_id: Optional[bytes] = None) -> "ModelWeights":
+        """tp_world > 1: this process's rank of a tensor-parallel model (one
+        process per GPU); nccl_id = tp_unique_id() made on rank 0 and shared
+        with every rank.  All ranks must then make the same calls."""
         path = gguf.path if isinstance(gguf, GGUFFile) else str(gguf)
         o = L.fa_model_opts()
         L.lib().fa_model_opts_default(C.byref(o))
         o.device, o.use_graphs, o.use_pdl = device, int(use_graphs), int(use_pdl)
         o.use_step_kernel = int(use_step_kernel)
         o.use_tc_prefill = int(use_tc_prefill)
+        o.tp_rank, o.tp_world = tp_rank, tp_world
+        uid = None
+        if tp_world > 1:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("tensor parallelism needs the 128-byte id from tp_unique_id() on rank 0")
+            uid = C.create_string_buffer(bytes(nccl_id), 128)
+            o.nccl_id = C.cast(uid, C.c_void_p)
         h = C.c_void_p()
         L.check(L.lib().fa_model_load(path.encode(), C.byref(o), C.byref(h)))
         c = L.fa_config()
@@ -161,6 +176,14 @@ class ModelWeights:
         L.check(L.lib().fa_decode_greedy(self._h, kv_cache._h, seq, first_token, pos, steps,
                                          ids.ctypes.data_as(C.POINTER(C.c_uint32))))
         return ids
+
+
+def tp_unique_id() -> bytes:
+    """a fresh NCCL unique id (rank 0 makes it; every rank passes it to
+    ModelWeights.load_from_gguf)"""
+    buf = C.create_string_buffer(128)
+    L.check(L.lib().fa_tp_unique_id(buf))
+    return buf.raw
 
 
 @dataclass

@@ -107,14 +107,33 @@ typedef struct {
   int32_t device;       /* CUDA device ordinal */
   int32_t use_graphs;   /* capture the decode step in a CUDA graph (default 1) */
   int32_t use_pdl;      /* programmatic dependent launch between kernels (default 1) */
-  int32_t tp_rank, tp_world;  /* tensor parallel rank/world (1 = no TP) */
-  const void *nccl_id;  /* 128-byte ncclUniqueId when tp_world > 1 */
+  int32_t tp_rank, tp_world;  /* tensor parallel rank/world (1 = no TP): rank r keeps query heads
+                                 [r*H/W, (r+1)*H/W), their KV heads and FFN columns [r*F/W, ...) of
+                                 wq/wk/wv/gate/up, the matching rows of wo/down, and an NCCL all-reduce
+                                 completes each o / down projection (src/model.rs:360-420 are the
+                                 projections split); embedding, norms and output head replicated */
+  const void *nccl_id;  /* 128-byte ncclUniqueId from fa_tp_unique_id on rank 0, when tp_world > 1 */
   int32_t use_step_kernel;  /* run each decode step as one persistent kernel when the
                                model qualifies (MMA-layout projections, untied head) */
   int32_t use_tc_prefill;   /* fa_prefill on the f16 tensor-core path (tcgen05 GEMMs, flash
                                attention): max-abs-rel 1e-2 of the f32 path instead of 1e-4 */
 } fa_model_opts;
 void fa_model_opts_default(fa_model_opts *o);
+
+/* Tensor parallelism (no reference counterpart: the reference runs on one
+ * CPU thread).  fa_tp_unique_id: a fresh 128-byte ncclUniqueId (rank 0 makes
+ * it and hands it to every rank's fa_model_load).  Every rank must then make
+ * the same sequence of model calls (each forward step runs collectives). */
+int fa_tp_unique_id(void *out128);
+/* the rank's share of a native weight W[K][N] (GGML blocks along N): axis 0
+ * rows [r*K/W, (r+1)*K/W), axis 1 columns [r*N/W, (r+1)*N/W) of every row.
+ * A Q4_K column share of 128 columns (half of a 256-column super-block, one
+ * KV head at eight-way parallelism) comes back as whole 144-byte blocks whose
+ * lower 128 columns hold the share and whose upper 128 dequantise to 0.
+ * *out_bytes = shard bytes, *row_bytes = its row stride; out_host NULL only
+ * reports sizes.  Host memory only: the load path's own shard step. */
+int fa_tp_shard(int32_t ggml_type, const void *bytes_host, uint32_t K, uint32_t N, int32_t axis, uint32_t rank,
+                uint32_t world, void *out_host, size_t cap, size_t *out_bytes, uint32_t *row_bytes);
 
 /* GGUFFile::open + ModelConfig::from_gguf + ModelWeights::load_from_gguf
  * (src/model.rs:252-298): weights are uploaded once in their native GGML
@@ -123,6 +142,10 @@ void fa_model_opts_default(fa_model_opts *o);
 int fa_model_load(const char *path, const fa_model_opts *opts, fa_model **out);
 void fa_model_free(fa_model *m);
 int fa_model_config(const fa_model *m, fa_config *cfg);
+/* tensor-parallel placement of this model: rank, world and the rank's share
+ * of query heads, KV heads (its KV cache holds these) and FFN columns */
+int fa_model_tp(const fa_model *m, int32_t *rank, int32_t *world, uint32_t *local_heads, uint32_t *local_kv_heads,
+                uint32_t *local_ff);
 /* bytes of weights resident on the device, and the algorithmic bytes one
  * decode step streams (all weight tensors + one embedding row) */
 int fa_model_weight_bytes(const fa_model *m, uint64_t *device_bytes, uint64_t *step_bytes);
