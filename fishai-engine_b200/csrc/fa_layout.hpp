@@ -11,6 +11,9 @@
 //
 //   Q4_0 (blk 32):  codes  r*w/2 + 16j     (byte i: col i low nibble, col i+16 high nibble)
 //                   d      4w + (r*w/32 + j)*2               f16
+//   Q4_1 (blk 32):  codes  as Q4_0;  d 4w + (r*w/32 + j)*2,  m 4w + w/2 + (r*w/32 + j)*2   f16
+//   Q5_0 (blk 32):  low 4 bits as the Q4_0 codes;  qh 4w + (r*w/32 + j)*4 (u32, bit i = col i's
+//                   fifth bit, as stored);  d 5w + (r*w/32 + j)*2   f16
 //   Q8_0 (blk 32):  codes  r*w + 32j       (byte i: col i, int8)
 //                   d      8w + (r*w/32 + j)*2               f16
 //   Q4_K (blk 256): codes  r*w/2 + 16j     (as Q4_0)
@@ -48,6 +51,8 @@ FA_HD inline uint32_t native_row_bytes(int type, uint32_t w) {
     case kF32: return 4 * w;
     case kF16: return 2 * w;
     case kQ4_0: return w / 32 * 18;
+    case kQ4_1: return w / 32 * 20;
+    case kQ5_0: return w / 32 * 22;
     case kQ8_0: return w / 32 * 34;
     case kQ4_K: return (w + 255) / 256 * 144;
     case kQ6_K: return w / 256 * 210;
@@ -59,7 +64,8 @@ FA_HD inline uint32_t type_block(int type) {
   return (type == kQ4_K || type == kQ6_K) ? 256u : (type == kF32 || type == kF16) ? 1u : 32u;
 }
 FA_HD inline bool gemv_type_supported(int type) {
-  return type == kF32 || type == kF16 || type == kQ4_0 || type == kQ8_0 || type == kQ4_K || type == kQ6_K;
+  return type == kF32 || type == kF16 || type == kQ4_0 || type == kQ4_1 || type == kQ5_0 || type == kQ8_0 ||
+         type == kQ4_K || type == kQ6_K;
 }
 
 // ---------------------------------------------------------------------------

@@ -110,6 +110,48 @@ struct RowOp<kQ4_0> {
   }
 };
 
+// Q4_1: value = d*q + m ; F = 0.5 + q/32 -> y = 32*acc - sum(16*x*d - x*m)
+template <>
+struct RowOp<kQ4_1> {
+  static constexpr float kScale = 32.0f;
+  __device__ __forceinline__ static void run(const uint8_t *G, uint32_t w, uint32_t r, const LaneK &lk, float x,
+                                             Acc &A) {
+    const uint4 c = *reinterpret_cast<const uint4 *>(G + r * (w / 2) + 16 * lk.j);
+    const uint8_t *dp = G + 4 * w + (r * (w / 32) + lk.j) * 2;
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(dp)), m = h2f(*reinterpret_cast<const uint16_t *>(dp + w / 2));
+    const float xd = x * d;
+    A.c0 += fmaf(16.0f, xd, -x * m);
+    acc_nibbles(c, xd, xd, A);
+  }
+};
+
+// Q5_0: value = d*(q-16), q = nibble | fifth bit << 4 ; F = 0.5 + q/64 (the
+// 5-bit code at bits 2-6 of the byte) -> y = 64*acc - 48*sum(x*d)
+template <>
+struct RowOp<kQ5_0> {
+  static constexpr float kScale = 64.0f;
+  // bits 0-3 of v -> bit 6 of bytes 0-3
+  __device__ __forceinline__ static uint32_t spread4(uint32_t v) { return ((v * 0x00204081u) & 0x01010101u) << 6; }
+  __device__ __forceinline__ static void run(const uint8_t *G, uint32_t w, uint32_t r, const LaneK &lk, float x,
+                                             Acc &A) {
+    const uint4 c = *reinterpret_cast<const uint4 *>(G + r * (w / 2) + 16 * lk.j);
+    const uint32_t qh = *reinterpret_cast<const uint32_t *>(G + 4 * w + (r * (w / 32) + lk.j) * 4);
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(G + 5 * w + (r * (w / 32) + lk.j) * 2));
+    const float xd = x * d;
+    A.c0 = fmaf(48.0f, xd, A.c0);
+    const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t lo = ((wv[t] << 2) & 0x3C3C3C3Cu) | spread4((qh >> (4 * t)) & 0xFu);
+      const uint32_t hi = ((wv[t] >> 2) & 0x3C3C3C3Cu) | spread4((qh >> (16 + 4 * t)) & 0xFu);
+      ffma2v(A.a[2 * t + 0], xd, magic_hi(lo, 0x7044), magic_hi(lo, 0x7144));
+      ffma2v(A.a[2 * t + 1], xd, magic_hi(lo, 0x7244), magic_hi(lo, 0x7344));
+      ffma2v(A.a[8 + 2 * t + 0], xd, magic_hi(hi, 0x7044), magic_hi(hi, 0x7144));
+      ffma2v(A.a[8 + 2 * t + 1], xd, magic_hi(hi, 0x7244), magic_hi(hi, 0x7344));
+    }
+  }
+};
+
 // Q6_K: value = (d*sc)*(q-32) ; F = 0.5 + q/128 -> y = 128*acc - 96*sum(xs)
 template <>
 struct RowOp<kQ6_K> {
@@ -449,6 +491,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvParams p) {
           case kQ6_K: stage_rows<kQ6_K>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
           case kQ8_0: stage_rows<kQ8_0>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
           case kQ4_0: stage_rows<kQ4_0>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
+          case kQ4_1: stage_rows<kQ4_1>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
+          case kQ5_0: stage_rows<kQ5_0>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
           case kF16: stage_rows<kF16>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
           default: stage_rows<kF32>(p, base, xrow, nrow, inv, it.ng, cd.width, cd.gbytes, G, gl, warp, lk, A); break;
         }
@@ -461,6 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvParams p) {
           case kQ6_K: flush<kQ6_K>(p, sm, cd, it.c, A, warp, lane, tid); break;
           case kQ8_0: flush<kQ8_0>(p, sm, cd, it.c, A, warp, lane, tid); break;
           case kQ4_0: flush<kQ4_0>(p, sm, cd, it.c, A, warp, lane, tid); break;
+          case kQ4_1: flush<kQ4_1>(p, sm, cd, it.c, A, warp, lane, tid); break;
+          case kQ5_0: flush<kQ5_0>(p, sm, cd, it.c, A, warp, lane, tid); break;
           case kF16: flush<kF16>(p, sm, cd, it.c, A, warp, lane, tid); break;
           default: flush<kF32>(p, sm, cd, it.c, A, warp, lane, tid); break;
         }

@@ -326,7 +326,8 @@ __device__ __forceinline__ void stage_advance(const GemvParams &p, uint32_t n_un
 // CTA-local unit u): wait, build the coefficients, run the MMAs, release the
 // slot.  slot / phase walk the ring.
 template <int T>
-__device__ __forceinline__ void segment(const GemvParams &p, const Smem &sm, const ChunkDesc &cd, uint32_t seg,
+__device__ __forceinline__ void segment(const uint32_t n_stages, const uint32_t stage_bytes, const uint64_t wait_ns,
+                                        const Smem &sm, const ChunkDesc &cd, uint32_t seg,
                                         uint32_t u, uint32_t warp, uint32_t lane, uint32_t tbl, uint32_t bsrc,
                                         uint32_t ring, uint32_t xs0, uint32_t &slot, uint32_t &phase, bool &ok,
                                         float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
@@ -338,9 +339,9 @@ __device__ __forceinline__ void segment(const GemvParams &p, const Smem &sm, con
     const uint32_t ng = min(sg, seg - done);
     // after a timed-out wait the warp keeps the loop structure but skips the
     // work; the error flag tells the host the result is void
-    if (ok && !mbar_wait_sleep(&sm.full[slot], phase, p.wait_limit_ns ? p.wait_limit_ns : kWaitLimitNs)) ok = false;
+    if (ok && !mbar_wait_sleep(&sm.full[slot], phase, wait_ns)) ok = false;
     if (active && ok) {
-      const uint32_t base = ring + slot * p.stage_bytes;
+      const uint32_t base = ring + slot * stage_bytes;
       build<T>(base, gbytes, w, warp, nblk, ng, xs0 + 64 * (u + done), lane, tbl, corr);
       __syncwarp();
       if (nt == 4) {
@@ -355,11 +356,24 @@ __device__ __forceinline__ void segment(const GemvParams &p, const Smem &sm, con
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[slot]);
     done += ng;
-    if (++slot == p.n_stages) {
+    if (++slot == n_stages) {
       slot = 0;
       phase ^= 1u;
     }
   }
+}
+
+// the persistent step kernel reads its launch parameters from global memory
+// (not the parameter space), which leaves fewer registers for the stage
+// loop: there the loop runs in its own function with its own allocation
+template <int T>
+__device__ __noinline__ void segment_call(const uint32_t n_stages, const uint32_t stage_bytes, const uint64_t wait_ns,
+                                          const Smem &sm, const ChunkDesc &cd, uint32_t seg, uint32_t u,
+                                          uint32_t warp, uint32_t lane, uint32_t tbl, uint32_t bsrc, uint32_t ring,
+                                          uint32_t xs0, uint32_t &slot, uint32_t &phase, bool &ok, float (&D)[4][4],
+                                          float (&Dh)[4][4], float (&corr)[2]) {
+  segment<T>(n_stages, stage_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D,
+             Dh, corr);
 }
 
 template <int T>
@@ -574,15 +588,25 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
   for (int t = 0; t < 4; ++t)
 #pragma unroll
     for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+  const uint32_t n_st = p.n_stages, st_bytes = p.stage_bytes;
+  const uint64_t wait_ns = p.wait_limit_ns ? p.wait_limit_ns : kWaitLimitNs;
   for (uint32_t u = 0, c = R.c0, g = R.g0; u < n_units; ++c, g = 0) {
     const ChunkDesc cd = p.chunks[c];
     const uint32_t seg = min(G - g, n_units - u);
+#define FA_SEG(T)                                                                                                  \
+  if constexpr (ATTN_PRO)                                                                                          \
+    segment<T>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh,  \
+               corr);                                                                                              \
+  else                                                                                                             \
+    segment_call<T>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, \
+                    Dh, corr)
     switch (cd.type) {
-      case kQ4_K: segment<kQ4_K>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-      case kQ6_K: segment<kQ6_K>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-      case kQ8_0: segment<kQ8_0>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-      default: segment<kQ4_0>(p, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+      case kQ4_K: FA_SEG(kQ4_K); break;
+      case kQ6_K: FA_SEG(kQ6_K); break;
+      case kQ8_0: FA_SEG(kQ8_0); break;
+      default: FA_SEG(kQ4_0); break;
     }
+#undef FA_SEG
     u += seg;
     // the CTA's rows of chunk c are done: its partial into its slot
     const uint32_t slot_p = cta * p.max_chunks_per_cta + (c - R.c0);

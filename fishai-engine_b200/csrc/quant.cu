@@ -86,6 +86,30 @@ __global__ void k_repack(int type, const uint8_t *__restrict__ src_a, const uint
       d[1] = pad ? 0 : b[1];
       break;
     }
+    case kQ4_1:
+    case kQ5_0: {
+      const uint32_t bb = type == kQ4_1 ? 20 : 22, co = type == kQ4_1 ? 4 : 6;  // block bytes, code offset
+      const uint8_t *b = row + (scol / 32) * bb;
+      uint8_t nib[32];
+      for (int i = 0; i < 16; ++i) {
+        nib[2 * i] = b[co + i] >> 4;  // element 2i: high nibble (src/quant.rs:183-188, :228-233)
+        nib[2 * i + 1] = b[co + i] & 0xF;
+      }
+      for (int i = 0; i < 16; ++i) G[r * (w / 2) + 16 * j + i] = pad ? 0 : (uint8_t)(nib[i] | (nib[i + 16] << 4));
+      if (type == kQ4_1) {
+        uint8_t *d = G + 4 * w + (r * (w / 32) + j) * 2, *m = d + w / 2;
+        for (int i = 0; i < 2; ++i) {
+          d[i] = pad ? 0 : b[i];
+          m[i] = pad ? 0 : b[2 + i];
+        }
+      } else {
+        uint8_t *qh = G + 4 * w + (r * (w / 32) + j) * 4, *d = G + 5 * w + (r * (w / 32) + j) * 2;
+        for (int i = 0; i < 4; ++i) qh[i] = pad ? 0 : b[2 + i];
+        d[0] = pad ? 0 : b[0];
+        d[1] = pad ? 0 : b[1];
+      }
+      break;
+    }
     case kQ4_K: {
       uint32_t s = j / 8, sb = (scol % 256) / 32;  // dest super-block slot, source sub-block
       const uint8_t *b = row + (scol / 256) * 144;
@@ -346,6 +370,22 @@ __global__ void k_unpack(int type, const uint8_t *__restrict__ src, uint64_t src
       uint8_t byte = G[r * (w / 2) + 16 * j + (i % 16)];
       int q = (i < 16) ? (byte & 0xF) : (byte >> 4);
       v = __fmul_rn((float)(q - 8), ld_h(G + 4 * w + (r * (w / 32) + j) * 2));
+      break;
+    }
+    case kQ4_1: {  // nib * d + m, two roundings as in src/quant.rs:190-191
+      uint8_t byte = G[r * (w / 2) + 16 * j + (i % 16)];
+      int q = (i < 16) ? (byte & 0xF) : (byte >> 4);
+      const uint8_t *d = G + 4 * w + (r * (w / 32) + j) * 2;
+      v = __fadd_rn(__fmul_rn((float)q, ld_h(d)), ld_h(d + w / 2));
+      break;
+    }
+    case kQ5_0: {  // ((nib | hb << 4) - 16) * d, src/quant.rs:236-240
+      uint8_t byte = G[r * (w / 2) + 16 * j + (i % 16)];
+      int q = (i < 16) ? (byte & 0xF) : (byte >> 4);
+      const uint8_t *qh = G + 4 * w + (r * (w / 32) + j) * 4;
+      const uint32_t hw = (uint32_t)qh[0] | ((uint32_t)qh[1] << 8) | ((uint32_t)qh[2] << 16) | ((uint32_t)qh[3] << 24);
+      q |= (int)((hw >> i) & 1u) << 4;
+      v = __fmul_rn((float)(q - 16), ld_h(G + 5 * w + (r * (w / 32) + j) * 2));
       break;
     }
     case kQ4_K: {

@@ -92,6 +92,42 @@ void q4_k_block(const float *x, uint8_t *o) {
     for (int l = 0; l < 32; ++l) qs[32 * j + l] = (uint8_t)(q[64 * j + l] | (q[64 * j + 32 + l] << 4));
 }
 
+// Q4_1 (value q*d + m, src/quant.rs:163-200): m = block minimum, d = range/15,
+// both f16; element 2j in the HIGH nibble of byte j, as the reference reads it
+void q4_1_block(const float *x, uint8_t *o) {
+  float lo = x[0], hi = x[0];
+  for (int i = 1; i < 32; ++i) {
+    lo = std::fmin(lo, x[i]);
+    hi = std::fmax(hi, x[i]);
+  }
+  const uint16_t dh = f32_to_f16((hi - lo) / 15.0f), mh = f32_to_f16(lo);
+  const float d = f16_to_f32(dh), m = f16_to_f32(mh);
+  put16(o, dh);
+  put16(o + 2, mh);
+  uint8_t q[32];
+  for (int i = 0; i < 32; ++i) q[i] = d > 0.0f ? (uint8_t)std::clamp((int)std::lround((x[i] - m) / d), 0, 15) : 0;
+  for (int j = 0; j < 16; ++j) o[4 + j] = (uint8_t)((q[2 * j] << 4) | q[2 * j + 1]);
+}
+
+// Q5_0 (value (q-16)*d, q = nibble | qh bit << 4, src/quant.rs:205-255):
+// d = max|x|/16 as f16; element 2j in the HIGH nibble of byte j, fifth bits
+// of elements 0..31 in the little-endian u32 after d
+void q5_0_block(const float *x, uint8_t *o) {
+  float amax = 0.0f;
+  for (int i = 0; i < 32; ++i) amax = std::fmax(amax, std::fabs(x[i]));
+  const uint16_t dh = f32_to_f16(amax / 16.0f);
+  const float d = f16_to_f32(dh);
+  put16(o, dh);
+  uint32_t qh = 0;
+  uint8_t q[32];
+  for (int i = 0; i < 32; ++i) {
+    q[i] = d > 0.0f ? (uint8_t)std::clamp((int)std::lround(x[i] / d) + 16, 0, 31) : 16;
+    qh |= (uint32_t)(q[i] >> 4) << i;
+  }
+  for (int b = 0; b < 4; ++b) o[2 + b] = (uint8_t)(qh >> (8 * b));
+  for (int j = 0; j < 16; ++j) o[6 + j] = (uint8_t)(((q[2 * j] & 0xF) << 4) | (q[2 * j + 1] & 0xF));
+}
+
 // Q6_K: 16 sub-blocks of 16 with a signed int8 scale each relative to an
 // f16 super-scale; 6-bit codes stored as 4 low bits (ql) + 2 high bits (qh).
 void q6_k_block(const float *x, uint8_t *o) {
@@ -139,6 +175,8 @@ size_t quantize_row(int t, const float *x, size_t n, uint8_t *out) {
       case FA_GGML_F16: put16(ob, f32_to_f16(*xb)); break;
       case FA_GGML_Q8_0: q8_0_block(xb, ob); break;
       case FA_GGML_Q4_0: q4_0_block(xb, ob); break;
+      case FA_GGML_Q4_1: q4_1_block(xb, ob); break;
+      case FA_GGML_Q5_0: q5_0_block(xb, ob); break;
       case FA_GGML_Q4_K: q4_k_block(xb, ob); break;
       case FA_GGML_Q6_K: q6_k_block(xb, ob); break;
       default: return 0;

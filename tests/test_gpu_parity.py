@@ -131,6 +131,21 @@ def test_q4_0_forward_parity(tmpdir_m):
     _forward_parity(p)
 
 
+def test_q4_1_q5_0_forward_parity(tmpdir_m):
+    """Q4_1 (q*d + m) and Q5_0 ((q-16)*d, fifth bit in qh) projections, the
+    reference's other block types (src/quant.rs:163-255), mixed in one model
+    (the CUDA-core GEMV's 8-row layout) with a Q8_0 head; hidden states and
+    logits at the f32 bar, then 12 greedy ids equal to the oracle's."""
+    p = synth.write(str(tmpdir_m / "q41q50.gguf"), 5, **_kquant_spec(
+        n_embd=256, n_heads=4, n_kv_heads=2, n_ff=512, vocab=2048, type_embd=O.Q4_1, type_q=O.Q4_1, type_k=O.Q5_0,
+        type_v=O.Q4_1, type_o=O.Q5_0, type_gate=O.Q4_1, type_up=O.Q4_1, type_down=O.Q5_0, type_out=O.Q8_0,
+        rope_base=10000.0))
+    _, dev, ref, _, _ = _forward_parity(p)
+    prompt = [5, 77, 1024, 9]
+    cfg = GenerationConfig(max_tokens=16, temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0)
+    assert GenerationState(dev, cfg).generate(prompt) == ref.generate(prompt, 16, fast=True).tolist()
+
+
 def test_f16_f32_tied_forward_parity(tmpdir_m):
     p = synth.write(str(tmpdir_m / "f.gguf"), 3, **_kquant_spec(
         n_embd=256, n_heads=4, n_kv_heads=2, n_ff=640, vocab=1000, type_embd=O.F16, type_q=O.F16, type_k=O.F32,
