@@ -20,6 +20,7 @@
 
 namespace fa {
 int synth_write(const char *path, const fa_synth_spec *s, uint64_t seed);
+int tokenizer_from_gguf(const Gguf &g, fa_tokenizer **out);
 uint32_t n_ff_of(uint32_t n_embd, float mult);
 }  // namespace fa
 
@@ -424,6 +425,12 @@ int fa_gguf_vocab_size(const fa_gguf *g, uint64_t *v, int *found) {
 }
 
 // ------------------------------------------------------------ config
+int fa_tokenizer_from_gguf(const fa_gguf *g, fa_tokenizer **out) {
+  API_NULL(g);
+  API_NULL(out);
+  return tokenizer_from_gguf(*g->g, out);
+}
+
 int fa_config_from_gguf(const fa_gguf *g, fa_config *cfg) {
   API_NULL(g);
   API_NULL(cfg);

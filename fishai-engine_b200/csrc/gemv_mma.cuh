@@ -363,19 +363,6 @@ __device__ __forceinline__ void segment(const uint32_t n_stages, const uint32_t 
   }
 }
 
-// the persistent step kernel reads its launch parameters from global memory
-// (not the parameter space), which leaves fewer registers for the stage
-// loop: there the loop runs in its own function with its own allocation
-template <int T>
-__device__ __noinline__ void segment_call(const uint32_t n_stages, const uint32_t stage_bytes, const uint64_t wait_ns,
-                                          const Smem &sm, const ChunkDesc &cd, uint32_t seg, uint32_t u,
-                                          uint32_t warp, uint32_t lane, uint32_t tbl, uint32_t bsrc, uint32_t ring,
-                                          uint32_t xs0, uint32_t &slot, uint32_t &phase, bool &ok, float (&D)[4][4],
-                                          float (&Dh)[4][4], float (&corr)[2]) {
-  segment<T>(n_stages, stage_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D,
-             Dh, corr);
-}
-
 template <int T>
 __device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc &cd, uint32_t slot, uint32_t warp,
                                             uint32_t lane, float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
@@ -384,6 +371,37 @@ __device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc
   else flush_warp<T, 2>(dst, lane, D, Dh, corr);
 }
 
+
+// The persistent step kernel reads its launch parameters from global memory
+// (not the parameter space), which leaves fewer registers for the stage loop.
+// There one chunk segment runs in a function of its own with its own
+// register allocation: the accumulators live only inside it (the stage loop,
+// then the flush of the slice into its partial slot, `dst`, or nothing when
+// dst is null), and the ring position goes in and comes back by value.
+struct RingPos {
+  uint32_t slot, phase, ok;
+};
+template <int T>
+__device__ __noinline__ RingPos segment_flush(const uint32_t n_stages, const uint32_t stage_bytes,
+                                              const uint64_t wait_ns, const Smem &sm, const ChunkDesc cd,
+                                              const uint32_t seg, const uint32_t u, const uint32_t warp,
+                                              const uint32_t lane, const uint32_t tbl, const uint32_t bsrc,
+                                              const uint32_t ring, const uint32_t xs0, RingPos rp, float *dst) {
+  float D[4][4], Dh[4][4], corr[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+  bool ok = rp.ok != 0;
+  segment<T>(n_stages, stage_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp.slot, rp.phase, ok,
+             D, Dh, corr);
+  if (ok && dst) {
+    if (min(64u, cd.width - 64 * warp) == 64) flush_warp<T, 4>(dst, lane, D, Dh, corr);
+    else flush_warp<T, 2>(dst, lane, D, Dh, corr);
+  }
+  rp.ok = ok ? 1u : 0u;
+  return rp;
+}
 
 // ---------------------------------------------------------------------------
 // Producer (one lane): the weight stages of CTA `cta` of launch p, pushed into
@@ -593,36 +611,42 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
   for (uint32_t u = 0, c = R.c0, g = R.g0; u < n_units; ++c, g = 0) {
     const ChunkDesc cd = p.chunks[c];
     const uint32_t seg = min(G - g, n_units - u);
-#define FA_SEG(T)                                                                                                  \
-  if constexpr (ATTN_PRO)                                                                                          \
-    segment<T>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh,  \
-               corr);                                                                                              \
-  else                                                                                                             \
-    segment_call<T>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, \
-                    Dh, corr)
-    switch (cd.type) {
-      case kQ4_K: FA_SEG(kQ4_K); break;
-      case kQ6_K: FA_SEG(kQ6_K); break;
-      case kQ8_0: FA_SEG(kQ8_0); break;
-      default: FA_SEG(kQ4_0); break;
-    }
-#undef FA_SEG
-    u += seg;
-    // the CTA's rows of chunk c are done: its partial into its slot
+    // the CTA's rows of chunk c: stages, then its partial into its slot
     const uint32_t slot_p = cta * p.max_chunks_per_cta + (c - R.c0);
-    if (ok && 64 * warp < cd.width) {
+    if constexpr (ATTN_PRO) {
       switch (cd.type) {
-        case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-        case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-        case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-        default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        case kQ4_K: segment<kQ4_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        case kQ6_K: segment<kQ6_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        case kQ8_0: segment<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+        default: segment<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
       }
+      if (ok && 64 * warp < cd.width) {
+        switch (cd.type) {
+          case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+          default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+      corr[0] = corr[1] = 0.0f;
+    } else {
+      float *dst = 64 * warp < cd.width ? p.part + (size_t)slot_p * p.CW + 64 * warp : nullptr;
+      RingPos rp{slot, phase, ok ? 1u : 0u};
+      switch (cd.type) {
+        case kQ4_K: rp = segment_flush<kQ4_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
+        case kQ6_K: rp = segment_flush<kQ6_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
+        case kQ8_0: rp = segment_flush<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
+        default: rp = segment_flush<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
+      }
+      slot = rp.slot;
+      phase = rp.phase;
+      ok = rp.ok != 0;
     }
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-    corr[0] = corr[1] = 0.0f;
+    u += seg;
     // publish: the last contributing CTA to arrive sums the partials and runs
     // the epilogue.  The contributors' partial slots are fetched while the
     // arrival atomic is in flight (only the last arriver uses them).

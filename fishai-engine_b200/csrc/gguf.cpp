@@ -67,12 +67,16 @@ bool read_value(Reader &r, uint32_t t, GgufMeta *m, int depth, std::string *err)
         if (it == 8) {
           std::string s;
           if (!r.str(&s, err)) return false;
+          m->arr_str.push_back(std::move(s));
         } else if (it == 9) {
           GgufMeta tmp;
           if (depth > 8 || !read_value(r, it, &tmp, depth + 1, err)) return false;
         } else {
-          if (r.pos + kScalarSize[it] > r.len) return *err = "truncated array", false;
-          r.pos += kScalarSize[it];
+          GgufMeta e;
+          if (!read_value(r, it, &e, depth + 1, err)) return *err = "truncated array", false;
+          const double v = it == 6 ? (double)e.f32 : it == 12 ? e.f64 : it == 7 ? (e.b ? 1.0 : 0.0)
+                         : (it == 1 || it == 3 || it == 5 || it == 11) ? (double)e.i : (double)e.u;
+          m->arr_num.push_back(v);
         }
       }
       return true;
@@ -190,6 +194,15 @@ bool Gguf::meta_bool(const std::string &key, bool *v) const {
   if (!m || m->type != 7) return false;
   return *v = m->b, true;
 }
+const std::vector<std::string> *Gguf::meta_str_array(const std::string &key) const {
+  const GgufMeta *m = meta(key);
+  return (m && m->type == 9 && m->arr_type == 8) ? &m->arr_str : nullptr;
+}
+const std::vector<double> *Gguf::meta_num_array(const std::string &key) const {
+  const GgufMeta *m = meta(key);
+  return (m && m->type == 9 && m->arr_type != 8 && m->arr_type != 9) ? &m->arr_num : nullptr;
+}
+
 bool Gguf::meta_string(const std::string &key, std::string *v) const {
   const GgufMeta *m = meta(key);
   if (!m || m->type != 8) return false;

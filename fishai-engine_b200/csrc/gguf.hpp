@@ -20,6 +20,8 @@ struct GgufMeta {
   std::string s;
   uint32_t arr_type = 0;
   uint64_t arr_len = 0;
+  std::vector<std::string> arr_str;  // string arrays (e.g. tokenizer.ggml.tokens / merges)
+  std::vector<double> arr_num;       // numeric arrays, each element widened exactly
 };
 
 struct GgufTensor {
@@ -52,6 +54,9 @@ class Gguf {
   bool meta_bool(const std::string &key, bool *v) const;
   bool meta_string(const std::string &key, std::string *v) const;
   bool vocab_size(uint64_t *v) const;
+  // array values: false when the key is absent or not an array of that kind
+  const std::vector<std::string> *meta_str_array(const std::string &key) const;
+  const std::vector<double> *meta_num_array(const std::string &key) const;
   const GgufTensor *tensor(const std::string &name) const;
   // bytes of a tensor by the next-offset rule; nullptr/0 when empty
   const uint8_t *tensor_data(const GgufTensor &t, size_t *nbytes) const;

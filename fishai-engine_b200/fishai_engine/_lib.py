@@ -94,6 +94,16 @@ SIGNATURES = {
     "fa_debug_set": ([_vp, C.c_int32, _u64], _i),
     "fa_model_tp": ([_vp, _pi, _pi, _pu32, _pu32, _pu32], _i),
     "fa_tp_unique_id": ([_vp], _i),
+    "fa_tokenizer_create": ([C.POINTER(C.c_char_p), _u32, _pf, _u32, C.POINTER(C.c_int32), _u32, C.c_char_p, _vp,
+                             C.POINTER(_vp)], _i),
+    "fa_tokenizer_from_gguf": ([_vp, C.POINTER(_vp)], _i),
+    "fa_tokenizer_free": ([_vp], None),
+    "fa_tokenizer_encode": ([_vp, C.c_char_p, _sz, C.c_int32, C.c_int32, _pu32, _sz, C.POINTER(_sz)], _i),
+    "fa_tokenizer_decode": ([_vp, _pu32, _sz, C.c_char_p, _sz, C.POINTER(_sz)], _i),
+    "fa_tokenizer_info": ([_vp, _pu32, _vp], _i),
+    "fa_tokenizer_piece": ([_vp, _u32, C.c_char_p, _sz, C.POINTER(_sz), C.POINTER(C.c_int32)], _i),
+    "fa_tokenizer_byte_token": ([_vp, _u32, _pu32], _i),
+    "fa_tokenizer_config_default": ([_vp], None),
     "fa_tp_shard": ([C.c_int32, _vp, _u32, _u32, C.c_int32, _u32, _u32, _vp, _sz, C.POINTER(_sz), _pu32], _i),
     "fa_kv_create": ([_vp, _u32, _u32, C.c_int32, C.POINTER(_vp)], _i),
     "fa_kv_free": ([_vp], None),

@@ -245,6 +245,43 @@ int fa_sdpa_host(const float *q_host, const float *k_host, const float *v_host, 
 int fa_sdpa_noalloc(const float *q_dev, const float *k_dev, const float *v_dev, uint32_t q_len, uint32_t kv_len,
                     uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, float *out_dev, void *stream);
 
+/* ------------------------------------------------------------ tokenizer */
+/* BpeTokenizer (src/tokenizer.rs:148-600): the text step before the token
+ * loop.  Ids -1 mean "none" (the reference's Option<u32>). */
+typedef struct {
+  int64_t bos_token_id, eos_token_id, eot_token_id, eom_token_id, unk_token_id;
+  int32_t add_bos, add_eos, add_space_prefix, remove_special_whitespaces, prepend_bos;
+} fa_tokenizer_config;
+typedef struct fa_tokenizer fa_tokenizer;
+/* TokenizerConfig::default (src/tokenizer.rs:130-144) */
+void fa_tokenizer_config_default(fa_tokenizer_config *cfg);
+/* BpeTokenizer::from_gguf (src/tokenizer.rs:202-286): token texts (UTF-8),
+ * scores and token types (shorter arrays leave the rest at 0 / Normal),
+ * merges as "left right" lines (rank = line index) or NULL, cfg or NULL for
+ * the default. */
+int fa_tokenizer_create(const char *const *texts, uint32_t n_tokens, const float *scores, uint32_t n_scores,
+                        const int32_t *types, uint32_t n_types, const char *merges, const fa_tokenizer_config *cfg,
+                        fa_tokenizer **out);
+/* the tokenizer a GGUF file carries: tokenizer.ggml.tokens / scores /
+ * token_type / merges and the config keys of parse_tokenizer_config_from_gguf
+ * (src/tokenizer.rs:520-553); FA_ERR_GGUF when the file has no token list */
+int fa_tokenizer_from_gguf(const fa_gguf *g, fa_tokenizer **out);
+void fa_tokenizer_free(fa_tokenizer *t);
+/* encode (src/tokenizer.rs:290-344) or, with with_special = 1,
+ * encode_with_special (src/tokenizer.rs:347-391); *n = ids produced (ids
+ * receives min(n, cap) of them) */
+int fa_tokenizer_encode(const fa_tokenizer *t, const char *text_utf8, size_t len, int32_t add_special,
+                        int32_t with_special, uint32_t *ids, size_t cap, size_t *n);
+/* decode (src/tokenizer.rs:394-408): *len = UTF-8 bytes (buf gets a NUL-
+ * terminated prefix of at most cap - 1) */
+int fa_tokenizer_decode(const fa_tokenizer *t, const uint32_t *ids, size_t n, char *buf, size_t cap, size_t *len);
+/* vocab_size / bos_token / eos_token (src/tokenizer.rs:420-433) and the config */
+int fa_tokenizer_info(const fa_tokenizer *t, uint32_t *vocab_size, fa_tokenizer_config *cfg);
+/* token_to_piece (src/tokenizer.rs:411-418) and the token's type; id out of range: FA_ERR_INVALID */
+int fa_tokenizer_piece(const fa_tokenizer *t, uint32_t id, char *buf, size_t cap, size_t *len, int32_t *type);
+/* the byte-fallback token of a byte value (bytes_to_tokens, src/tokenizer.rs:441-447) */
+int fa_tokenizer_byte_token(const fa_tokenizer *t, uint32_t byte_value, uint32_t *id);
+
 /* ------------------------------------------------------------- sampling */
 typedef struct {
   float temperature;            /* 0 = greedy */
