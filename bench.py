@@ -257,6 +257,41 @@ def profile_gemm(args):
     return 0
 
 
+def profile_kernels(args):
+    """A compact workload that launches every token-path kernel class a few
+    times, for ncu captures (one kernel per capture with -k): a 2048-token
+    tensor-core prefill of a one-layer 8B-shaped Q4_K_M model (RMSNorm rows,
+    token GEMMs with their split fixups, RoPE + KV append, causal flash
+    attention, SwiGLU rows), then two batched decode steps of 64 sequences at
+    context 256 on the one-layer Q8_0 model (batched RoPE, decode attention,
+    the sampler with T 0.8 / top-k 40 / top-p 0.9)."""
+    import numpy as np
+
+    from fishai_engine import synth, _lib as L
+    from fishai_engine.model import ModelWeights
+    from fishai_engine.sampling import Sampler, SamplerConfig
+
+    m = ModelWeights.load_from_gguf(synth.cached_preset(PRESET, n_layers=1), use_tc_prefill=True)
+    V = m.config.vocab_size
+    prompt = np.random.default_rng(2).integers(3, V, 2048).tolist()
+    m.prefill(prompt, 0, m.new_kv_cache(2056, dtype=L.KV_F16), want_logits=False)
+    m.close()
+    mb = ModelWeights.load_from_gguf(synth.cached_preset(BATCH_PRESET, n_layers=1), use_tc_prefill=True)
+    B, P = 64, 256
+    kv = mb.new_kv_cache(P + 16, dtype=L.KV_F16, n_seq=B)
+    rng = np.random.default_rng(3)
+    last = []
+    for r in range(B):
+        pr = rng.integers(3, V, P).tolist()
+        mb.prefill(pr, 0, kv, seq=r, want_logits=False)
+        last.append(pr[-1])
+    smp = Sampler(SamplerConfig(0.8, 40, 0.9, 1.0, 0.0, 0.0), V, seeds=[1000 + r for r in range(B)])
+    ids = mb.decode_batch(kv, last, [P] * B, smp, 2)
+    mb.close()
+    print(json.dumps({"profile_kernels": "ok", "ids": ids[-1][:4].tolist()}), flush=True)
+    return 0
+
+
 def kv_read_bytes(cfg, kv_elem, ctx):
     return 2 * cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * kv_elem * ctx
 
@@ -457,6 +492,8 @@ def main():
                     help="--profile-gemm on the Q8_0 model of the batched-decode workload")
     ap.add_argument("--model-layers", type=int, default=0,
                     help="reduced-depth model of the same shapes for the whole run (0: the full 32 layers)")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="a compact workload launching every token-path kernel class (for ncu captures)")
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
@@ -464,6 +501,8 @@ def main():
         return profile_one(args)
     if args.profile_gemm:
         return profile_gemm(args)
+    if args.profile_kernels:
+        return profile_kernels(args)
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3

@@ -372,37 +372,6 @@ __device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc
 }
 
 
-// The persistent step kernel reads its launch parameters from global memory
-// (not the parameter space), which leaves fewer registers for the stage loop.
-// There one chunk segment runs in a function of its own with its own
-// register allocation: the accumulators live only inside it (the stage loop,
-// then the flush of the slice into its partial slot, `dst`, or nothing when
-// dst is null), and the ring position goes in and comes back by value.
-struct RingPos {
-  uint32_t slot, phase, ok;
-};
-template <int T>
-__device__ __noinline__ RingPos segment_flush(const uint32_t n_stages, const uint32_t stage_bytes,
-                                              const uint64_t wait_ns, const Smem &sm, const ChunkDesc cd,
-                                              const uint32_t seg, const uint32_t u, const uint32_t warp,
-                                              const uint32_t lane, const uint32_t tbl, const uint32_t bsrc,
-                                              const uint32_t ring, const uint32_t xs0, RingPos rp, float *dst) {
-  float D[4][4], Dh[4][4], corr[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int t = 0; t < 4; ++t)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-  bool ok = rp.ok != 0;
-  segment<T>(n_stages, stage_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp.slot, rp.phase, ok,
-             D, Dh, corr);
-  if (ok && dst) {
-    if (min(64u, cd.width - 64 * warp) == 64) flush_warp<T, 4>(dst, lane, D, Dh, corr);
-    else flush_warp<T, 2>(dst, lane, D, Dh, corr);
-  }
-  rp.ok = ok ? 1u : 0u;
-  return rp;
-}
-
 // ---------------------------------------------------------------------------
 // Producer (one lane): the weight stages of CTA `cta` of launch p, pushed into
 // the ring.  s counts stages through the ring across launches (slot s % NS,
@@ -613,39 +582,25 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     const uint32_t seg = min(G - g, n_units - u);
     // the CTA's rows of chunk c: stages, then its partial into its slot
     const uint32_t slot_p = cta * p.max_chunks_per_cta + (c - R.c0);
-    if constexpr (ATTN_PRO) {
-      switch (cd.type) {
-        case kQ4_K: segment<kQ4_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-        case kQ6_K: segment<kQ6_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-        case kQ8_0: segment<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-        default: segment<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
-      }
-      if (ok && 64 * warp < cd.width) {
-        switch (cd.type) {
-          case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-          case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-          case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-          default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
-      corr[0] = corr[1] = 0.0f;
-    } else {
-      float *dst = 64 * warp < cd.width ? p.part + (size_t)slot_p * p.CW + 64 * warp : nullptr;
-      RingPos rp{slot, phase, ok ? 1u : 0u};
-      switch (cd.type) {
-        case kQ4_K: rp = segment_flush<kQ4_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
-        case kQ6_K: rp = segment_flush<kQ6_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
-        case kQ8_0: rp = segment_flush<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
-        default: rp = segment_flush<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, rp, dst); break;
-      }
-      slot = rp.slot;
-      phase = rp.phase;
-      ok = rp.ok != 0;
+    switch (cd.type) {
+      case kQ4_K: segment<kQ4_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+      case kQ6_K: segment<kQ6_K>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+      case kQ8_0: segment<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
+      default: segment<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
     }
+    if (ok && 64 * warp < cd.width) {
+      switch (cd.type) {
+        case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
+    corr[0] = corr[1] = 0.0f;
     u += seg;
     // publish: the last contributing CTA to arrive sums the partials and runs
     // the epilogue.  The contributors' partial slots are fetched while the

@@ -335,32 +335,6 @@ __device__ __forceinline__ void attn_item(const AttnParams &p, uint32_t split, u
   if (gtid == 0) atomicAdd(done, 1u);
 }
 
-// The phases as separate (not inlined) functions: each gets its own register
-// allocation, so the GEMV inner loop keeps the 96-register, spill-free code
-// of the standalone GEMV instead of sharing the allocation with the phase
-// loop and the attention code (the call saves the loop's state once per
-// phase).
-__device__ __noinline__ void gemv_phase(const GemvParams &p, const Smem &sm, uint32_t tid, uint32_t warp,
-                                        uint32_t lane, uint32_t &slot, uint32_t &phase, bool &ok) {
-  consume<false>(p, blockIdx.x, sm, tid, warp, lane, slot, phase, ok);
-}
-
-template <bool F16, int REP>
-__device__ __noinline__ void attn_phase(const StepParams &sp, uint32_t layer, const Smem &sm, uint32_t warp,
-                                        uint32_t lane, uint32_t *done) {
-  const uint32_t n_items = sp.attn.splits * sp.attn.kv.n_kv, slots = gridDim.x * sp.attn_groups;
-  const uint32_t grp = warp / 4;
-  if (grp < sp.attn_groups) {
-    AttnParams ap = sp.attn;
-    ap.layer = layer;
-    float *scr = reinterpret_cast<float *>(sm.tbl) + grp * attn_scratch_floats(REP, ap.kv.head_dim);
-    for (uint32_t it = blockIdx.x * sp.attn_groups + grp; it < n_items; it += slots) {
-      const uint32_t kvh = it / ap.splits, split = it % ap.splits;
-      attn_item<F16, REP>(ap, split, kvh, warp % 4, lane, 2 + grp, scr, done);
-    }
-  }
-}
-
 }  // namespace
 
 template <bool F16, int REP>
@@ -390,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams sp) {
     __syncwarp();  // reconverge the producer warp before the final block barrier
   } else {
     uint32_t slot = 0, phase = 0;
+    constexpr uint32_t rep = REP;
     for (uint32_t q = 0; q < sp.n_phases; ++q) {
       const StepPhase ph = sp.phases[q];
       if (ph.kind == kPhEmbed) {
@@ -398,12 +373,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const StepParams sp) {
         const GemvParams &p = sp.gemv[ph.idx];
         if (!cta_units(p, blockIdx.x)) continue;
         if (!wait_phase(sp, ph, epoch, sm, tid)) ok = false;
-        gemv_phase(p, sm, tid, warp, lane, slot, phase, ok);
+        consume<false>(p, blockIdx.x, sm, tid, warp, lane, slot, phase, ok);
       } else {  // attention of layer ph.idx: items (split, kv head) over (CTA, group)
-        const uint32_t n_items = sp.attn.splits * sp.attn.kv.n_kv;
+        const uint32_t n_items = sp.attn.splits * sp.attn.kv.n_kv, slots = gridDim.x * sp.attn_groups;
         if (blockIdx.x * sp.attn_groups >= n_items) continue;
         if (!wait_phase(sp, ph, epoch, sm, tid)) continue;
-        attn_phase<F16, REP>(sp, ph.idx, sm, warp, lane, sp.done + q);
+        const uint32_t grp = warp / 4;
+        if (grp < sp.attn_groups) {
+          AttnParams ap = sp.attn;
+          ap.layer = ph.idx;
+          float *scr = reinterpret_cast<float *>(sm.tbl) + grp * attn_scratch_floats(rep, ap.kv.head_dim);
+          for (uint32_t it = blockIdx.x * sp.attn_groups + grp; it < n_items; it += slots) {
+            const uint32_t kvh = it / ap.splits, split = it % ap.splits;
+            attn_item<F16, REP>(ap, split, kvh, warp % 4, lane, 2 + grp, scr, sp.done + q);
+          }
+        }
         epi::consumer_bar<kWarps>();  // the scratch overlays the GEMV tables and x slice
       }
     }
