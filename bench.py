@@ -226,7 +226,7 @@ def profile_one(args):
     from fishai_engine.model import ModelWeights
 
     path = synth.cached_preset(PRESET, n_layers=args.layers)
-    m = ModelWeights.load_from_gguf(path, gemv_chunk=args.gemv_chunk)
+    m = ModelWeights.load_from_gguf(path)
     avg, nbytes = C.c_float(), C.c_uint64()
     L.check(L.lib().fa_profile_gemv(m._h, PROFILE_KINDS[args.profile], args.reps, C.byref(avg), C.byref(nbytes)))
     print(json.dumps({"profile": args.profile, "layers": args.layers, "reps": args.reps,
@@ -481,8 +481,6 @@ def main():
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode figure (0: skip)")
     ap.add_argument("--batch-prompt", type=int, default=4096)
     ap.add_argument("--batch-steps", type=int, default=128)
-    ap.add_argument("--gemv-chunk", type=int, choices=[0, 256, 512, 1024], default=0,
-                    help="column-chunk width of the tensor-core weight layout (0: chosen per projection)")
     ap.add_argument("--step-kernel", type=int, choices=[0, 1], default=0,
                     help="1: each decode step is one persistent kernel launch")
     ap.add_argument("--profile", choices=list(PROFILE_KINDS), default=None,
@@ -535,7 +533,7 @@ def main():
     path = synth.cached_preset(PRESET, **ml)
 
     m = ModelWeights.load_from_gguf(path, device=local, use_step_kernel=bool(args.step_kernel),
-                                    use_tc_prefill=True, gemv_chunk=args.gemv_chunk)
+                                    use_tc_prefill=True)
     cfg = m.config
     step_kernel = m.step_kernel_active
     dev_bytes, step_weight_bytes = m.weight_bytes()

@@ -127,7 +127,7 @@ uint32_t gemv_mma_table_offset();
 uint32_t gemv_mma_table_words();  // 32-bit words of the table area (kProAttn's head weights live there)
 uint32_t gemv_mma_ring_offset(uint32_t max_units);
 // row groups per pipeline stage for chunks of this type and group size
-uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type, uint32_t width);
+uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type);
 
 struct AttnParams {
   const float *q;          // [H*hd] (per query row when q_rows > 1)

@@ -22,12 +22,8 @@
 // slow); weights are static, so it never waits for the previous kernel.  The
 // consumers load the CTA's slice of x once (normalised when the launch has an
 // RMSNorm prologue); each of the 16 consumer warps owns one 64-column slice
-// of a 1024-wide chunk, builds the B coefficients of its slice for the stage
-// in a private table and runs 4 (Q6_K: 8) MMAs per group.  Narrower chunks
-// (256 columns for the qkv, o and down projections, so that a chunk has only
-// a few contributing CTAs) share each slice between 16 / slices warps, each
-// taking every n-th row group of a stage; their sums are added in shared
-// memory before the partial is published.
+// of the 1024-wide chunk, builds the B coefficients of its slice for the stage
+// in a private table and runs 4 (Q6_K: 8) MMAs per group.
 // At the end of its rows of a chunk a CTA publishes the chunk partial; the last
 // CTA to arrive sums the partials in a fixed order and runs the fused
 // epilogue (gemv_epi.cuh).
@@ -66,7 +62,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_mma(const GemvParams p) {
   if (!ok && p.state) atomicOr(&p.state->err, kErrWaitTimeout);
 }
 
-uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type, uint32_t w) { return stage_groups(gbytes, type, w); }
+uint32_t gemv_mma_stage_groups(uint32_t gbytes, int type) { return stage_groups(gbytes, type); }
 uint32_t gemv_mma_table_offset() { return kOffTbl; }
 uint32_t gemv_mma_table_words() { return kWarps * kTblWords; }
 uint32_t gemv_mma_ring_offset(uint32_t max_units) { return ring_offset(max_units); }

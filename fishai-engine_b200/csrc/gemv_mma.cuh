@@ -147,20 +147,10 @@ struct Geo<kQ4_0> {
   static constexpr bool PAIR_LANES = true;
 };
 
-// Chunks narrower than 16 slices share their slices between warps: warp w
-// takes slice w % ns and every lanes-th row group of a stage starting at
-// w / ns (lanes = 16 / ns "group lanes"); the lanes' sums of a slice are
-// added in shared memory (lane order) when the chunk segment is flushed.
-__host__ __device__ inline uint32_t chunk_slices(uint32_t w) { return (w + 63) / 64; }
-__host__ __device__ inline uint32_t group_lanes(uint32_t w) {
-  const uint32_t l = kWarps / chunk_slices(w);
-  return l < 1 ? 1 : l;
-}
-
-// groups per stage for a chunk of this type, group size and width (a warp's
-// coefficient table holds its groups x blocks <= 8)
-__host__ __device__ inline uint32_t stage_groups(uint32_t gbytes, int type, uint32_t w) {
-  const uint32_t cap = ((type == kQ6_K || type == kQ8_0) ? 2u : kMaxStageGroups) * group_lanes(w);
+// groups per stage for a chunk of this type and group size (the coefficient
+// table holds groups x blocks <= 8)
+__host__ __device__ inline uint32_t stage_groups(uint32_t gbytes, int type) {
+  const uint32_t cap = (type == kQ6_K || type == kQ8_0) ? 2u : kMaxStageGroups;
   const uint32_t n = kStageTarget / gbytes;
   return n < 1 ? 1 : (n > cap ? cap : n);
 }
@@ -169,19 +159,17 @@ __host__ __device__ inline uint32_t stage_groups(uint32_t gbytes, int type, uint
 // xs).  Table word of (group gi, block j, split s, row pair p): (gi*J + j)*24
 // + s*8 + (p%4)*2 + (p%8)/4, so fragment lane (g, c) reads words (g*4+c)*2, +1.
 // All addresses are shared-window byte addresses.
-// ng = this warp's groups of the stage: stage groups g0, g0 + gs, g0 + 2 gs, ...
 template <int T>
 __device__ __forceinline__ void build(uint32_t stage, uint32_t gbytes, uint32_t w, uint32_t slice, uint32_t nblk,
-                                      uint32_t ng, uint32_t g0, uint32_t gs, uint32_t xs, uint32_t lane,
-                                      uint32_t tbl, float (&corr)[2]) {
+                                      uint32_t ng, uint32_t xs, uint32_t lane, uint32_t tbl, float (&corr)[2]) {
   constexpr int J = Geo<T>::J;
   const uint32_t p = Geo<T>::PAIR_LANES ? lane : (lane & 15), jb = Geo<T>::PAIR_LANES ? 0 : (lane >> 4);
   if (p >= 8 * ng || jb >= nblk) return;
-  const uint32_t gi = p >> 3, rr = 2 * (p & 7), ga = g0 + gi * gs;  // table group, stage group
-  const uint2 xb = lds64(xs + 64 * ga + 8 * (p & 7));
+  const uint2 xb = lds64(xs + 8 * p);
   const float2 x = make_float2(__uint_as_float(xb.x), __uint_as_float(xb.y));
   const float2 xs96 = __fmul2_rn(x, make_float2(kBScale, kBScale));
-  const uint32_t G = stage + ga * gbytes;
+  const uint32_t gi = p >> 3, rr = 2 * (p & 7);
+  const uint32_t G = stage + gi * gbytes;
   const uint32_t dst = tbl + 4 * (gi * J * 24 + (p & 3) * 2 + ((p >> 2) & 1));
   if constexpr (T == kQ4_K) {
     // the slice's two sub-blocks are adjacent 12-bit fields: 24 bits at bit 24*(slice%4)
@@ -284,7 +272,7 @@ __device__ __forceinline__ void mma_group(uint32_t G, uint32_t w, uint32_t slice
 
 // D -> column values of this warp's slice, minus the block corrections, into
 // the chunk partial (rows m >= 8 of the 4-bit layouts carry an extra x16)
-template <int T, int NT, bool SMEM = false>
+template <int T, int NT>
 __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)[4][4], float (&Dh)[4][4],
                                            float (&corr)[2]) {
   constexpr int kOff = Geo<T>::PAIR_LANES ? 16 : 8;  // builder lanes sharing a block
@@ -307,15 +295,8 @@ __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)
     else cr = __shfl_sync(0xFFFFFFFFu, corr[0], 16 * (t >> 1));
     const float cv = __fmul_rn(Geo<T>::kCorr, cr);
     if (c == 0) {
-      const float v0 = __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv);
-      const float v8 = __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[2], d[3]), lo8), kHi), cv);
-      if constexpr (SMEM) {
-        dst[16 * t + g] = v0;
-        dst[16 * t + g + 8] = v8;
-      } else {
-        __stcg(dst + 16 * t + g, v0);
-        __stcg(dst + 16 * t + g + 8, v8);
-      }
+      __stcg(dst + 16 * t + g, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv));
+      __stcg(dst + 16 * t + g + 8, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[2], d[3]), lo8), kHi), cv));
     }
   }
 }
@@ -351,28 +332,25 @@ __device__ __forceinline__ void segment(const uint32_t n_stages, const uint32_t 
                                         uint32_t ring, uint32_t xs0, uint32_t &slot, uint32_t &phase, bool &ok,
                                         float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
   const uint32_t w = cd.width, sg = cd.sgroups, gbytes = cd.gbytes;
-  const uint32_t ns = chunk_slices(w), gl_n = group_lanes(w), slice = warp % ns, gl = warp / ns;
-  const bool active = gl < gl_n;
-  const uint32_t nt = active ? min(64u, w - 64 * slice) / 16 : 0;
+  const bool active = 64 * warp < w;
+  const uint32_t nt = active ? min(64u, w - 64 * warp) / 16 : 0;
   const uint32_t nblk = (nt == 4) ? Geo<T>::J : Geo<T>::J / 2;
   for (uint32_t done = 0; done < seg;) {
     const uint32_t ng = min(sg, seg - done);
     // after a timed-out wait the warp keeps the loop structure but skips the
     // work; the error flag tells the host the result is void
     if (ok && !mbar_wait_sleep(&sm.full[slot], phase, wait_ns)) ok = false;
-    if (active && ok && gl < ng) {
+    if (active && ok) {
       const uint32_t base = ring + slot * stage_bytes;
-      const uint32_t ngw = (ng - gl + gl_n - 1) / gl_n;  // this warp's groups: gl, gl + gl_n, ...
-      build<T>(base, gbytes, w, slice, nblk, ngw, gl, gl_n, xs0 + 64 * (u + done), lane, tbl, corr);
+      build<T>(base, gbytes, w, warp, nblk, ng, xs0 + 64 * (u + done), lane, tbl, corr);
       __syncwarp();
       if (nt == 4) {
 #pragma unroll
         for (uint32_t gi = 0; gi < kMaxStageGroups; ++gi)
-          if (gi < ngw)
-            mma_group<T, 4>(base + (gl + gi * gl_n) * gbytes, w, slice, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
+          if (gi < ng) mma_group<T, 4>(base + gi * gbytes, w, warp, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
       } else {
-        for (uint32_t gi = 0; gi < ngw; ++gi)
-          mma_group<T, 2>(base + (gl + gi * gl_n) * gbytes, w, slice, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
+        for (uint32_t gi = 0; gi < ng; ++gi)
+          mma_group<T, 2>(base + gi * gbytes, w, warp, lane, bsrc + gi * Geo<T>::J * 96, D, Dh);
       }
     }
     __syncwarp();
@@ -385,37 +363,12 @@ __device__ __forceinline__ void segment(const uint32_t n_stages, const uint32_t 
   }
 }
 
-// The CTA's partial of a chunk into its slot.  One warp per slice writes its
-// column values directly; with several group lanes per slice every warp
-// writes its values into shared memory (red, 64 floats per warp, which
-// overlays the coefficient tables) and the lanes' values of each column are
-// added in lane order.  Called by every consumer warp.
 template <int T>
-__device__ __forceinline__ void flush_chunk(const GemvParams &p, const ChunkDesc &cd, uint32_t slot, uint32_t tid,
-                                            uint32_t warp, uint32_t lane, float *red, bool ok, float (&D)[4][4],
-                                            float (&Dh)[4][4], float (&corr)[2]) {
-  const uint32_t w = cd.width, ns = chunk_slices(w), gl_n = group_lanes(w), slice = warp % ns, gl = warp / ns;
-  float *dst = p.part + (size_t)slot * p.CW;
-  if (gl_n == 1) {
-    if (ok && 64 * warp < w) {
-      if (min(64u, w - 64 * warp) == 64) flush_warp<T, 4>(dst + 64 * warp, lane, D, Dh, corr);
-      else flush_warp<T, 2>(dst + 64 * warp, lane, D, Dh, corr);
-    }
-    return;
-  }
-  epi::consumer_bar<kWarps>();  // every warp is past its last stage: the tables are free
-  if (gl < gl_n) {
-    if (min(64u, w - 64 * slice) == 64) flush_warp<T, 4, true>(red + 64 * warp, lane, D, Dh, corr);
-    else flush_warp<T, 2, true>(red + 64 * warp, lane, D, Dh, corr);
-  }
-  epi::consumer_bar<kWarps>();
-  for (uint32_t col = tid; col < w; col += kWarps * 32) {
-    const uint32_t sl = col / 64, c = col % 64;
-    float v = 0.0f;
-    for (uint32_t g = 0; g < gl_n; ++g) v += red[(g * ns + sl) * 64 + c];
-    if (ok) __stcg(dst + col, v);
-  }
-  epi::consumer_bar<kWarps>();  // the tables are written again by the next segment
+__device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc &cd, uint32_t slot, uint32_t warp,
+                                            uint32_t lane, float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
+  float *dst = p.part + (size_t)slot * p.CW + 64 * warp;
+  if (min(64u, cd.width - 64 * warp) == 64) flush_warp<T, 4>(dst, lane, D, Dh, corr);
+  else flush_warp<T, 2>(dst, lane, D, Dh, corr);
 }
 
 
@@ -635,13 +588,12 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       case kQ8_0: segment<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
       default: segment<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
     }
-    {
-      float *red = reinterpret_cast<float *>(sm.tbl);
+    if (ok && 64 * warp < cd.width) {
       switch (cd.type) {
-        case kQ4_K: flush_chunk<kQ4_K>(p, cd, slot_p, tid, warp, lane, red, ok, D, Dh, corr); break;
-        case kQ6_K: flush_chunk<kQ6_K>(p, cd, slot_p, tid, warp, lane, red, ok, D, Dh, corr); break;
-        case kQ8_0: flush_chunk<kQ8_0>(p, cd, slot_p, tid, warp, lane, red, ok, D, Dh, corr); break;
-        default: flush_chunk<kQ4_0>(p, cd, slot_p, tid, warp, lane, red, ok, D, Dh, corr); break;
+        case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        case kQ8_0: flush_slice<kQ8_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
+        default: flush_slice<kQ4_0>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
       }
     }
 #pragma unroll

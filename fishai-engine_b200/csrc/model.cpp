@@ -162,21 +162,8 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
                       bool paired, uint32_t K, const std::vector<uint32_t> &widths, uint32_t CW, void *staging,
                       void *staging2, uint32_t cw_div = 1) {
   bool mma = K % 16 == 0 && 1024 % cw_div == 0;
-  uint32_t Nmax = 0;
-  for (size_t i = 0; i < parts.size(); ++i) {
-    mma = mma && mma_type(parts[i].type) && widths[paired ? 0 : i] % 32 == 0;
-    Nmax = std::max(Nmax, paired ? 2 * widths[0] : widths[i]);
-  }
-  // tensor-core layout: 1024-column chunks for the wide launches; narrower
-  // projections use 256-column chunks, so each chunk has only a few
-  // contributing CTAs and its last arriver sums a few small partials
-  if (mma) {
-    CW = m.gemv_chunk ? m.gemv_chunk : (Nmax >= 16384 ? 1024u : 256u);
-    if (CW % cw_div) CW = 1024;
-    // a gate/up chunk holds CW/2 columns of each: whole 256-column K-quant
-    // super-blocks need CW >= 512
-    if (paired && (parts[0].type == kQ4_K || parts[0].type == kQ6_K)) CW = std::max(CW, 512u);
-  }
+  for (size_t i = 0; i < parts.size(); ++i) mma = mma && mma_type(parts[i].type) && widths[paired ? 0 : i] % 32 == 0;
+  if (mma) CW = 1024;
   P.mma = mma;
   P.K = K;
   P.K8 = (K + 7) / 8 * 8;
@@ -229,7 +216,7 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
       d.type = (uint16_t)a.type;
       d.width = (uint16_t)w;
       d.out_col = out_base[i] + c0;
-      d.sgroups = mma ? gemv_mma_stage_groups(d.gbytes, a.type, w) : 0;
+      d.sgroups = mma ? gemv_mma_stage_groups(d.gbytes, a.type) : 0;
       P.chunks.push_back(d);
       max_gb = std::max(max_gb, d.gbytes);
     }
@@ -355,9 +342,6 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   device = o.device;
   pdl = o.use_pdl != 0;
   graphs = o.use_graphs != 0;
-  if (o.gemv_chunk && o.gemv_chunk != 256 && o.gemv_chunk != 512 && o.gemv_chunk != 1024)
-    return fail(FA_ERR_INVALID, "gemv_chunk must be 0, 256, 512 or 1024");
-  gemv_chunk = (uint32_t)o.gemv_chunk;
   want_step = o.use_step_kernel != 0;
   want_tc_prefill = o.use_tc_prefill != 0;
   CUDA_TRY(cudaSetDevice(device));

@@ -87,7 +87,6 @@ struct Model {
   float *ar_send = nullptr;      // decode step, ranks > 0: o / down partial sums [d]
   int device = 0;
   bool pdl = true, graphs = true;
-  uint32_t gemv_chunk = 0;  // forced tensor-core chunk width (0: per projection)
   cudaStream_t stream = nullptr;
   std::unique_ptr<Gguf> gguf;
   std::vector<LayerW> layers;

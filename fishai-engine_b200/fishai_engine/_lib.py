@@ -37,7 +37,7 @@ class fa_config(C.Structure):
 class fa_model_opts(C.Structure):
     _fields_ = [("device", C.c_int32), ("use_graphs", C.c_int32), ("use_pdl", C.c_int32), ("tp_rank", C.c_int32),
                 ("tp_world", C.c_int32), ("nccl_id", C.c_void_p), ("use_step_kernel", C.c_int32),
-                ("use_tc_prefill", C.c_int32), ("gemv_chunk", C.c_int32)]
+                ("use_tc_prefill", C.c_int32)]
 
 
 class fa_sampler_config(C.Structure):

@@ -70,8 +70,7 @@ class ModelWeights:
     @classmethod
     def load_from_gguf(cls, gguf, config: Optional[ModelConfig] = None, device: int = 0, use_graphs: bool = True,
                        use_pdl: bool = True, use_step_kernel: bool = False, use_tc_prefill: bool = False,
-                       tp_rank: int = 0, tp_world: int = 1, nccl_id: Optional[bytes] = None,
-                       gemv_chunk: int = 0) -> "ModelWeights":
+                       tp_rank: int = 0, tp_world: int = 1, nccl_id: Optional[bytes] = None) -> "ModelWeights":
         """tp_world > 1: this process's rank of a tensor-parallel model (one
         process per GPU); nccl_id = tp_unique_id() made on rank 0 and shared
         with every rank.  All ranks must then make the same calls."""
@@ -82,7 +81,6 @@ class ModelWeights:
         o.use_step_kernel = int(use_step_kernel)
         o.use_tc_prefill = int(use_tc_prefill)
         o.tp_rank, o.tp_world = tp_rank, tp_world
-        o.gemv_chunk = gemv_chunk
         uid = None
         if tp_world > 1:
             if nccl_id is None or len(nccl_id) != 128:

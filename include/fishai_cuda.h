@@ -117,9 +117,6 @@ typedef struct {
                                model qualifies (MMA-layout projections, untied head) */
   int32_t use_tc_prefill;   /* fa_prefill on the f16 tensor-core path (tcgen05 GEMMs, flash
                                attention): max-abs-rel 1e-2 of the f32 path instead of 1e-4 */
-  int32_t gemv_chunk;       /* column-chunk width of the tensor-core weight layout: 0 = chosen
-                               per projection (256 for widths below 16384, else 1024), or
-                               256 / 512 / 1024 for every projection */
 } fa_model_opts;
 void fa_model_opts_default(fa_model_opts *o);
 
