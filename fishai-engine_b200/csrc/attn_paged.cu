@@ -105,9 +105,14 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
   }
   __syncthreads();
   pdl_launch_dependents();
-  pdl_wait();
+  // early_kv (a step graph): len and the K/V rows of positions below len come
+  // from earlier steps, i.e. earlier graph launches that completed before this
+  // one began, so those tiles are fetched while the qkv launch is finishing;
+  // the tile holding position len (written by that launch) waits for it
+  if (!p.early_kv) pdl_wait();
 
-  uint32_t T = p.state->len + 1;
+  const uint32_t len = p.state->len;
+  uint32_t T = len + 1;
   if (T > p.kv.max_pages * 16) {  // beyond the cache: the qkv launch has flagged it; read what exists
     T = p.kv.max_pages * 16;
     if (tid == 0 && split == 0 && kvh == 0) atomicOr(&p.state->err, kErrContext);
@@ -132,9 +137,16 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
       bulk_g2s(dk + G::tile_bytes, base + kv_index(page, 1, kvh, 0, 0, KVH, HD) * G::esz, G::page_bytes, b);
     }
   };
+  const bool newest = t1 == len + 1;  // this split ends at position len
+  auto early = [&](uint32_t j) { return p.early_kv && !(newest && j + 1 == n_tiles); };
   if (warp == 0) {
-    if (n_tiles > 0) issue(0);
-    if (n_tiles > 1) issue(1);
+    if (n_tiles > 0 && early(0)) issue(0);
+    if (n_tiles > 1 && early(1)) issue(1);
+  }
+  if (p.early_kv) pdl_wait();
+  if (warp == 0) {
+    if (n_tiles > 0 && !early(0)) issue(0);
+    if (n_tiles > 1 && !early(1)) issue(1);
   }
 
   float q[REP][DPL], o[REP][DPL];

@@ -143,6 +143,9 @@ struct AttnParams {
   float *out;              // [H*hd] combined attention output
   SeqState *state;         // T = len + 1
   int partials_only;       // batch-1 paged kernel: leave the split partials for the consumer (kProAttn)
+  int early_kv;            // batch-1 paged kernel inside a step graph: K/V tiles of positions below
+                           // len are fetched before the wait for the qkv launch (earlier steps,
+                           // i.e. earlier graph launches, wrote them)
   const SeqState *row_states;  // batched decode: per query row state (T = len + 1), cache sequence row_seq0 + row
   uint32_t row_seq0;
   void *out_h;             // batched decode: non-null -> the combined output as f16 [rows][H*hd] here

@@ -609,23 +609,20 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     uint32_t slot_k = 0;
     if (tid < n) slot_k = __ldg(p.contrib + cd.contrib_off + tid);
     epi::consumer_bar<kWarps>();
-    if (tid == 0) {
-      __threadfence();  // the CTA's partial (ordered before by the barrier) is visible first
-      const uint32_t old = atomicAdd(p.counters + c, 1u);
+    if (tid == 0) {  // releases the CTA's partial (ordered before by the barrier)
+      const uint32_t old = atom_add_acq_rel_gpu(p.counters + c, 1u);
       sm.flag[0] = (old + 1 == n) ? 1u : 0u;
     }
     epi::consumer_bar<kWarps>();
-    if (sm.flag[0]) {
-      __threadfence();
+    if (sm.flag[0]) {  // the final arrival acquired every contributor's partial
       uint32_t *slots = sm.tbl + kSlotWord;
       if (tid < n) slots[tid] = slot_k;
       epi::consumer_bar<kWarps>();
       epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), slots, cd, c, tid, warp, lane);
       if (tid == 0) p.counters[c] = 0;  // ready for the next use of the chunk counters
       if (p.done) {  // chunk complete: count it for the launches that wait on this one
-        __threadfence();
         epi::consumer_bar<kWarps>();
-        if (tid == 0) atomicAdd(p.done, 1u);
+        if (tid == 0) red_add_release_gpu(p.done, 1u);
       }
     }
     epi::consumer_bar<kWarps>();

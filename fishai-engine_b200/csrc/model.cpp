@@ -636,6 +636,7 @@ int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t se
   ap.out = w.attn_out;
   ap.state = st;
   ap.partials_only = attn_fused(l) ? 1 : 0;
+  ap.early_kv = capturing_step && pdl ? 1 : 0;
   return launch_attention(ap, pdl, stream) ? fail(FA_ERR_CUDA, "attention launch failed") : FA_OK;
 }
 
@@ -833,7 +834,9 @@ int Model::run_steps(const KvCache &kv, uint32_t seq, uint32_t n) {
       graph = nullptr;
     }
     CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    capturing_step = true;
     rc = one_step();
+    capturing_step = false;
     cudaGraph_t gr = nullptr;
     cudaError_t ce = cudaStreamEndCapture(stream, &gr);
     if (rc) {

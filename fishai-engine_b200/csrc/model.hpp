@@ -87,6 +87,7 @@ struct Model {
   float *ar_send = nullptr;      // decode step, ranks > 0: o / down partial sums [d]
   int device = 0;
   bool pdl = true, graphs = true;
+  bool capturing_step = false;  // the per-step graph is being captured
   cudaStream_t stream = nullptr;
   std::unique_ptr<Gguf> gguf;
   std::vector<LayerW> layers;
