@@ -490,6 +490,8 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
   // squares partials (one round trip), then normalised once inv is known
   constexpr uint32_t kPre = 8, NT = kWarps * 32;
   const uint32_t nx = n_units * 16;
+  uint32_t qkv_pos = 0, qkv_slot = 0;  // qkv launches: read with the first x batch, kept for the epilogue
+  if (p.epi == kEpiQkv && tid == 0) qkv_pos = p.state->pos, qkv_slot = p.state->len;
   if (ATTN_PRO && p.pro == kProAttn) {
     attn_prologue(p, sm, start, G, nx, tid, warp, lane);
   } else {
@@ -566,6 +568,10 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     }
   }
   }
+  if (p.epi == kEpiQkv && tid == 0) {
+    reinterpret_cast<uint32_t *>(sm.red)[epi::kQkvPos] = qkv_pos;
+    reinterpret_cast<uint32_t *>(sm.red)[epi::kQkvSlot] = qkv_slot;
+  }
   epi::consumer_bar<kWarps>();
   const uint32_t tbl = smem_u32(sm.tbl + warp * kTblWords);
   const uint32_t bsrc = (lane >> 2) < 3 ? tbl + 8 * ((lane >> 2) * 4 + (lane & 3)) : smem_u32(sm.zero) + 8 * (lane & 3);
@@ -618,7 +624,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       uint32_t *slots = sm.tbl + kSlotWord;
       if (tid < n) slots[tid] = slot_k;
       epi::consumer_bar<kWarps>();
-      epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), slots, cd, c, tid, warp, lane);
+      epi::epilogue<kWarps>(p, sm.red, reinterpret_cast<float *>(sm.tbl), slots, cd, c, tid, warp, lane, true);
       if (tid == 0) p.counters[c] = 0;  // ready for the next use of the chunk counters
       if (p.done) {  // chunk complete: count it for the launches that wait on this one
         epi::consumer_bar<kWarps>();
