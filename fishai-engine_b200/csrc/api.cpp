@@ -572,6 +572,7 @@ int fa_debug_set(fa_model *fm, int32_t key, uint64_t value) {
   Model &m = fm->m;
   if (key == FA_DEBUG_WAIT_LIMIT_NS) m.dbg_wait_ns = value;
   else if (key == FA_DEBUG_WITHHOLD_WEIGHTS) m.dbg_withhold = value ? 1u : 0u;
+  else if (key == FA_DEBUG_FIXED_ORDER_SUMS) m.dbg_fixed_order = value != 0;
   else return fail(FA_ERR_INVALID, "fa_debug_set: unknown key");
   drop_graph(m);  // captured launches hold the old parameters
   return FA_OK;
@@ -1037,6 +1038,19 @@ int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, ui
         p.epi = kind == 2 ? kEpiSwiglu : kEpiStore;
         p.out = kind == 2 ? m.ws.h : m.ws.logits;  // scratch destination
         p.state = m.ws.state;
+        if (m.use_red()) {  // the launches of the decode step (o and down add into x, gate/up into gu)
+          p.epi = kEpiRed;
+          p.out = kind == 2 ? m.ws.gu : m.ws.x;
+          if (kind == 2) {
+            p.ssq = nullptr;
+            p.n_ssq = 0;
+            p.red_half = m.cfg.n_ff_used;
+          } else if (kind == 3) {
+            p.pro = kProSwiglu;
+            p.in = m.ws.gu;
+            p.in2 = m.ws.gu + m.cfg.n_ff_used;
+          }
+        }
         return launch_gemv(p, m.pdl, m.stream) ? fail(FA_ERR_CUDA, "gemv launch failed") : FA_OK;
       }
     }

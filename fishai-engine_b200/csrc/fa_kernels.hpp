@@ -39,6 +39,7 @@ enum : int {
   kProRmsNorm = 1,  // x = in[k] * (1/sqrt(sum(ssq)/n + eps)) * norm_w[k]      (src/tensor.rs:280-290)
   kProAttn = 2,     // x = decode attention output combined from its split partials:
                     //   x[h*hd + d] = sum_s o_s[d] e_s / sum_s l_s e_s, e_s = exp(m_s - max_s m_s)
+  kProSwiglu = 3,   // x = silu(in[k]) * in2[k] (gate and up sums of a kEpiRed launch) (src/model.rs:413-417)
 };
 enum : int {
   kEpiStore = 0,    // y[col] = v
@@ -46,6 +47,9 @@ enum : int {
   kEpiQkv = 2,      // RoPE(q,k) (src/model.rs:367-368), q -> qbuf, k/v -> KV cache at pos (src/kv_cache.rs:50-54)
   kEpiSwiglu = 3,   // h[n] = silu(gate[n]) * up[n]                         (src/model.rs:413-417)
   kEpiLogits = 4,   // logits[col] = v ; running argmax in SeqState          (src/model.rs:436-452)
+  kEpiRed = 5,      // out[col] += v by every contributing CTA (vector red.add, no last arriver):
+                    //   red_half = 0: out[out_col + i]; else the chunk's gate half to out[out_col/2 + i]
+                    //   and its up half to out[red_half + out_col/2 + i - width/2]
 };
 
 struct KvView {
@@ -88,8 +92,11 @@ struct GemvParams {
   int pro;
   const float *in;         // [K8]
   const float *norm_w;     // [K8]
-  const float *ssq;        // sum-of-squares partials of `in`
+  const float *in2;        // kProSwiglu: the up sums
+  const float *ssq;        // sum-of-squares partials of `in` (n_ssq = 0: the prologue sums the squares of in)
   uint32_t n_ssq;
+  float *zero;             // optional: zeroed by the launch after it waits for the previous one
+  uint32_t n_zero;         // floats at `zero` (multiple of 4)
   float eps;
   // epilogue
   int epi;
@@ -98,6 +105,7 @@ struct GemvParams {
   uint32_t attn_splits, attn_hd;
   float *resid;            // kEpiResid
   float *ssq_out;          // kEpiResid: [n_chunks]
+  uint32_t red_half;       // kEpiRed: offset of the up half of a gate/up launch (0: plain columns)
   // qkv
   uint32_t q_dim, kv_dim;
   const float *rope_tab;   // [max_pos][head_dim]: cos,sin pairs

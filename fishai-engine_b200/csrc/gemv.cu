@@ -529,6 +529,9 @@ int gemv_init() {
 
 int launch_gemv(const GemvParams &p, bool pdl, cudaStream_t st) {
   if (p.mma) return launch_gemv_mma(p, pdl, st);
+  // the red.add epilogue, the SwiGLU prologue and buffer clearing exist on
+  // the tensor-core path only
+  if (p.epi == kEpiRed || p.pro == kProSwiglu || p.zero) return -1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_ctas);
   cfg.blockDim = dim3(kThreads);

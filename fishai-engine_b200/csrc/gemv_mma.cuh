@@ -271,8 +271,9 @@ __device__ __forceinline__ void mma_group(uint32_t G, uint32_t w, uint32_t slice
 }
 
 // D -> column values of this warp's slice, minus the block corrections, into
-// the chunk partial (rows m >= 8 of the 4-bit layouts carry an extra x16)
-template <int T, int NT>
+// the chunk partial (rows m >= 8 of the 4-bit layouts carry an extra x16);
+// STAGE: into the warp's shared-memory staging row instead (kEpiRed)
+template <int T, int NT, bool STAGE = false>
 __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)[4][4], float (&Dh)[4][4],
                                            float (&corr)[2]) {
   constexpr int kOff = Geo<T>::PAIR_LANES ? 16 : 8;  // builder lanes sharing a block
@@ -295,8 +296,15 @@ __device__ __forceinline__ void flush_warp(float *dst, uint32_t lane, float (&D)
     else cr = __shfl_sync(0xFFFFFFFFu, corr[0], 16 * (t >> 1));
     const float cv = __fmul_rn(Geo<T>::kCorr, cr);
     if (c == 0) {
-      __stcg(dst + 16 * t + g, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv));
-      __stcg(dst + 16 * t + g + 8, __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[2], d[3]), lo8), kHi), cv));
+      const float v0 = __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[0], d[1]), lo0), kYScale), cv);
+      const float v1 = __fsub_rn(__fmul_rn(__fadd_rn(__fadd_rn(d[2], d[3]), lo8), kHi), cv);
+      if constexpr (STAGE) {
+        dst[16 * t + g] = v0;
+        dst[16 * t + g + 8] = v1;
+      } else {
+        __stcg(dst + 16 * t + g, v0);
+        __stcg(dst + 16 * t + g + 8, v1);
+      }
     }
   }
 }
@@ -369,6 +377,28 @@ __device__ __forceinline__ void flush_slice(const GemvParams &p, const ChunkDesc
   float *dst = p.part + (size_t)slot * p.CW + 64 * warp;
   if (min(64u, cd.width - 64 * warp) == 64) flush_warp<T, 4>(dst, lane, D, Dh, corr);
   else flush_warp<T, 2>(dst, lane, D, Dh, corr);
+}
+
+// kEpiRed: the warp's slice values go through its staging row (the warp's
+// coefficient table, free between segments) and leave as one 16-byte vector
+// red.add per lane into the destination, so split chunks need no partial
+// slots, arrival counter or last-arriver pass.  Every column quad lies in one
+// half of a gate/up chunk (widths are multiples of 64).
+template <int T>
+__device__ __forceinline__ void flush_red(const GemvParams &p, const ChunkDesc &cd, float *stage, uint32_t warp,
+                                          uint32_t lane, float (&D)[4][4], float (&Dh)[4][4], float (&corr)[2]) {
+  const uint32_t ncol = min(64u, cd.width - 64 * warp);
+  if (ncol == 64) flush_warp<T, 4, true>(stage, lane, D, Dh, corr);
+  else flush_warp<T, 2, true>(stage, lane, D, Dh, corr);
+  __syncwarp();
+  if (4 * lane < ncol) {
+    const float4 v = reinterpret_cast<const float4 *>(stage)[lane];
+    const uint32_t i = 64 * warp + 4 * lane, half = cd.width / 2;
+    float *dst = !p.red_half ? p.out + cd.out_col + i
+                             : p.out + cd.out_col / 2 + (i < half ? i : p.red_half + i - half);
+    atomicAdd(reinterpret_cast<float4 *>(dst), v);
+  }
+  __syncwarp();  // the staging row is the next segment's table
 }
 
 
@@ -481,9 +511,15 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
                                         uint32_t warp, uint32_t lane, uint32_t &slot, uint32_t &phase, bool &ok) {
   if (cta >= p.n_ctas) return;
   const CtaRange R = p.ranges[cta];
-  const bool norm = p.pro == kProRmsNorm;
+  const bool norm = p.pro == kProRmsNorm, swiglu = p.pro == kProSwiglu;
   const uint32_t G = p.K / 16, start = R.c0 * G + R.g0, end = R.c1 * G + R.g1;
   const uint32_t n_units = end > start ? end - start : 0;
+  if (p.zero) {  // this CTA's share of the buffer the launch clears (float4 stores)
+    const uint32_t n4 = p.n_zero / 4, per = (n4 + p.n_ctas - 1) / p.n_ctas;
+    const uint32_t z0 = min(n4, cta * per), z1 = min(n4, z0 + per);
+    for (uint32_t i = z0 + tid; i < z1; i += kWarps * 32)
+      reinterpret_cast<float4 *>(p.zero)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
   if (!n_units) return;
   // the CTA's rows of x, in unit order: xs[16u + r] = x[16 g(u) + r]; the
   // first batch of x and norm weights is loaded together with the sum-of-
@@ -503,7 +539,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       if (i < nx) {
         const uint32_t k = 16 * ((start + i / 16) % G) + (i & 15);
         xr[j] = __ldcg(p.in + k);
-        wr[j] = norm ? __ldg(p.norm_w + k) : 1.0f;
+        wr[j] = norm ? __ldg(p.norm_w + k) : (swiglu ? __ldcg(p.in2 + k) : 1.0f);
       }
     }
   };
@@ -562,8 +598,10 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
 #pragma unroll
       for (uint32_t j = 0; j < kPre; ++j) {
         const uint32_t i = base + j * NT + tid;
-        // rms_norm (src/tensor.rs:280-290): (x * inv) * w
-        if (i < nx) sm.xs[i] = norm ? __fmul_rn(__fmul_rn(xr[j], inv), wr[j]) : xr[j];
+        // rms_norm (src/tensor.rs:280-290): (x * inv) * w; swiglu: silu(gate) * up
+        if (i < nx)
+          sm.xs[i] = norm ? __fmul_rn(__fmul_rn(xr[j], inv), wr[j])
+                          : (swiglu ? __fmul_rn(epi::silu_ref(xr[j]), wr[j]) : xr[j]);
       }
     }
   }
@@ -594,7 +632,16 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       case kQ8_0: segment<kQ8_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
       default: segment<kQ4_0>(n_st, st_bytes, wait_ns, sm, cd, seg, u, warp, lane, tbl, bsrc, ring, xs0, slot, phase, ok, D, Dh, corr); break;
     }
-    if (ok && 64 * warp < cd.width) {
+    const bool red = p.epi == kEpiRed;
+    if (ok && red && 64 * warp < cd.width) {
+      float *stage = reinterpret_cast<float *>(sm.tbl) + warp * kTblWords;
+      switch (cd.type) {
+        case kQ4_K: flush_red<kQ4_K>(p, cd, stage, warp, lane, D, Dh, corr); break;
+        case kQ6_K: flush_red<kQ6_K>(p, cd, stage, warp, lane, D, Dh, corr); break;
+        case kQ8_0: flush_red<kQ8_0>(p, cd, stage, warp, lane, D, Dh, corr); break;
+        default: flush_red<kQ4_0>(p, cd, stage, warp, lane, D, Dh, corr); break;
+      }
+    } else if (ok && 64 * warp < cd.width) {
       switch (cd.type) {
         case kQ4_K: flush_slice<kQ4_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
         case kQ6_K: flush_slice<kQ6_K>(p, cd, slot_p, warp, lane, D, Dh, corr); break;
@@ -608,6 +655,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
       for (int i = 0; i < 4; ++i) D[t][i] = Dh[t][i] = 0.0f;
     corr[0] = corr[1] = 0.0f;
     u += seg;
+    if (red) continue;  // the red.adds complete the chunk: no publish, no epilogue
     // publish: the last contributing CTA to arrive sums the partials and runs
     // the epilogue.  The contributors' partial slots are fetched while the
     // arrival atomic is in flight (only the last arriver uses them).

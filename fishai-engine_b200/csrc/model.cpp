@@ -498,6 +498,8 @@ int Model::load(const std::string &path, const fa_model_opts &o) {
   if (!part || !counters) return fail(FA_ERR_OOM, "GEMV scratch allocation failed");
   CUDA_TRY(cudaMemset(counters, 0, (size_t)max_chunks * sizeof(uint32_t)));
   if ((rc = alloc_workspace(ws))) return rc;
+  red_ok = W == 1 && !tied && head.mma && cfg.n_ff_used % 4 == 0;
+  for (const LayerW &lw : layers) red_ok = red_ok && lw.qkv.mma && lw.o.mma && lw.gateup.mma && lw.down.mma;
   if (W > 1) {
     // the collective replaces the epilogues' sum-of-squares partials with a
     // prologue that squares x itself: the tensor-core GEMV's mode only
@@ -589,9 +591,13 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
   p.norm_w = lw.attn_norm;
   p.ssq = l == 0 ? w.ssq_e : w.ssq_d;
   p.n_ssq = l == 0 ? embed_ctas : layers[l - 1].down.parts();
-  if (l > 0 && tp.world > 1) {  // x came from an all-reduce: the prologue sums its squares itself
+  if (l > 0 && (tp.world > 1 || use_red())) {  // x came from an all-reduce or red.adds: the prologue sums its squares
     p.ssq = nullptr;
     p.n_ssq = 0;
+  }
+  if (use_red()) {  // the gate/up sums of the previous layer were read by its down launch, which completed
+    p.zero = w.gu;
+    p.n_zero = 2 * cfg.n_ff_used;
   }
   p.eps = cfg.norm_eps;
   p.epi = kEpiQkv;
@@ -657,10 +663,14 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.state = st;
   // tensor parallel: rank 0 adds its partial sums to the residual in place,
   // the others store theirs; the all-reduce then leaves x + sum on every rank
-  const bool part = tp.world > 1 && tp.rank > 0;
+  const bool part = tp.world > 1 && tp.rank > 0, red = use_red();
   if (part) {
     p.epi = kEpiStore;
     p.out = ar_send;
+  }
+  if (red) {  // x += o: every CTA adds its split-K piece into the residual
+    p.epi = kEpiRed;
+    p.out = w.x;
   }
   int rc;
   if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "o gemv launch failed");
@@ -675,6 +685,13 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.epi = kEpiSwiglu;
   p.out = w.h;
   p.state = st;
+  if (red) {  // gate and up sums into gu (zeroed by this layer's qkv launch); SwiGLU in down's prologue
+    p.ssq = nullptr;
+    p.n_ssq = 0;
+    p.epi = kEpiRed;
+    p.out = w.gu;
+    p.red_half = cfg.n_ff_used;
+  }
   if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "gate/up gemv launch failed");
   p = gemv_base(lw.down);
   p.pro = kProPlain;
@@ -683,6 +700,13 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   p.resid = w.x;
   p.ssq_out = w.ssq_d;
   p.state = st;
+  if (red) {  // x += down(silu(gate) * up)
+    p.pro = kProSwiglu;
+    p.in = w.gu;
+    p.in2 = w.gu + cfg.n_ff_used;
+    p.epi = kEpiRed;
+    p.out = w.x;
+  }
   if (part) {
     p.epi = kEpiStore;
     p.out = ar_send;
@@ -703,8 +727,9 @@ int Model::enqueue_head(Workspace &w, SeqState *st) {
     p.pro = kProRmsNorm;
     p.in = w.x;
     p.norm_w = out_norm;
-    p.ssq = tp.world > 1 ? nullptr : ssq_in;
-    p.n_ssq = tp.world > 1 ? 0 : n_ssq;
+    const bool self_ssq = tp.world > 1 || (use_red() && L > 0);
+    p.ssq = self_ssq ? nullptr : ssq_in;
+    p.n_ssq = self_ssq ? 0 : n_ssq;
     p.eps = cfg.norm_eps;
     p.epi = kEpiLogits;
     p.out = w.logits;
@@ -757,9 +782,12 @@ int Model::alloc_workspace(Workspace &w) {
   w.ssq_o = (float *)dmalloc((size_t)n_ssq_o * 4);
   w.ssq_d = (float *)dmalloc((size_t)n_ssq_d * 4);
   w.state = (SeqState *)dmalloc(sizeof(SeqState));
+  const size_t gu_floats = 2 * (size_t)cfg.n_ff_used + 8;
+  w.gu = (float *)dmalloc(gu_floats * 4);
   if (!w.x || !w.q || !w.h || !w.logits || !w.attn_part || !w.attn_out || !w.attn_cnt || !w.ssq_e || !w.ssq_o ||
-      !w.ssq_d || !w.state)
+      !w.ssq_d || !w.state || !w.gu)
     return fail(FA_ERR_OOM, "workspace allocation failed");
+  CUDA_TRY(cudaMemset(w.gu, 0, gu_floats * 4));
   CUDA_TRY(cudaMemset(w.state, 0, sizeof(SeqState)));
   CUDA_TRY(cudaMemset(w.attn_cnt, 0, cfg.n_kv_heads * 4));
   CUDA_TRY(cudaMemset(w.x, 0, ((size_t)d + 8) * 4));

@@ -46,6 +46,7 @@ struct Workspace {
   float *x = nullptr, *q = nullptr, *h = nullptr, *logits = nullptr, *attn_part = nullptr, *attn_out = nullptr;
   uint32_t *attn_cnt = nullptr;
   float *ssq_e = nullptr, *ssq_o = nullptr, *ssq_d = nullptr;
+  float *gu = nullptr;         // red.add mode: gate sums [F] then up sums [F] (zero outside gate/up..down)
   float *hidden = nullptr;     // optional per-layer dump target
   SeqState *state = nullptr;
   uint32_t *ids = nullptr;     // generated ids (device)
@@ -114,6 +115,13 @@ struct Model {
   // copies / use a shorter wait limit
   uint32_t dbg_withhold = 0;
   uint64_t dbg_wait_ns = 0;
+  // batch-1 projections o, gate/up and down reduce their split-K pieces by
+  // red.add into the destination (kEpiRed; SwiGLU and the RMSNorm sums move
+  // to the next launch's prologue).  Needs every GEMV on the tensor-core
+  // path, an untied head and one rank.  dbg_fixed_order: the fixed-order
+  // last-arriver reduction instead (bit-reproducible run to run).
+  bool red_ok = false, dbg_fixed_order = false;
+  bool use_red() const { return red_ok && !dbg_fixed_order; }
   uint64_t device_bytes = 0, step_bytes = 0;
   // persistent decode-step kernel (all GEMVs in the MMA layout, untied head)
   bool want_step = false;            // requested by the load options

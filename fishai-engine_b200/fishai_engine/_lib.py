@@ -16,7 +16,7 @@ ERR_INVALID, ERR_GGUF, ERR_UNSUPPORTED, ERR_OOM, ERR_CUDA, ERR_NCCL, ERR_CONTEXT
 
 F32, F16, Q4_0, Q4_1, Q5_0, Q8_0, Q4_K, Q6_K = 0, 1, 2, 3, 6, 8, 12, 14
 KV_F32, KV_F16 = 0, 1
-DEBUG_WAIT_LIMIT_NS, DEBUG_WITHHOLD_WEIGHTS = 1, 2
+DEBUG_WAIT_LIMIT_NS, DEBUG_WITHHOLD_WEIGHTS, DEBUG_FIXED_ORDER_SUMS = 1, 2, 3
 
 
 class FishaiError(RuntimeError):

@@ -172,6 +172,13 @@ int fa_model_step_launches(const fa_model *m, uint32_t *n);
  * faults or hangs: every wait is bounded and the context stays usable. */
 #define FA_DEBUG_WAIT_LIMIT_NS 1
 #define FA_DEBUG_WITHHOLD_WEIGHTS 2
+/* FA_DEBUG_FIXED_ORDER_SUMS: value 1 makes the batch-1 o, gate/up and down
+ * projections sum their split-K pieces in a fixed order (the last CTA of a
+ * chunk adds the published partials), so a step is bit-reproducible run to
+ * run; 0 (the default) lets every CTA add its piece into the destination with
+ * a vector red.add, which removes a reduction pass per launch but leaves the
+ * order of the f32 additions to the hardware. */
+#define FA_DEBUG_FIXED_ORDER_SUMS 3
 int fa_debug_set(fa_model *m, int32_t key, uint64_t value);
 
 /* ------------------------------------------------------------- KV cache */

@@ -77,8 +77,10 @@ def _model_pair(path, resident=False, step=False):
     return dev, O.Model(path, resident=resident, threads=os.cpu_count() or 4)
 
 
-def _forward_parity(path, n_tokens=6, kv_dtype=L.KV_F32, check_hidden=True, seed=0, step=False):
+def _forward_parity(path, n_tokens=6, kv_dtype=L.KV_F32, check_hidden=True, seed=0, step=False, fixed=False):
     dev, ref = _model_pair(path, step=step)
+    if fixed:  # split-K pieces summed in a fixed order instead of red.add
+        L.check(L.lib().fa_debug_set(dev._h, L.DEBUG_FIXED_ORDER_SUMS, 1))
     V = dev.config.vocab_size
     rng = np.random.default_rng(seed)
     toks = rng.integers(3, V, n_tokens).tolist()
@@ -122,6 +124,21 @@ def _kquant_spec(**kw):
 def test_kquant_mix_forward_parity(tmpdir_m):
     p = synth.write(str(tmpdir_m / "kq.gguf"), 7, **_kquant_spec())
     _forward_parity(p)
+
+
+def test_kquant_mix_fixed_order_sums_parity(tmpdir_m):
+    """The fixed-order split-K reduction (last arriver per chunk) at the same
+    bars as the default red.add one, and bit-reproducible: the same token
+    stepped twice from the same cache state gives identical logits."""
+    p = synth.write(str(tmpdir_m / "kq_fixed.gguf"), 7, **_kquant_spec())
+    _, dev, _, kv_d, _ = _forward_parity(p, fixed=True, check_hidden=False)
+    a = dev.forward([17], 6, kv_d)
+    kv2 = dev.new_kv_cache(64, dtype=L.KV_F32)
+    toks = [int(x) for x in np.random.default_rng(0).integers(3, dev.config.vocab_size, 6)]
+    for i, t in enumerate(toks):
+        dev.forward([t], i, kv2)
+    b = dev.forward([17], 6, kv2)
+    assert np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
 
 
 def test_q4_0_forward_parity(tmpdir_m):
