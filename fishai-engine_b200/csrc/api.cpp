@@ -1023,7 +1023,7 @@ int fa_profile_gemv(fa_model *fm, int32_t kind, uint32_t reps, float *avg_ms, ui
   auto launch = [&](uint32_t i) -> int {
     const uint32_t l = i % L;
     switch (kind) {
-      case 0: return m.enqueue_qkv(l, m.ws, kvh.kv, 0, m.ws.state);
+      case 0: return m.enqueue_qkv(l, m.ws, kvh.kv, 0, m.ws.state, m.raw_qkv_ok());
       case 4: return m.enqueue_head(m.ws, m.ws.state);
       default: {
         const LayerW &lw = m.layers[l];

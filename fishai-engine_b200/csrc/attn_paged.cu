@@ -138,7 +138,10 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
     }
   };
   const bool newest = t1 == len + 1;  // this split ends at position len
-  auto early = [&](uint32_t j) { return p.early_kv && !(newest && j + 1 == n_tiles); };
+  // raw q/k/v: the row of position len is patched into its tile from
+  // registers, so that tile needs nothing from the qkv launch either
+  const bool raw = p.qkv_raw != nullptr;
+  auto early = [&](uint32_t j) { return p.early_kv && (raw || !(newest && j + 1 == n_tiles)); };
   if (warp == 0) {
     if (n_tiles > 0 && early(0)) issue(0);
     if (n_tiles > 1 && early(1)) issue(1);
@@ -150,7 +153,8 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
   }
 
   float q[REP][DPL], o[REP][DPL];
-  const float *qrow = p.q + (uint64_t)kvh * REP * HD + lane * DPL;
+  float knew[DPL], vnew[DPL];  // raw mode: this token's k (rotated) and v, dims of this lane
+  const float *qrow = (raw ? p.qkv_raw : p.q) + (uint64_t)kvh * REP * HD + lane * DPL;
 #pragma unroll
   for (int h = 0; h < REP; ++h)
 #pragma unroll
@@ -158,6 +162,54 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
       q[h][j] = __ldcg(qrow + h * HD + j);
       o[h][j] = 0.0f;
     }
+  if (raw) {
+    // RoPE, half-split (src/model.rs:367-368, src/tensor.rs rope): dim dd
+    // pairs with dd +- hd/2, held by lane +- 16 at the same j; the same f32
+    // steps as the qkv epilogue of the fixed-order path
+    const uint32_t qd = p.n_heads * HD, pos = p.state->pos;
+    const float *krow = p.qkv_raw + qd + (uint64_t)kvh * HD + lane * DPL;
+#pragma unroll
+    for (uint32_t j = 0; j < DPL; ++j) {
+      knew[j] = __ldcg(krow + j);
+      vnew[j] = __ldcg(krow + KVH * HD + j);
+    }
+    if (pos < p.rope_max) {
+      const bool lo = lane < 16;
+      const float *cs = p.rope_tab + (uint64_t)pos * HD + 2 * ((lane * DPL) % (HD / 2));
+      float cth[DPL], sth[DPL];
+#pragma unroll
+      for (uint32_t j = 0; j < DPL; ++j) {
+        cth[j] = __ldg(cs + 2 * j);
+        sth[j] = __ldg(cs + 2 * j + 1);
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < DPL; ++j) {
+        float pv[REP + 1];
+#pragma unroll
+        for (int h = 0; h < REP; ++h) pv[h] = __shfl_xor_sync(0xFFFFFFFFu, q[h][j], 16);
+        pv[REP] = __shfl_xor_sync(0xFFFFFFFFu, knew[j], 16);
+#pragma unroll
+        for (int h = 0; h <= REP; ++h) {
+          const float v = h < REP ? q[h][j] : knew[j];
+          const float r = lo ? __fsub_rn(__fmul_rn(v, cth[j]), __fmul_rn(pv[h], sth[j]))
+                             : __fadd_rn(__fmul_rn(pv[h], sth[j]), __fmul_rn(v, cth[j]));
+          if (h < REP) q[h][j] = r;
+          else knew[j] = r;
+        }
+      }
+    } else if (tid == 0 && split == 0 && kvh == 0) {
+      atomicOr(&p.state->err, kErrContext);
+    }
+    if (F16) {  // the cache holds f16: this step attends to the rounded values, as later steps will
+#pragma unroll
+      for (uint32_t j = 0; j < DPL; ++j) {
+        knew[j] = __half2float(__float2half_rn(knew[j]));
+        vnew[j] = __half2float(__float2half_rn(vnew[j]));
+      }
+    }
+  }
+  // raw mode: tile and row of position len in this CTA's range (newest split)
+  const uint32_t j_new = newest ? (len - t0) / kPT : ~0u, r_new = newest ? (len - t0) % kPT : 0;
   float m_me = -INFINITY, l_me = 0.0f;  // lane h < REP: softmax state of head h
   bool ok = true;
   float *scw = sc + warp * NV;
@@ -167,6 +219,21 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
     if (ok && !mbar_wait_sleep(&bar[j & 1], (j >> 1) & 1)) ok = false;
     const uint8_t *kt = tiles + (j & 1) * 2 * G::tile_bytes + (size_t)warp * kPP * HD * G::esz;
     const uint8_t *vt = kt + G::tile_bytes;
+    if (raw && ok && j == j_new && warp == r_new / kPP) {
+      // the copied row of position len is stale: this token's k / v replace it
+      uint8_t *kr = tiles + (j & 1) * 2 * G::tile_bytes + (size_t)r_new * HD * G::esz + lane * DPL * G::esz;
+#pragma unroll
+      for (uint32_t d = 0; d < DPL; ++d) {
+        if (F16) {
+          reinterpret_cast<__half *>(kr)[d] = __float2half_rn(knew[d]);
+          reinterpret_cast<__half *>(kr + G::tile_bytes)[d] = __float2half_rn(vnew[d]);
+        } else {
+          reinterpret_cast<float *>(kr)[d] = knew[d];
+          reinterpret_cast<float *>(kr + G::tile_bytes)[d] = vnew[d];
+        }
+      }
+      __syncwarp();
+    }
     if (ok) {
       // partial dots of this lane's dims: v[i * REP + h]
       float v[NV];
@@ -267,6 +334,28 @@ __global__ void __launch_bounds__(kPW * 32) k_attn_paged(const AttnParams p) {
     if (lane == 0) atomicOr(&p.state->err, kErrWaitTimeout);
     if (tid == 0)
       for (uint32_t j = n_tiles > 2 ? n_tiles - 2 : 0; j < n_tiles; ++j) mbar_wait_sleep(&bar[j & 1], (j >> 1) & 1);
+  }
+  if (raw && newest && warp == 0) {
+    // append this token's k / v at slot len (src/kv_cache.rs:50-54); every
+    // copy of this CTA has landed, so nothing reads the row meanwhile
+    if (len / 16 < p.kv.max_pages) {
+      const uint32_t page = __ldg(pt + len / 16);
+      const uint64_t lb = (uint64_t)p.layer * p.kv.layer_stride;
+      const uint64_t ik = lb + kv_index(page, 0, kvh, len % 16, lane * DPL, KVH, HD);
+      const uint64_t iv = lb + kv_index(page, 1, kvh, len % 16, lane * DPL, KVH, HD);
+#pragma unroll
+      for (uint32_t d = 0; d < DPL; ++d) {
+        if (F16) {
+          reinterpret_cast<__half *>(p.kv.base)[ik + d] = __float2half_rn(knew[d]);
+          reinterpret_cast<__half *>(p.kv.base)[iv + d] = __float2half_rn(vnew[d]);
+        } else {
+          reinterpret_cast<float *>(p.kv.base)[ik + d] = knew[d];
+          reinterpret_cast<float *>(p.kv.base)[iv + d] = vnew[d];
+        }
+      }
+    } else if (lane == 0) {
+      atomicOr(&p.state->err, kErrContext);
+    }
   }
   __syncthreads();
   // merge the warps (fixed order) into the split partial

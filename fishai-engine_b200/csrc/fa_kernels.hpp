@@ -154,6 +154,12 @@ struct AttnParams {
   int early_kv;            // batch-1 paged kernel inside a step graph: K/V tiles of positions below
                            // len are fetched before the wait for the qkv launch (earlier steps,
                            // i.e. earlier graph launches, wrote them)
+  const float *qkv_raw;    // batch-1 paged kernel: non-null -> this token's q | k | v are the qkv launch's
+                           // red.add sums [H*hd | n_kv*hd | n_kv*hd]: the kernel applies RoPE to q and k
+                           // (src/model.rs:367-368), uses the new k / v for position len and appends
+                           // them to the cache (src/kv_cache.rs:50-54); q is unused
+  const float *rope_tab;   // with qkv_raw: [rope_max][hd] cos, sin pairs
+  uint32_t rope_max;
   const SeqState *row_states;  // batched decode: per query row state (T = len + 1), cache sequence row_seq0 + row
   uint32_t row_seq0;
   void *out_h;             // batched decode: non-null -> the combined output as f16 [rows][H*hd] here

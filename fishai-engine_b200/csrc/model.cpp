@@ -583,7 +583,12 @@ int Model::enqueue_embed(Workspace &w, SeqState *st) {
   return launch_embed(ep, pdl, stream) ? fail(FA_ERR_CUDA, "embed launch failed") : FA_OK;
 }
 
-int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
+bool Model::raw_qkv_ok() const {
+  // the batch-1 paged attention takes raw q/k/v; its o projection combines the splits
+  return use_red() && !layers.empty() && attn_fused(0) && (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim % 4 == 0;
+}
+
+int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st, bool raw) {
   const LayerW &lw = layers[l];
   GemvParams p = gemv_base(lw.qkv);
   p.pro = kProRmsNorm;
@@ -610,6 +615,10 @@ int Model::enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq
   p.seq = seq;
   p.layer = l;
   p.state = st;
+  if (raw) {  // q | k | v sums by red.add; RoPE and the cache append happen in the attention
+    p.epi = kEpiRed;
+    p.out = w.qkv_raw;
+  }
   return launch_gemv(p, pdl, stream) ? fail(FA_ERR_CUDA, "qkv gemv launch failed") : FA_OK;
 }
 
@@ -627,7 +636,7 @@ bool Model::attn_fused(uint32_t l) const {
          (uint64_t)cfg.n_heads * (attn_splits + 1) <= gemv_mma_table_words();
 }
 
-int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st) {
+int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st, bool raw) {
   AttnParams ap{};
   ap.q = w.q;
   ap.q_rows = 1;
@@ -643,10 +652,15 @@ int Model::enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t se
   ap.state = st;
   ap.partials_only = attn_fused(l) ? 1 : 0;
   ap.early_kv = capturing_step && pdl ? 1 : 0;
+  if (raw) {
+    ap.qkv_raw = w.qkv_raw;
+    ap.rope_tab = rope_tab;
+    ap.rope_max = rope_max;
+  }
   return launch_attention(ap, pdl, stream) ? fail(FA_ERR_CUDA, "attention launch failed") : FA_OK;
 }
 
-int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump) {
+int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump, bool raw) {
   const LayerW &lw = layers[l];
   GemvParams p = gemv_base(lw.o);
   p.pro = kProPlain;
@@ -671,6 +685,10 @@ int Model::enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidd
   if (red) {  // x += o: every CTA adds its split-K piece into the residual
     p.epi = kEpiRed;
     p.out = w.x;
+  }
+  if (raw) {  // the attention, which read the raw q/k/v sums, has completed
+    p.zero = w.qkv_raw;
+    p.n_zero = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim;
   }
   int rc;
   if (launch_gemv(p, pdl, stream)) return fail(FA_ERR_CUDA, "o gemv launch failed");
@@ -754,10 +772,12 @@ int Model::enqueue_head(Workspace &w, SeqState *st) {
 int Model::enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump) {
   int rc;
   if ((rc = enqueue_embed(w, w.state))) return rc;
+  const bool raw = raw_qkv_ok();
   for (uint32_t l = 0; l < cfg.n_layers; ++l) {
-    if ((rc = enqueue_qkv(l, w, kv, seq, w.state))) return rc;
-    if ((rc = enqueue_attn(l, w, kv, seq, w.state))) return rc;
-    if ((rc = enqueue_post_attn(l, w, w.state, hidden_dump ? hidden_dump + (size_t)l * cfg.n_embd : nullptr))) return rc;
+    if ((rc = enqueue_qkv(l, w, kv, seq, w.state, raw))) return rc;
+    if ((rc = enqueue_attn(l, w, kv, seq, w.state, raw))) return rc;
+    if ((rc = enqueue_post_attn(l, w, w.state, hidden_dump ? hidden_dump + (size_t)l * cfg.n_embd : nullptr, raw)))
+      return rc;
   }
   if ((rc = enqueue_head(w, w.state))) return rc;
   if (launch_step_end(w.state, w.ids, w.max_ids, pdl, stream)) return fail(FA_ERR_CUDA, "step_end launch failed");
@@ -782,12 +802,14 @@ int Model::alloc_workspace(Workspace &w) {
   w.ssq_o = (float *)dmalloc((size_t)n_ssq_o * 4);
   w.ssq_d = (float *)dmalloc((size_t)n_ssq_d * 4);
   w.state = (SeqState *)dmalloc(sizeof(SeqState));
-  const size_t gu_floats = 2 * (size_t)cfg.n_ff_used + 8;
+  const size_t gu_floats = 2 * (size_t)cfg.n_ff_used + 8, qkv_floats = qd + 2 * (size_t)cfg.n_kv_heads * cfg.head_dim + 8;
   w.gu = (float *)dmalloc(gu_floats * 4);
+  w.qkv_raw = (float *)dmalloc(qkv_floats * 4);
   if (!w.x || !w.q || !w.h || !w.logits || !w.attn_part || !w.attn_out || !w.attn_cnt || !w.ssq_e || !w.ssq_o ||
-      !w.ssq_d || !w.state || !w.gu)
+      !w.ssq_d || !w.state || !w.gu || !w.qkv_raw)
     return fail(FA_ERR_OOM, "workspace allocation failed");
   CUDA_TRY(cudaMemset(w.gu, 0, gu_floats * 4));
+  CUDA_TRY(cudaMemset(w.qkv_raw, 0, qkv_floats * 4));
   CUDA_TRY(cudaMemset(w.state, 0, sizeof(SeqState)));
   CUDA_TRY(cudaMemset(w.attn_cnt, 0, cfg.n_kv_heads * 4));
   CUDA_TRY(cudaMemset(w.x, 0, ((size_t)d + 8) * 4));

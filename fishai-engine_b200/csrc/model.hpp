@@ -47,6 +47,7 @@ struct Workspace {
   uint32_t *attn_cnt = nullptr;
   float *ssq_e = nullptr, *ssq_o = nullptr, *ssq_d = nullptr;
   float *gu = nullptr;         // red.add mode: gate sums [F] then up sums [F] (zero outside gate/up..down)
+  float *qkv_raw = nullptr;    // raw-qkv mode: q | k | v sums of the qkv launch (zero outside qkv..attention)
   float *hidden = nullptr;     // optional per-layer dump target
   SeqState *state = nullptr;
   uint32_t *ids = nullptr;     // generated ids (device)
@@ -169,12 +170,17 @@ struct Model {
   int ensure_rope(uint32_t max_pos);
   // pieces of one token step (embed -> layers -> head -> step_end)
   int enqueue_embed(Workspace &w, SeqState *st);
-  int enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
-  int enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st);
+  // raw: the single-token step's form — qkv adds its sums into w.qkv_raw
+  // (red.add) and the attention applies RoPE and appends the new K/V itself;
+  // the o launch then clears qkv_raw.  Multi-token calls (all tokens' K/V
+  // appended before any attention) use the qkv epilogue instead.
+  bool raw_qkv_ok() const;
+  int enqueue_qkv(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st, bool raw = false);
+  int enqueue_attn(uint32_t l, Workspace &w, const KvCache &kv, uint32_t seq, SeqState *st, bool raw = false);
   // layer l's o projection combines the batch-1 attention's split partials
   // in its prologue (the attention then leaves them uncombined)
   bool attn_fused(uint32_t l) const;
-  int enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump);
+  int enqueue_post_attn(uint32_t l, Workspace &w, SeqState *st, float *hidden_dump, bool raw = false);
   int enqueue_head(Workspace &w, SeqState *st);
   int enqueue_step(const KvCache &kv, uint32_t seq, Workspace &w, float *hidden_dump);
   int setup_step_kernel();                               // eligibility + device tables (at load)
