@@ -100,7 +100,7 @@ struct Model {
   float *out_norm = nullptr;
   float *rope_tab = nullptr;
   uint32_t rope_max = 0;
-  uint32_t attn_splits = 32;
+  uint32_t attn_splits = 24;
   int n_sm = 148;
   float *part = nullptr;         // GEMV chunk partials, shared by every launch
   uint32_t *counters = nullptr;  // GEMV chunk arrival counters
