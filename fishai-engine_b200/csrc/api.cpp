@@ -1121,7 +1121,7 @@ extern "C" int fa_gemm_tokens(fa_model *fm, int32_t proj, uint32_t layer, const 
   std::vector<uint16_t> xb((size_t)T * K);
   for (size_t i = 0; i < xb.size(); ++i) xb[i] = f32_to_f16(x_host[i]);
   DevBuf x, y, err, part;
-  const uint64_t part_floats = qgemm_part_floats(256, (uint32_t)m.n_sm);  // stream-K partial tiles
+  const uint64_t part_floats = qgemm_part_floats(512, (uint32_t)m.n_sm);  // stream-K partial tiles
   API_CUDA(cudaMalloc(&part.p, part_floats * 4));
   API_CUDA(cudaMalloc(&x.p, xb.size() * 2));
   API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));
@@ -1167,7 +1167,7 @@ extern "C" int fa_profile_gemm(fa_model *fm, int32_t proj, uint32_t layer, uint3
   API_CUDA(cudaSetDevice(m.device));
   const uint32_t K = P->K, N = P->n_out;
   DevBuf x, y, part;
-  const uint64_t part_floats = qgemm_part_floats(256, (uint32_t)m.n_sm);  // stream-K partial tiles
+  const uint64_t part_floats = qgemm_part_floats(512, (uint32_t)m.n_sm);  // stream-K partial tiles
   API_CUDA(cudaMalloc(&part.p, part_floats * 4));
   API_CUDA(cudaMalloc(&x.p, (size_t)T * K * 2));
   API_CUDA(cudaMalloc(&y.p, (size_t)T * N * 4));

@@ -1103,7 +1103,7 @@ int Model::ensure_prefill_ws(uint32_t cap) {
 }
 
 int Model::ensure_qg_part(uint64_t floats) {
-  floats = std::max<uint64_t>(floats, qgemm_part_floats(256, (uint32_t)n_sm));
+  floats = std::max<uint64_t>(floats, qgemm_part_floats(512, (uint32_t)n_sm));
   if (floats <= qg_part_floats) return FA_OK;
   float *q = (float *)dmalloc(floats * 4);
   if (!q) return fail(FA_ERR_OOM, "GEMM split-K workspace allocation failed");

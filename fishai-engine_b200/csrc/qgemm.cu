@@ -50,23 +50,31 @@ constexpr uint32_t kPfWarp = 544;
 
 // PF: the launch stages its weight bytes through the prefetch ring (every
 // chunk Q8_0 or Q4_0); otherwise the dequant warps load them directly.
+// BN = 512: a token-tile pair — two B tiles of 256 tokens per stage, two
+// N = 256 MMAs per 16-row step into the two halves of TMEM, so each
+// dequantised A stage serves 512 tokens (the accumulator is not double
+// buffered: the epilogue of a pair runs before the next pair's MMAs)
 template <uint32_t BN, bool PF>
 struct QCfg {
+  static constexpr uint32_t kN = BN > 256 ? 256 : BN;          // N of one MMA instruction
+  static constexpr uint32_t kHalves = BN / kN;                 // B tiles (TMA boxes, MMAs) per stage
+  static constexpr uint32_t kAccBufs = BN > 256 ? 1 : 2;       // accumulators in TMEM
   static constexpr uint32_t kBTile = BN * kBK * 2;
   static constexpr uint32_t kStage = kATile + kBTile;
   // A/B stages (without the ring: as many as 192 KB holds, at most 8) and
   // the ring's depth in k-steps
   static constexpr uint32_t kFit = (192 * 1024) / kStage > 8 ? 8 : (192 * 1024) / kStage;
-  static constexpr uint32_t kStages = PF ? (BN == 64 ? 6 : (BN == 128 ? 5 : 3)) : kFit;
+  static constexpr uint32_t kStages = PF ? (BN == 64 ? 6 : (BN == 128 ? 5 : (BN == 256 ? 3 : 2))) : kFit;
   static constexpr uint32_t kPf = PF ? 4 : 0;
   static constexpr uint32_t kPfStage = kDeq * kPfWarp;  // one region per dequant warp
   static constexpr uint32_t kPfOff = kStages * kStage;
   static constexpr uint32_t kBarOff = kPfOff + kPf * kPfStage;
   static constexpr uint32_t kSmem = 1024 + kBarOff + 256;   // 1 KB alignment slack, barriers
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
-  static constexpr uint32_t kTmemCols = 2 * BN;
-  // tcgen05 instruction descriptor: f32 D, f16 A and B (format 0), both K-major, M = 128, N = BN
-  static constexpr uint32_t kIdesc = (1u << 4) | ((BN >> 3) << 17) | ((kBM >> 4) << 24);
+  static constexpr uint32_t kTmemCols = kAccBufs * BN;
+  static_assert(kTmemCols <= 512, "tensor memory columns");
+  // tcgen05 instruction descriptor: f32 D, f16 A and B (format 0), both K-major, M = 128, N = kN
+  static constexpr uint32_t kIdesc = (1u << 4) | ((kN >> 3) << 17) | ((kBM >> 4) << 24);
 };
 
 struct QBars {
@@ -467,7 +475,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       mbar_init(&b.full_b[s], 1);
       mbar_init(&b.empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (uint32_t a = 0; a < C::kAccBufs; ++a) {
       mbar_init(&b.acc_full[a], 1);
       mbar_init(&b.acc_empty[a], 4);
     }
@@ -501,7 +509,10 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
         for (uint32_t ks = sg.ks0; ks < sg.ks1; ++ks) {
           if (!qwait(&b.empty[s], ph, b)) goto tma_out;
           mbar_arrive_expect_tx(&b.full_b[s], C::kBTile);
-          tma_load_2d(base + s * C::kStage + kATile, &xmap, (int32_t)(ks * kBK), (int32_t)(tt * BN), &b.full_b[s]);
+#pragma unroll
+          for (uint32_t h = 0; h < C::kHalves; ++h)
+            tma_load_2d(base + s * C::kStage + kATile + h * (C::kN * kBK * 2), &xmap, (int32_t)(ks * kBK),
+                        (int32_t)(tt * BN + h * C::kN), &b.full_b[s]);
           pending |= 1u << s;
           last_ph = (last_ph & ~(1u << s)) | ((ph ^ 1u) << s);  // consumer parity of this load
           if (++s == C::kStages) {
@@ -537,7 +548,10 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           const uint32_t a0 = sbase + s * C::kStage, b0 = a0 + kATile;
 #pragma unroll
           for (uint32_t kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(dt, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + 32 * kk), C::kIdesc, (ks != wo.ks0) || kk);
+#pragma unroll
+            for (uint32_t h = 0; h < C::kHalves; ++h)
+              umma_f16(dt + h * C::kN, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + h * (C::kN * kBK * 2) + 32 * kk),
+                       C::kIdesc, (ks != wo.ks0) || kk);
           umma_commit(&b.empty[s]);
         }
         __syncwarp();
@@ -550,7 +564,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       if (!ok) break;
       if (lane == 0) umma_commit(&b.acc_full[acc]);
       __syncwarp();
-      if (++acc == 2) {
+      if (++acc == C::kAccBufs) {
         acc = 0;
         aph ^= 1u;
       }
@@ -718,7 +732,7 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&b.acc_empty[acc]);
-      if (++acc == 2) {
+      if (++acc == C::kAccBufs) {
         acc = 0;
         aph ^= 1u;
       }
@@ -798,9 +812,9 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 }  // namespace
 
 int qgemm_init() {
-  if (!set_smem<64, 0>() || !set_smem<128, 0>() || !set_smem<256, 0>() || !set_smem<64, kQ8_0>() ||
-      !set_smem<128, kQ8_0>() || !set_smem<256, kQ8_0>() || !set_smem<64, kQ4_0>() || !set_smem<128, kQ4_0>() ||
-      !set_smem<256, kQ4_0>())
+  if (!set_smem<64, 0>() || !set_smem<128, 0>() || !set_smem<256, 0>() || !set_smem<512, 0>() ||
+      !set_smem<64, kQ8_0>() || !set_smem<128, kQ8_0>() || !set_smem<256, kQ8_0>() || !set_smem<512, kQ8_0>() ||
+      !set_smem<64, kQ4_0>() || !set_smem<128, kQ4_0>() || !set_smem<256, kQ4_0>() || !set_smem<512, kQ4_0>())
     return -1;
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;
@@ -834,19 +848,23 @@ uint64_t qgemm_part_floats(uint32_t bn, uint32_t n_sm) { return (uint64_t)2 * n_
 
 int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
   if (!p0.T || !p0.n_tiles || p0.K % 16 || !p0.w || !p0.out || p0.ldo % 4) return -1;  // fixup: float4 rows
-  const uint32_t t_tiles = (p0.T + map.bn - 1) / map.bn, ksteps = (p0.K / 16 + 3) / 4;
+  // more than one 256-token tile: token-tile pairs (one dequantised weight
+  // stage per 512 tokens) over the same 256-row TMA boxes
+  const uint32_t bn = (map.bn == 256 && p0.T > 256) ? 512 : map.bn;
+  const uint32_t t_tiles = (p0.T + bn - 1) / bn, ksteps = (p0.K / 16 + 3) / 4;
   const uint64_t W = (uint64_t)p0.n_tiles * t_tiles * ksteps;
   const uint32_t grid = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(n_sm, W / kMinSk));
-  if (!p0.part || p0.part_floats < qgemm_part_floats(map.bn, grid) || ksteps + 1 > kFixupSlots) return -1;
+  if (!p0.part || p0.part_floats < qgemm_part_floats(bn, grid) || ksteps + 1 > kFixupSlots) return -1;
   int rc;
-  switch (map.bn) {
+  switch (bn) {
     case 64: rc = launch_bn<64>(p0, map.bytes, grid, st); break;
     case 128: rc = launch_bn<128>(p0, map.bytes, grid, st); break;
     case 256: rc = launch_bn<256>(p0, map.bytes, grid, st); break;
+    case 512: rc = launch_bn<512>(p0, map.bytes, grid, st); break;
     default: return -1;
   }
   if (rc || grid < 2) return rc;
-  return launch_pdl(k_qg_fixup, dim3(grid - 1, map.bn * kBM / 1024), dim3(256), 0, st, p0, map.bn, grid);
+  return launch_pdl(k_qg_fixup, dim3(grid - 1, bn * kBM / 1024), dim3(256), 0, st, p0, bn, grid);
 }
 
 }  // namespace fa
