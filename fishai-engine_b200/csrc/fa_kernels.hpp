@@ -243,8 +243,10 @@ struct QgParams {
   uint32_t *err;             // kErrWaitTimeout on a bounded-wait expiry (may be null)
   float *part;               // stream-K partial tiles: 2 slots per CTA of 128 x BN floats
   uint64_t part_floats;      // capacity of part (>= qgemm_part_floats(bn, n_sm))
-  uint32_t prefetch;         // kQ8_0 / kQ4_0: every chunk has that type (weights through the prefetch ring); 0: direct loads
+  uint32_t prefetch;         // kQ8_0 / kQ4_0: every chunk has that type (weights through the prefetch ring);
+                             // kPfAny: any mix of the MMA types through the same ring; 0: direct loads
 };
+constexpr uint32_t kPfAny = 1;  // QgParams::prefetch: mixed-type prefetch ring
 struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
   alignas(64) unsigned char bytes[128];
   uint32_t bn;               // tokens per tile: 64, 128 or 256

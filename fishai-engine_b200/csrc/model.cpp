@@ -304,6 +304,15 @@ static int build_plan(Model &m, GemvPlan &P, const std::vector<TensorRef> &parts
     P.qg_prefetch = nc && (P.chunks[0].type == kQ8_0 || P.chunks[0].type == kQ4_0) ? P.chunks[0].type : 0u;
     for (uint32_t c = 0; c < nc; ++c)
       if (P.chunks[c].type != P.qg_prefetch) P.qg_prefetch = 0;
+    if (!P.qg_prefetch) {
+      // the mixed-type ring copies whole super-block headers, d and scale
+      // vectors with 16-byte cp.async: K-quant chunks of whole super-blocks
+      bool any = nc > 0;
+      for (const ChunkDesc &d : P.chunks)
+        any = any && d.offset % 16 == 0 && d.gbytes % 16 == 0 &&
+              ((d.type != kQ4_K && d.type != kQ6_K) || d.width % 256 == 0);
+      P.qg_prefetch = any ? kPfAny : 0u;
+    }
     P.d_qg_tiles = (QgTile *)m.dmalloc(P.qg_tiles.size() * sizeof(QgTile));
     if (!P.d_qg_tiles) return fail(FA_ERR_OOM, "GEMM tile table allocation failed");
     CUDA_TRY(cudaMemcpy(P.d_qg_tiles, P.qg_tiles.data(), P.qg_tiles.size() * sizeof(QgTile), cudaMemcpyHostToDevice));

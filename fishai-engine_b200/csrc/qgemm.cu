@@ -45,11 +45,14 @@ constexpr uint32_t kEpi0 = 2 + kDeq;             // first epilogue warp
 constexpr uint32_t kQThreads = (kEpi0 + 4) * 32; // 704
 constexpr uint32_t kATile = kBM * kBK * 2;       // 16 KB
 
-// Shared memory of one weight prefetch slot of a dequant warp (codes + scales)
-constexpr uint32_t kPfWarp = 544;
+// Shared memory of one weight prefetch slot of a dequant warp (codes + scales):
+// Q8_0 / Q4_0 544 bytes, Q4_K 640 (512 code bytes, 8 row headers), Q6_K 448
+constexpr uint32_t kPfWarp = 640;
 
 // PF: the launch stages its weight bytes through the prefetch ring (every
-// chunk Q8_0 or Q4_0); otherwise the dequant warps load them directly.
+// chunk Q8_0 or Q4_0, or kPfAny: any mix of the four MMA types with
+// K-quant widths of whole super-blocks); otherwise the dequant warps load
+// them directly.
 // BN = 512: a token-tile pair — two B tiles of 256 tokens per stage, two
 // N = 256 MMAs per 16-row step into the two halves of TMEM, so each
 // dequantised A stage serves 512 tokens (the accumulator is not double
@@ -162,16 +165,17 @@ __device__ __forceinline__ uint32_t h2_u32(__half2 v) { return *reinterpret_cast
 // Q4_K unit of one warp of a pair: all four tiles of the 64-column slice i,
 // rows 2c, 2c+1 (th = 0) or 2c+8, 2c+9 (th = 1) of lane l = 4g + c, so each
 // warp reads the scale headers of its own two rows only.
-__device__ __forceinline__ void deq_unit_q4k_rows(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th,
-                                                  uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
+// qv: the lane's code words (one per tile), hr[jj]: the header of row
+// 2c + 8th + jj of the slice's super-block; i3 = slice index & 3
+__device__ __forceinline__ void deq_q4k_vals(uint4 qv, const uint4 (&hr)[2], uint32_t i3, uint32_t th, uint32_t lane,
+                                             uint32_t a, uint32_t n0, uint32_t k0) {
   const uint32_t g = lane >> 2, c = lane & 3;
-  const uint4 qv = ldg128(G + 512 * i + 16 * lane);  // Q4_K slices are whole (4 tiles): one word per tile
   const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-  const uint32_t r0 = 2 * c + 8 * th, s = i >> 2, f0 = 2 * (i & 3);
+  const uint32_t r0 = 2 * c + 8 * th, f0 = 2 * i3;
   float sa[2][2], sb[2][2];  // [row][32-column block]
 #pragma unroll
   for (int jj = 0; jj < 2; ++jj) {
-    const uint4 h = ldg128(G + 8 * w + (16 * s + r0 + jj) * 16);
+    const uint4 h = hr[jj];
     const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
     const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
     const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
@@ -198,19 +202,23 @@ __device__ __forceinline__ void deq_unit_q4k_rows(const uint8_t *G, uint32_t w, 
     }
   }
 }
+__device__ __forceinline__ void deq_unit_q4k_rows(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th,
+                                                  uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t r0 = 2 * (lane & 3) + 8 * th, s = i >> 2;
+  const uint4 qv = ldg128(G + 512 * i + 16 * lane);  // Q4_K slices are whole (4 tiles): one word per tile
+  const uint4 hr[2] = {ldg128(G + 8 * w + (16 * s + r0) * 16), ldg128(G + 8 * w + (16 * s + r0 + 1) * 16)};
+  deq_q4k_vals(qv, hr, i & 3, th, lane, a, n0, k0);
+}
 
 // Q6_K unit: value = d * sc * (q - 32), sc per (row, 16-column sub-block
 // 4i + t), computed in f32 and rounded once to f16.
-__device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
-                                             uint32_t a, uint32_t n0, uint32_t k0) {
-  const uint32_t g = lane >> 2, c = lane & 3, s = i >> 2;
-  const uint32_t nt = min(64u, w - 64 * i) / 16;
+// qv: low-nibble words of tiles 2th, 2th+1; hw: their high-bit word; sa:
+// the f16 d of rows rr[j]; scb[tt][j]: the int8 sub-scale byte of tile
+// 2th + tt, row rr[j]
+__device__ __forceinline__ void deq_q6k_vals(uint2 qv, uint32_t hw, const float (&sa)[4], const uint32_t (&scb)[2][4],
+                                             uint32_t th, uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-  const uint2 qv = ldg64(G + 512 * i + 4 * nt * lane + 8 * th);  // low nibbles: a word per tile
-  const uint32_t hw = ldg32(G + 8 * w + 256 * i + 8 * lane + 4 * th);  // high bit pairs
-  float sa[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) sa[j] = h2f(__ldg(reinterpret_cast<const uint16_t *>(G + 13 * w + (16 * s + rr[j]) * 2)));
 #pragma unroll
   for (uint32_t tt = 0; tt < 2; ++tt) {
     const uint32_t t = 2 * th + tt;
@@ -218,7 +226,7 @@ __device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint3
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       // the int8 sub-scale s as (s + 128) - 128: exact, without the slow I2F path
-      const float sc = u2f_small((uint32_t)__ldg(G + 12 * w + 16 * (4 * i + t) + rr[j]) ^ 0x80u) - 128.0f;
+      const float sc = u2f_small(scb[tt][j] ^ 0x80u) - 128.0f;
       A[j] = sa[j] * sc;
       B[j] = A[j] * 32.0f;
     }
@@ -246,6 +254,23 @@ __device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint3
       }
     }
   }
+}
+__device__ __forceinline__ void deq_unit_q6k(const uint8_t *G, uint32_t w, uint32_t i, uint32_t th, uint32_t lane,
+                                             uint32_t a, uint32_t n0, uint32_t k0) {
+  const uint32_t c = lane & 3, s = i >> 2;
+  const uint32_t nt = min(64u, w - 64 * i) / 16;
+  const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  const uint2 qv = ldg64(G + 512 * i + 4 * nt * lane + 8 * th);  // low nibbles: a word per tile
+  const uint32_t hw = ldg32(G + 8 * w + 256 * i + 8 * lane + 4 * th);  // high bit pairs
+  float sa[4];
+  uint32_t scb[2][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sa[j] = h2f(__ldg(reinterpret_cast<const uint16_t *>(G + 13 * w + (16 * s + rr[j]) * 2)));
+#pragma unroll
+    for (uint32_t tt = 0; tt < 2; ++tt) scb[tt][j] = __ldg(G + 12 * w + 16 * (4 * i + 2 * th + tt) + rr[j]);
+  }
+  deq_q6k_vals(qv, hw, sa, scb, th, lane, a, n0, k0);
 }
 
 // Q8_0 / Q4_0 unit from its code words q (Q8_0: two words per tile; Q4_0:
@@ -356,6 +381,16 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t lds8(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void zero_unit(uint32_t th, uint32_t lane, uint32_t a, uint32_t n0, uint32_t k0) {
   const uint32_t g = lane >> 2, c = lane & 3;
@@ -456,11 +491,118 @@ struct PfCursor {
   }
 };
 
+// The same for launches of mixed types (kPfAny): the warp's group base in
+// the current k-step, the chunk's width and type and the slice index; the
+// fetch picks the unit's bytes by type.
+struct PfCursorAny {
+  const uint8_t *G;
+  uint64_t step;
+  uint32_t k, ks, tt, nt, gi, si, th, lane, w, i, type;
+  bool active;
+  __device__ void tile(const QgParams &p) {
+    if (nt >= p.n_tiles) return;
+    const QgTile tl = p.tiles[nt];
+    const ChunkDesc cd = p.chunks[tl.chunk];
+    i = tl.col0 / 64 + si;
+    w = cd.width;
+    type = cd.type;
+    active = 64 * si < tl.ncols && 2 * th < min(64u, w - 64 * i) / 16;
+    G = p.w + cd.offset + (uint64_t)(4 * ks + gi) * cd.gbytes;
+    step = 4ull * cd.gbytes;
+  }
+  __device__ PfCursorAny(const QgParams &p, uint32_t k0, uint32_t KS, uint32_t t_tiles, uint32_t gi_, uint32_t si_,
+                         uint32_t th_, uint32_t lane_)
+      : gi(gi_), si(si_), th(th_), lane(lane_), active(false) {
+    const uint32_t x = k0 / KS;
+    k = k0;
+    ks = k0 % KS;
+    tt = x % t_tiles;
+    nt = x / t_tiles;
+    tile(p);
+  }
+  __device__ void next(const QgParams &p, uint32_t KS, uint32_t t_tiles) {
+    ++k;
+    if (++ks < KS) {
+      G += step;
+      return;
+    }
+    ks = 0;
+    if (++tt == t_tiles) {
+      tt = 0;
+      ++nt;
+    }
+    tile(p);
+  }
+};
+__device__ __forceinline__ void cpa4(uint32_t dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+// the unit's bytes into slot R (layout per type: see deq_from_slot); type
+// index 0 Q4_K, 1 Q6_K, 2 Q8_0, 3 Q4_0
+__device__ __forceinline__ uint32_t pf_type_index(uint32_t type) {
+  return type == kQ4_K ? 0u : type == kQ6_K ? 1u : type == kQ8_0 ? 2u : 3u;
+}
+__device__ __forceinline__ void fetch_unit(const PfCursorAny &fc, uint32_t R, uint32_t lane) {
+  const uint8_t *G = fc.G;
+  const uint32_t w = fc.w, i = fc.i, th = fc.th, s = i >> 2, nt16 = min(64u, w - 64 * i) / 16;
+  switch (fc.type) {
+    case kQ4_K:  // [0, 512) code words (16 B per lane), [512, 640) headers of rows 8th .. 8th + 7
+      cpa16(R + 16 * lane, G + 512 * i + 16 * lane);
+      if (lane < 8) cpa16(R + 512 + 16 * lane, G + 8 * w + (16 * s + 8 * th + lane) * 16);
+      break;
+    case kQ6_K:  // [0, 256) low words, [256, 384) high words, [384, 416) the 16 rows' d, [416, 448) sub-scales
+      cpa8(R + 8 * lane, G + 512 * i + 4 * nt16 * lane + 8 * th);
+      cpa4(R + 256 + 4 * lane, G + 8 * w + 256 * i + 8 * lane + 4 * th);
+      if (lane < 2) cpa16(R + 384 + 16 * lane, G + 13 * w + 32 * s + 16 * lane);
+      else if (lane < 4) cpa16(R + 416 + 16 * (lane - 2), G + 12 * w + 16 * (4 * i + 2 * th) + 16 * (lane - 2));
+      break;
+    case kQ8_0:  // as the single-type ring
+      cpa16(R + 16 * lane, G + 1024 * i + 8 * nt16 * lane + 16 * th);
+      if (lane < 2) cpa16(R + 512 + 16 * lane, G + 16 * w + 32 * (2 * i + th) + 16 * lane);
+      break;
+    default:
+      cpa8(R + 8 * lane, G + 512 * i + 4 * nt16 * lane + 8 * th);
+      if (lane < 2) cpa16(R + 512 + 16 * lane, G + 8 * w + 32 * (2 * i + th) + 16 * lane);
+      break;
+  }
+}
+// dequantise the unit in slot R (type index ti, slice index & 3 = i3)
+__device__ __forceinline__ void deq_from_slot(uint32_t R, uint32_t ti, uint32_t i3, uint32_t th, uint32_t lane,
+                                              uint32_t a, uint32_t n0, uint32_t k0, uint32_t o0, uint32_t o1) {
+  const uint32_t c = lane & 3;
+  if (ti == 0) {
+    const uint4 qv = lds128(R + 16 * lane);
+    const uint4 hr[2] = {lds128(R + 512 + 32 * c), lds128(R + 512 + 32 * c + 16)};
+    deq_q4k_vals(qv, hr, i3, th, lane, a, n0, k0);
+  } else if (ti == 1) {
+    const uint2 qv = lds64(R + 8 * lane);
+    const uint32_t hw = lds32(R + 256 + 4 * lane);
+    const uint32_t rr[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+    float sa[4];
+    uint32_t scb[2][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sa[j] = h2f((uint16_t)lds16(R + 384 + 2 * rr[j]));
+#pragma unroll
+      for (uint32_t tt = 0; tt < 2; ++tt) scb[tt][j] = lds8(R + 416 + 16 * tt + rr[j]);
+    }
+    deq_q6k_vals(qv, hw, sa, scb, th, lane, a, n0, k0);
+  } else {
+    const uint32_t d01 = lds32(R + 512 + 4 * c), d23 = lds32(R + 512 + 4 * c + 16);
+    if (ti == 2) {
+      deq_pairs_q0<kQ8_0>(lds128(R + 16 * lane), d01, d23, th, a + o0, a + o1);
+    } else {
+      const uint2 v = lds64(R + 8 * lane);
+      deq_pairs_q0<kQ4_0>(make_uint4(v.x, v.y, 0u, 0u), d01, d23, th, a + o0, a + o1);
+    }
+  }
+}
+
 // PT: 0 = the dequant warps load the weights directly; kQ8_0 / kQ4_0 = every
 // chunk has that type and the weights go through the prefetch ring
 template <uint32_t BN, int PT>
 __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const __grid_constant__ CUtensorMap xmap) {
-  constexpr bool PF = PT != 0;
+  constexpr bool PF = PT != 0;  // kQ8_0 / kQ4_0 (single-type ring) or kPfAny
   using C = QCfg<BN, PF>;
   extern __shared__ __align__(1024) uint8_t qsm_raw[];
   const uint32_t raw = smem_u32(qsm_raw), pad = (1024u - (raw & 1023u)) & 1023u;
@@ -579,7 +721,59 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     // ---- dequantisation: unit (group gi, slice si, block th) of every stage ----
     const uint32_t d = warp - 2, gi = d >> 2, si = (d >> 1) & 1, th = d & 1;
     uint32_t s = 0, ph = 1;
-    if constexpr (PF) {
+    if constexpr (PT == kPfAny) {
+      // The unit bytes of k-step j + kPf - 1 are copied (cp.async, one group
+      // per k-step) while k-step j is dequantised; per slot the fetch records
+      // 1 dequantise / 2 zero rows past K / 0 nothing, the type index and
+      // the slice index & 3 (8 bits per slot).
+      static_assert((C::kPf & (C::kPf - 1)) == 0 && C::kPf <= 4, "ring depth");
+      const uint64_t Wk = (uint64_t)p.n_tiles * t_tiles * ksteps;
+      const uint32_t k0 = sk_start(blockIdx.x, Wk, gridDim.x), kend = sk_start(blockIdx.x + 1, Wk, gridDim.x);
+      const uint32_t pf0 = sbase + C::kPfOff + d * kPfWarp;
+      uint32_t o0, o1;
+      q0_store_offsets(lane, 64 * si, 16 * gi, o0, o1);
+      PfCursorAny fc(p, k0, ksteps, t_tiles, gi, si, th, lane);
+      uint32_t fslot = 0, cslot = 0, flags = 0;
+      auto fetch = [&]() {
+        uint32_t f = 0;
+        if (fc.k < kend) {
+          if (fc.active) {
+            if (4 * fc.ks + gi < G16) {
+              fetch_unit(fc, pf0 + fslot * C::kPfStage, lane);
+              f = 1u | (pf_type_index(fc.type) << 2) | ((fc.i & 3u) << 4);
+            } else {
+              f = 2;
+            }
+          }
+          fc.next(p, ksteps, t_tiles);
+        }
+        cpa_commit();
+        flags = (flags & ~(0xFFu << (8 * fslot))) | (f << (8 * fslot));
+        fslot = (fslot + 1) & (C::kPf - 1);
+      };
+#pragma unroll 1
+      for (uint32_t j = 0; j + 1 < C::kPf; ++j) fetch();
+      for (uint32_t n = kend - k0; n; --n) {
+        fetch();
+        cpa_wait<C::kPf - 1>();  // this lane's copies for the k-step have landed
+        __syncwarp();            // ... and every other lane's
+        if (!qwait_warp(&b.empty[s], ph, b)) break;
+        const uint32_t f = (flags >> (8 * cslot)) & 0xFFu, a = sbase + s * C::kStage;
+        if ((f & 3u) == 1u)
+          deq_from_slot(pf0 + cslot * C::kPfStage, (f >> 2) & 3u, (f >> 4) & 3u, th, lane, a, 64 * si, 16 * gi, o0, o1);
+        else if ((f & 3u) == 2u)
+          zero_unit(th, lane, a, 64 * si, 16 * gi);
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b.full_a[s]);
+        if (++s == C::kStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+        cslot = (cslot + 1) & (C::kPf - 1);
+      }
+      cpa_wait<0>();  // no copy may still be writing shared memory when the CTA exits
+    } else if constexpr (PF) {
       // The weight bytes of k-step j + kPf - 1 are copied while k-step j is
       // dequantised (one cp.async group per k-step, empty where the unit has
       // no weights), so each warp has kPf - 1 k-steps of loads in flight.
@@ -799,6 +993,8 @@ int launch_bn(const QgParams &p, const void *tmap, uint32_t grid, cudaStream_t s
     return launch_pdl(k_qgemm<BN, kQ8_0>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
   if (p.prefetch == kQ4_0)
     return launch_pdl(k_qgemm<BN, kQ4_0>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
+  if (p.prefetch == kPfAny)
+    return launch_pdl(k_qgemm<BN, kPfAny>, dim3(grid), dim3(kQThreads), QCfg<BN, true>::kSmem, st, p, *m);
   return launch_pdl(k_qgemm<BN, 0>, dim3(grid), dim3(kQThreads), QCfg<BN, false>::kSmem, st, p, *m);
 }
 template <uint32_t BN, int PT>
@@ -814,7 +1010,8 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 int qgemm_init() {
   if (!set_smem<64, 0>() || !set_smem<128, 0>() || !set_smem<256, 0>() || !set_smem<512, 0>() ||
       !set_smem<64, kQ8_0>() || !set_smem<128, kQ8_0>() || !set_smem<256, kQ8_0>() || !set_smem<512, kQ8_0>() ||
-      !set_smem<64, kQ4_0>() || !set_smem<128, kQ4_0>() || !set_smem<256, kQ4_0>() || !set_smem<512, kQ4_0>())
+      !set_smem<64, kQ4_0>() || !set_smem<128, kQ4_0>() || !set_smem<256, kQ4_0>() || !set_smem<512, kQ4_0>() ||
+      !set_smem<64, kPfAny>() || !set_smem<128, kPfAny>() || !set_smem<256, kPfAny>() || !set_smem<512, kPfAny>())
     return -1;
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;

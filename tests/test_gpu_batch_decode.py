@@ -53,6 +53,9 @@ def path(request, tmp_path_factory):
 @pytest.mark.parametrize("kv_dtype", [L.KV_F16, L.KV_F32])
 def test_batch_decode_matches_oracle(path, cfg, kv_dtype):
     dev = ModelWeights.load_from_gguf(path)
+    # the replay check at the end needs two prefills that leave bit-identical
+    # caches: the fixed-order split-K sums (the default red.add order varies)
+    L.check(L.lib().fa_debug_set(dev._h, L.DEBUG_FIXED_ORDER_SUMS, 1))
     ref = O.Model(path, threads=os.cpu_count() or 4)
     V = dev.config.vocab_size
     lens = [7, 20, 33, 1, 50]
