@@ -171,21 +171,21 @@ __device__ __forceinline__ void deq_q4k_vals(uint4 qv, const uint4 (&hr)[2], uin
                                              uint32_t a, uint32_t n0, uint32_t k0) {
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
-  const uint32_t r0 = 2 * c + 8 * th, f0 = 2 * i3;
+  const uint32_t r0 = 2 * c + 8 * th;
   float sa[2][2], sb[2][2];  // [row][32-column block]
+  // the slice's two 12-bit (sc | m << 6) fields are adjacent: 24 bits at
+  // bit 24 * i3 of the 96-bit field area, one funnel shift (i3 is warp-uniform)
+  const uint32_t fs = (24 * i3) & 31;
 #pragma unroll
   for (int jj = 0; jj < 2; ++jj) {
     const uint4 h = hr[jj];
     const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
     const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-    const unsigned long long lo = ((unsigned long long)h.z << 32) | h.y;
+    const uint32_t F = __funnelshift_r(i3 < 2 ? h.y : (i3 == 2 ? h.z : h.w), i3 < 2 ? h.z : h.w, fs);
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
-      const uint32_t bit = 12 * (f0 + b);
-      const uint32_t fld = bit < 64 ? (uint32_t)((bit + 12 <= 64) ? (lo >> bit) : ((lo >> bit) | ((unsigned long long)h.w << (64 - bit))))
-                                    : (h.w >> (bit - 64));
-      sa[jj][b] = d * u2f_small(fld & 63u);
-      sb[jj][b] = dm * u2f_small((fld >> 6) & 63u);
+      sa[jj][b] = d * u2f_small((F >> (12 * b)) & 63u);
+      sb[jj][b] = dm * u2f_small((F >> (12 * b + 6)) & 63u);
     }
   }
 #pragma unroll
