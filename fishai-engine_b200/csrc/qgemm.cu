@@ -915,9 +915,11 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
           for (int j = 0; j < 32; ++j) {
             const uint32_t t = t0 + c0 + j;
             if (t < p.T) {
-              float *o = wo.whole ? p.out + (size_t)t * p.ldo + col_out + m : slot + (size_t)(c0 + j) * kBM + m;
+              const bool direct = wo.whole || p.red;
+              float *o = direct ? p.out + (size_t)t * p.ldo + col_out + m : slot + (size_t)(c0 + j) * kBM + m;
               const float y = __uint_as_float(v[j]);
-              if (add) *o += y;
+              if (!wo.whole && p.red) atomicAdd(o, y);  // a piece of a split tile: red.add, no fixup
+              else if (add) *o += y;
               else *o = y;
             }
           }
@@ -1043,8 +1045,13 @@ int qgemm_make_xmap(QgXMap *map, const void *x_f16, uint32_t K, uint32_t T_rows,
 
 uint64_t qgemm_part_floats(uint32_t bn, uint32_t n_sm) { return (uint64_t)2 * n_sm * kBM * bn; }
 
-int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
-  if (!p0.T || !p0.n_tiles || p0.K % 16 || !p0.w || !p0.out || p0.ldo % 4) return -1;  // fixup: float4 rows
+int launch_qgemm(const QgParams &p_in, const QgXMap &map, uint32_t n_sm, cudaStream_t st) {
+  if (!p_in.T || !p_in.n_tiles || p_in.K % 16 || !p_in.w || !p_in.out || p_in.ldo % 4) return -1;  // fixup: float4 rows
+  // red.add of split pieces only for 64-token tiles: a piece is 8K values
+  // there (decode batches), but 64K in a 512-token pair, where the atomics
+  // cost more than the fixup launch (measured: 2048-token prefill -16%)
+  QgParams p0 = p_in;
+  if (map.bn > 64) p0.red = 0;
   // more than one 256-token tile: token-tile pairs (one dequantised weight
   // stage per 512 tokens) over the same 256-row TMA boxes
   const uint32_t bn = (map.bn == 256 && p0.T > 256) ? 512 : map.bn;
@@ -1060,7 +1067,7 @@ int launch_qgemm(const QgParams &p0, const QgXMap &map, uint32_t n_sm, cudaStrea
     case 512: rc = launch_bn<512>(p0, map.bytes, grid, st); break;
     default: return -1;
   }
-  if (rc || grid < 2) return rc;
+  if (rc || grid < 2 || p0.red) return rc;
   return launch_pdl(k_qg_fixup, dim3(grid - 1, bn * kBM / 1024), dim3(256), 0, st, p0, bn, grid);
 }
 
