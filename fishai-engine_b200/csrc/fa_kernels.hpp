@@ -273,14 +273,18 @@ int launch_embed_rows(const void *emb, int type, const uint32_t *tok, uint32_t T
                       uint32_t *err, cudaStream_t st);
 int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, uint32_t d, void *out, uint32_t *err,
                        cudaStream_t st);
-int launch_rope_kv_rows(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                         uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
                         void *qh, uint32_t *err, cudaStream_t st);
 int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st);
-int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st);
+// clear: the gate/up rows read are left zero (the batched-decode GEMMs add
+// their split tiles into that buffer by red.add)
+int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st,
+                       bool clear = false);
 int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st);
 // batched decode: per-row RoPE + KV append (row r = cache sequence seq0 + r at
-// states[r].pos / .len, q -> qf f32), f32 -> f16 with the range flag, and the
+// states[r].pos / .len, q -> qf f32; the q|k|v rows read are left zero for
+// the next step's red.add GEMM), f32 -> f16 with the range flag, and the
 // per-step bookkeeping (positions + 1, ids -> hist[step][r], step + 1)
 int launch_rope_kv_batch(float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,

@@ -1102,9 +1102,6 @@ int Model::ensure_prefill_ws(uint32_t cap) {
   if (tp.rank > 0) w.Y = (float *)dmalloc((size_t)cap * d * 4);
   if (!w.tok || !w.err || !w.X || !w.QKV || !w.GU || !w.Xn || !w.Qh || !w.Ob || !w.Hb || (tp.rank > 0 && !w.Y))
     return fail(FA_ERR_OOM, "prefill workspace allocation failed");
-  // the token GEMMs add split tiles into these; the row kernels keep them zero
-  CUDA_TRY(cudaMemsetAsync(w.QKV, 0, (size_t)cap * qkv_n * 4, stream));
-  CUDA_TRY(cudaMemsetAsync(w.GU, 0, (size_t)cap * gu_n * 4, stream));
   const uint32_t bns[3] = {64, 128, 256};
   for (int b = 0; b < 3; ++b)
     if (qgemm_make_xmap(&w.mxn[b], w.Xn, d, cap, bns[b]) || qgemm_make_xmap(&w.mob[b], w.Ob, qd, cap, bns[b]) ||
@@ -1139,9 +1136,10 @@ int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *ou
   p.epi = epi;
   p.err = pws.err;
   p.prefetch = P.qg_prefetch;
-  // split tiles by red.add into a destination that is zero (store: the row
-  // kernels clear what they read) or the residual; one rank only (the
-  // partial-sum buffers of tensor-parallel ranks are not kept zero)
+  // split tiles by red.add into a destination that is zero (store: the
+  // batched-decode row kernels clear what they read) or the residual; one
+  // rank only (the partial-sum buffers of tensor-parallel ranks are not kept
+  // zero); the launcher keeps it to 64-token tiles
   p.red = red && tp.world == 1 && !dbg_fixed_order ? 1u : 0u;
   return launch_qgemm(p, map, (uint32_t)n_sm, stream) ? fail(FA_ERR_CUDA, "token GEMM launch failed") : FA_OK;
 }
@@ -1167,7 +1165,7 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
       const LayerW &lw = layers[l];
       if (launch_norm_rows_h(pws.X, lw.attn_norm, cfg.norm_eps, T, d, pws.Xn, pws.err, stream))
         return fail(FA_ERR_CUDA, "norm launch failed");
-      if ((rc = run_qgemm(lw.qkv, pws.mxn[b], T, pws.QKV, qkv_n, kQgStore, true))) return rc;
+      if ((rc = run_qgemm(lw.qkv, pws.mxn[b], T, pws.QKV, qkv_n, kQgStore))) return rc;
       if (launch_rope_kv_rows(pws.QKV, T, Hq, Hkv, hd, rope_tab, rope_max, pos0, len0, kvv, seq, l, pws.Qh, pws.err,
                               stream))
         return fail(FA_ERR_CUDA, "rope launch failed");
@@ -1188,14 +1186,14 @@ int Model::prefill_tc(KvCache &kv, uint32_t seq, const uint32_t *toks, uint32_t 
       // theirs in Y; the all-reduce leaves X + sum on every rank
       float *o_dst = tp.rank > 0 ? pws.Y : pws.X;
       const int o_epi = tp.rank > 0 ? kQgStore : kQgResid;
-      if ((rc = run_qgemm(lw.o, pws.mob[b], T, o_dst, d, o_epi, true))) return rc;
+      if ((rc = run_qgemm(lw.o, pws.mob[b], T, o_dst, d, o_epi))) return rc;
       if (tp.world > 1 && (rc = tp_reduce(pws.X, pws.Y, (size_t)T * d))) return rc;
       if (launch_norm_rows_h(pws.X, lw.ffn_norm, cfg.norm_eps, T, d, pws.Xn, pws.err, stream))
         return fail(FA_ERR_CUDA, "norm launch failed");
-      if ((rc = run_qgemm(lw.gateup, pws.mxn[b], T, pws.GU, gu_n, kQgStore, true))) return rc;
+      if ((rc = run_qgemm(lw.gateup, pws.mxn[b], T, pws.GU, gu_n, kQgStore))) return rc;
       if (launch_swiglu_rows(pws.GU, T, F, lw.gateup.CW, pws.Hb, pws.err, stream))
         return fail(FA_ERR_CUDA, "swiglu launch failed");
-      if ((rc = run_qgemm(lw.down, pws.mhb[b], T, o_dst, d, o_epi, true))) return rc;
+      if ((rc = run_qgemm(lw.down, pws.mhb[b], T, o_dst, d, o_epi))) return rc;
       if (tp.world > 1 && (rc = tp_reduce(pws.X, pws.Y, (size_t)T * d))) return rc;
     }
   }
@@ -1301,7 +1299,7 @@ int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams
     if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
       return fail(FA_ERR_CUDA, "norm launch failed");
     if ((rc = run_qgemm(lw.gateup, bws.mxn, b, bws.GU, gu_n, kQgStore, true))) return rc;
-    if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream))
+    if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream, true))
       return fail(FA_ERR_CUDA, "swiglu launch failed");
     if ((rc = run_qgemm(lw.down, bws.mhb, b, o_dst, d, o_epi, true))) return rc;
     if (tp.world > 1 && (rc = tp_reduce(bws.X, bws.Y, (size_t)b * d))) return rc;

@@ -105,21 +105,15 @@ __global__ void k_norm_rows_h(const float *x, const float *w, float eps, uint32_
 }
 
 // one CTA per token; rows of QKV: [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)]
-__global__ void k_rope_kv_rows(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+__global__ void k_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                uint32_t rope_max, uint32_t pos0, uint32_t len0, KvView kv, uint32_t seq, uint32_t layer,
                                __half *qh, uint32_t *err) {
   pdl_enter();
   const uint32_t t = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
-  float *row = qkv + (size_t)t * (qd + 2 * kd);
+  const float *row = qkv + (size_t)t * (qd + 2 * kd);
   const uint32_t pos = pos0 + t, slot = len0 + t;
-  // the row is left zero for the next token GEMM's red.adds (every path)
-  auto clear_row = [&]() {
-    __syncthreads();
-    for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) row[j] = 0.0f;
-  };
   if (pos >= rope_max || slot / 16 >= kv.max_pages) {
     if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
-    clear_row();
     return;
   }
   const float *cs = rope + (size_t)pos * hd;
@@ -143,23 +137,21 @@ __global__ void k_rope_kv_rows(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv
       else reinterpret_cast<float *>(kv.base)[idx] = v;
     }
   }
-  clear_row();
 }
 
 // The same with four elements per work unit (hd % 4 == 0): a q or k head's
 // unit is dims (d, d + 1) and their rotation partners (d + hd/2, d + hd/2 + 1)
 // for d even < hd/2 (one float4 of cos/sin), a v unit four consecutive dims;
 // paired loads and stores, the same per-element rounding.
-__global__ void k_rope_kv_rows4(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd,
+__global__ void k_rope_kv_rows4(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd,
                                 const float *rope, uint32_t rope_max, uint32_t pos0, uint32_t len0, KvView kv,
                                 uint32_t seq, uint32_t layer, __half *qh, uint32_t *err) {
   pdl_enter();
   const uint32_t t = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
-  float *row = qkv + (size_t)t * (qd + 2 * kd);
+  const float *row = qkv + (size_t)t * (qd + 2 * kd);
   const uint32_t pos = pos0 + t, slot = len0 + t;
   if (pos >= rope_max || slot / 16 >= kv.max_pages) {
     if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
-    for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) row[j] = 0.0f;  // zero for the next red.adds
     return;
   }
   const float *cs = rope + (size_t)pos * hd;
@@ -175,9 +167,6 @@ __global__ void k_rope_kv_rows4(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hk
       const uint32_t head = u / upr, dd = 2 * (u % upr), hb = head * hd;
       const float2 x = *reinterpret_cast<const float2 *>(row + hb + dd);
       const float2 y = *reinterpret_cast<const float2 *>(row + hb + dd + half);
-      // each element is read by one unit: left zero for the next token GEMM's red.adds
-      *reinterpret_cast<float2 *>(row + hb + dd) = make_float2(0.0f, 0.0f);
-      *reinterpret_cast<float2 *>(row + hb + dd + half) = make_float2(0.0f, 0.0f);
       const float4 c = *reinterpret_cast<const float4 *>(cs + 2 * dd);  // cos, sin of dd and dd + 1
       const float a0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(y.x, c.y));
       const float a1 = __fsub_rn(__fmul_rn(x.y, c.z), __fmul_rn(y.y, c.w));
@@ -195,7 +184,6 @@ __global__ void k_rope_kv_rows4(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hk
     } else {
       const uint32_t kc = 4 * (u - n_rot);
       const float4 v = *reinterpret_cast<const float4 *>(row + qd + kd + kc);
-      *reinterpret_cast<float4 *>(row + qd + kd + kc) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       const uint64_t idx = lbase + kv_index(page, 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
       put2(idx, v.x, v.y);
       put2(idx + 2, v.z, v.w);
@@ -683,15 +671,17 @@ __global__ void __launch_bounds__(128, 3) k_attn_decode_rows(const AttnParams p,
 
 // gate/up launch space: chunk c (width w_c) holds gate f in [c*CW/2, +w_c/2)
 // at c*CW + local, then the same up columns
-__global__ void k_swiglu_rows(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
+__global__ void k_swiglu_rows(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err, uint32_t clear) {
   pdl_enter();
   const uint32_t t = blockIdx.y, f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= F) return;
   const uint32_t c = f / (CW / 2), local = f - c * (CW / 2), wc = min(CW, 2 * F - c * CW);
   float *row = gu + (size_t)t * 2 * F;
   const float gv = row[c * CW + local], uv = row[c * CW + wc / 2 + local];
-  row[c * CW + local] = 0.0f;  // left zero for the next token GEMM's red.adds
-  row[c * CW + wc / 2 + local] = 0.0f;
+  if (clear) {  // left zero for the next token GEMM's red.adds
+    row[c * CW + local] = 0.0f;
+    row[c * CW + wc / 2 + local] = 0.0f;
+  }
   const float v = gv * (1.0f / (1.0f + expf(-gv))) * uv;
   if (!(fabsf(v) <= kHalfMax) && err) atomicOr(err, kErrRange);
   h[(size_t)t * F + f] = __float2half_rn(v);
@@ -700,7 +690,7 @@ __global__ void k_swiglu_rows(float *gu, uint32_t F, uint32_t CW, __half *h, uin
 // The same, four consecutive columns per thread (F % 4 == 0, CW % 32 == 0:
 // the four stay inside one chunk half and the loads are float4-aligned),
 // streaming loads, one 8-byte store; the same per-element arithmetic.
-__global__ void k_swiglu_rows4(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
+__global__ void k_swiglu_rows4(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err, uint32_t clear) {
   pdl_enter();
   const uint32_t t = blockIdx.y, f = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (f >= F) return;
@@ -708,8 +698,10 @@ __global__ void k_swiglu_rows4(float *gu, uint32_t F, uint32_t CW, __half *h, ui
   float *row = gu + (size_t)t * 2 * F + (size_t)c * CW + local;
   const float4 g4 = __ldcs(reinterpret_cast<const float4 *>(row));
   const float4 u4 = __ldcs(reinterpret_cast<const float4 *>(row + wc / 2));
-  *reinterpret_cast<float4 *>(row) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // left zero for the next red.adds
-  *reinterpret_cast<float4 *>(row + wc / 2) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (clear) {  // left zero for the next token GEMM's red.adds
+    *reinterpret_cast<float4 *>(row) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    *reinterpret_cast<float4 *>(row + wc / 2) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
   const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
   float v[4];
   bool bad = false;
@@ -950,7 +942,7 @@ int launch_norm_rows_h(const float *x, const float *w, float eps, uint32_t T, ui
                        cudaStream_t st) {
   return launch_pdl(k_norm_rows_h, dim3(T), dim3(256), 0, st, x, w, eps, d, (__half *)out, err);
 }
-int launch_rope_kv_rows(float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                         uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
                         void *qh, uint32_t *err, cudaStream_t st) {
   const auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
@@ -966,10 +958,12 @@ int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
   if (p.hd == 64) return p.kv.f16 ? launch_attn_hd<64, true>(p, st) : launch_attn_hd<64, false>(p, st);
   return -1;
 }
-int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
+int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st,
+                       bool clear) {
+  const uint32_t c = clear ? 1u : 0u;
   if (F % 4 == 0 && CW % 32 == 0 && reinterpret_cast<uintptr_t>(gu) % 16 == 0 && reinterpret_cast<uintptr_t>(h) % 8 == 0)
-    return launch_pdl(k_swiglu_rows4, dim3((F / 4 + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
-  return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
+    return launch_pdl(k_swiglu_rows4, dim3((F / 4 + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err, c);
+  return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err, c);
 }
 int launch_rope_kv_batch(float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,

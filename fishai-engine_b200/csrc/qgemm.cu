@@ -905,23 +905,31 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
       const bool mine = m < tl.ncols;
       // a whole tile goes to the output; a piece of a split tile to the
       // CTA's partial slot ([token][column] within the tile)
-      const bool add = wo.whole && p.epi == kQgResid;
+      // per tile one of three stores: the output (+= for a residual
+      // launch), a piece into the CTA's partial slot, or (red launches) a
+      // piece added into the output by red.add
+      const int mode = wo.whole ? (p.epi == kQgResid ? 1 : 0) : (p.red ? 3 : 2);
       float *slot = p.part + (size_t)(2 * blockIdx.x + (wo.first ? 0 : 1)) * kBM * BN;
+      float *obase = mode == 2 ? slot + m : p.out + (size_t)t0 * p.ldo + col_out + m;
+      const size_t ostride = mode == 2 ? kBM : p.ldo;
+      const uint32_t tn = p.T > t0 ? min(BN, p.T - t0) : 0u;  // valid tokens of the tile
       for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((32 * q4) << 16) + acc * BN + c0, v);
         if (mine) {
+          float *o = obase + (size_t)c0 * ostride;
+          if (mode == 1) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint32_t t = t0 + c0 + j;
-            if (t < p.T) {
-              const bool direct = wo.whole || p.red;
-              float *o = direct ? p.out + (size_t)t * p.ldo + col_out + m : slot + (size_t)(c0 + j) * kBM + m;
-              const float y = __uint_as_float(v[j]);
-              if (!wo.whole && p.red) atomicAdd(o, y);  // a piece of a split tile: red.add, no fixup
-              else if (add) *o += y;
-              else *o = y;
-            }
+            for (uint32_t j = 0; j < 32; ++j)
+              if (c0 + j < tn) o[(size_t)j * ostride] += __uint_as_float(v[j]);
+          } else if (mode == 3) {
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j)
+              if (c0 + j < tn) atomicAdd(o + (size_t)j * ostride, __uint_as_float(v[j]));
+          } else {
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j)
+              if (c0 + j < tn) o[(size_t)j * ostride] = __uint_as_float(v[j]);
           }
         }
       }
