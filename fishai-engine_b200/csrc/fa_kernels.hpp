@@ -247,6 +247,8 @@ struct QgParams {
                              // kPfAny: any mix of the MMA types through the same ring; 0: direct loads
   uint32_t red;              // 1: the pieces of split tiles are added into out by red.add (out holds zeros for
                              // kQgStore, the residual for kQgResid) and no fixup launch runs; 0: partial slots + fixup
+  float *zero;               // optional: cleared by the epilogue warps after the wait for the previous kernel
+  uint64_t n_zero;           // floats at `zero` (multiple of 4)
 };
 constexpr uint32_t kPfAny = 1;  // QgParams::prefetch: mixed-type prefetch ring
 struct QgXMap {              // TMA tensor map of an f16 activation buffer X[T_rows][K]
@@ -277,16 +279,12 @@ int launch_rope_kv_rows(const float *qkv, uint32_t T, uint32_t Hq, uint32_t Hkv,
                         uint32_t rope_max, uint32_t pos0, uint32_t len0, const KvView &kv, uint32_t seq, uint32_t layer,
                         void *qh, uint32_t *err, cudaStream_t st);
 int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st);
-// clear: the gate/up rows read are left zero (the batched-decode GEMMs add
-// their split tiles into that buffer by red.add)
-int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st,
-                       bool clear = false);
+int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st);
 int launch_last_row(const float *X, uint32_t row, uint32_t d, float *x, float *ssq, uint32_t n_ssq, cudaStream_t st);
 // batched decode: per-row RoPE + KV append (row r = cache sequence seq0 + r at
-// states[r].pos / .len, q -> qf f32; the q|k|v rows read are left zero for
-// the next step's red.add GEMM), f32 -> f16 with the range flag, and the
+// states[r].pos / .len, q -> qf f32), f32 -> f16 with the range flag, and the
 // per-step bookkeeping (positions + 1, ids -> hist[step][r], step + 1)
-int launch_rope_kv_batch(float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st);
 // batched decode attention on the tensor cores (mma.sync): grid (splits,

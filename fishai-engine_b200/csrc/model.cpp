@@ -1121,7 +1121,8 @@ int Model::ensure_qg_part(uint64_t floats) {
   return FA_OK;
 }
 
-int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi, bool red) {
+int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi, bool red,
+                     float *zero, uint64_t n_zero) {
   QgParams p{};
   p.part = qg_part;
   p.part_floats = qg_part_floats;
@@ -1136,11 +1137,13 @@ int Model::run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *ou
   p.epi = epi;
   p.err = pws.err;
   p.prefetch = P.qg_prefetch;
-  // split tiles by red.add into a destination that is zero (store: the
-  // batched-decode row kernels clear what they read) or the residual; one
+  // split tiles by red.add into a destination that is zero (store: a later
+  // batched-decode GEMM clears it, see `zero`) or the residual; one
   // rank only (the partial-sum buffers of tensor-parallel ranks are not kept
   // zero); the launcher keeps it to 64-token tiles
   p.red = red && tp.world == 1 && !dbg_fixed_order ? 1u : 0u;
+  p.zero = zero;
+  p.n_zero = n_zero;
   return launch_qgemm(p, map, (uint32_t)n_sm, stream) ? fail(FA_ERR_CUDA, "token GEMM launch failed") : FA_OK;
 }
 
@@ -1247,7 +1250,7 @@ int Model::ensure_batch_ws(uint32_t b) {
       !w.err || !w.step || !w.states)
     return fail(FA_ERR_OOM, "batched decode workspace allocation failed");
   CUDA_TRY(cudaMemset(w.counters, 0, (size_t)b * KVH * 4));
-  // the token GEMMs add split tiles into these; the row kernels keep them zero
+  // the token GEMMs add split tiles into these; the o / down GEMMs clear them
   CUDA_TRY(cudaMemset(w.QKV, 0, (size_t)b * qkv_n * 4));
   CUDA_TRY(cudaMemset(w.GU, 0, (size_t)b * gu_n * 4));
   const uint32_t bn = b <= 64 ? 64 : b <= 128 ? 128 : 256;
@@ -1294,14 +1297,16 @@ int Model::enqueue_batch_step(const KvCache &kv, uint32_t b, const SamplerParams
     if (launch_attn_decode_rows(ap, stream)) return fail(FA_ERR_CUDA, "batched attention launch failed");
     float *o_dst = tp.rank > 0 ? bws.Y : bws.X;  // as in prefill_tc
     const int o_epi = tp.rank > 0 ? kQgStore : kQgResid;
-    if ((rc = run_qgemm(lw.o, bws.moh, b, o_dst, d, o_epi, true))) return rc;
+    // o clears q|k|v (read by the RoPE kernel before it) for the next layer's
+    // qkv red.adds; down clears gate/up (read by SwiGLU) likewise
+    if ((rc = run_qgemm(lw.o, bws.moh, b, o_dst, d, o_epi, true, bws.QKV, (uint64_t)b * qkv_n))) return rc;
     if (tp.world > 1 && (rc = tp_reduce(bws.X, bws.Y, (size_t)b * d))) return rc;
     if (launch_norm_rows_h(bws.X, lw.ffn_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))
       return fail(FA_ERR_CUDA, "norm launch failed");
     if ((rc = run_qgemm(lw.gateup, bws.mxn, b, bws.GU, gu_n, kQgStore, true))) return rc;
-    if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream, true))
+    if (launch_swiglu_rows(bws.GU, b, F, lw.gateup.CW, bws.Hb, bws.err, stream))
       return fail(FA_ERR_CUDA, "swiglu launch failed");
-    if ((rc = run_qgemm(lw.down, bws.mhb, b, o_dst, d, o_epi, true))) return rc;
+    if ((rc = run_qgemm(lw.down, bws.mhb, b, o_dst, d, o_epi, true, bws.GU, (uint64_t)b * gu_n))) return rc;
     if (tp.world > 1 && (rc = tp_reduce(bws.X, bws.Y, (size_t)b * d))) return rc;
   }
   if (launch_norm_rows_h(bws.X, out_norm, cfg.norm_eps, b, d, bws.Xn, bws.err, stream))

@@ -138,8 +138,10 @@ struct Model {
   bool want_tc_prefill = false, tc_ok = false;
   PrefillWs pws;
   int ensure_prefill_ws(uint32_t cap);
-  // red: split tiles by red.add (out kept zero by its consumer, or the residual)
-  int run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi, bool red = false);
+  // red: split tiles by red.add (into a zeroed out, or the residual); zero:
+  // a buffer the launch clears after its wait for the previous kernel
+  int run_qgemm(const GemvPlan &P, const QgXMap &map, uint32_t T, float *out, uint32_t ldo, int epi, bool red = false,
+                float *zero = nullptr, uint64_t n_zero = 0);
   // prompt tokens [0, n) at positions start_pos.., appended after the cache's
   // current length; leaves the last token's logits in ws.logits and the
   // argmax in ws.state->argmax_key

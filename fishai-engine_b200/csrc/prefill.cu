@@ -671,17 +671,13 @@ __global__ void __launch_bounds__(128, 3) k_attn_decode_rows(const AttnParams p,
 
 // gate/up launch space: chunk c (width w_c) holds gate f in [c*CW/2, +w_c/2)
 // at c*CW + local, then the same up columns
-__global__ void k_swiglu_rows(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err, uint32_t clear) {
+__global__ void k_swiglu_rows(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
   pdl_enter();
   const uint32_t t = blockIdx.y, f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= F) return;
   const uint32_t c = f / (CW / 2), local = f - c * (CW / 2), wc = min(CW, 2 * F - c * CW);
-  float *row = gu + (size_t)t * 2 * F;
+  const float *row = gu + (size_t)t * 2 * F;
   const float gv = row[c * CW + local], uv = row[c * CW + wc / 2 + local];
-  if (clear) {  // left zero for the next token GEMM's red.adds
-    row[c * CW + local] = 0.0f;
-    row[c * CW + wc / 2 + local] = 0.0f;
-  }
   const float v = gv * (1.0f / (1.0f + expf(-gv))) * uv;
   if (!(fabsf(v) <= kHalfMax) && err) atomicOr(err, kErrRange);
   h[(size_t)t * F + f] = __float2half_rn(v);
@@ -690,18 +686,14 @@ __global__ void k_swiglu_rows(float *gu, uint32_t F, uint32_t CW, __half *h, uin
 // The same, four consecutive columns per thread (F % 4 == 0, CW % 32 == 0:
 // the four stay inside one chunk half and the loads are float4-aligned),
 // streaming loads, one 8-byte store; the same per-element arithmetic.
-__global__ void k_swiglu_rows4(float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err, uint32_t clear) {
+__global__ void k_swiglu_rows4(const float *gu, uint32_t F, uint32_t CW, __half *h, uint32_t *err) {
   pdl_enter();
   const uint32_t t = blockIdx.y, f = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (f >= F) return;
   const uint32_t hw = CW / 2, c = f / hw, local = f - c * hw, wc = min(CW, 2 * F - c * CW);
-  float *row = gu + (size_t)t * 2 * F + (size_t)c * CW + local;
+  const float *row = gu + (size_t)t * 2 * F + (size_t)c * CW + local;
   const float4 g4 = __ldcs(reinterpret_cast<const float4 *>(row));
   const float4 u4 = __ldcs(reinterpret_cast<const float4 *>(row + wc / 2));
-  if (clear) {  // left zero for the next token GEMM's red.adds
-    *reinterpret_cast<float4 *>(row) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    *reinterpret_cast<float4 *>(row + wc / 2) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  }
   const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
   float v[4];
   bool bad = false;
@@ -735,29 +727,20 @@ __global__ void k_last_row(const float *X, uint32_t row, uint32_t d, float *x, f
 // ---- batched decode: row r is cache sequence seq0 + r at its own position ----
 // The same with the four-element units of k_rope_kv_rows4 (hd % 4 == 0),
 // grid (rows, unit blocks): one unit per thread, q kept in f32.
-__global__ void k_rope_kv_batch4(float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+__global__ void k_rope_kv_batch4(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                  uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
                                  float *qf, uint32_t *err) {
   pdl_enter();
   const uint32_t r = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
   const uint32_t upr = half / 2, n_rot = (Hq + Hkv) * upr, n_units = n_rot + kd / 4;
   const uint32_t u = blockIdx.y * blockDim.x + threadIdx.x;
-  float *row = qkv + (size_t)r * (qd + 2 * kd);
+  const float *row = qkv + (size_t)r * (qd + 2 * kd);
   const uint32_t pos = st[r].pos, slot = st[r].len;
-  if (u >= n_units) return;
-  // the unit's elements are read by this thread only: left zero for the next
-  // token GEMM's red.adds, on every path
-  float *ux = u < n_rot ? row + (u / upr) * hd + 2 * (u % upr) : row + qd + kd + 4 * (u - n_rot);
   if (pos >= rope_max || slot / 16 >= kv.max_pages) {
     if (u == 0 && err) atomicOr(err, kErrContext);
-    if (u < n_rot) {
-      *reinterpret_cast<float2 *>(ux) = make_float2(0.0f, 0.0f);
-      *reinterpret_cast<float2 *>(ux + half) = make_float2(0.0f, 0.0f);
-    } else {
-      *reinterpret_cast<float4 *>(ux) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
     return;
   }
+  if (u >= n_units) return;
   const uint32_t page = kv.page_table[(seq0 + r) * kv.max_pages + slot / 16];
   const uint64_t lbase = (uint64_t)layer * kv.layer_stride;
   auto put2 = [&](uint64_t idx, float a, float b) {  // two consecutive cache elements
@@ -768,8 +751,6 @@ __global__ void k_rope_kv_batch4(float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t
     const uint32_t head = u / upr, dd = 2 * (u % upr), hb = head * hd;
     const float2 x = *reinterpret_cast<const float2 *>(row + hb + dd);
     const float2 y = *reinterpret_cast<const float2 *>(row + hb + dd + half);
-    *reinterpret_cast<float2 *>(ux) = make_float2(0.0f, 0.0f);
-    *reinterpret_cast<float2 *>(ux + half) = make_float2(0.0f, 0.0f);
     const float4 c = *reinterpret_cast<const float4 *>(rope + (size_t)pos * hd + 2 * dd);  // cos, sin of dd, dd + 1
     const float a0 = __fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(y.x, c.y));
     const float a1 = __fsub_rn(__fmul_rn(x.y, c.z), __fmul_rn(y.y, c.w));
@@ -787,28 +768,21 @@ __global__ void k_rope_kv_batch4(float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t
   } else {
     const uint32_t kc = 4 * (u - n_rot);
     const float4 v = *reinterpret_cast<const float4 *>(row + qd + kd + kc);
-    *reinterpret_cast<float4 *>(ux) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     const uint64_t idx = lbase + kv_index(page, 1, kc / hd, slot % 16, kc % hd, kv.n_kv, hd);
     put2(idx, v.x, v.y);
     put2(idx + 2, v.z, v.w);
   }
 }
 
-__global__ void k_rope_kv_batch(float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+__global__ void k_rope_kv_batch(const float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                                 uint32_t rope_max, const SeqState *st, KvView kv, uint32_t seq0, uint32_t layer,
                                 float *qf, uint32_t *err) {
   pdl_enter();
   const uint32_t r = blockIdx.x, half = hd / 2, qd = Hq * hd, kd = Hkv * hd;
-  float *row = qkv + (size_t)r * (qd + 2 * kd);
+  const float *row = qkv + (size_t)r * (qd + 2 * kd);
   const uint32_t pos = st[r].pos, slot = st[r].len;
-  // the row is left zero for the next token GEMM's red.adds (every path)
-  auto clear_row = [&]() {
-    __syncthreads();
-    for (uint32_t j = threadIdx.x; j < qd + 2 * kd; j += blockDim.x) row[j] = 0.0f;
-  };
   if (pos >= rope_max || slot / 16 >= kv.max_pages) {
     if (threadIdx.x == 0 && err) atomicOr(err, kErrContext);
-    clear_row();
     return;
   }
   const float *cs = rope + (size_t)pos * hd;
@@ -853,7 +827,6 @@ __global__ void k_rope_kv_batch(float *qkv, uint32_t Hq, uint32_t Hkv, uint32_t 
       }
     }
   }
-  clear_row();
 }
 
 // after the sampler: positions advance, the sampled ids (already the next
@@ -958,14 +931,12 @@ int launch_attn_rows(const AttnRowsParams &p, cudaStream_t st) {
   if (p.hd == 64) return p.kv.f16 ? launch_attn_hd<64, true>(p, st) : launch_attn_hd<64, false>(p, st);
   return -1;
 }
-int launch_swiglu_rows(float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st,
-                       bool clear) {
-  const uint32_t c = clear ? 1u : 0u;
+int launch_swiglu_rows(const float *gu, uint32_t T, uint32_t F, uint32_t CW, void *h, uint32_t *err, cudaStream_t st) {
   if (F % 4 == 0 && CW % 32 == 0 && reinterpret_cast<uintptr_t>(gu) % 16 == 0 && reinterpret_cast<uintptr_t>(h) % 8 == 0)
-    return launch_pdl(k_swiglu_rows4, dim3((F / 4 + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err, c);
-  return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err, c);
+    return launch_pdl(k_swiglu_rows4, dim3((F / 4 + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
+  return launch_pdl(k_swiglu_rows, dim3((F + 255) / 256, T), dim3(256), 0, st, gu, F, CW, (__half *)h, err);
 }
-int launch_rope_kv_batch(float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
+int launch_rope_kv_batch(const float *qkv, uint32_t b, uint32_t Hq, uint32_t Hkv, uint32_t hd, const float *rope,
                          uint32_t rope_max, const SeqState *states, const KvView &kv, uint32_t seq0, uint32_t layer,
                          float *qf, uint32_t *err, cudaStream_t st) {
   const auto a16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };

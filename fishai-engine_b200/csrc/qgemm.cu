@@ -895,6 +895,12 @@ __global__ void __launch_bounds__(kQThreads, 1) k_qgemm(const QgParams p, const 
     const uint32_t q4 = warp & 3, m = 32 * q4 + lane;
     uint32_t acc = 0, aph = 0;
     pdl_wait();
+    if (p.zero) {  // this CTA's share of the buffer the launch clears (the epilogue warps are idle until the first tile)
+      const uint64_t n4 = p.n_zero / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+      const uint64_t z0 = min(n4, (uint64_t)blockIdx.x * per), z1 = min(n4, z0 + per);
+      for (uint64_t i = z0 + (tid - kEpi0 * 32); i < z1; i += 128)
+        reinterpret_cast<float4 *>(p.zero)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     SegIter it(blockIdx.x, gridDim.x, p.n_tiles, t_tiles, ksteps);
     Seg wo;
     while (it.next(wo)) {
