@@ -37,6 +37,18 @@ def test_library_exports_every_declared_symbol():
     assert b"sm_100a" in lib.fa_version()
 
 
+def test_python_constants_match_header():
+    """Every #define FA_* of the C header has the same value in the ctypes
+    mirror (status codes, ggml types, KV dtypes, debug keys)."""
+    hdr = open(os.path.join(ROOT, "include", "fishai_cuda.h")).read()
+    defs = {m.group(1): int(m.group(2)) for m in re.finditer(r"^#define FA_([A-Z0-9_]+) \(?(-?\d+)\)?", hdr, re.M)}
+    assert len(defs) >= 20
+    for name, val in defs.items():
+        py = name[len("GGML_"):] if name.startswith("GGML_") else name
+        assert hasattr(L, py), name
+        assert getattr(L, py) == val, (name, getattr(L, py), val)
+
+
 def test_gguf_minimal(tmp_path):  # src/gguf.rs:1041-1097
     g = GGUFFile.open(_write(tmp_path, "m.gguf", gb.minimal_gguf()))
     assert g.version == 3 and g.alignment == 32 and g.tensor_names() == ["test.weight"]
