@@ -544,6 +544,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     }
   };
   load_batch(0);
+  float inv_self = 0.0f;  // the norm factor when this CTA summed the squares itself
   if (norm && p.n_ssq == 0) {
     // no sum-of-squares partials (x is the result of a tensor-parallel
     // all-reduce): each consumer thread squares its float4 share of x, the
@@ -566,12 +567,12 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
     if (lane == 0) sm.red[warp] = s;
     epi::consumer_bar<kWarps>();
-    if (tid == 0) {
-      float t = 0.0f;
-      for (uint32_t w = 0; w < (uint32_t)kWarps; ++w) t += sm.red[w];
-      sm.red[96] = 1.0f / sqrtf(t / (float)p.K + p.eps);
-    }
-    epi::consumer_bar<kWarps>();
+    // every thread adds the warps' sums in warp order itself (the same value
+    // everywhere), so no second barrier is needed before x is normalised
+    float t = 0.0f;
+#pragma unroll
+    for (uint32_t w = 0; w < (uint32_t)kWarps; ++w) t += sm.red[w];
+    inv_self = 1.0f / sqrtf(t / (float)p.K + p.eps);
   } else if (norm) {
     if (warp == 0) {  // lane-strided partial sums in index order, every load in flight
       float s = 0.0f;
@@ -592,7 +593,7 @@ __device__ __forceinline__ void consume(const GemvParams &p, uint32_t cta, const
     epi::consumer_bar<kWarps>();
   }
   {
-    const float inv = norm ? sm.red[96] : 1.0f;
+    const float inv = norm ? (p.n_ssq == 0 ? inv_self : sm.red[96]) : 1.0f;
     for (uint32_t base = 0; base < nx; base += kPre * NT) {
       if (base) load_batch(base);
 #pragma unroll
