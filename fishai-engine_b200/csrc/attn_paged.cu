@@ -20,6 +20,12 @@
 // unnormalised o) goes to global memory; either the consumer combines the
 // splits (the o projection's kProAttn prologue, partials_only) or the last
 // split CTA of the kv head does, in split order.
+// Raw form (qkv_raw, the decode step): q, k and v of this token arrive as the
+// qkv launch's red.add sums; each CTA rotates q and the new k (RoPE, half
+// split) in registers, the CTA whose range ends at position len writes the
+// new k / v into its copy of the last tile before use and appends them to
+// the cache at the end, so every tile can be requested before the wait for
+// the qkv launch.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 

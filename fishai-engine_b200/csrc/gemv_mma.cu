@@ -24,9 +24,11 @@
 // RMSNorm prologue); each of the 16 consumer warps owns one 64-column slice
 // of the 1024-wide chunk, builds the B coefficients of its slice for the stage
 // in a private table and runs 4 (Q6_K: 8) MMAs per group.
-// At the end of its rows of a chunk a CTA publishes the chunk partial; the last
-// CTA to arrive sums the partials in a fixed order and runs the fused
-// epilogue (gemv_epi.cuh).
+// At the end of its rows of a chunk a CTA either adds its piece straight into
+// the destination with one vector red.add per lane (kEpiRed, the decode
+// step's form: the epilogue work moves into the next launch's prologue), or
+// publishes the chunk partial and the last CTA to arrive sums the partials in
+// a fixed order and runs the fused epilogue (gemv_epi.cuh).
 #include "gemv_mma.cuh"
 
 namespace fa {
