@@ -1,6 +1,6 @@
 """Parity of the sm_100a path (through the C ABI) against the oracle, the C
-restatement of the reference CPU path.  Tolerances (from the north-star
-parity criteria): dequantised blocks bit-exact; hidden states and logits
+restatement of the reference CPU path.  Tolerances (the project's parity
+criteria): dequantised blocks bit-exact; hidden states and logits
 max-abs-rel <= 1e-4 on the f32 path; greedy ids identical."""
 import os
 
