@@ -4,7 +4,7 @@
  * CPU restatement of the fishai-engine reference CPU path (a Rust crate that
  * cannot be compiled in this image: no cargo/rustc).  Only tests/, the
  * __graft_entry__ smoke check and bench.py's CPU-baseline leg may load this
- * library, and only as the checker or as the timed CPU baseline; the product
+ * library, and only as the test oracle or as the timed CPU baseline; the product
  * (fishai-engine_b200/) never links or calls it.
  *
  * Every function cites the reference file:line whose behaviour it restates.

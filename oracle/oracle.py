@@ -3,7 +3,7 @@
 ctypes front end to oracle/build/liboracle.so, the C restatement of the
 fishai-engine reference CPU path (see fa_oracle.h for the deviations D1-D4).
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
-this module, and only as the checker or the timed CPU baseline.
+this module, and only as the test oracle or the timed CPU baseline.
 """
 from __future__ import annotations
 
